@@ -1,0 +1,269 @@
+"""numpy restatement of the reference NVFP4 quantisers (test infrastructure only).
+
+Every function cites the reference lines it restates (paths relative to the
+reference project root).  All arithmetic is float32 with IEEE round-to-nearest
+(numpy's float32 ``/``, ``*``, ``+`` and ``np.rint`` are correctly rounded,
+exactly like the reference's eager torch CPU ops), so outputs are bit-exact.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+FLT_MAX = np.float32(3.402823466e38)
+FLT_MIN_NORMAL = np.float32(1.17549435e-38)
+
+# src/mcl4_coe/nvfp4.py:160-165 — magnitudes of the 8 E2M1 codes.
+E2M1_LEVELS = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0], dtype=np.float32)
+
+
+def round_up(value: int, multiple: int) -> int:
+    """src/mcl4_coe/nvfp4.py:45-46."""
+    return (value + multiple - 1) // multiple * multiple
+
+
+# --------------------------------------------------------------------------
+# float8 e4m3fn and bfloat16 conversions (the torch CPU semantics the
+# reference relies on through ``.to(torch.float8_e4m3fn)`` / ``.to(bf16)``).
+# --------------------------------------------------------------------------
+
+def f32_to_e4m3(x: np.ndarray) -> np.ndarray:
+    """float32 -> float8_e4m3fn bit patterns, round-to-nearest-even.
+
+    Restates PyTorch's c10 ``fp8e4m3fn_from_fp32_value`` (used by
+    ``.to(torch.float8_e4m3fn)`` at src/mcl4_coe/nvfp4.py:215 and :931):
+    magnitudes >= 480 become NaN (0x7F); magnitudes below 2**-6 round to a
+    multiple of 2**-9 (subnormal codes 0..8); the rest round the fp32
+    mantissa to 3 bits with ties to even.
+    """
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    bits = x.view(np.uint32)
+    sign = ((bits >> np.uint32(24)) & np.uint32(0x80)).astype(np.uint8)
+    mag_bits = bits & np.uint32(0x7FFFFFFF)
+    mag = mag_bits.view(np.float32)
+    out = np.zeros(x.shape, dtype=np.uint8)
+    nan_or_big = mag_bits >= np.uint32(1087 << 20)  # >= 480.0 or NaN
+    small = mag_bits < np.uint32(121 << 23)  # < 2**-6
+    normal = ~(nan_or_big | small)
+    out[nan_or_big] = 0x7F
+    out[small] = np.rint(mag[small] * np.float32(512.0)).astype(np.uint8)
+    nb = mag_bits[normal]
+    odd = (nb >> np.uint32(20)) & np.uint32(1)
+    r = (nb + np.uint32(0x7FFFF) + odd) >> np.uint32(20)
+    out[normal] = (r - np.uint32((127 - 7) << 3)).astype(np.uint8)
+    return out | sign
+
+
+def e4m3_to_f32(codes: np.ndarray) -> np.ndarray:
+    """float8_e4m3fn bit patterns -> float32 (exact)."""
+    c = np.asarray(codes, dtype=np.uint8)
+    sign = np.where((c & 0x80) != 0, np.float32(-1.0), np.float32(1.0))
+    e = ((c >> 3) & 0x0F).astype(np.int32)
+    m = (c & 0x07).astype(np.float32)
+    val = np.where(e == 0, m * np.float32(2.0 ** -9),
+                   (np.float32(1.0) + m / np.float32(8.0)) * np.exp2(e - 7).astype(np.float32))
+    val = np.where((c & 0x7F) == 0x7F, np.float32(np.nan), val)
+    return (sign * val).astype(np.float32)
+
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """float32 -> bfloat16 bit patterns with round-to-nearest-even (torch ``.to(bf16)``)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    b = x.view(np.uint32).astype(np.uint64)
+    rounded = ((b + np.uint64(0x7FFF) + ((b >> np.uint64(16)) & np.uint64(1))) >> np.uint64(16)).astype(np.uint16)
+    nan = np.isnan(x)
+    if nan.any():
+        rounded = rounded.copy()
+        rounded[nan] = ((b[nan] >> np.uint64(16)) | np.uint64(0x40)).astype(np.uint16)
+    return rounded
+
+
+def bf16_bits_to_f32(b: np.ndarray) -> np.ndarray:
+    return (np.asarray(b, dtype=np.uint16).astype(np.uint32) << np.uint32(16)).view(np.float32)
+
+
+def round_bf16(x: np.ndarray) -> np.ndarray:
+    """float32 -> nearest bfloat16 value, returned as float32."""
+    return bf16_bits_to_f32(f32_to_bf16_bits(x))
+
+
+# --------------------------------------------------------------------------
+# E2M1 code rounding and the quantisers.
+# --------------------------------------------------------------------------
+
+def e2m1_codes(values: np.ndarray) -> np.ndarray:
+    """src/mcl4_coe/nvfp4.py:186-194 (deterministic branch).
+
+    ``m = min(|v|, 6)``; ``u = 2m`` (m <= 2), ``m + 2`` (m <= 4) else
+    ``0.5 m + 4``, each step rounded to float32; ``code = rint(u)`` (ties to
+    even) or'ed with ``signbit(v) << 3`` (so ``-0.0`` maps to code 8).
+    """
+    v = np.asarray(values, dtype=np.float32)
+    m = np.minimum(np.abs(v), np.float32(6.0))
+    u = np.where(m <= np.float32(2.0), m * np.float32(2.0),
+                 np.where(m <= np.float32(4.0), m + np.float32(2.0),
+                          m * np.float32(0.5) + np.float32(4.0)))
+    code = np.rint(u).astype(np.uint8)
+    return code | (np.signbit(v).astype(np.uint8) << np.uint8(3))
+
+
+def _pack_codes(codes: np.ndarray) -> np.ndarray:
+    """src/mcl4_coe/nvfp4.py:224 — even column in the low nibble."""
+    return (codes[..., 0::2] | (codes[..., 1::2] << np.uint8(4))).astype(np.uint8)
+
+
+def _inverse_decoding(decoding: np.ndarray) -> np.ndarray:
+    """src/mcl4_coe/nvfp4.py:217-221: ``1/dec`` clamped to FLT_MAX, 0 where dec <= 0."""
+    with np.errstate(divide="ignore", over="ignore", invalid="ignore"):
+        inv = np.minimum(np.float32(1.0) / decoding, FLT_MAX)
+    return np.where(decoding > 0, inv, np.float32(0.0)).astype(np.float32)
+
+
+def quantize_nvfp4_core(values: np.ndarray, two_dimensional: bool, causal_row_scale: bool):
+    """src/mcl4_coe/nvfp4.py:197-225 (``stochastic=False``).
+
+    Returns ``(packed uint8 [R, C/2], block_scales e4m3 bits [R, C/16],
+    global_scale float32 [1])``.  With ``two_dimensional`` the scale is shared
+    by each 16x16 tile and repeated over its 16 rows (:210-212); with
+    ``causal_row_scale`` (and 1-D blocks) the global scale is 1 (:204-205).
+    """
+    values = np.ascontiguousarray(values, dtype=np.float32)
+    rows, cols = values.shape
+    if causal_row_scale and not two_dimensional:
+        g = np.ones(1, dtype=np.float32)
+    else:
+        amax = np.abs(values).max() if values.size else np.float32(0.0)
+        g = np.where(amax > 0, np.float32(amax) / np.float32(2688.0), np.float32(1.0))
+        g = np.maximum(g, FLT_MIN_NORMAL).astype(np.float32).reshape(1)
+    absv = np.abs(values)
+    if two_dimensional:
+        tile = absv.reshape(rows // 16, 16, cols // 16, 16).max(axis=(1, 3))
+        block_amax = np.repeat(tile, 16, axis=0)
+    else:
+        block_amax = absv.reshape(rows, cols // 16, 16).max(axis=-1)
+    denom = np.float32(6.0) * g[0]
+    scales = f32_to_e4m3(np.minimum(block_amax / denom, np.float32(448.0)))
+    decoding = e4m3_to_f32(scales) * g[0]
+    inv = _inverse_decoding(decoding)
+    normalized = (values.reshape(rows, cols // 16, 16) * inv[..., None]).reshape(rows, cols)
+    codes = e2m1_codes(normalized)
+    return _pack_codes(codes), scales, g
+
+
+def quantize_activations(x: np.ndarray):
+    """Activation mode used by the MoE path: 1x16 row blocks, global scale 1.
+
+    src/mcl4_coe/nvfp4.py:197-225 with ``two_dimensional=False,
+    causal_row_scale=True`` — the math of the Triton kernel launched at
+    src/mcl4_coe/nvfp4.py:1074-1086 (whose only divergence, ``-0.0`` getting
+    code 0 instead of 8 at :731, is not followed: the torch core is the oracle).
+    """
+    packed, scales, _ = quantize_nvfp4_core(x, False, True)
+    return packed, scales
+
+
+def quantize_grouped_weights(w_batch: np.ndarray):
+    """src/mcl4_coe/nvfp4.py:923-952 (``_quantize_grouped_weights_core``).
+
+    ``w_batch`` float32 ``[D, N, K]``.  Returns ``(b_fwd [D, K/2, N],
+    bs_fwd [D, N, K/16], bg [D], b_bwd [D, N/2, K], bs_bwd [D, K, N/16])`` with
+    the e4m3 scales as uint8 bit patterns.  One float32 scale per expert
+    (``amax/2688``, :928-929); one e4m3 scale per 16x16 tile (:930-931).
+    """
+    w = np.ascontiguousarray(w_batch, dtype=np.float32)
+    d, n, k = w.shape
+    w_abs = np.abs(w)
+    amax = w_abs.reshape(d, -1).max(axis=1)
+    bg = np.where(amax > 0, amax / np.float32(2688.0), np.float32(1.0))
+    bg = np.maximum(bg, FLT_MIN_NORMAL).astype(np.float32)
+    block_amax = w_abs.reshape(d, n // 16, 16, k // 16, 16).max(axis=(2, 4))
+    denom = (np.float32(6.0) * bg).reshape(d, 1, 1)
+    bs_tiles = f32_to_e4m3(np.minimum(block_amax / denom, np.float32(448.0)))
+
+    bs_fwd = np.repeat(bs_tiles, 16, axis=1)  # [d, n, k/16]
+    inv_fwd = _inverse_decoding(e4m3_to_f32(bs_fwd) * bg.reshape(d, 1, 1))
+    norm_fwd = (w.reshape(d, n, k // 16, 16) * inv_fwd[..., None]).reshape(d, n, k)
+    b_fwd = np.ascontiguousarray(_pack_codes(e2m1_codes(norm_fwd)).transpose(0, 2, 1))
+
+    w_t = np.ascontiguousarray(w.transpose(0, 2, 1))
+    bs_bwd = np.repeat(bs_tiles.transpose(0, 2, 1), 16, axis=1)  # [d, k, n/16]
+    inv_bwd = _inverse_decoding(e4m3_to_f32(bs_bwd) * bg.reshape(d, 1, 1))
+    norm_bwd = (w_t.reshape(d, k, n // 16, 16) * inv_bwd[..., None]).reshape(d, k, n)
+    b_bwd = np.ascontiguousarray(_pack_codes(e2m1_codes(norm_bwd)).transpose(0, 2, 1))
+    return b_fwd, np.ascontiguousarray(bs_fwd), bg, b_bwd, np.ascontiguousarray(bs_bwd)
+
+
+# --------------------------------------------------------------------------
+# Scale swizzle (cuBLASLt / tcgen05 block-scale atom) and dequantisation.
+# --------------------------------------------------------------------------
+
+def swizzle_scales(scales: np.ndarray) -> np.ndarray:
+    """src/mcl4_coe/nvfp4.py:131-144: 128-row x 4-scale atoms, inner 32x4x4.
+
+    Element ``(r, c)`` lands at byte
+    ``((r//128) * Cp/4 + c//4) * 512 + (r%32) * 16 + ((r%128)//32) * 4 + c%4``.
+    """
+    s = np.asarray(scales, dtype=np.uint8)
+    rows, cols = s.shape
+    rp, cp = round_up(rows, 128), round_up(cols, 4)
+    padded = np.zeros((rp, cp), dtype=np.uint8)
+    padded[:rows, :cols] = s
+    return np.ascontiguousarray(
+        padded.reshape(rp // 128, 4, 32, cp // 4, 4).transpose(0, 3, 2, 1, 4).reshape(rp, cp))
+
+
+def unswizzle_scales(swizzled: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    """src/mcl4_coe/nvfp4.py:147-156 (bit patterns instead of float32)."""
+    s = np.asarray(swizzled, dtype=np.uint8)
+    rp, cp = s.shape
+    return np.ascontiguousarray(
+        s.reshape(rp // 128, cp // 4, 32, 4, 4).transpose(0, 3, 2, 1, 4).reshape(rp, cp)[:rows, :cols])
+
+
+def decode_codes(packed: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    """Unpack E2M1 nibbles to float32 values (src/mcl4_coe/nvfp4.py:271-278)."""
+    raw = np.asarray(packed, dtype=np.uint8)
+    c0 = raw & 0x0F
+    c1 = (raw >> 4) & 0x0F
+    codes = np.stack((c0, c1), axis=-1).reshape(rows, cols)
+    sign = np.where((codes & 0x08) != 0, np.float32(-1.0), np.float32(1.0))
+    return (sign * E2M1_LEVELS[codes & 0x07]).astype(np.float32)
+
+
+def dequantize(packed: np.ndarray, scales_rowmajor: np.ndarray, g, rows: int, cols: int) -> np.ndarray:
+    """src/mcl4_coe/nvfp4.py:263-281 with row-major (unswizzled) scales."""
+    vals = decode_codes(packed, rows, cols)
+    dec = e4m3_to_f32(scales_rowmajor) * np.float32(np.asarray(g, dtype=np.float32).reshape(-1)[0])
+    return (vals.reshape(rows, cols // 16, 16) * dec[..., None]).reshape(rows, cols).astype(np.float32)
+
+
+def fake_quantize_activations(x: np.ndarray) -> np.ndarray:
+    """Quantise-then-dequantise rows of ``x`` (1x16 blocks, g = 1)."""
+    rows, cols = x.shape
+    packed, scales = quantize_activations(x)
+    return dequantize(packed, scales, np.float32(1.0), rows, cols)
+
+
+def dequantize_grouped_weight(b_fwd: np.ndarray, bs_fwd: np.ndarray, bg: np.ndarray, e: int) -> np.ndarray:
+    """Dense float32 ``[N, K]`` weight of expert ``e`` from the reference cache layout."""
+    kh, n = b_fwd.shape[1], b_fwd.shape[2]
+    packed_nk = np.ascontiguousarray(b_fwd[e].T)  # [N, K/2]
+    return dequantize(packed_nk, bs_fwd[e], bg[e], n, 2 * kh)
+
+
+# --------------------------------------------------------------------------
+# The kernel-side ("MMA") layout of the same bytes.
+# --------------------------------------------------------------------------
+
+def weights_to_mma_layout(b_fwd: np.ndarray, bs_fwd: np.ndarray):
+    """Reference cache layout -> the layout the tcgen05 kernels read.
+
+    Packed codes become K-major ``[E, N, K/2]`` (``b_fwd.transpose``); the
+    per-16 scales of each expert are swizzled into 128x4 atoms
+    (:func:`swizzle_scales`), giving ``[E, N/128 * K/64 * 512]`` bytes.  The
+    bytes themselves are unchanged.
+    """
+    e, kh, n = b_fwd.shape
+    packed = np.ascontiguousarray(b_fwd.transpose(0, 2, 1))
+    sw = np.stack([swizzle_scales(bs_fwd[i]).reshape(-1) for i in range(e)])
+    return packed, sw
