@@ -1,0 +1,357 @@
+#!/usr/bin/env python
+"""NVFP4 MoE-layer tokens/s on B200 — the reference's headline metric.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl ours|reference]
+
+One step = one forward of the MoE layer (router top-k, permutation + NVFP4
+activation quantisation, grouped gate/up GEMM with fused SwiGLU, grouped down
+GEMM, weighted combine) over T tokens of synthetic input resident in HBM.
+Default workload: the OLMoE-style headline configuration (configs[2]:
+T=32768, d=2048, E=64, top-8, F=1024).  Synthetic data: x ~ N(0,1) bf16,
+router and expert weights ~ N(0, 0.02) fp32, quantised to NVFP4 once (the
+quantised-weight cache is reused across steps, as in the reference).
+
+Multi-GPU (torchrun, one process per GPU): weak scaling, every rank runs the
+full layer on its own T tokens with a replica of all experts (no collective on
+the data path); the expert-parallel layout is not used by this bench.
+
+``--impl reference`` times the reference path's CPU implementation (the numpy
+restatement in ``oracle/``) on this host's cores, rank 0 only, on a bounded
+token sample per step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+METRIC = "NVFP4 MoE-layer tokens/s"
+UNIT = "tokens/s"
+
+CONFIGS = {
+    "c0": dict(name="c0_cpu_runnable", seed=0, t=2048, d=256, e=8, k=2, f=512),
+    "c1": dict(name="c1_mitotic", seed=1, t=16384, d=1024, e=32, k=4, f=512),
+    "c2": dict(name="c2_olmoe_prefill", seed=2, t=32768, d=2048, e=64, k=8, f=1024),
+    "c3": dict(name="c3_granite_zipf", seed=3, t=65536, d=1536, e=32, k=8, f=512, zipf=True),
+    "c4": dict(name="c4_decode", seed=4, t=64, d=2048, e=64, k=8, f=1024),
+}
+KERNELS_PER_FORWARD = 6  # router, route-scan, permute+quantise, gate/up GEMM, down GEMM, combine
+
+
+def load_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return dict(hbm_gbs=float(d["hbm_gbs"]), bf16=float(d["bf16_tflops"]),
+                    bf16_sustained=float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), source="measured")
+    return dict(hbm_gbs=6650.0, bf16=1590.0, bf16_sustained=1400.0, source="fallback")
+
+
+# ---------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples nvidia-smi clocks / throttle reasons of one GPU while the timed region runs."""
+
+    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str):
+        self.uuid = uuid
+        self.proc = None
+        self.tmp = None
+
+    def start(self):
+        try:
+            self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "100"], stdout=self.tmp, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.tmp.flush()
+        rows = [ln.split(", ") for ln in Path(self.tmp.name).read_text().splitlines() if ln.strip()]
+        os.unlink(self.tmp.name)
+        mine = [r for r in rows if len(r) >= 9 and self.uuid and self.uuid in r[0]]
+        if not mine:
+            return None
+        def num(v):
+            try:
+                return float(v)
+            except ValueError:
+                return float("nan")
+        loaded = [r for r in mine if num(r[4]) >= 50.0] or mine
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for r in loaded for n, v in zip(names, r[5:9]) if v.strip() == "Active"})
+        return {"sm_mhz": statistics.median(num(r[1]) for r in loaded), "sm_max_mhz": num(loaded[0][2]),
+                "power_w_max": max(num(r[3]) for r in loaded), "samples_under_load": len(loaded),
+                "reasons": reasons}
+
+
+# ---------------------------------------------------------------------------- our arm
+def build_layer(pkg, cfg, device, rank):
+    import torch
+
+    g = torch.Generator(device=device)
+    g.manual_seed(cfg["seed"])
+    moe = pkg.SparseMoE(pkg.MoEConfig(d_model=cfg["d"], expert_hidden_dim=cfg["f"], num_experts=cfg["e"],
+                                      top_k=cfg["k"])).to(device)
+    with torch.no_grad():
+        moe.router.weight.copy_(torch.randn(moe.router.weight.shape, generator=g, device=device) * 0.02)
+        for ex in moe.experts:
+            ex.up_proj.weight.copy_(torch.randn(ex.up_proj.weight.shape, generator=g, device=device) * 0.02)
+            ex.down_proj.weight.copy_(torch.randn(ex.down_proj.weight.shape, generator=g, device=device) * 0.02)
+    if cfg.get("zipf"):
+        moe.router_logit_bias = (2.0 * torch.log(1.0 / torch.arange(1, cfg["e"] + 1, device=device,
+                                                                      dtype=torch.float32)))
+    gx = torch.Generator(device=device)
+    gx.manual_seed(cfg["seed"] * 1000 + 17 + rank)
+    x = torch.randn((cfg["t"], cfg["d"]), generator=gx, device=device).to(torch.bfloat16)
+    moe.requires_grad_(False)
+    return moe, x
+
+
+def cpu_baseline_ours(moe, x, cfg, sample: int) -> dict:
+    """The oracle (numpy restatement of the reference path) on a token sample, on this host."""
+    import torch
+
+    sys.path.insert(0, str(ROOT))
+    from oracle import moe_ref, nvfp4_ref as nr
+
+    pkg = sys.modules["mcl4coe_b200"]
+    experts = moe_ref.QuantizedExperts.__new__(moe_ref.QuantizedExperts)
+    deq = {}
+    for proj in ("up_proj", "down_proj"):
+        ref = pkg.export_reference_cache(moe.experts, proj)
+        b = ref["B_fwd"].cpu().numpy()
+        s = ref["Bs_fwd"].view(torch.uint8).cpu().numpy()
+        gsc = ref["Bg"].cpu().numpy()
+        deq[proj] = [nr.dequantize_grouped_weight(b, s, gsc, e) for e in range(cfg["e"])]
+    experts.up, experts.dn = deq["up_proj"], deq["down_proj"]
+    xs = x[:sample].float().cpu().numpy()
+    wr = moe.router.weight.detach().float().cpu().numpy()
+    bias = None if moe.router_logit_bias is None else moe.router_logit_bias.cpu().numpy()
+    moe_ref.moe_forward(xs[:8], wr, experts, cfg["k"], True, None, bias)  # warm-up
+    times = []
+    for _ in range(3):
+        t0 = time.perf_counter()
+        moe_ref.moe_forward(xs, wr, experts, cfg["k"], True, None, bias)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {"value": sample / t, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{sample} tokens of {cfg['name']} per run, median of 3 runs, numpy/BLAS on all host threads"}
+
+
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, str(ROOT))
+    from __graft_entry__ import load_package
+
+    pkg = load_package()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch with torchrun for N > 1")
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    cfg = CONFIGS[args.config]
+    T, d, E, k, F = cfg["t"], cfg["d"], cfg["e"], cfg["k"], cfg["f"]
+    moe, x = build_layer(pkg, cfg, dev, rank)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    K, W = args.steps, args.warmup
+    with torch.inference_mode():
+        for _ in range(W):
+            moe(x)
+        torch.cuda.synchronize()
+        # stage events: 6 per step, recorded once beforehand so their handles exist
+        stage_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(K)]
+        for evs in stage_ev:
+            for ev in evs:
+                ev.record()
+        torch.cuda.synchronize()
+        uuid = str(torch.cuda.get_device_properties(dev).uuid)
+        sampler = ClockSampler(uuid).start()
+        time.sleep(0.3)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize()
+        start.record()
+        for i in range(K):
+            moe.stage_events = stage_ev[i]
+            moe(x)
+        end.record()
+        torch.cuda.synchronize()
+        barrier()
+        moe.stage_events = None
+        clocks = sampler.stop()
+        elapsed_ms = max_over_ranks(start.elapsed_time(end))
+        stage_ms = [statistics.mean(evs[j].elapsed_time(evs[j + 1]) for evs in stage_ev) for j in range(5)]
+
+        # end to end through the public API with host buffers
+        x_host = x.cpu().pin_memory()
+        out_host = torch.empty((T, d), dtype=torch.bfloat16).pin_memory()
+        stats_host = torch.empty((3,), dtype=torch.float32).pin_memory()
+        x_dev = torch.empty_like(x)
+        for _ in range(max(1, W)):
+            x_dev.copy_(x_host, non_blocking=True)
+            o, aux, z, _ = moe(x_dev)
+            out_host.copy_(o, non_blocking=True)
+        torch.cuda.synchronize()
+        e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize()
+        e_start.record()
+        for _ in range(K):
+            x_dev.copy_(x_host, non_blocking=True)
+            o, aux, z, _ = moe(x_dev)
+            out_host.copy_(o, non_blocking=True)
+            stats_host[0:1].copy_(aux.reshape(1), non_blocking=True)
+            stats_host[1:2].copy_(z.reshape(1), non_blocking=True)
+        e_end.record()
+        torch.cuda.synchronize()
+        barrier()
+        e2e_ms = max_over_ranks(e_start.elapsed_time(e_end))
+
+    ms_per_step = elapsed_ms / K
+    value = T * world / (ms_per_step / 1e3)
+    peaks = load_peaks()
+    fp4_peak = 4.0 * peaks["bf16"]  # dense FP4 = 4x dense BF16 on Blackwell (9 vs 2.25 PFLOP/s nominal)
+    gemm1_flops = 4.0 * T * k * d * F
+    achieved = gemm1_flops / (stage_ms[2] / 1e3) / 1e12
+    traffic = None
+    tp = ROOT / "profiles" / "traffic.json"
+    if tp.exists():
+        traffic = json.loads(tp.read_text()).get(args.config, {}).get("gateup_gemm_bytes")
+    layer_tflops = 6.0 * T * k * d * F / (ms_per_step / 1e3) / 1e12
+    result = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "nvfp4 (e2m1 + e4m3/16) x nvfp4 -> fp32 accumulate, bf16 I/O, fp32 router",
+        "data": "synthetic (x~N(0,1) bf16, weights~N(0,0.02) fp32 quantised to NVFP4, seeded torch RNG on device)",
+        "config": {"workload": cfg["name"], "tokens_per_gpu": T, "d_model": d, "num_experts": E, "top_k": k,
+                   "expert_ffn": F, "parallelism": "replicas" if world > 1 else "single",
+                   "l2": "no flush: x (%.0f MB) and NVFP4 weights (%.0f MB) exceed the 126 MB L2" % (
+                       T * d * 2 / 1e6, E * 3 * d * F * (0.5 + 1 / 16) / 1e6)},
+        "stages_ms": dict(zip(("route", "permute_quant", "gateup_gemm", "down_gemm", "combine"),
+                              [round(s, 4) for s in stage_ms])),
+        "layer_fp4_tflops": layer_tflops,
+        "roofline": {"bound": "tensor", "kernel": "grouped_gemm_fp4 (gate/up, SwiGLU+requant epilogue)",
+                     "achieved": achieved, "peak": fp4_peak, "unit": "TFLOP/s", "frac": achieved / fp4_peak,
+                     "traffic": traffic,
+                     "peak_source": f"4 x {peaks['source']} dense bf16 {peaks['bf16']} TFLOP/s "
+                                    "(MEASURED_PEAKS.json; FP4 dense = 4x BF16 dense)"},
+        "e2e": {"value": T * world / (e2e_ms / K / 1e3), "unit": UNIT, "h2d_bytes_per_step": T * d * 2,
+                "d2h_bytes_per_step": T * d * 2 + 8},
+        "gpu_launches": KERNELS_PER_FORWARD * K,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline_ours(moe, x, cfg, args.cpu_sample)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------- reference arm
+def run_reference(args) -> None:
+    """The reference path's CPU implementation (oracle port), rank 0 only."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    sys.path.insert(0, str(ROOT))
+    from oracle import moe_ref
+
+    cfg = CONFIGS[args.config]
+    T, d, E, k, F = cfg["t"], cfg["d"], cfg["e"], cfg["k"], cfg["f"]
+    r = np.random.Generator(np.random.PCG64(cfg["seed"]))
+    wr = (r.standard_normal((E, d), dtype=np.float32) * 0.02).astype(np.float32)
+    w_up = (r.standard_normal((E, 2 * F, d), dtype=np.float32) * 0.02).astype(np.float32)
+    w_dn = (r.standard_normal((E, d, F), dtype=np.float32) * 0.02).astype(np.float32)
+    experts = moe_ref.QuantizedExperts(w_up, w_dn)  # weight quantisation: cached, not timed (as in the reference)
+    del w_up, w_dn
+    bias = (2.0 * np.log(1.0 / np.arange(1, E + 1))).astype(np.float32) if cfg.get("zipf") else None
+    sample = min(T, args.cpu_sample)
+    x = r.standard_normal((T, d), dtype=np.float32)
+    times = []
+    for i in range(args.warmup + args.steps):
+        lo = (i * sample) % max(1, T - sample + 1)
+        xs = x[lo:lo + sample]
+        t0 = time.perf_counter()
+        moe_ref.moe_forward(xs, wr, experts, k, True, None, bias)
+        if i >= args.warmup:
+            times.append(time.perf_counter() - t0)
+    step = statistics.mean(times)
+    value = sample / step
+    res = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": step * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32 math on NVFP4-dequantised operands",
+        "data": "synthetic (numpy PCG64, same shapes and distributions)",
+        "config": {"workload": cfg["name"], "tokens_per_gpu": T, "d_model": d, "num_experts": E, "top_k": k,
+                   "expert_ffn": F, "parallelism": "host cpu"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+                         "sample": f"{sample} tokens of {cfg['name']} per step (numpy restatement of the "
+                                   "reference SparseMoE forward on dequantised NVFP4, all host threads)"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(res), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    ap.add_argument("--cpu-sample", type=int, default=256)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,185 @@
+/*
+ * mcl4moe — C ABI of the B200 (sm_100a) NVFP4 SwiGLU mixture-of-experts layer.
+ *
+ * Plain C: raw device pointers, sizes and a CUDA stream.  Nothing here
+ * allocates device memory: every buffer, including scratch ("workspace"), is
+ * owned and passed in by the caller.  Every function returns an int status
+ * (MCL4MOE_OK == 0) and never aborts the process; kernels are launched on the
+ * given stream and run asynchronously unless stated otherwise.
+ *
+ * Reference: mESmaC/MCL4-COE, src/mcl4_coe/nvfp4.py and
+ * src/mcl4_coe/backbone.py.  Each entry point names the reference function it
+ * replaces.
+ *
+ * Data formats (identical bytes to the reference quantiser):
+ *   NVFP4 value  : E2M1 code, 4 bits; two per byte, even element in the low nibble.
+ *   block scale  : float8 e4m3fn per 16 consecutive K elements (per 16x16 tile
+ *                  for weights, repeated over the tile's 16 rows).
+ *   global scale : float32; 1.0 for activations, amax/2688 per expert for weights.
+ *   "swizzled" scales: the 128-row x 4-scale atoms of the reference's
+ *                  _swizzle_scales (nvfp4.py:131-144): scale (r, c) of a matrix
+ *                  with C scales per row sits at byte
+ *                  ((r/128)*(C/4) + c/4)*512 + (r%32)*16 + ((r%128)/32)*4 + c%4.
+ *   Weights, kernel layout: packed codes K-major [E, N, K/2] (the transpose of
+ *                  the reference cache's B_fwd [E, K/2, N]) + swizzled scales
+ *                  [E, N*K/16] + global scales [E].
+ */
+#ifndef MCL4MOE_H_
+#define MCL4MOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same object as cudaStream_t / CUstream; NULL is the legacy default stream. */
+typedef struct CUstream_st* mcl4moe_stream_t;
+
+enum mcl4moe_status {
+  MCL4MOE_OK = 0,
+  MCL4MOE_ERR_INVALID = 1,      /* bad shape, null pointer or misalignment (the reference raises ValueError) */
+  MCL4MOE_ERR_UNSUPPORTED = 2,  /* not an sm_100 device, or a shape outside the kernels' tiling */
+  MCL4MOE_ERR_CUDA = 3,         /* a CUDA runtime call or kernel launch failed */
+  MCL4MOE_ERR_TIMEOUT = 4,      /* a device-side wait gave up; see mcl4moe_read_error */
+  MCL4MOE_ERR_WORKSPACE = 5     /* workspace smaller than the matching *_workspace_size */
+};
+
+/* Human-readable name of a status code (static storage). */
+const char* mcl4moe_status_string(int status);
+
+/* ABI version, major*10000 + minor*100 + patch. */
+int mcl4moe_version(void);
+
+/* 1 when the current CUDA device can run the kernels (compute capability 10.x). */
+int mcl4moe_device_supported(void);
+
+/* Synchronise ``stream`` and read then clear the device error word that the
+ * kernels set when a bounded device-side wait gives up (0 = no error; 1xx =
+ * TMA producer, 2xx = MMA issuer, 3xx = epilogue).  Blocking. */
+int mcl4moe_read_error(int32_t* device_error_word, int32_t* host_value, mcl4moe_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Weight quantisation.
+ * Replaces _quantize_grouped_weights_core (src/mcl4_coe/nvfp4.py:923-952)
+ * and the dirty-expert refresh of _get_or_build_grouped_nvfp4_cache
+ * (src/mcl4_coe/nvfp4.py:1010-1044).
+ *
+ * Quantises ``n`` fp32 weight matrices W_i [N, K] (host array of device
+ * pointers; row-major, contiguous) into slots ``slots[i]`` (host array) of
+ * the kernel-layout cache: packed [E, N, K/2], scales [E, Np*K/16] (swizzled,
+ * Np = N rounded up to 128; the padding rows are not written), global_scale [E].  The optional ref_* outputs (NULL to skip) receive the
+ * reference cache layout at the same slots: B_fwd [E, K/2, N],
+ * Bs_fwd [E, N, K/16], B_bwd [E, N/2, K], Bs_bwd [E, K, N/16].
+ * amax_scratch: device float32 [n].  Requires N % 16 == 0, K % 64 == 0.
+ * ------------------------------------------------------------------------ */
+int mcl4moe_quantize_weights(const float* const* w_ptrs, const int32_t* slots, int n, int N, int K,
+                             uint8_t* packed, uint8_t* scales, float* global_scale, uint8_t* ref_b_fwd,
+                             uint8_t* ref_bs_fwd, uint8_t* ref_b_bwd, uint8_t* ref_bs_bwd, float* amax_scratch,
+                             mcl4moe_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Activation quantisation, 1x16 row blocks with global scale 1.
+ * Replaces _quantize_nvfp4_core(x, two_dimensional=False,
+ * stochastic=False, causal_row_scale=True) (src/mcl4_coe/nvfp4.py:197-225)
+ * and its Triton launch _nvfp4_quantize_1d_kernel (src/mcl4_coe/nvfp4.py:735,
+ * launched :1074-1086).
+ * x: bf16 [rows, cols] with row stride ld_x (elements); packed [rows, cols/2];
+ * scales [rows, cols/16] row-major when swizzled == 0, else the swizzled
+ * atoms (rows padded to 128).  cols % 64 == 0.
+ * ------------------------------------------------------------------------ */
+int mcl4moe_quantize_activations(const uint16_t* x, int64_t rows, int cols, int64_t ld_x, uint8_t* packed,
+                                 uint8_t* scales, int swizzled, mcl4moe_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Router, top-k and routing statistics.
+ * Replaces the routing part of SparseMoE.forward
+ * (src/mcl4_coe/backbone.py:787-883, loop branch :913-1004):
+ * fp32 logits x @ Wr^T (+ optional additive bias), softmax, top-k with
+ * optional renormalisation, selection mask, counts, aux and z loss.
+ * Tokens with valid[t] == 0 are not routed (loop-branch semantics).
+ * logits_in (nullable) replaces the router product: then x and wr are unused.
+ * Outputs: topk_idx int32 [T, k], topk_w fp32 [T, k] (0 for invalid tokens),
+ * logits_out fp32 [T, E] (nullable), sel_mask fp32 [T, E] (nullable),
+ * counts int32 [E], stats fp32 [3 + E]: {aux_loss, z_loss, n_routed,
+ * counts_fraction[E]} (the layer's aux, router_z_loss and counts outputs).
+ * Requires E <= 256, k <= min(E, 32), d % 32 == 0.
+ * ------------------------------------------------------------------------ */
+size_t mcl4moe_route_workspace_size(int T, int E, int k);
+int mcl4moe_route(const uint16_t* x, const float* wr, const float* logit_bias, const float* logits_in,
+                  const uint8_t* valid, int T, int d, int E, int k, int norm_topk_prob, int32_t* topk_idx,
+                  float* topk_w, float* logits_out, float* sel_mask, int32_t* counts, float* stats,
+                  void* workspace, size_t workspace_bytes, mcl4moe_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Full MoE layer forward.
+ * Replaces SparseMoE.forward for the routing configuration without mitotic
+ * pairs / lineage / coverage penalty / dense subset
+ * (src/mcl4_coe/backbone.py:618-911): route -> stable expert-major permute
+ * -> NVFP4 activation quantisation -> grouped gate/up GEMM with fused SwiGLU
+ * and NVFP4 re-quantisation -> grouped down GEMM with the routing weight
+ * -> k-way combine.  Shapes: d % 256 == 0, F % 256 == 0, E <= 256,
+ * k <= min(E, 32).
+ * ------------------------------------------------------------------------ */
+typedef struct mcl4moe_moe_args {
+  /* inputs */
+  const uint16_t* x;          /* bf16 [T, d] */
+  const float* router_w;      /* fp32 [E, d] */
+  const float* logit_bias;    /* fp32 [E] or NULL */
+  const uint8_t* valid;       /* uint8 [T] or NULL */
+  const uint8_t* w_up;        /* kernel-layout NVFP4 up_proj [E, 2F, d/2] (gate rows first) */
+  const uint8_t* w_up_scales; /* [E, 2F*d/16] swizzled */
+  const float* w_up_g;        /* [E] */
+  const uint8_t* w_dn;        /* kernel-layout NVFP4 down_proj [E, d, F/2] */
+  const uint8_t* w_dn_scales; /* [E, d*F/16] swizzled */
+  const float* w_dn_g;        /* [E] */
+  int T, d, E, k, F;
+  int norm_topk_prob;
+  /* outputs */
+  uint16_t* out;              /* bf16 [T, d] */
+  float* stats;               /* fp32 [3 + E]: aux, z, n_routed, counts[E] */
+  float* sel_mask;            /* fp32 [T, E] or NULL (last_selected_mask) */
+  int32_t* topk_idx;          /* int32 [T, k] or NULL */
+  float* topk_w;              /* fp32 [T, k] or NULL */
+  int32_t* offs;              /* int32 [E] inclusive ends of the expert segments, or NULL */
+  int32_t* perm;              /* int32 [T*k] stable argsort of the selected experts, or NULL */
+  uint16_t* h_debug;          /* bf16 [M_cap, F] SwiGLU output in padded order, or NULL */
+  int32_t* error_word;        /* device int32, set by a timed-out device wait; may be NULL */
+  void* workspace;
+  size_t workspace_bytes;
+  /* Optional cudaEvent_t[6] (NULL to skip): recorded on the stream before
+   * routing and after routing, permutation, gate/up GEMM, down GEMM and combine. */
+  void* const* stage_events;
+} mcl4moe_moe_args;
+
+size_t mcl4moe_moe_workspace_size(int T, int d, int E, int k, int F);
+int mcl4moe_moe_forward(const mcl4moe_moe_args* args, mcl4moe_stream_t stream);
+
+/* Capacity in rows of the padded, expert-major activation buffers
+ * (sum over experts of count rounded up to 128, bounded by T*k + 127*E). */
+int64_t mcl4moe_padded_rows(int T, int E, int k);
+
+/* Device pointer of a named region inside a forward workspace (for tests and
+ * debugging): 0 xq, 1 xs, 2 hq, 3 hs, 4 y, 5 pad_start, 6 slot_pos, 7 sorted_w. */
+void* mcl4moe_workspace_region(void* workspace, int region, int T, int d, int E, int k, int F);
+
+/* ------------------------------------------------------------------------
+ * Grouped NVFP4 linear on rows already grouped by expert.
+ * Replaces nvfp4_grouped_linear(inputs, experts, proj_name, offs)
+ * (src/mcl4_coe/nvfp4.py:1219-1227 -> _NVFP4GroupedLinear.forward :1051-1110):
+ * out[m, :] = bf16((quant(x[m]) . W_e^T) * g_e) for rows m of expert e, i.e.
+ * rows [offs[e-1], offs[e]) (inclusive ends, int32 on the device).
+ * x bf16 [M, K]; w kernel-layout [E, N, K/2] + scales + g; out bf16 [M, N].
+ * K % 256 == 0, N % 256 == 0.
+ * ------------------------------------------------------------------------ */
+size_t mcl4moe_grouped_linear_workspace_size(int64_t M, int K, int E);
+int mcl4moe_grouped_linear(const uint16_t* x, int64_t M, int K, const int32_t* offs, int E, const uint8_t* w,
+                           const uint8_t* w_scales, const float* w_g, int N, uint16_t* out, int32_t* error_word,
+                           void* workspace, size_t workspace_bytes, mcl4moe_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MCL4MOE_H_ */

@@ -1,0 +1,314 @@
+// extern "C" entry points of libmcl4moe (declared in include/mcl4moe.h).
+// Host-side validation mirrors the reference's ValueError conditions
+// (src/mcl4_coe/nvfp4.py:243-249, :297-304; src/mcl4_coe/backbone.py:95-112)
+// and maps them to MCL4MOE_ERR_INVALID; shapes the kernels' tiling cannot
+// serve return MCL4MOE_ERR_UNSUPPORTED.  Nothing here allocates memory.
+#include <cstring>
+
+#include "kernels.cuh"
+
+using namespace mcl4;
+
+namespace {
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+struct MoeWorkspace {
+  RouteWorkspace route;
+  int32_t* topk_idx;
+  float* topk_w;
+  int32_t* slot_pos;
+  float* sorted_w;
+  uint8_t* xq;
+  uint8_t* xs;
+  uint8_t* hq;
+  uint8_t* hs;
+  uint16_t* y;
+  int32_t* counts;
+  float* stats;
+  int32_t* err;
+  size_t bytes;
+};
+
+MoeWorkspace moe_workspace(void* base, int T, int d, int E, int k, int F) {
+  MoeWorkspace w{};
+  uint8_t* p = static_cast<uint8_t*>(base);
+  w.route = route_workspace(base, T, E, k);
+  size_t off = w.route.bytes;
+  auto take = [&](size_t bytes) {
+    uint8_t* r = p ? p + off : nullptr;
+    off += align256(bytes);
+    return r;
+  };
+  const int64_t mcap = padded_rows_cap(T, E, k);
+  w.topk_idx = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * size_t(T) * k));
+  w.topk_w = reinterpret_cast<float*>(take(sizeof(float) * size_t(T) * k));
+  w.slot_pos = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * size_t(T) * k));
+  w.sorted_w = reinterpret_cast<float*>(take(sizeof(float) * size_t(mcap)));
+  w.xq = take(size_t(mcap) * d / 2);
+  w.xs = take(size_t(mcap) * d / 16);
+  w.hq = take(size_t(mcap) * F / 2);
+  w.hs = take(size_t(mcap) * F / 16);
+  w.y = reinterpret_cast<uint16_t*>(take(sizeof(uint16_t) * size_t(mcap) * d));
+  w.counts = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * E));
+  w.stats = reinterpret_cast<float*>(take(sizeof(float) * (3 + E)));
+  w.err = reinterpret_cast<int32_t*>(take(sizeof(int32_t)));
+  w.bytes = off;
+  return w;
+}
+
+int check_moe_shape(int T, int d, int E, int k, int F) {
+  if (T < 0 || d <= 0 || E <= 0 || k <= 0 || F <= 0 || k > E) return MCL4MOE_ERR_INVALID;
+  if (E > kMaxExperts || k > kMaxTopK) return MCL4MOE_ERR_UNSUPPORTED;
+  if (d % 256 != 0 || F % 256 != 0) return MCL4MOE_ERR_UNSUPPORTED;
+  if (int64_t(T) * k > (int64_t(1) << 30)) return MCL4MOE_ERR_UNSUPPORTED;
+  return MCL4MOE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* mcl4moe_status_string(int status) {
+  switch (status) {
+    case MCL4MOE_OK: return "ok";
+    case MCL4MOE_ERR_INVALID: return "invalid argument";
+    case MCL4MOE_ERR_UNSUPPORTED: return "unsupported device or shape";
+    case MCL4MOE_ERR_CUDA: return "CUDA error";
+    case MCL4MOE_ERR_TIMEOUT: return "device-side wait timed out";
+    case MCL4MOE_ERR_WORKSPACE: return "workspace too small";
+    default: return "unknown status";
+  }
+}
+
+int mcl4moe_version(void) { return 100; }
+
+int mcl4moe_device_supported(void) {
+  int dev = 0, major = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return 0;
+  return major == 10 ? 1 : 0;
+}
+
+int mcl4moe_read_error(int32_t* device_error_word, int32_t* host_value, mcl4moe_stream_t stream) {
+  if (!device_error_word || !host_value) return MCL4MOE_ERR_INVALID;
+  int32_t v = 0;
+  if (cudaMemcpyAsync(&v, device_error_word, sizeof(v), cudaMemcpyDeviceToHost, stream) != cudaSuccess)
+    return MCL4MOE_ERR_CUDA;
+  if (cudaStreamSynchronize(stream) != cudaSuccess) return MCL4MOE_ERR_CUDA;
+  *host_value = v;
+  if (v != 0) {
+    if (cudaMemsetAsync(device_error_word, 0, sizeof(int32_t), stream) != cudaSuccess) return MCL4MOE_ERR_CUDA;
+    if (cudaStreamSynchronize(stream) != cudaSuccess) return MCL4MOE_ERR_CUDA;
+    return MCL4MOE_ERR_TIMEOUT;
+  }
+  return MCL4MOE_OK;
+}
+
+int mcl4moe_quantize_weights(const float* const* w_ptrs, const int32_t* slots, int n, int N, int K, uint8_t* packed,
+                             uint8_t* scales, float* global_scale, uint8_t* ref_b_fwd, uint8_t* ref_bs_fwd,
+                             uint8_t* ref_b_bwd, uint8_t* ref_bs_bwd, float* amax_scratch, mcl4moe_stream_t stream) {
+  if (n < 0 || N <= 0 || K <= 0 || !w_ptrs || !slots || !packed || !scales || !global_scale || !amax_scratch)
+    return MCL4MOE_ERR_INVALID;
+  if (N % 16 != 0 || K % 16 != 0) return MCL4MOE_ERR_INVALID;  // src/mcl4_coe/nvfp4.py:248-249
+  if (K % 64 != 0) return MCL4MOE_ERR_UNSUPPORTED;
+  for (int i = 0; i < n; ++i)
+    if (!w_ptrs[i] || !aligned16(w_ptrs[i]) || slots[i] < 0) return MCL4MOE_ERR_INVALID;
+  if (n == 0) return MCL4MOE_OK;
+  return launch_quantize_weights(w_ptrs, slots, n, N, K, packed, scales, global_scale, ref_b_fwd, ref_bs_fwd,
+                                 ref_b_bwd, ref_bs_bwd, amax_scratch, stream);
+}
+
+int mcl4moe_quantize_activations(const uint16_t* x, int64_t rows, int cols, int64_t ld_x, uint8_t* packed,
+                                 uint8_t* scales, int swizzled, mcl4moe_stream_t stream) {
+  if (rows < 0 || cols <= 0 || ld_x < cols || !x || !packed || !scales) return MCL4MOE_ERR_INVALID;
+  if (cols % 16 != 0) return MCL4MOE_ERR_INVALID;
+  if (cols % 64 != 0 || ld_x % 8 != 0 || !aligned16(x)) return MCL4MOE_ERR_UNSUPPORTED;
+  return launch_quantize_activations(x, rows, cols, ld_x, packed, scales, swizzled, stream);
+}
+
+size_t mcl4moe_route_workspace_size(int T, int E, int k) { return route_workspace(nullptr, T, E, k).bytes; }
+
+int mcl4moe_route(const uint16_t* x, const float* wr, const float* logit_bias, const float* logits_in,
+                  const uint8_t* valid, int T, int d, int E, int k, int norm_topk_prob, int32_t* topk_idx,
+                  float* topk_w, float* logits_out, float* sel_mask, int32_t* counts, float* stats, void* workspace,
+                  size_t workspace_bytes, mcl4moe_stream_t stream) {
+  if (T < 0 || E <= 0 || k <= 0 || k > E || !topk_idx || !topk_w || !workspace) return MCL4MOE_ERR_INVALID;
+  if (E > kMaxExperts || k > kMaxTopK) return MCL4MOE_ERR_UNSUPPORTED;
+  if (!logits_in) {
+    if (!x || !wr || d <= 0) return MCL4MOE_ERR_INVALID;
+    if (d % 32 != 0 || !aligned16(x) || !aligned16(wr)) return MCL4MOE_ERR_UNSUPPORTED;
+  }
+  const RouteWorkspace ws = route_workspace(workspace, T, E, k);
+  if (workspace_bytes < ws.bytes) return MCL4MOE_ERR_WORKSPACE;
+  return launch_route(x, wr, logit_bias, logits_in, valid, T, d, E, k, norm_topk_prob, topk_idx, topk_w, logits_out,
+                      sel_mask, counts, stats, nullptr, ws, stream);
+}
+
+int64_t mcl4moe_padded_rows(int T, int E, int k) { return padded_rows_cap(T, E, k); }
+
+size_t mcl4moe_moe_workspace_size(int T, int d, int E, int k, int F) {
+  if (check_moe_shape(T, d, E, k, F) != MCL4MOE_OK) return 0;
+  return moe_workspace(nullptr, T, d, E, k, F).bytes;
+}
+
+void* mcl4moe_workspace_region(void* workspace, int region, int T, int d, int E, int k, int F) {
+  const MoeWorkspace w = moe_workspace(workspace, T, d, E, k, F);
+  switch (region) {
+    case 0: return w.xq;
+    case 1: return w.xs;
+    case 2: return w.hq;
+    case 3: return w.hs;
+    case 4: return w.y;
+    case 5: return w.route.pad_start;
+    case 6: return w.slot_pos;
+    case 7: return w.sorted_w;
+    default: return nullptr;
+  }
+}
+
+int mcl4moe_moe_forward(const mcl4moe_moe_args* a, mcl4moe_stream_t stream) {
+  if (!a) return MCL4MOE_ERR_INVALID;
+  int st = check_moe_shape(a->T, a->d, a->E, a->k, a->F);
+  if (st != MCL4MOE_OK) return st;
+  if (!a->out || !a->stats || !a->workspace || (a->T > 0 && (!a->x || !a->router_w))) return MCL4MOE_ERR_INVALID;
+  if (!a->w_up || !a->w_up_scales || !a->w_up_g || !a->w_dn || !a->w_dn_scales || !a->w_dn_g)
+    return MCL4MOE_ERR_INVALID;
+  if (!aligned16(a->x) || !aligned16(a->out) || !aligned16(a->w_up) || !aligned16(a->w_dn) ||
+      !aligned16(a->w_up_scales) || !aligned16(a->w_dn_scales) || !aligned16(a->router_w) ||
+      (a->h_debug && !aligned16(a->h_debug)))
+    return MCL4MOE_ERR_INVALID;
+  const MoeWorkspace w = moe_workspace(a->workspace, a->T, a->d, a->E, a->k, a->F);
+  if (a->workspace_bytes < w.bytes) return MCL4MOE_ERR_WORKSPACE;
+  cudaStream_t s = stream;
+  const int T = a->T, d = a->d, E = a->E, k = a->k, F = a->F;
+  int32_t* err = a->error_word ? a->error_word : w.err;
+  int32_t* topk_idx = a->topk_idx ? a->topk_idx : w.topk_idx;
+  float* topk_w = a->topk_w ? a->topk_w : w.topk_w;
+
+  auto mark = [&](int i) -> int {
+    if (a->stage_events == nullptr || a->stage_events[i] == nullptr) return MCL4MOE_OK;
+    return cudaEventRecord(static_cast<cudaEvent_t>(a->stage_events[i]), s) == cudaSuccess ? MCL4MOE_OK
+                                                                                            : MCL4MOE_ERR_CUDA;
+  };
+  if ((st = mark(0)) != MCL4MOE_OK) return st;
+  st = launch_route(a->x, a->router_w, a->logit_bias, nullptr, a->valid, T, d, E, k, a->norm_topk_prob, topk_idx,
+                    topk_w, nullptr, a->sel_mask, w.counts, a->stats, a->offs, w.route, s);
+  if (st != MCL4MOE_OK) return st;
+  if ((st = mark(1)) != MCL4MOE_OK) return st;
+  if (T == 0) {
+    for (int i = 2; i < 6; ++i)
+      if ((st = mark(i)) != MCL4MOE_OK) return st;
+    return MCL4MOE_OK;
+  }
+  st = launch_permute_quantize(a->x, a->valid, topk_idx, topk_w, T, d, E, k, w.route, w.slot_pos, w.sorted_w, a->perm,
+                               w.xq, w.xs, s);
+  if (st != MCL4MOE_OK) return st;
+  if ((st = mark(2)) != MCL4MOE_OK) return st;
+  const int64_t mcap = padded_rows_cap(T, E, k);
+
+  GemmArgs g1{};
+  g1.pad_start = w.route.pad_start;
+  g1.row_count = w.route.counts;
+  g1.a_scales = w.xs;
+  g1.b_scales = a->w_up_scales;
+  g1.b_g = a->w_up_g;
+  g1.E = E;
+  g1.K = d;
+  g1.N_total = 2 * F;
+  g1.n_tiles = F / 128;
+  g1.mode = 0;
+  g1.F = F;
+  g1.hq = w.hq;
+  g1.hs = w.hs;
+  g1.h_dbg = a->h_debug;
+  g1.err = err;
+  st = launch_grouped_gemm(w.xq, mcap, a->w_up, g1, s);
+  if (st != MCL4MOE_OK) return st;
+  if ((st = mark(3)) != MCL4MOE_OK) return st;
+
+  GemmArgs g2{};
+  g2.pad_start = w.route.pad_start;
+  g2.row_count = w.route.counts;
+  g2.a_scales = w.hs;
+  g2.b_scales = a->w_dn_scales;
+  g2.b_g = a->w_dn_g;
+  g2.E = E;
+  g2.K = F;
+  g2.N_total = d;
+  g2.n_tiles = d / 256;
+  g2.mode = 1;
+  g2.row_w = w.sorted_w;
+  g2.y = w.y;
+  g2.ldy = d;
+  g2.err = err;
+  st = launch_grouped_gemm(w.hq, mcap, a->w_dn, g2, s);
+  if (st != MCL4MOE_OK) return st;
+  if ((st = mark(4)) != MCL4MOE_OK) return st;
+  st = launch_combine(w.y, w.slot_pos, a->valid, T, k, d, a->out, s);
+  if (st != MCL4MOE_OK) return st;
+  return mark(5);
+}
+
+size_t mcl4moe_grouped_linear_workspace_size(int64_t M, int K, int E) {
+  if (M < 0 || K <= 0 || E <= 0) return 0;
+  const int64_t mcap = ((M + int64_t(127) * E) + 127) / 128 * 128;
+  size_t off = 0;
+  off += align256(sizeof(int32_t) * (E + 1));  // pad_start
+  off += align256(sizeof(int32_t) * E);        // offs_start
+  off += align256(sizeof(int32_t) * E);        // counts
+  off += align256(size_t(mcap) * K / 2);       // xq
+  off += align256(size_t(mcap) * K / 16);      // xs
+  off += align256(sizeof(int32_t));            // error word
+  return off;
+}
+
+int mcl4moe_grouped_linear(const uint16_t* x, int64_t M, int K, const int32_t* offs, int E, const uint8_t* w,
+                           const uint8_t* w_scales, const float* w_g, int N, uint16_t* out, int32_t* error_word,
+                           void* workspace, size_t workspace_bytes, mcl4moe_stream_t stream) {
+  if (M < 0 || K <= 0 || N <= 0 || E <= 0 || !offs || !w || !w_scales || !w_g || !out || !workspace)
+    return MCL4MOE_ERR_INVALID;
+  if (M > 0 && !x) return MCL4MOE_ERR_INVALID;
+  if (K % 16 != 0) return MCL4MOE_ERR_INVALID;
+  if (K % 256 != 0 || N % 256 != 0 || E > kMaxExperts) return MCL4MOE_ERR_UNSUPPORTED;
+  if (!aligned16(x) || !aligned16(out) || !aligned16(w) || !aligned16(w_scales)) return MCL4MOE_ERR_INVALID;
+  if (workspace_bytes < mcl4moe_grouped_linear_workspace_size(M, K, E)) return MCL4MOE_ERR_WORKSPACE;
+  if (M == 0) return MCL4MOE_OK;
+  const int64_t mcap = ((M + int64_t(127) * E) + 127) / 128 * 128;
+  uint8_t* p = static_cast<uint8_t*>(workspace);
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    uint8_t* r = p + off;
+    off += align256(bytes);
+    return r;
+  };
+  int32_t* pad_start = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * (E + 1)));
+  int32_t* offs_start = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * E));
+  int32_t* counts = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * E));
+  uint8_t* xq = take(size_t(mcap) * K / 2);
+  uint8_t* xs = take(size_t(mcap) * K / 16);
+  int32_t* err = error_word ? error_word : reinterpret_cast<int32_t*>(take(sizeof(int32_t)));
+  cudaStream_t s = stream;
+  int st = launch_pad_from_offs(offs, E, pad_start, offs_start, counts, s);
+  if (st != MCL4MOE_OK) return st;
+  st = launch_quantize_grouped_rows(x, M, K, offs, pad_start, counts, E, xq, xs, s);
+  if (st != MCL4MOE_OK) return st;
+  GemmArgs g{};
+  g.pad_start = pad_start;
+  g.row_count = counts;
+  g.out_row_base = offs_start;
+  g.a_scales = xs;
+  g.b_scales = w_scales;
+  g.b_g = w_g;
+  g.E = E;
+  g.K = K;
+  g.N_total = N;
+  g.n_tiles = N / 256;
+  g.mode = 1;
+  g.y = out;
+  g.ldy = N;
+  g.err = err;
+  return launch_grouped_gemm(xq, mcap, w, g, s);
+}
+
+}  // extern "C"

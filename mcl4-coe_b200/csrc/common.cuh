@@ -1,0 +1,239 @@
+// Shared device helpers for the NVFP4 MoE kernels (sm_100a only).
+//
+// Numerics follow the reference quantiser (src/mcl4_coe/nvfp4.py:186-225 and
+// :923-952) operation by operation: every multiply / add / divide is an IEEE
+// float32 round-to-nearest operation (explicit __fmul_rn / __fadd_rn /
+// __fdiv_rn / __frcp_rn so the compiler cannot contract or approximate), and
+// the library is built without fast-math so denormals are kept.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+
+#include "../../include/mcl4moe.h"
+
+namespace mcl4 {
+
+constexpr float kFltMax = 3.402823466e38f;
+constexpr float kFltMinNormal = 1.17549435e-38f;
+
+// ---------------------------------------------------------------- numerics
+
+__device__ __forceinline__ float bf16_to_f32(uint16_t b) {
+  return __uint_as_float(static_cast<uint32_t>(b) << 16);
+}
+
+// float32 -> bfloat16 bits, round to nearest even (torch ``.to(bfloat16)``).
+__device__ __forceinline__ uint16_t f32_to_bf16(float f) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+
+__device__ __forceinline__ float round_bf16(float f) { return bf16_to_f32(f32_to_bf16(f)); }
+
+// float32 in [0, 448] -> e4m3fn bits with round-to-nearest-even (the hardware
+// cvt.rn.satfinite conversion; the callers clamp to 448 first, exactly as
+// src/mcl4_coe/nvfp4.py:215 does, so saturation never differs from torch).
+__device__ __forceinline__ uint32_t f32_to_e4m3(float v) {
+  return static_cast<uint32_t>(__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3));
+}
+
+// e4m3fn bits (sign bit clear) -> float32, exact.
+__device__ __forceinline__ float e4m3_to_f32(uint32_t c) {
+  uint32_t e = (c >> 3) & 0xF, m = c & 7;
+  if (e == 0) return __fmul_rn(static_cast<float>(m), 0.001953125f);  // m * 2^-9
+  return __uint_as_float(((e + 120u) << 23) | (m << 20));
+}
+
+// src/mcl4_coe/nvfp4.py:217-221 — 1/dec clamped to FLT_MAX, 0 when dec <= 0.
+__device__ __forceinline__ float inverse_decoding(float dec) {
+  return dec > 0.f ? fminf(__frcp_rn(dec), kFltMax) : 0.f;
+}
+
+// src/mcl4_coe/nvfp4.py:186-194 (deterministic branch): m = min(|v|, 6);
+// u = 2m | m+2 | m/2+4 (each float32-rounded); code = rint(u) | signbit<<3.
+__device__ __forceinline__ uint32_t e2m1_code(float v) {
+  const float m = fminf(fabsf(v), 6.0f);
+  float u;
+  if (m <= 2.0f) u = __fmul_rn(m, 2.0f);
+  else if (m <= 4.0f) u = __fadd_rn(m, 2.0f);
+  else u = __fadd_rn(__fmul_rn(m, 0.5f), 4.0f);
+  return static_cast<uint32_t>(__float2int_rn(u)) | ((__float_as_uint(v) >> 31) << 3);
+}
+
+// Quantise one 16-element row block with global scale 1 (the activation mode,
+// src/mcl4_coe/nvfp4.py:204-224 with causal_row_scale=True):
+// returns the e4m3 scale byte; writes the 8 packed bytes (low nibble = even).
+__device__ __forceinline__ uint32_t quantize_block16(const float (&v)[16], uint2& packed) {
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  const uint32_t s = f32_to_e4m3(fminf(__fdiv_rn(amax, 6.0f), 448.0f));
+  const float inv = inverse_decoding(e4m3_to_f32(s));
+  uint32_t lo = 0, hi = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) lo |= e2m1_code(__fmul_rn(v[i], inv)) << (4 * i);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) hi |= e2m1_code(__fmul_rn(v[8 + i], inv)) << (4 * i);
+  packed = make_uint2(lo, hi);
+  return s;
+}
+
+// Byte offset of scale (row r, 16-block c) in the 128x4 scale atoms
+// (src/mcl4_coe/nvfp4.py:131-144; the layout tcgen05 block-scaled MMA reads).
+__device__ __host__ __forceinline__ uint64_t swizzled_scale_offset(uint64_t r, uint32_t c, uint32_t blocks_per_row) {
+  const uint64_t atom = (r >> 7) * (blocks_per_row >> 2) + (c >> 2);
+  return atom * 512 + (r & 31) * 16 + ((r >> 5) & 3) * 4 + (c & 3);
+}
+
+// ---------------------------------------------------------------- PTX wrappers
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(bar),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for phase ``parity`` of an mbarrier, giving up after ``kWaitLimitNs``:
+// on time-out the error word gets ``code`` (first writer wins) and false is
+// returned, so no kernel can spin forever on a barrier nobody completes.
+constexpr uint64_t kWaitLimitNs = 1000ull * 1000ull * 1000ull;  // 1 s
+
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int32_t* err, int32_t code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((++spins & 63u) == 0) {
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        if (err) atomicCAS(err, 0, code);
+        return false;
+      }
+      if (err && *reinterpret_cast<volatile int32_t*>(err) != 0) return false;  // another role gave up
+    }
+  }
+}
+
+// 2-D TMA tile load into shared memory, completion counted on ``bar`` (no multicast).
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int32_t x, int32_t y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(tmap), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+// Plain bulk copy global -> shared (16-byte aligned, size % 16 == 0).
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const void* tmap) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
+}
+
+// ---- tcgen05 (5th-generation tensor core, tensor memory)
+
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Arrive on ``bar`` once every tcgen05 operation this thread issued so far has completed.
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// Copy one 128-row x 4-scale atom (512 B, no swizzle, 16-B rows, 8-row core
+// matrices 128 B apart) from shared memory into 4 TMEM columns, replicated
+// over the four 32-lane sub-partitions.
+__device__ __forceinline__ void tc_copy_scales(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+// D(tmem) (+)= A(smem) * B(smem)^T with NVFP4 operands and UE4M3 scales per 16 K.
+__device__ __forceinline__ void tc_mma_nvf4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
+// 32 lanes x 16 consecutive 32-bit columns -> 16 registers per thread.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor (tcgen05 format, version 1).
+// layout: 0 = no swizzle, 2 = 128-byte swizzle.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes, uint32_t layout) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFF);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFF) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFF) << 32;
+  d |= 1ull << 46;  // descriptor version for sm_100
+  d |= static_cast<uint64_t>(layout & 7) << 61;
+  return d;
+}
+
+// Instruction descriptor of kind::mxf4nvf4: E2M1 A and B (format 1), K-major
+// both, UE4M3 scales, fp32 accumulate, M x N, dense K = 64.
+__host__ __device__ constexpr uint32_t idesc_nvf4(uint32_t m, uint32_t n) {
+  return (1u << 7) | (1u << 10) | ((n >> 3) << 17) | (0u << 23) | ((m >> 4) << 24);
+}
+
+}  // namespace mcl4

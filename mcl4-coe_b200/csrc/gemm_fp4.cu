@@ -1,0 +1,372 @@
+// Grouped NVFP4 x NVFP4 GEMM on the 5th-generation tensor cores (tcgen05,
+// kind::mxf4nvf4, UE4M3 scale per 16 K), persistent over ragged expert
+// segments.  Replaces the reference's Triton tl.dot_scaled kernel
+// _nvfp4_grouped_mm_kernel (src/mcl4_coe/nvfp4.py:798-874):
+//   out[m, n] = bf16( sum_k deq(A)[m, k] * deq(B_e)[n, k] * g_a * g_b[e] )
+// for the rows m of expert e, with g_a = 1 (activations).
+//
+// Layout: A rows are grouped by expert and each expert segment is padded to a
+// multiple of 128 rows (pad_start[E+1]); every 128-row M block therefore
+// belongs to exactly one expert and its scales are whole 128x4 atoms.
+// Tile 128 x 256, K step 256 (one 128-byte swizzle row of packed FP4).
+//
+// Warp roles (320 threads, one CTA per SM):
+//   warp 0      TMA producer: A tile, two 128-row B halves, 3 scale bulk copies
+//   warp 1      TMEM owner + single-thread MMA issuer (scales smem -> TMEM, 4 MMAs)
+//   warps 2..9  epilogue: TMEM -> registers, then
+//               mode 0 (gate/up): SwiGLU in bf16 and NVFP4 re-quantisation of h
+//                                 (src/mcl4_coe/backbone.py:572-574)
+//               mode 1 (down):    bf16(acc*g) [* bf16(routing weight)] to bf16 rows
+//                                 (src/mcl4_coe/backbone.py:903)
+// Pipelines: 4 smem stages (full/empty mbarriers); one 256-column fp32
+// accumulator released by the epilogue right after it is read, so the next
+// tile's MMAs overlap the epilogue math.  Scale factors live in a per-stage
+// TMEM ring so a stage's scales are only overwritten after the MMAs that read
+// them completed.  Every wait is bounded (error word instead of a hang).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "kernels.cuh"
+
+namespace mcl4 {
+
+namespace {
+
+constexpr int kBM = 128, kBN = 256, kBK = 256;
+constexpr int kStages = 4;
+constexpr uint32_t kATile = kBM * kBK / 2;   // 16384
+constexpr uint32_t kBHalf = 128 * kBK / 2;    // 16384 (128 rows)
+constexpr uint32_t kSFA = kBM * kBK / 16;     // 2048
+constexpr uint32_t kSFBHalf = 128 * kBK / 16;  // 2048
+constexpr uint32_t kStageBytes = kATile + 2 * kBHalf + kSFA + 2 * kSFBHalf;  // 55296
+constexpr uint32_t kOffB = kATile, kOffSFA = kATile + 2 * kBHalf, kOffSFB = kOffSFA + kSFA;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kSfCol0 = 256;          // accumulator uses columns [0, 256)
+constexpr uint32_t kSfColsPerStage = 48;   // SFA 4 x 4 + SFB 4 x 8
+constexpr uint32_t kIdesc = idesc_nvf4(128, 256);
+constexpr size_t kSmemBytes = size_t(kStages) * kStageBytes + 1024 /*align*/ + 256 /*barriers*/ +
+                              sizeof(int32_t) * (kMaxExperts + 1);
+
+static_assert(kSfCol0 + kStages * kSfColsPerStage <= kTmemCols, "TMEM budget");
+static_assert(kStageBytes % 1024 == 0, "stage must keep 1024-byte alignment for 128B swizzle");
+
+struct TileCoord {
+  int e, mb, nt;
+};
+
+__device__ __forceinline__ int find_expert(const int32_t* pad_s, int E, int row) {
+  int lo = 0, hi = E + 1;  // upper_bound(pad_s[0..E], row) - 1
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (pad_s[mid] <= row) lo = mid + 1;
+    else hi = mid;
+  }
+  return lo - 1;
+}
+
+__device__ __forceinline__ float silu_bf16(float g) {
+  // F.silu on a bf16 tensor: g / (1 + exp(-g)) in float32, rounded to bf16.
+  return round_bf16(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kThreads, 1)
+    grouped_gemm_fp4_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                            GemmArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - raw_addr);
+  const uint32_t bar_base = base + kStages * kStageBytes;
+  auto full_bar = [&](int s) { return bar_base + 8u * s; };
+  auto empty_bar = [&](int s) { return bar_base + 8u * (kStages + s); };
+  const uint32_t tfull_bar = bar_base + 8u * (2 * kStages);
+  const uint32_t tempty_bar = bar_base + 8u * (2 * kStages + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kStages * kStageBytes + 8 * (2 * kStages + 2));
+  int32_t* pad_s = reinterpret_cast<int32_t*>(smem + kStages * kStageBytes + 256);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int E = args.E;
+
+  for (int i = tid; i <= E; i += kThreads) pad_s[i] = args.pad_start[i];
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    mbar_init(tfull_bar, 1);
+    mbar_init(tempty_bar, kEpiWarps);
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int total_mb = pad_s[E] / kBM;
+  const int n_tiles = args.n_tiles;
+  const int total_tiles = total_mb * n_tiles;
+  const int kblocks = args.K / kBK;
+  const uint32_t sf_row_stride = uint32_t(args.K / 64) * 512u;  // bytes per 128-row scale block
+  auto coord = [&](int t) {
+    TileCoord c;
+    c.mb = t / n_tiles;
+    c.nt = t - c.mb * n_tiles;
+    c.e = find_expert(pad_s, E, c.mb * kBM);
+    return c;
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        const TileCoord c = coord(t);
+        int lr0, lr1;  // local B rows of the two 128-row halves
+        if (args.mode == 0) {
+          lr0 = c.nt * 128;
+          lr1 = args.F + c.nt * 128;
+        } else {
+          lr0 = c.nt * kBN;
+          lr1 = lr0 + 128;
+        }
+        const int brow = c.e * args.N_total;
+        const uint8_t* bsc = args.b_scales + size_t(c.e) * (size_t(args.N_total) * args.K / 16);
+        const uint8_t* asc = args.a_scales + size_t(c.mb) * sf_row_stride;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u, args.err, 101)) {
+            ok = false;
+            break;
+          }
+          const uint32_t st = base + stage * kStageBytes;
+          mbar_arrive_expect_tx(full_bar(stage), kStageBytes);
+          tma_load_2d(st, &tmap_a, kb * (kBK / 2), c.mb * kBM, full_bar(stage));
+          tma_load_2d(st + kOffB, &tmap_b, kb * (kBK / 2), brow + lr0, full_bar(stage));
+          tma_load_2d(st + kOffB + kBHalf, &tmap_b, kb * (kBK / 2), brow + lr1, full_bar(stage));
+          bulk_load(st + kOffSFA, asc + kb * 2048, kSFA, full_bar(stage));
+          bulk_load(st + kOffSFB, bsc + size_t(lr0 / 128) * sf_row_stride + kb * 2048, kSFBHalf, full_bar(stage));
+          bulk_load(st + kOffSFB + kSFBHalf, bsc + size_t(lr1 / 128) * sf_row_stride + kb * 2048, kSFBHalf,
+                    full_bar(stage));
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        if (!mbar_wait(tempty_bar, acc_phase ^ 1u, args.err, 201)) break;
+        tc_fence_after();
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, args.err, 202)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t st = base + stage * kStageBytes;
+          const uint32_t sf_col = tmem_base + kSfCol0 + stage * kSfColsPerStage;
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            tc_copy_scales(sf_col + 4 * ks, smem_desc(st + kOffSFA + 512 * ks, 0, 128, 0));
+            tc_copy_scales(sf_col + 16 + 8 * ks, smem_desc(st + kOffSFB + 512 * ks, 0, 128, 0));
+            tc_copy_scales(sf_col + 16 + 8 * ks + 4, smem_desc(st + kOffSFB + kSFBHalf + 512 * ks, 0, 128, 0));
+          }
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint64_t adesc = smem_desc(st + 32 * ks, 16, 1024, 2);
+            const uint64_t bdesc = smem_desc(st + kOffB + 32 * ks, 16, 1024, 2);
+            tc_mma_nvf4(tmem_base, adesc, bdesc, kIdesc, sf_col + 4 * ks, sf_col + 16 + 8 * ks,
+                        (kb | ks) != 0 ? 1u : 0u);
+          }
+          tc_commit(empty_bar(stage));
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(tfull_bar);
+        acc_phase ^= 1u;
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;             // TMEM lane quarter this warp may access
+    const int ch = (warp - 2) >> 2;     // column half handled by this warp
+    const int row_in_tile = q * 32 + lane;
+    const uint32_t lane_addr = tmem_base + (uint32_t(q * 32) << 16);
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+      const TileCoord c = coord(t);
+      if (!mbar_wait(tfull_bar, acc_phase, args.err, 301)) break;
+      acc_phase ^= 1u;
+      tc_fence_after();
+      uint32_t v[8][16];
+      if (args.mode == 0) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          tmem_ld16(lane_addr + ch * 64 + 16 * i, v[i]);            // gate columns
+          tmem_ld16(lane_addr + 128 + ch * 64 + 16 * i, v[4 + i]);  // value columns
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) tmem_ld16(lane_addr + ch * 128 + 16 * i, v[i]);
+      }
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty_bar);  // accumulator may be overwritten now
+
+      const int64_t p = int64_t(c.mb) * kBM + row_in_tile;  // padded row
+      const int local = int(p - pad_s[c.e]);
+      const bool row_valid = args.row_count == nullptr || local < args.row_count[c.e];
+      const float gb = args.b_g[c.e];
+      if (args.mode == 0) {
+        const int F = args.F;
+        const int hb0 = c.nt * 8 + ch * 4;  // first 16-column block of h handled here
+        uint32_t sword = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float h[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float g = round_bf16(__fmul_rn(__uint_as_float(v[i][j]), gb));
+            const float u = round_bf16(__fmul_rn(__uint_as_float(v[4 + i][j]), gb));
+            h[j] = round_bf16(__fmul_rn(silu_bf16(g), u));
+          }
+          uint2 pk;
+          const uint32_t s = quantize_block16(h, pk);
+          sword |= s << (8 * i);
+          *reinterpret_cast<uint2*>(args.hq + p * (F / 2) + (hb0 + i) * 8) = pk;
+          if (args.h_dbg != nullptr) {
+            uint32_t o[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              o[j] = uint32_t(f32_to_bf16(h[2 * j])) | (uint32_t(f32_to_bf16(h[2 * j + 1])) << 16);
+            uint4* dst = reinterpret_cast<uint4*>(args.h_dbg + p * F + (hb0 + i) * 16);
+            dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+            dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+          }
+        }
+        *reinterpret_cast<uint32_t*>(args.hs + swizzled_scale_offset(uint64_t(p), uint32_t(hb0), uint32_t(F / 16))) =
+            sword;
+      } else if (row_valid) {
+        const int64_t dst_row = args.out_row_base ? int64_t(args.out_row_base[c.e]) + local : p;
+        const float wv = args.row_w ? round_bf16(args.row_w[p]) : 1.0f;
+        uint16_t* dst = args.y + dst_row * args.ldy + c.nt * kBN + ch * 128;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          uint32_t o[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            float a0 = round_bf16(__fmul_rn(__uint_as_float(v[i][2 * j]), gb));
+            float a1 = round_bf16(__fmul_rn(__uint_as_float(v[i][2 * j + 1]), gb));
+            if (args.row_w) {
+              a0 = __fmul_rn(a0, wv);
+              a1 = __fmul_rn(a1, wv);
+            }
+            o[j] = uint32_t(f32_to_bf16(a0)) | (uint32_t(f32_to_bf16(a1)) << 16);
+          }
+          uint4* d4 = reinterpret_cast<uint4*>(dst + 16 * i);
+          d4[0] = make_uint4(o[0], o[1], o[2], o[3]);
+          d4[1] = make_uint4(o[4], o[5], o[6], o[7]);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D map over a [rows, row_bytes] uint8 matrix, box 128 bytes x 128 rows, 128B swizzle.
+bool make_tmap(CUtensorMap* m, const void* base, uint64_t row_bytes, uint64_t rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {row_bytes, rows};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {128, 128};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+int launch_grouped_gemm(const uint8_t* a, int64_t a_rows, const uint8_t* b, const GemmArgs& args,
+                        cudaStream_t stream) {
+  if (args.K % kBK != 0 || args.E < 1 || args.E > kMaxExperts) return MCL4MOE_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) | reinterpret_cast<uintptr_t>(args.a_scales) |
+       reinterpret_cast<uintptr_t>(args.b_scales)) & 15)
+    return MCL4MOE_ERR_INVALID;
+  CUtensorMap ta, tb;
+  if (!make_tmap(&ta, a, uint64_t(args.K) / 2, uint64_t(a_rows))) return MCL4MOE_ERR_CUDA;
+  if (!make_tmap(&tb, b, uint64_t(args.K) / 2, uint64_t(args.E) * args.N_total)) return MCL4MOE_ERR_CUDA;
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(grouped_gemm_fp4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes)) !=
+        cudaSuccess)
+      return MCL4MOE_ERR_CUDA;
+    configured = true;
+  }
+  grouped_gemm_fp4_kernel<<<num_sms(), kThreads, kSmemBytes, stream>>>(ta, tb, args);
+  return cudaGetLastError() == cudaSuccess ? MCL4MOE_OK : MCL4MOE_ERR_CUDA;
+}
+
+}  // namespace mcl4

@@ -1,0 +1,105 @@
+// Internal launch interface shared by the kernel files and the C ABI (api.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace mcl4 {
+
+constexpr int kMaxWeightBatch = 256;  // weight matrices per quantiser launch
+constexpr int kMaxExperts = 256;
+constexpr int kMaxTopK = 32;
+constexpr int kRouteTokens = 64;      // tokens per router CTA (= permutation chunk)
+
+// ---- workspace layout of the routing stage (all offsets 256-byte aligned)
+struct RouteWorkspace {
+  int32_t* local_rank;   // [T, k]  rank of slot (t, j) among its expert's slots in the chunk
+  int32_t* chunk_excl;   // [C, E]  chunk counts, then (after the scan) exclusive prefix over chunks
+  float* part_probs;     // [C, E]  per-chunk sum of routed probabilities
+  float* part_misc;      // [C, 2]  per-chunk sum of lse^2 and routed-token count
+  int32_t* pad_start;    // [E + 1] padded row start of each expert (multiple of 128)
+  int32_t* offs_start;   // [E]     unpadded row start of each expert
+  int32_t* counts;       // [E]     routed slots per expert
+  size_t bytes;
+};
+
+inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+inline RouteWorkspace route_workspace(void* base, int T, int E, int k) {
+  RouteWorkspace w{};
+  const int C = (T + kRouteTokens - 1) / kRouteTokens;
+  uint8_t* p = static_cast<uint8_t*>(base);
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    uint8_t* r = p ? p + off : nullptr;
+    off += align256(bytes);
+    return r;
+  };
+  w.local_rank = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * size_t(T) * k));
+  w.chunk_excl = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * size_t(C) * E));
+  w.part_probs = reinterpret_cast<float*>(take(sizeof(float) * size_t(C) * E));
+  w.part_misc = reinterpret_cast<float*>(take(sizeof(float) * size_t(C) * 2));
+  w.pad_start = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * (E + 1)));
+  w.offs_start = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * E));
+  w.counts = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * E));
+  w.bytes = off;
+  return w;
+}
+
+inline int64_t padded_rows_cap(int64_t T, int E, int k) {
+  const int64_t m = T * k + int64_t(127) * E;
+  return (m + 127) / 128 * 128;
+}
+
+// ---- launchers (return MCL4MOE_* status)
+int launch_quantize_weights(const float* const* w_ptrs, const int32_t* slots, int n, int N, int K, uint8_t* packed,
+                            uint8_t* scales, float* gscale, uint8_t* rb, uint8_t* rbs, uint8_t* rbb, uint8_t* rbbs,
+                            float* amax, cudaStream_t stream);
+
+int launch_quantize_activations(const uint16_t* x, int64_t rows, int cols, int64_t ld_x, uint8_t* packed,
+                                uint8_t* scales, int swizzled, cudaStream_t stream);
+
+// Router + top-k + chunk ranks + scan (+ statistics), writes topk/sel_mask/stats and fills ``ws``.
+int launch_route(const uint16_t* x, const float* wr, const float* bias, const float* logits_in, const uint8_t* valid,
+                 int T, int d, int E, int k, int norm_topk, int32_t* topk_idx, float* topk_w, float* logits_out,
+                 float* sel_mask, int32_t* counts_out, float* stats, int32_t* offs_out, const RouteWorkspace& ws,
+                 cudaStream_t stream);
+
+// Scatter each routed token's NVFP4 row into its k padded expert-major slots.
+int launch_permute_quantize(const uint16_t* x, const uint8_t* valid, const int32_t* topk_idx, const float* topk_w,
+                            int T, int d, int E, int k, const RouteWorkspace& ws, int32_t* slot_pos, float* sorted_w,
+                            int32_t* perm, uint8_t* xq, uint8_t* xs, cudaStream_t stream);
+
+// Grouped-linear helpers: padded layout from inclusive ends, and row scatter.
+int launch_pad_from_offs(const int32_t* offs, int E, int32_t* pad_start, int32_t* offs_start, int32_t* counts,
+                         cudaStream_t stream);
+int launch_quantize_grouped_rows(const uint16_t* x, int64_t M, int K, const int32_t* offs, const int32_t* pad_start,
+                                 const int32_t* counts, int E, uint8_t* xq, uint8_t* xs, cudaStream_t stream);
+
+// out[t] = bf16(sum_j y[slot_pos[t, j]]) for valid tokens, 0 otherwise.
+int launch_combine(const uint16_t* y, const int32_t* slot_pos, const uint8_t* valid, int T, int k, int d, uint16_t* out,
+                   cudaStream_t stream);
+
+// ---- grouped block-scaled FP4 GEMM (tcgen05)
+struct GemmArgs {
+  const int32_t* pad_start;     // [E + 1]
+  const int32_t* row_count;     // [E] valid rows per expert (stores of rows beyond are skipped)
+  const int32_t* out_row_base;  // [E] destination row of an expert's first row (nullptr: padded row index)
+  const uint8_t* a_scales;      // swizzled, padded rows
+  const uint8_t* b_scales;      // [E, N_total*K/16] swizzled
+  const float* b_g;             // [E]
+  int E, K, N_total, n_tiles, mode;
+  int F;                        // mode 0: columns of h (gate rows [0,F), value rows [F,2F) of B)
+  uint8_t* hq;                  // mode 0: [M, F/2]
+  uint8_t* hs;                  // mode 0: swizzled [M/128 * F/64 * 512]
+  uint16_t* h_dbg;              // mode 0: bf16 [M, F] or nullptr
+  const float* row_w;           // mode 1: per padded row weight or nullptr
+  uint16_t* y;                  // mode 1: bf16 output
+  int64_t ldy;
+  int32_t* err;
+};
+
+int launch_grouped_gemm(const uint8_t* a, int64_t a_rows, const uint8_t* b, const GemmArgs& args, cudaStream_t stream);
+
+int num_sms();
+
+}  // namespace mcl4

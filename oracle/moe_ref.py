@@ -137,8 +137,8 @@ class QuantizedExperts:
     src/mcl4_coe/nvfp4.py:962-1048, built once and reused)."""
 
     def __init__(self, w_up: np.ndarray, w_dn: np.ndarray):
-        self.up_q = nr.quantize_grouped_weights(np.asarray(w_up, dtype=np.float32))
-        self.dn_q = nr.quantize_grouped_weights(np.asarray(w_dn, dtype=np.float32))
+        self.up_q = nr.quantize_grouped_weights(np.asarray(w_up, dtype=np.float32), with_bwd=False)
+        self.dn_q = nr.quantize_grouped_weights(np.asarray(w_dn, dtype=np.float32), with_bwd=False)
         n_exp = w_up.shape[0]
         self.up = [nr.dequantize_grouped_weight(self.up_q[0], self.up_q[1], self.up_q[2], e) for e in range(n_exp)]
         self.dn = [nr.dequantize_grouped_weight(self.dn_q[0], self.dn_q[1], self.dn_q[2], e) for e in range(n_exp)]

@@ -162,12 +162,13 @@ def quantize_activations(x: np.ndarray):
     return packed, scales
 
 
-def quantize_grouped_weights(w_batch: np.ndarray):
+def quantize_grouped_weights(w_batch: np.ndarray, with_bwd: bool = True):
     """src/mcl4_coe/nvfp4.py:923-952 (``_quantize_grouped_weights_core``).
 
     ``w_batch`` float32 ``[D, N, K]``.  Returns ``(b_fwd [D, K/2, N],
     bs_fwd [D, N, K/16], bg [D], b_bwd [D, N/2, K], bs_bwd [D, K, N/16])`` with
-    the e4m3 scales as uint8 bit patterns.  One float32 scale per expert
+    the e4m3 scales as uint8 bit patterns (the transposed copies are ``None``
+    when ``with_bwd`` is false).  One float32 scale per expert
     (``amax/2688``, :928-929); one e4m3 scale per 16x16 tile (:930-931).
     """
     w = np.ascontiguousarray(w_batch, dtype=np.float32)
@@ -184,6 +185,8 @@ def quantize_grouped_weights(w_batch: np.ndarray):
     inv_fwd = _inverse_decoding(e4m3_to_f32(bs_fwd) * bg.reshape(d, 1, 1))
     norm_fwd = (w.reshape(d, n, k // 16, 16) * inv_fwd[..., None]).reshape(d, n, k)
     b_fwd = np.ascontiguousarray(_pack_codes(e2m1_codes(norm_fwd)).transpose(0, 2, 1))
+    if not with_bwd:
+        return b_fwd, np.ascontiguousarray(bs_fwd), bg, None, None
 
     w_t = np.ascontiguousarray(w.transpose(0, 2, 1))
     bs_bwd = np.repeat(bs_tiles.transpose(0, 2, 1), 16, axis=1)  # [d, k, n/16]

@@ -1,0 +1,65 @@
+"""Host-side behaviour of the drop-in module that needs no GPU."""
+
+import pytest
+import torch
+
+
+def _cfg(pkg, **kw):
+    base = dict(d_model=256, expert_hidden_dim=256, num_experts=4, top_k=2)
+    base.update(kw)
+    return pkg.MoEConfig(**base)
+
+
+def test_parameter_names_match_the_reference_module(moe_pkg):
+    # src/mcl4_coe/backbone.py:182-183, :216-220
+    moe = moe_pkg.SparseMoE(_cfg(moe_pkg))
+    keys = set(moe.state_dict().keys())
+    expected = {"router.weight"}
+    for i in range(4):
+        expected |= {f"experts.{i}.up_proj.weight", f"experts.{i}.down_proj.weight"}
+    assert keys == expected
+    assert moe.experts[0].up_proj.weight.shape == (512, 256)  # [2F, d], gate rows first
+    assert moe.experts[0].down_proj.weight.shape == (256, 256)
+    assert moe.router.weight.shape == (4, 256)
+
+
+def test_config_validation_mirrors_reference():
+    from __graft_entry__ import load_package
+
+    pkg = load_package()
+    with pytest.raises(ValueError):
+        pkg.MoEConfig(num_experts=2, top_k=3)
+    with pytest.raises(ValueError):
+        pkg.MoEConfig(d_model=0)
+
+
+def test_no_cpu_fallback(moe_pkg):
+    moe = moe_pkg.SparseMoE(_cfg(moe_pkg))
+    with torch.no_grad(), pytest.raises(ValueError, match="CUDA"):
+        moe(torch.zeros(2, 3, 256))
+
+
+def test_cache_rejects_cpu_weights(moe_pkg):
+    moe = moe_pkg.SparseMoE(_cfg(moe_pkg))
+    with pytest.raises(ValueError, match="CUDA"):
+        moe_pkg.get_or_build_grouped_cache(moe.experts, "up_proj")
+
+
+def test_mitotic_pairs_round_trip_through_state_dict(moe_pkg):
+    # src/mcl4_coe/backbone.py:579-616
+    a = moe_pkg.SparseMoE(_cfg(moe_pkg))
+    a.mitotic_pairs = [(0, 3), (1, 2)]
+    sd = a.state_dict()
+    assert "mitotic_pairs_tensor" in sd
+    b = moe_pkg.SparseMoE(_cfg(moe_pkg))
+    b.load_state_dict(sd)
+    assert b.mitotic_pairs == [(0, 3), (1, 2)]
+
+
+def test_unsupported_routing_variants_raise(moe_pkg):
+    moe = moe_pkg.SparseMoE(_cfg(moe_pkg))
+    assert moe._unsupported_routing(None, None, None) is None
+    moe.mitotic_pairs = [(0, 1)]
+    assert moe._unsupported_routing(None, None, None) == "mitotic twin routing"
+    moe.mitotic_pairs = []
+    assert moe._unsupported_routing(None, [0, 1], None) == "dense expert subsets"
