@@ -145,7 +145,9 @@ typedef struct mcl4moe_moe_args {
   int32_t* offs;              /* int32 [E] inclusive ends of the expert segments, or NULL */
   int32_t* perm;              /* int32 [T*k] stable argsort of the selected experts, or NULL */
   uint16_t* h_debug;          /* bf16 [M_cap, F] SwiGLU output in padded order, or NULL */
-  int32_t* error_word;        /* device int32, set by a timed-out device wait; may be NULL */
+  int32_t* error_word;        /* device int32 set by a timed-out device wait, or NULL to use one inside the
+                                 workspace (cleared on every call).  A caller-owned word is sticky: while it
+                                 is nonzero the GEMM kernels skip their work. */
   void* workspace;
   size_t workspace_bytes;
   /* Optional cudaEvent_t[6] (NULL to skip): recorded on the stream before
@@ -161,7 +163,8 @@ int mcl4moe_moe_forward(const mcl4moe_moe_args* args, mcl4moe_stream_t stream);
 int64_t mcl4moe_padded_rows(int T, int E, int k);
 
 /* Device pointer of a named region inside a forward workspace (for tests and
- * debugging): 0 xq, 1 xs, 2 hq, 3 hs, 4 y, 5 pad_start, 6 slot_pos, 7 sorted_w. */
+ * debugging): 0 xq, 1 xs, 2 hq, 3 hs, 4 y, 5 pad_start, 6 slot_pos, 7 sorted_w,
+ * 8 the int32 device error word used when args.error_word is NULL. */
 void* mcl4moe_workspace_region(void* workspace, int region, int T, int d, int E, int k, int F);
 
 /* ------------------------------------------------------------------------

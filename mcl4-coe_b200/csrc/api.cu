@@ -163,6 +163,7 @@ void* mcl4moe_workspace_region(void* workspace, int region, int T, int d, int E,
     case 5: return w.route.pad_start;
     case 6: return w.slot_pos;
     case 7: return w.sorted_w;
+    case 8: return w.err;
     default: return nullptr;
   }
 }
@@ -171,7 +172,7 @@ int mcl4moe_moe_forward(const mcl4moe_moe_args* a, mcl4moe_stream_t stream) {
   if (!a) return MCL4MOE_ERR_INVALID;
   int st = check_moe_shape(a->T, a->d, a->E, a->k, a->F);
   if (st != MCL4MOE_OK) return st;
-  if (!a->out || !a->stats || !a->workspace || (a->T > 0 && (!a->x || !a->router_w))) return MCL4MOE_ERR_INVALID;
+  if (!a->stats || !a->workspace || (a->T > 0 && (!a->x || !a->router_w || !a->out))) return MCL4MOE_ERR_INVALID;
   if (!a->w_up || !a->w_up_scales || !a->w_up_g || !a->w_dn || !a->w_dn_scales || !a->w_dn_g)
     return MCL4MOE_ERR_INVALID;
   if (!aligned16(a->x) || !aligned16(a->out) || !aligned16(a->w_up) || !aligned16(a->w_dn) ||
@@ -182,7 +183,10 @@ int mcl4moe_moe_forward(const mcl4moe_moe_args* a, mcl4moe_stream_t stream) {
   if (a->workspace_bytes < w.bytes) return MCL4MOE_ERR_WORKSPACE;
   cudaStream_t s = stream;
   const int T = a->T, d = a->d, E = a->E, k = a->k, F = a->F;
+  // A caller-owned error word is sticky (kernels skip work while it is
+  // nonzero); the workspace's own word is cleared for every call.
   int32_t* err = a->error_word ? a->error_word : w.err;
+  if (!a->error_word && cudaMemsetAsync(w.err, 0, sizeof(int32_t), s) != cudaSuccess) return MCL4MOE_ERR_CUDA;
   int32_t* topk_idx = a->topk_idx ? a->topk_idx : w.topk_idx;
   float* topk_w = a->topk_w ? a->topk_w : w.topk_w;
 
@@ -289,6 +293,7 @@ int mcl4moe_grouped_linear(const uint16_t* x, int64_t M, int K, const int32_t* o
   uint8_t* xs = take(size_t(mcap) * K / 16);
   int32_t* err = error_word ? error_word : reinterpret_cast<int32_t*>(take(sizeof(int32_t)));
   cudaStream_t s = stream;
+  if (!error_word && cudaMemsetAsync(err, 0, sizeof(int32_t), s) != cudaSuccess) return MCL4MOE_ERR_CUDA;
   int st = launch_pad_from_offs(offs, E, pad_start, offs_start, counts, s);
   if (st != MCL4MOE_OK) return st;
   st = launch_quantize_grouped_rows(x, M, K, offs, pad_start, counts, E, xq, xs, s);

@@ -80,6 +80,90 @@ __device__ __forceinline__ uint32_t quantize_block16(const float (&v)[16], uint2
   return s;
 }
 
+// ---- packed bf16x2 helpers (low half = even element)
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ float bf16x2_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16x2_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+// Exact: the product of two bf16 values fits in float32, rounded once to bf16 (RN).
+__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t bf16x2_max(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+// 8 float32 values -> 8 E2M1 nibbles (element 0 in the low nibble) with the
+// reference's rounding, for products of a bfloat16 value and a global-scale-1
+// inverse block scale.  The hardware conversion rounds to nearest-even on the
+// E2M1 grid; the reference (src/mcl4_coe/nvfp4.py:188-193) rounds u = m+2 or
+// u = m/2+4 to float32 first, which differs only at |n| = 2.5+2^-22,
+// 5+2^-21 (reference one code lower) and 3.5-2^-22 (one code higher).  The
+// third value is not reachable from bf16 inputs (checked exhaustively over
+// every bf16 value and e4m3 scale), the first two are corrected here.
+__device__ __forceinline__ uint32_t e2m1x8_act(const float (&n)[8]) {
+  uint32_t w;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
+      "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+      : "=r"(w)
+      : "f"(n[0]), "f"(n[1]), "f"(n[2]), "f"(n[3]), "f"(n[4]), "f"(n[5]), "f"(n[6]), "f"(n[7]));
+  uint32_t fix = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) fix |= ((__float_as_uint(n[i]) & 0x7F7FFFFFu) == 0x40200001u ? 1u : 0u) << (4 * i);
+  return w - fix;
+}
+
+// Scale of one 16-element activation block (g = 1) and its inverse:
+// s = e4m3(min(amax/6, 448)), inv = min(1/dec, FLT_MAX) (src/mcl4_coe/nvfp4.py:215-221).
+__device__ __forceinline__ uint32_t act_block_scale(float amax, float& inv) {
+  const uint32_t s = f32_to_e4m3(fminf(__fdiv_rn(amax, 6.0f), 448.0f));
+  inv = inverse_decoding(e4m3_to_f32(s));
+  return s;
+}
+
+// Quantise 16 bf16 values (8 packed words) of one activation block.
+__device__ __forceinline__ uint32_t quantize_block16_bf16(const uint32_t (&w)[8], uint2& packed) {
+  uint32_t mx = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) mx = bf16x2_max(mx, w[i] & 0x7FFF7FFFu);
+  float inv;
+  const uint32_t s = act_block_scale(fmaxf(bf16x2_lo(mx), bf16x2_hi(mx)), inv);
+  float n[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    n[2 * i] = __fmul_rn(bf16x2_lo(w[i]), inv);
+    n[2 * i + 1] = __fmul_rn(bf16x2_hi(w[i]), inv);
+  }
+  packed.x = e2m1x8_act(n);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    n[2 * i] = __fmul_rn(bf16x2_lo(w[4 + i]), inv);
+    n[2 * i + 1] = __fmul_rn(bf16x2_hi(w[4 + i]), inv);
+  }
+  packed.y = e2m1x8_act(n);
+  return s;
+}
+
+// SiLU of a bf16-rounded gate value: g / (1 + 2^(-g log2 e)) with the
+// hardware exp2 and reciprocal approximations (a few float32 ulps).
+__device__ __forceinline__ float silu_f32(float g) {
+  float e, r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(g * -1.4426950408889634f));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + e));
+  return g * r;
+}
+
 // Byte offset of scale (row r, 16-block c) in the 128x4 scale atoms
 // (src/mcl4_coe/nvfp4.py:131-144; the layout tcgen05 block-scaled MMA reads).
 __device__ __host__ __forceinline__ uint64_t swizzled_scale_offset(uint64_t r, uint32_t c, uint32_t blocks_per_row) {
@@ -204,6 +288,19 @@ __device__ __forceinline__ void tc_mma_nvf4(uint32_t d_tmem, uint64_t a_desc, ui
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns -> 32 registers per thread.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
       : "memory");
 }
 

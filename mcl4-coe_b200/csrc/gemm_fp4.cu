@@ -10,10 +10,10 @@
 // belongs to exactly one expert and its scales are whole 128x4 atoms.
 // Tile 128 x 256, K step 256 (one 128-byte swizzle row of packed FP4).
 //
-// Warp roles (320 threads, one CTA per SM):
+// Warp roles (576 threads, one CTA per SM):
 //   warp 0      TMA producer: A tile, two 128-row B halves, 3 scale bulk copies
 //   warp 1      TMEM owner + single-thread MMA issuer (scales smem -> TMEM, 4 MMAs)
-//   warps 2..9  epilogue: TMEM -> registers, then
+//   warps 2..17 epilogue: TMEM -> registers, then
 //               mode 0 (gate/up): SwiGLU in bf16 and NVFP4 re-quantisation of h
 //                                 (src/mcl4_coe/backbone.py:572-574)
 //               mode 1 (down):    bf16(acc*g) [* bf16(routing weight)] to bf16 rows
@@ -42,7 +42,7 @@ constexpr uint32_t kSFA = kBM * kBK / 16;     // 2048
 constexpr uint32_t kSFBHalf = 128 * kBK / 16;  // 2048
 constexpr uint32_t kStageBytes = kATile + 2 * kBHalf + kSFA + 2 * kSFBHalf;  // 55296
 constexpr uint32_t kOffB = kATile, kOffSFA = kATile + 2 * kBHalf, kOffSFB = kOffSFA + kSFA;
-constexpr int kEpiWarps = 8;
+constexpr int kEpiWarps = 16;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kSfCol0 = 256;          // accumulator uses columns [0, 256)
@@ -66,11 +66,6 @@ __device__ __forceinline__ int find_expert(const int32_t* pad_s, int E, int row)
     else hi = mid;
   }
   return lo - 1;
-}
-
-__device__ __forceinline__ float silu_bf16(float g) {
-  // F.silu on a bf16 tensor: g / (1 + exp(-g)) in float32, rounded to bf16.
-  return round_bf16(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
 }
 
 }  // namespace
@@ -214,8 +209,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;             // TMEM lane quarter this warp may access
-    const int ch = (warp - 2) >> 2;     // column half handled by this warp
+    // 16 warps: lane quarter q = warp % 4 (the TMEM lanes a warp may read),
+    // column group sub = 0..3 (32 h columns in mode 0, 64 output columns in mode 1).
+    const int q = warp & 3;
+    const int sub = (warp - 2) >> 2;
     const int row_in_tile = q * 32 + lane;
     const uint32_t lane_addr = tmem_base + (uint32_t(q * 32) << 16);
     uint32_t acc_phase = 0;
@@ -224,16 +221,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(tfull_bar, acc_phase, args.err, 301)) break;
       acc_phase ^= 1u;
       tc_fence_after();
-      uint32_t v[8][16];
+      uint32_t va[32], vb[32];
       if (args.mode == 0) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          tmem_ld16(lane_addr + ch * 64 + 16 * i, v[i]);            // gate columns
-          tmem_ld16(lane_addr + 128 + ch * 64 + 16 * i, v[4 + i]);  // value columns
-        }
+        tmem_ld32(lane_addr + sub * 32, va);        // gate columns
+        tmem_ld32(lane_addr + 128 + sub * 32, vb);  // value columns
       } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) tmem_ld16(lane_addr + ch * 128 + 16 * i, v[i]);
+        tmem_ld32(lane_addr + sub * 64, va);
+        tmem_ld32(lane_addr + sub * 64 + 32, vb);
       }
       tmem_wait_ld();
       tc_fence_before();
@@ -245,54 +239,63 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool row_valid = args.row_count == nullptr || local < args.row_count[c.e];
       const float gb = args.b_g[c.e];
       if (args.mode == 0) {
+        // up = bf16(acc * g); h = bf16(bf16(silu(gate)) * value) (src/mcl4_coe/backbone.py:572-574),
+        // then NVFP4 with 1x16 row scales (src/mcl4_coe/nvfp4.py:197-225).
         const int F = args.F;
-        const int hb0 = c.nt * 8 + ch * 4;  // first 16-column block of h handled here
+        const int hb0 = c.nt * 8 + sub * 2;  // first 16-column block of h handled here
+        uint32_t packed[4];
         uint32_t sword = 0;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float h[16];
+        for (int blk = 0; blk < 2; ++blk) {
+          uint32_t hh[8];
+          uint32_t mx = 0;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const float g = round_bf16(__fmul_rn(__uint_as_float(v[i][j]), gb));
-            const float u = round_bf16(__fmul_rn(__uint_as_float(v[4 + i][j]), gb));
-            h[j] = round_bf16(__fmul_rn(silu_bf16(g), u));
+          for (int pr = 0; pr < 8; ++pr) {
+            const int j = blk * 16 + 2 * pr;
+            const uint32_t gg = pack_bf16x2(__uint_as_float(va[j]) * gb, __uint_as_float(va[j + 1]) * gb);
+            const uint32_t uu = pack_bf16x2(__uint_as_float(vb[j]) * gb, __uint_as_float(vb[j + 1]) * gb);
+            const uint32_t ss = pack_bf16x2(silu_f32(bf16x2_lo(gg)), silu_f32(bf16x2_hi(gg)));
+            hh[pr] = bf16x2_mul(ss, uu);
+            mx = bf16x2_max(mx, hh[pr] & 0x7FFF7FFFu);
           }
-          uint2 pk;
-          const uint32_t s = quantize_block16(h, pk);
-          sword |= s << (8 * i);
-          *reinterpret_cast<uint2*>(args.hq + p * (F / 2) + (hb0 + i) * 8) = pk;
-          if (args.h_dbg != nullptr) {
-            uint32_t o[8];
+          float inv;
+          sword |= act_block_scale(fmaxf(bf16x2_lo(mx), bf16x2_hi(mx)), inv) << (8 * blk);
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-              o[j] = uint32_t(f32_to_bf16(h[2 * j])) | (uint32_t(f32_to_bf16(h[2 * j + 1])) << 16);
-            uint4* dst = reinterpret_cast<uint4*>(args.h_dbg + p * F + (hb0 + i) * 16);
-            dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-            dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+          for (int half = 0; half < 2; ++half) {
+            float n[8];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              n[2 * i] = __fmul_rn(bf16x2_lo(hh[half * 4 + i]), inv);
+              n[2 * i + 1] = __fmul_rn(bf16x2_hi(hh[half * 4 + i]), inv);
+            }
+            packed[blk * 2 + half] = e2m1x8_act(n);
+          }
+          if (args.h_dbg != nullptr) {
+            uint4* dst = reinterpret_cast<uint4*>(args.h_dbg + p * F + (hb0 + blk) * 16);
+            dst[0] = make_uint4(hh[0], hh[1], hh[2], hh[3]);
+            dst[1] = make_uint4(hh[4], hh[5], hh[6], hh[7]);
           }
         }
-        *reinterpret_cast<uint32_t*>(args.hs + swizzled_scale_offset(uint64_t(p), uint32_t(hb0), uint32_t(F / 16))) =
-            sword;
+        *reinterpret_cast<uint4*>(args.hq + p * (F / 2) + hb0 * 8) =
+            make_uint4(packed[0], packed[1], packed[2], packed[3]);
+        *reinterpret_cast<uint16_t*>(args.hs +
+                                     swizzled_scale_offset(uint64_t(p), uint32_t(hb0), uint32_t(F / 16))) =
+            uint16_t(sword);
       } else if (row_valid) {
+        // y = bf16(acc * g) [* bf16(routing weight), rounded to bf16] (src/mcl4_coe/backbone.py:903)
         const int64_t dst_row = args.out_row_base ? int64_t(args.out_row_base[c.e]) + local : p;
-        const float wv = args.row_w ? round_bf16(args.row_w[p]) : 1.0f;
-        uint16_t* dst = args.y + dst_row * args.ldy + c.nt * kBN + ch * 128;
+        const uint32_t ww = args.row_w ? pack_bf16x2(args.row_w[p], args.row_w[p]) : 0u;
+        uint4* dst = reinterpret_cast<uint4*>(args.y + dst_row * args.ldy + c.nt * kBN + sub * 64);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          uint32_t o[8];
+          const uint32_t* src = i < 4 ? va + 8 * i : vb + 8 * (i - 4);
+          uint32_t o[4];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            float a0 = round_bf16(__fmul_rn(__uint_as_float(v[i][2 * j]), gb));
-            float a1 = round_bf16(__fmul_rn(__uint_as_float(v[i][2 * j + 1]), gb));
-            if (args.row_w) {
-              a0 = __fmul_rn(a0, wv);
-              a1 = __fmul_rn(a1, wv);
-            }
-            o[j] = uint32_t(f32_to_bf16(a0)) | (uint32_t(f32_to_bf16(a1)) << 16);
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t yy = pack_bf16x2(__uint_as_float(src[2 * j]) * gb, __uint_as_float(src[2 * j + 1]) * gb);
+            o[j] = args.row_w ? bf16x2_mul(yy, ww) : yy;
           }
-          uint4* d4 = reinterpret_cast<uint4*>(dst + 16 * i);
-          d4[0] = make_uint4(o[0], o[1], o[2], o[3]);
-          d4[1] = make_uint4(o[4], o[5], o[6], o[7]);
+          dst[i] = make_uint4(o[0], o[1], o[2], o[3]);
         }
       }
     }

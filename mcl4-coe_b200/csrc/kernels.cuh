@@ -19,6 +19,8 @@ struct RouteWorkspace {
   int32_t* pad_start;    // [E + 1] padded row start of each expert (multiple of 128)
   int32_t* offs_start;   // [E]     unpadded row start of each expert
   int32_t* counts;       // [E]     routed slots per expert
+  float* probs_sum;      // [E]     sum of routed probabilities per expert
+  uint32_t* done;        // [1]     finished-expert counter of the scan (zeroed by the router)
   size_t bytes;
 };
 
@@ -41,6 +43,8 @@ inline RouteWorkspace route_workspace(void* base, int T, int E, int k) {
   w.pad_start = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * (E + 1)));
   w.offs_start = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * E));
   w.counts = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * E));
+  w.probs_sum = reinterpret_cast<float*>(take(sizeof(float) * E));
+  w.done = reinterpret_cast<uint32_t*>(take(sizeof(uint32_t)));
   w.bytes = off;
   return w;
 }

@@ -167,14 +167,8 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const uint16_t* __restri
       const uint4* src = reinterpret_cast<const uint4*>(x + row * ld_x + b * 16);
       uint4 u0 = __ldg(src), u1 = __ldg(src + 1);
       const uint32_t wds[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-      float v[16];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        v[2 * i] = bf16_to_f32(uint16_t(wds[i] & 0xFFFFu));
-        v[2 * i + 1] = bf16_to_f32(uint16_t(wds[i] >> 16));
-      }
       uint2 pk;
-      s = quantize_block16(v, pk);
+      s = quantize_block16_bf16(wds, pk);
       *reinterpret_cast<uint2*>(packed + row * (cols / 2) + b * 8) = pk;
     }
     if (!swizzled) {

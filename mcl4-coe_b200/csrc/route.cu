@@ -65,6 +65,7 @@ __global__ void __launch_bounds__(kRouteThreads) router_kernel(
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int chunk = blockIdx.x;
   const int t0 = chunk * kRouteTokens;
+  if (chunk == 0 && tid == 0) *ws.done = 0u;  // the scan kernel runs after this one
 
   // ------------------------------------------------ logits
   if (logits_in != nullptr) {
@@ -277,65 +278,116 @@ __global__ void __launch_bounds__(kRouteThreads) router_kernel(
   }
 }
 
-// Single CTA: per-expert exclusive prefix over chunks, expert offsets, statistics.
-__global__ void __launch_bounds__(256) route_scan_kernel(int C, int E, int k, RouteWorkspace ws, int32_t* counts_out,
-                                                         float* stats, int32_t* offs_out) {
-  __shared__ int32_t cnt_s[kMaxExperts];
-  __shared__ float psum_s[kMaxExperts];
-  __shared__ float misc_s[2];
-  const int tid = threadIdx.x;
-  for (int e = tid; e < E; e += blockDim.x) {
-    int32_t run = 0;
-    float ps = 0.f;
-    for (int c = 0; c < C; ++c) {
-      const int32_t v = ws.chunk_excl[int64_t(c) * E + e];
-      ws.chunk_excl[int64_t(c) * E + e] = run;
-      run += v;
-      ps = __fadd_rn(ps, ws.part_probs[int64_t(c) * E + e]);
-    }
-    cnt_s[e] = run;
-    psum_s[e] = ps;
+// One CTA per expert: exclusive prefix of the expert's per-chunk slot counts
+// (a block-wide scan over chunks) and its probability sum.  The last CTA to
+// finish (counted with an atomic after a memory fence; no CTA waits on
+// another) lays out the expert segments and finalises the statistics.
+namespace {
+
+__device__ __forceinline__ int32_t block_exclusive_scan(int32_t v, int32_t* tmp, int32_t& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int32_t x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int32_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
   }
-  if (tid == 0) {
-    float l2 = 0.f, nv = 0.f;
-    for (int c = 0; c < C; ++c) {
-      l2 = __fadd_rn(l2, ws.part_misc[2 * c]);
-      nv = __fadd_rn(nv, ws.part_misc[2 * c + 1]);
+  if (lane == 31) tmp[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int32_t w = lane < nw ? tmp[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
     }
-    misc_s[0] = l2;
-    misc_s[1] = nv;
+    if (lane < nw) tmp[32 + lane] = w;
   }
   __syncthreads();
+  total = tmp[32 + nw - 1];
+  const int32_t before = warp ? tmp[32 + warp - 1] : 0;
+  __syncthreads();
+  return before + x - v;
+}
+
+// Deterministic block sum: fixed xor tree in each warp, warps added in order.
+__device__ __forceinline__ float block_sum(float v, float* tmp) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if (lane == 0) tmp[warp] = v;
+  __syncthreads();
+  float s = 0.f;
+  for (int w = 0; w < nw; ++w) s = __fadd_rn(s, tmp[w]);
+  __syncthreads();
+  return s;
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(256) route_scan_kernel(int C, int E, int k, RouteWorkspace ws, int32_t* counts_out,
+                                                         float* stats, int32_t* offs_out) {
+  __shared__ int32_t itmp[64];
+  __shared__ float ftmp[32];
+  __shared__ bool is_last;
+  const int tid = threadIdx.x;
+  const int e = blockIdx.x;
+  const int per = (C + blockDim.x - 1) / blockDim.x;
+  const int c0 = tid * per, c1 = min(C, c0 + per);
+  int32_t mine = 0;
+  float ps = 0.f;
+  for (int c = c0; c < c1; ++c) {
+    mine += ws.chunk_excl[int64_t(c) * E + e];
+    ps = __fadd_rn(ps, ws.part_probs[int64_t(c) * E + e]);
+  }
+  int32_t total;
+  int32_t run = block_exclusive_scan(mine, itmp, total);
+  for (int c = c0; c < c1; ++c) {
+    const int32_t v = ws.chunk_excl[int64_t(c) * E + e];
+    ws.chunk_excl[int64_t(c) * E + e] = run;
+    run += v;
+  }
+  const float psum = block_sum(ps, ftmp);
   if (tid == 0) {
-    int32_t run = 0, prun = 0;
-    for (int e = 0; e < E; ++e) {
-      ws.offs_start[e] = run;
-      ws.pad_start[e] = prun;
-      ws.counts[e] = cnt_s[e];
-      run += cnt_s[e];
-      prun += (cnt_s[e] + 127) / 128 * 128;
-      if (offs_out) offs_out[e] = run;
-      if (counts_out) counts_out[e] = cnt_s[e];
+    ws.counts[e] = total;
+    ws.probs_sum[e] = psum;
+    __threadfence();
+    is_last = atomicAdd(ws.done, 1u) == uint32_t(E - 1);
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+
+  // ---- last CTA: expert layout and statistics
+  float l2 = 0.f, nv = 0.f;
+  for (int c = c0; c < c1; ++c) {
+    l2 = __fadd_rn(l2, ws.part_misc[2 * c]);
+    nv = __fadd_rn(nv, ws.part_misc[2 * c + 1]);
+  }
+  const float lse2 = block_sum(l2, ftmp);
+  const float n = block_sum(nv, ftmp);
+  if (tid == 0) {
+    int32_t urun = 0, prun = 0;
+    float aux = 0.f;
+    const float denom = n * float(k);
+    for (int x = 0; x < E; ++x) {
+      const int32_t cnt = __ldcg(ws.counts + x);
+      ws.offs_start[x] = urun;
+      ws.pad_start[x] = prun;
+      urun += cnt;
+      prun += (cnt + 127) / 128 * 128;
+      if (offs_out) offs_out[x] = urun;
+      if (counts_out) counts_out[x] = cnt;
+      if (stats) {
+        const float cf = n > 0.f ? __fdiv_rn(float(cnt), denom) : 0.f;
+        stats[3 + x] = cf;
+        if (n > 0.f) aux = __fadd_rn(aux, __fmul_rn(cf, __fdiv_rn(__ldcg(ws.probs_sum + x), n)));
+      }
     }
     ws.pad_start[E] = prun;
     if (stats) {
-      const float n = misc_s[1];
-      float aux = 0.f;
-      if (n > 0.f) {
-        const float denom = n * float(k);
-        for (int e = 0; e < E; ++e) {
-          const float cf = __fdiv_rn(float(cnt_s[e]), denom);
-          const float mp = __fdiv_rn(psum_s[e], n);
-          stats[3 + e] = cf;
-          aux = __fadd_rn(aux, __fmul_rn(cf, mp));
-        }
-        stats[0] = __fmul_rn(float(E), aux);
-        stats[1] = __fdiv_rn(misc_s[0], n);
-      } else {
-        for (int e = 0; e < E; ++e) stats[3 + e] = 0.f;
-        stats[0] = 0.f;
-        stats[1] = 0.f;
-      }
+      stats[0] = n > 0.f ? __fmul_rn(float(E), aux) : 0.f;
+      stats[1] = n > 0.f ? __fdiv_rn(lse2, n) : 0.f;
       stats[2] = n;
     }
   }
@@ -377,7 +429,10 @@ int launch_route(const uint16_t* x, const float* wr, const float* bias, const fl
     if (st != MCL4MOE_OK) return st;
   }
   const int C = (T + kRouteTokens - 1) / kRouteTokens;
-  route_scan_kernel<<<1, 256, 0, stream>>>(C, E, k, ws, counts_out, stats, offs_out);
+  if (T == 0) {  // no router CTA ran: reset the finished-expert counter here
+    if (cudaMemsetAsync(ws.done, 0, sizeof(uint32_t), stream) != cudaSuccess) return MCL4MOE_ERR_CUDA;
+  }
+  route_scan_kernel<<<E, 256, 0, stream>>>(C, E, k, ws, counts_out, stats, offs_out);
   return cudaGetLastError() == cudaSuccess ? MCL4MOE_OK : MCL4MOE_ERR_CUDA;
 }
 
@@ -429,13 +484,7 @@ __global__ void __launch_bounds__(256) permute_quant_kernel(
       const uint4* src = reinterpret_cast<const uint4*>(x + int64_t(t) * d + b * 16);
       uint4 u0 = __ldg(src), u1 = __ldg(src + 1);
       const uint32_t wds[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-      float v[16];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        v[2 * i] = bf16_to_f32(uint16_t(wds[i] & 0xFFFFu));
-        v[2 * i + 1] = bf16_to_f32(uint16_t(wds[i] >> 16));
-      }
-      s = quantize_block16(v, pk);
+      s = quantize_block16_bf16(wds, pk);
     }
     const int base_lane = lane & ~3;
     uint32_t word = 0;
@@ -523,13 +572,7 @@ __global__ void __launch_bounds__(256) quant_grouped_rows_kernel(const uint16_t*
       const uint4* src = reinterpret_cast<const uint4*>(x + m * K + b * 16);
       uint4 u0 = __ldg(src), u1 = __ldg(src + 1);
       const uint32_t wds[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-      float v[16];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        v[2 * i] = bf16_to_f32(uint16_t(wds[i] & 0xFFFFu));
-        v[2 * i + 1] = bf16_to_f32(uint16_t(wds[i] >> 16));
-      }
-      s = quantize_block16(v, pk);
+      s = quantize_block16_bf16(wds, pk);
       *reinterpret_cast<uint2*>(xq + p * (K / 2) + b * 8) = pk;
     }
     const int base_lane = lane & ~3;

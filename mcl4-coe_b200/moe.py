@@ -263,6 +263,17 @@ class SparseMoE(nn.Module):
                 res["hs"] = region(3, mcap * F // 16).clone()
         return res
 
+    def read_device_error(self) -> int:
+        """Synchronise and return the error word of the last forward (0 = every
+        device-side wait completed; 1xx/2xx/3xx = TMA producer / MMA issuer /
+        epilogue wait of a GEMM gave up after its time limit)."""
+        if self._ws is None or self._ws_key is None:
+            return 0
+        T, d, E, k, F, _ = self._ws_key
+        lib = _lib.load()
+        off = lib.mcl4moe_workspace_region(self._ws.data_ptr(), 8, T, d, E, k, F) - self._ws.data_ptr()
+        return int(self._ws[off:off + 4].view(torch.int32).item())
+
     # ------------------------------------------------------------------ state dict
     def _save_to_state_dict(self, destination: dict, prefix: str, keep_vars: bool) -> None:
         super()._save_to_state_dict(destination, prefix, keep_vars)

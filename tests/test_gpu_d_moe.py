@@ -53,6 +53,7 @@ def test_layer_matches_oracle(moe_pkg, name):
     valid = None if c["valid"] is None else torch.from_numpy(c["valid"].astype(bool)).to(DEV)
     det = moe.forward_details(x_tensor(c, DEV), valid)
     torch.cuda.synchronize()
+    assert moe.read_device_error() == 0
     experts = moe_ref.QuantizedExperts(c["w_up"], c["w_dn"])
     r = moe_ref.route(_x_np(c), c["wr"], c["k"], c["norm_topk_prob"], c["valid"], c["logit_bias"])
     act = r.active
@@ -159,6 +160,7 @@ def test_full_size_headline_config(moe_pkg):
         out2 = moe(x)[0]
     torch.cuda.synchronize()
     out = det["out"]
+    assert moe.read_device_error() == 0
     assert torch.equal(out, out2), "forward is not deterministic"
     assert torch.isfinite(out.float()).all()
     counts = det["counts"].cpu().numpy()
@@ -191,6 +193,7 @@ def test_decode_config(moe_pkg):
     x = x_tensor(c, DEV)
     det = moe.forward_details(x)
     torch.cuda.synchronize()
+    assert moe.read_device_error() == 0
     ref_cache = {p: moe_pkg.export_reference_cache(moe.experts, p) for p in ("up_proj", "down_proj")}
     w_up = dequant_reference_layout(ref_cache["up_proj"]["B_fwd"], ref_cache["up_proj"]["Bs_fwd"].view(torch.uint8),
                                     ref_cache["up_proj"]["Bg"])
@@ -219,3 +222,18 @@ def test_forward_requires_no_grad(moe_pkg):
     moe = build_module(moe_pkg, c, DEV)
     with pytest.raises(NotImplementedError):
         moe(x_tensor(c, DEV))
+
+
+def test_garbage_workspace_does_not_leak_into_results(moe_pkg):
+    """A recycled (non-zero) workspace must not change anything: every region the
+    kernels read is written first, and the device error word is cleared per call."""
+    c = moe_case(25, 64, 2048, 64, 8, 1024)
+    moe = build_module(moe_pkg, c, DEV)
+    x = x_tensor(c, DEV)
+    with torch.no_grad():
+        ref = moe(x)[0].clone()
+        moe._ws.fill_(0xA5)
+        got = moe(x)[0]
+    torch.cuda.synchronize()
+    assert moe.read_device_error() == 0
+    assert torch.equal(ref, got)
