@@ -341,12 +341,16 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--tokens", type=int, default=0, help="override the configuration's token count (profiling)")
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--cpu-sample", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.tokens > 0:
+        CONFIGS[args.config] = dict(CONFIGS[args.config], t=args.tokens,
+                                    name=f"{CONFIGS[args.config]['name']}_t{args.tokens}")
     if args.impl == "reference":
         run_reference(args)
     else:

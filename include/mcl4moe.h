@@ -99,14 +99,17 @@ int mcl4moe_quantize_activations(const uint16_t* x, int64_t rows, int cols, int6
  * fp32 logits x @ Wr^T (+ optional additive bias), softmax, top-k with
  * optional renormalisation, selection mask, counts, aux and z loss.
  * Tokens with valid[t] == 0 are not routed (loop-branch semantics).
- * logits_in (nullable) replaces the router product: then x and wr are unused.
+ * logits_in (nullable) are final logits (any bias already added) that replace
+ * the router product: then x, wr and logit_bias are unused.
  * Outputs: topk_idx int32 [T, k], topk_w fp32 [T, k] (0 for invalid tokens),
  * logits_out fp32 [T, E] (nullable), sel_mask fp32 [T, E] (nullable),
  * counts int32 [E], stats fp32 [3 + E]: {aux_loss, z_loss, n_routed,
  * counts_fraction[E]} (the layer's aux, router_z_loss and counts outputs).
- * Requires E <= 256, k <= min(E, 32), d % 32 == 0.
+ * The router product runs on the tensor cores with the fp32 weight split into
+ * three bf16 parts (fp32-accurate logits).  Requires E <= 256,
+ * k <= min(E, 32), d % 64 == 0.
  * ------------------------------------------------------------------------ */
-size_t mcl4moe_route_workspace_size(int T, int E, int k);
+size_t mcl4moe_route_workspace_size(int T, int E, int k, int d);
 int mcl4moe_route(const uint16_t* x, const float* wr, const float* logit_bias, const float* logits_in,
                   const uint8_t* valid, int T, int d, int E, int k, int norm_topk_prob, int32_t* topk_idx,
                   float* topk_w, float* logits_out, float* sel_mask, int32_t* counts, float* stats,

@@ -101,7 +101,7 @@ def load() -> ctypes.CDLL:
     lib.mcl4moe_quantize_activations.argtypes = [c_void_p, c_int64, c_int, c_int64, c_void_p, c_void_p, c_int,
                                                  c_void_p]
     lib.mcl4moe_route_workspace_size.restype = c_size_t
-    lib.mcl4moe_route_workspace_size.argtypes = [c_int, c_int, c_int]
+    lib.mcl4moe_route_workspace_size.argtypes = [c_int, c_int, c_int, c_int]
     lib.mcl4moe_route.restype = c_int
     lib.mcl4moe_route.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
                                   c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,

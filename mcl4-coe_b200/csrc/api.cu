@@ -33,7 +33,7 @@ struct MoeWorkspace {
 MoeWorkspace moe_workspace(void* base, int T, int d, int E, int k, int F) {
   MoeWorkspace w{};
   uint8_t* p = static_cast<uint8_t*>(base);
-  w.route = route_workspace(base, T, E, k);
+  w.route = route_workspace(base, T, E, k, d);
   size_t off = w.route.bytes;
   auto take = [&](size_t bytes) {
     uint8_t* r = p ? p + off : nullptr;
@@ -127,7 +127,9 @@ int mcl4moe_quantize_activations(const uint16_t* x, int64_t rows, int cols, int6
   return launch_quantize_activations(x, rows, cols, ld_x, packed, scales, swizzled, stream);
 }
 
-size_t mcl4moe_route_workspace_size(int T, int E, int k) { return route_workspace(nullptr, T, E, k).bytes; }
+size_t mcl4moe_route_workspace_size(int T, int E, int k, int d) {
+  return route_workspace(nullptr, T, E, k, d > 0 ? d : 0).bytes;
+}
 
 int mcl4moe_route(const uint16_t* x, const float* wr, const float* logit_bias, const float* logits_in,
                   const uint8_t* valid, int T, int d, int E, int k, int norm_topk_prob, int32_t* topk_idx,
@@ -137,12 +139,12 @@ int mcl4moe_route(const uint16_t* x, const float* wr, const float* logit_bias, c
   if (E > kMaxExperts || k > kMaxTopK) return MCL4MOE_ERR_UNSUPPORTED;
   if (!logits_in) {
     if (!x || !wr || d <= 0) return MCL4MOE_ERR_INVALID;
-    if (d % 32 != 0 || !aligned16(x) || !aligned16(wr)) return MCL4MOE_ERR_UNSUPPORTED;
+    if (d % 64 != 0 || !aligned16(x) || !aligned16(wr)) return MCL4MOE_ERR_UNSUPPORTED;
   }
-  const RouteWorkspace ws = route_workspace(workspace, T, E, k);
+  const RouteWorkspace ws = route_workspace(workspace, T, E, k, d > 0 ? d : 0);
   if (workspace_bytes < ws.bytes) return MCL4MOE_ERR_WORKSPACE;
   return launch_route(x, wr, logit_bias, logits_in, valid, T, d, E, k, norm_topk_prob, topk_idx, topk_w, logits_out,
-                      sel_mask, counts, stats, nullptr, ws, stream);
+                      sel_mask, counts, stats, nullptr, nullptr, ws, stream);
 }
 
 int64_t mcl4moe_padded_rows(int T, int E, int k) { return padded_rows_cap(T, E, k); }
@@ -197,7 +199,7 @@ int mcl4moe_moe_forward(const mcl4moe_moe_args* a, mcl4moe_stream_t stream) {
   };
   if ((st = mark(0)) != MCL4MOE_OK) return st;
   st = launch_route(a->x, a->router_w, a->logit_bias, nullptr, a->valid, T, d, E, k, a->norm_topk_prob, topk_idx,
-                    topk_w, nullptr, a->sel_mask, w.counts, a->stats, a->offs, w.route, s);
+                    topk_w, nullptr, a->sel_mask, w.counts, a->stats, a->offs, err, w.route, s);
   if (st != MCL4MOE_OK) return st;
   if ((st = mark(1)) != MCL4MOE_OK) return st;
   if (T == 0) {

@@ -218,6 +218,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
       const TileCoord c = coord(t);
+      // per-tile scalars first: their load latency overlaps the MMAs of this tile
+      const int64_t p = int64_t(c.mb) * kBM + row_in_tile;  // padded row
+      const int local = int(p - pad_s[c.e]);
+      const float gb = __ldg(args.b_g + c.e);
+      const int rows_e = args.row_count ? __ldg(args.row_count + c.e) : (1 << 30);
+      const float wrow = (args.mode == 1 && args.row_w && local < rows_e) ? __ldg(args.row_w + p) : 0.f;
       if (!mbar_wait(tfull_bar, acc_phase, args.err, 301)) break;
       acc_phase ^= 1u;
       tc_fence_after();
@@ -234,10 +240,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar);  // accumulator may be overwritten now
 
-      const int64_t p = int64_t(c.mb) * kBM + row_in_tile;  // padded row
-      const int local = int(p - pad_s[c.e]);
-      const bool row_valid = args.row_count == nullptr || local < args.row_count[c.e];
-      const float gb = args.b_g[c.e];
+      const bool row_valid = local < rows_e;
       if (args.mode == 0) {
         // up = bf16(acc * g); h = bf16(bf16(silu(gate)) * value) (src/mcl4_coe/backbone.py:572-574),
         // then NVFP4 with 1x16 row scales (src/mcl4_coe/nvfp4.py:197-225).
@@ -284,7 +287,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else if (row_valid) {
         // y = bf16(acc * g) [* bf16(routing weight), rounded to bf16] (src/mcl4_coe/backbone.py:903)
         const int64_t dst_row = args.out_row_base ? int64_t(args.out_row_base[c.e]) + local : p;
-        const uint32_t ww = args.row_w ? pack_bf16x2(args.row_w[p], args.row_w[p]) : 0u;
+        const uint32_t ww = pack_bf16x2(wrow, wrow);
         uint4* dst = reinterpret_cast<uint4*>(args.y + dst_row * args.ldy + c.nt * kBN + sub * 64);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {

@@ -8,7 +8,7 @@ namespace mcl4 {
 constexpr int kMaxWeightBatch = 256;  // weight matrices per quantiser launch
 constexpr int kMaxExperts = 256;
 constexpr int kMaxTopK = 32;
-constexpr int kRouteTokens = 64;      // tokens per router CTA (= permutation chunk)
+constexpr int kRouteTokens = 128;     // tokens per router CTA (= permutation chunk)
 
 // ---- workspace layout of the routing stage (all offsets 256-byte aligned)
 struct RouteWorkspace {
@@ -21,12 +21,13 @@ struct RouteWorkspace {
   int32_t* counts;       // [E]     routed slots per expert
   float* probs_sum;      // [E]     sum of routed probabilities per expert
   uint32_t* done;        // [1]     finished-expert counter of the scan (zeroed by the router)
+  uint16_t* wsplit;      // [3][E_pad][d] bf16 parts of the router weight (hi, mid, lo)
   size_t bytes;
 };
 
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-inline RouteWorkspace route_workspace(void* base, int T, int E, int k) {
+inline RouteWorkspace route_workspace(void* base, int T, int E, int k, int d) {
   RouteWorkspace w{};
   const int C = (T + kRouteTokens - 1) / kRouteTokens;
   uint8_t* p = static_cast<uint8_t*>(base);
@@ -45,6 +46,7 @@ inline RouteWorkspace route_workspace(void* base, int T, int E, int k) {
   w.counts = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * E));
   w.probs_sum = reinterpret_cast<float*>(take(sizeof(float) * E));
   w.done = reinterpret_cast<uint32_t*>(take(sizeof(uint32_t)));
+  w.wsplit = reinterpret_cast<uint16_t*>(take(sizeof(uint16_t) * 3 * size_t((E + 15) / 16 * 16) * size_t(d)));
   w.bytes = off;
   return w;
 }
@@ -65,8 +67,8 @@ int launch_quantize_activations(const uint16_t* x, int64_t rows, int cols, int64
 // Router + top-k + chunk ranks + scan (+ statistics), writes topk/sel_mask/stats and fills ``ws``.
 int launch_route(const uint16_t* x, const float* wr, const float* bias, const float* logits_in, const uint8_t* valid,
                  int T, int d, int E, int k, int norm_topk, int32_t* topk_idx, float* topk_w, float* logits_out,
-                 float* sel_mask, int32_t* counts_out, float* stats, int32_t* offs_out, const RouteWorkspace& ws,
-                 cudaStream_t stream);
+                 float* sel_mask, int32_t* counts_out, float* stats, int32_t* offs_out, int32_t* err,
+                 const RouteWorkspace& ws, cudaStream_t stream);
 
 // Scatter each routed token's NVFP4 row into its k padded expert-major slots.
 int launch_permute_quantize(const uint16_t* x, const uint8_t* valid, const int32_t* topk_idx, const float* topk_w,

@@ -1,0 +1,666 @@
+// Router: logits, softmax, top-k, routing statistics and per-chunk stable
+// ranks; then the per-expert scan that lays out the expert segments.
+//
+// Restates the routing part of SparseMoE.forward
+// (src/mcl4_coe/backbone.py:787-883, loop branch :913-1004):
+//   logits = x.float() @ Wr.float()^T (+ bias)   probs = softmax(logits)
+//   w, sel = topk(probs, k)  (w /= max(sum w, 1e-9) when norm_topk_prob)
+//   counts, aux = E * sum(counts * mean probs), z = mean(logsumexp^2)
+//
+// Router product on the tensor cores: x is bf16, so x_k * w_k is exact in
+// float32 when w is bf16.  The fp32 router weight is split exactly-enough
+// into three bf16 parts (hi = bf16(w), mid = bf16(w - hi), lo = bf16(w - hi -
+// mid), 24 mantissa bits in total) and the three products accumulate into
+// one fp32 TMEM accumulator (tcgen05 kind::f16, M = 128 tokens, N = E padded
+// to 16).  The result agrees with an fp32 SIMT / CPU product to ~1e-6
+// relative, like any other fp32 summation order.
+//
+// Stable permutation: each CTA routes 128 consecutive tokens (a "chunk") and
+// ranks the chunk's slots per expert in token order with warp ballots; the
+// scan kernel turns per-chunk counts into per-expert prefixes (one CTA per
+// expert) and the last CTA to finish lays out the padded expert segments.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "kernels.cuh"
+
+namespace mcl4 {
+
+namespace {
+
+constexpr int kTailThreads = 256;  // 8 warps run the tail
+constexpr int kTcThreads = 64 + kTailThreads;
+
+__device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    unsigned long long w = __shfl_xor_sync(0xffffffffu, v, o);
+    v = w > v ? w : v;
+  }
+  return v;
+}
+__device__ __forceinline__ float warp_max_f(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_sum_f(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+struct TailSmem {
+  float* logits;  // [128][E + 1]
+  int32_t* sel;   // [128][k]
+  int32_t* rank;  // [128][k]
+  int32_t* gcount;  // [4][E]
+  float* red;     // [8][E + 2]
+  int lds;
+};
+
+__host__ __device__ inline size_t tail_smem_bytes(int E, int k) {
+  return sizeof(float) * kRouteTokens * (E + 1) + 2 * sizeof(int32_t) * kRouteTokens * k +
+         sizeof(int32_t) * 4 * E + sizeof(float) * 8 * (E + 2) + 64;
+}
+
+__device__ inline TailSmem carve_tail(uint8_t* base, int E, int k) {
+  TailSmem t;
+  t.lds = E + 1;
+  t.logits = reinterpret_cast<float*>(base);
+  t.sel = reinterpret_cast<int32_t*>(t.logits + kRouteTokens * t.lds);
+  t.rank = t.sel + kRouteTokens * k;
+  t.gcount = t.rank + kRouteTokens * k;
+  t.red = reinterpret_cast<float*>(t.gcount + 4 * E);
+  return t;
+}
+
+// Softmax / top-k / statistics / stable ranks of one 128-token chunk whose
+// logits (bias included) are in ``s.logits``.  Runs on 256 threads with ids
+// ``g`` 0..255; ``sync()`` is a barrier over exactly those threads.
+template <int EW, class Sync>
+__device__ void route_tail(const TailSmem& s, int g, int chunk, int T, int E, int k, int norm_topk,
+                           const uint8_t* __restrict__ valid, int32_t* __restrict__ topk_idx,
+                           float* __restrict__ topk_w, float* __restrict__ logits_out, float* __restrict__ sel_mask,
+                           const RouteWorkspace& ws, Sync sync) {
+  const int lane = g & 31, warp = g >> 5;
+  const int t0 = chunk * kRouteTokens;
+  float prob_acc[EW];
+#pragma unroll
+  for (int i = 0; i < EW; ++i) prob_acc[i] = 0.f;
+  float lse2_acc = 0.f, nval_acc = 0.f;
+  for (int tok = warp * 16; tok < warp * 16 + 16; ++tok) {
+    const int t = t0 + tok;
+    if (t >= T) {
+      if (lane < k) s.sel[tok * k + lane] = -1;
+      continue;
+    }
+    float l[EW];
+#pragma unroll
+    for (int i = 0; i < EW; ++i) {
+      const int e = lane + 32 * i;
+      l[i] = e < E ? s.logits[tok * s.lds + e] : -INFINITY;
+      if (logits_out != nullptr && e < E) logits_out[int64_t(t) * E + e] = l[i];
+    }
+    const bool routed = valid == nullptr || valid[t] != 0;
+    if (!routed) {
+      if (lane < k) {
+        topk_idx[int64_t(t) * k + lane] = -1;
+        topk_w[int64_t(t) * k + lane] = 0.f;
+        s.sel[tok * k + lane] = -1;
+      }
+      if (sel_mask != nullptr)
+#pragma unroll
+        for (int i = 0; i < EW; ++i)
+          if (lane + 32 * i < E) sel_mask[int64_t(t) * E + lane + 32 * i] = 0.f;
+      continue;
+    }
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < EW; ++i) m = fmaxf(m, l[i]);
+    m = warp_max_f(m);
+    float p[EW], sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < EW; ++i) {
+      p[i] = (lane + 32 * i < E) ? expf(__fsub_rn(l[i], m)) : 0.f;
+      sum = __fadd_rn(sum, p[i]);
+    }
+    sum = warp_sum_f(sum);
+    const float inv_s = __frcp_rn(sum);
+    const float lse = __fadd_rn(m, logf(sum));
+    lse2_acc = __fadd_rn(lse2_acc, __fmul_rn(lse, lse));
+    nval_acc += 1.f;
+#pragma unroll
+    for (int i = 0; i < EW; ++i) {
+      p[i] = __fmul_rn(p[i], inv_s);
+      prob_acc[i] = __fadd_rn(prob_acc[i], p[i]);
+    }
+    // top-k: largest probability first, ties to the lower expert index
+    uint32_t taken = 0;
+    int my_e = -1;
+    float my_p = 0.f;
+    for (int j = 0; j < k; ++j) {
+      unsigned long long best = 0;
+#pragma unroll
+      for (int i = 0; i < EW; ++i) {
+        const int e = lane + 32 * i;
+        if (e < E && !((taken >> i) & 1u)) {
+          const unsigned long long key =
+              (static_cast<unsigned long long>(__float_as_uint(p[i])) << 32) | (0xFFFFFFFFu - uint32_t(e));
+          best = key > best ? key : best;
+        }
+      }
+      best = warp_max_u64(best);
+      const int e_star = int(0xFFFFFFFFu - uint32_t(best & 0xFFFFFFFFull));
+      if ((e_star & 31) == lane) taken |= 1u << (e_star >> 5);
+      if (lane == j) {
+        my_e = e_star;
+        my_p = __uint_as_float(uint32_t(best >> 32));
+      }
+    }
+    float w = my_p;
+    if (norm_topk) {
+      float total = 0.f;
+      for (int j = 0; j < k; ++j) total = __fadd_rn(total, __shfl_sync(0xffffffffu, my_p, j));
+      w = __fdiv_rn(my_p, fmaxf(total, 1e-9f));
+    }
+    if (lane < k) {
+      topk_idx[int64_t(t) * k + lane] = my_e;
+      topk_w[int64_t(t) * k + lane] = w;
+      s.sel[tok * k + lane] = my_e;
+    }
+    if (sel_mask != nullptr)
+#pragma unroll
+      for (int i = 0; i < EW; ++i)
+        if (lane + 32 * i < E) sel_mask[int64_t(t) * E + lane + 32 * i] = ((taken >> i) & 1u) ? 1.f : 0.f;
+  }
+#pragma unroll
+  for (int i = 0; i < EW; ++i)
+    if (lane + 32 * i < E) s.red[warp * (E + 2) + lane + 32 * i] = prob_acc[i];
+  if (lane == 0) {
+    s.red[warp * (E + 2) + E] = lse2_acc;
+    s.red[warp * (E + 2) + E + 1] = nval_acc;
+  }
+  sync();
+
+  // per-chunk statistics, warps added in a fixed order
+  for (int e = g; e < E + 2; e += kTailThreads) {
+    float a = 0.f;
+    for (int w8 = 0; w8 < 8; ++w8) a = __fadd_rn(a, s.red[w8 * (E + 2) + e]);
+    if (e < E) ws.part_probs[int64_t(chunk) * E + e] = a;
+    else ws.part_misc[int64_t(chunk) * 2 + (e - E)] = a;
+  }
+
+  // stable ranks: warps 0..3 rank 32 tokens each with ballots, in token order
+  if (warp < 4) {
+    const int tok = warp * 32 + lane;
+    uint32_t mw[EW];
+#pragma unroll
+    for (int i = 0; i < EW; ++i) mw[i] = 0;
+    for (int j = 0; j < k; ++j) {
+      const int e = s.sel[tok * k + j];
+      if (e >= 0) {
+#pragma unroll
+        for (int i = 0; i < EW; ++i)
+          if ((e >> 5) == i) mw[i] |= 1u << (e & 31);
+      }
+    }
+    const uint32_t lt = (1u << lane) - 1u;
+#pragma unroll
+    for (int i = 0; i < EW; ++i) {
+      for (int b = 0; b < 32; ++b) {
+        const int e = i * 32 + b;
+        if (e >= E) break;
+        const bool has = (mw[i] >> b) & 1u;
+        const uint32_t bal = __ballot_sync(0xffffffffu, has);
+        if (has) {
+          const int r = __popc(bal & lt);
+          for (int j = 0; j < k; ++j)
+            if (s.sel[tok * k + j] == e) s.rank[tok * k + j] = r;
+        }
+        if (lane == 0) s.gcount[warp * E + e] = __popc(bal);
+      }
+    }
+  }
+  sync();
+  for (int e = g; e < E; e += kTailThreads)
+    ws.chunk_excl[int64_t(chunk) * E + e] = s.gcount[e] + s.gcount[E + e] + s.gcount[2 * E + e] + s.gcount[3 * E + e];
+  for (int i = g; i < kRouteTokens * k; i += kTailThreads) {
+    const int tok = i / k;
+    const int e = s.sel[i];
+    if (t0 + tok < T) {
+      int r = 0;
+      if (e >= 0) {
+        r = s.rank[i];
+        for (int gi = 0; gi < (tok >> 5); ++gi) r += s.gcount[gi * E + e];
+      }
+      ws.local_rank[int64_t(t0) * k + i] = r;
+    }
+  }
+}
+
+struct BlockSync {
+  __device__ void operator()() const { __syncthreads(); }
+};
+struct TailBarrier {  // named barrier 1 over the 256 tail threads of the tensor-core router
+  __device__ void operator()() const { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+};
+
+}  // namespace
+
+// ---------------------------------------------------------------- weight split
+
+// Wr fp32 [E, d] -> three bf16 parts [3][E_pad][d]; rows E..E_pad-1 are zero.
+__global__ void __launch_bounds__(256) router_split_kernel(const float* __restrict__ wr, int E, int E_pad, int d,
+                                                           uint16_t* __restrict__ wsplit) {
+  const int64_t n = int64_t(E_pad) * d;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+    const int e = int(i / d);
+    const float w = e < E ? wr[i] : 0.f;
+    const uint16_t hi = f32_to_bf16(w);
+    const float r1 = __fsub_rn(w, bf16_to_f32(hi));
+    const uint16_t mid = f32_to_bf16(r1);
+    const float r2 = __fsub_rn(r1, bf16_to_f32(mid));
+    wsplit[i] = hi;
+    wsplit[n + i] = mid;
+    wsplit[2 * n + i] = f32_to_bf16(r2);
+  }
+}
+
+// ---------------------------------------------------------------- tensor-core router
+
+struct RouterTcArgs {
+  const float* bias;
+  const uint8_t* valid;
+  int T, d, E, E_pad, k, norm_topk, stages;
+  uint32_t tmem_cols;
+  int32_t* topk_idx;
+  float* topk_w;
+  float* logits_out;
+  float* sel_mask;
+  int32_t* err;
+};
+
+template <int EW>
+__global__ void __launch_bounds__(kTcThreads) router_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                                                               const __grid_constant__ CUtensorMap tmap_w,
+                                                               RouterTcArgs a, RouteWorkspace ws) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - raw_addr);
+  const uint32_t a_bytes = kRouteTokens * 128;            // 128 tokens x 64 bf16
+  const uint32_t b_part = uint32_t(a.E_pad) * 128;        // E_pad rows x 64 bf16
+  const uint32_t stage_bytes = a_bytes + 3 * b_part;
+  const uint32_t region = uint32_t(a.stages) * stage_bytes;
+  const size_t tail_bytes = tail_smem_bytes(a.E, a.k);
+  const uint32_t bar_base = base + uint32_t(((region > tail_bytes ? region : tail_bytes) + 15) & ~size_t(15));
+  auto full_bar = [&](int s) { return bar_base + 8u * s; };
+  auto empty_bar = [&](int s) { return bar_base + 8u * (4 + s); };
+  const uint32_t tfull_bar = bar_base + 64;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + (bar_base - base) + 72);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int chunk = blockIdx.x;
+  const int t0 = chunk * kRouteTokens;
+  if (chunk == 0 && tid == 0) *ws.done = 0u;  // the scan kernel runs after this one
+  if (tid == 0) {
+    for (int s = 0; s < a.stages; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    mbar_init(tfull_bar, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), a.tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int kblocks = a.d / 64;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tmap_x);
+      prefetch_tmap(&tmap_w);
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!mbar_wait(empty_bar(stage), phase ^ 1u, a.err, 111)) break;
+        const uint32_t st = base + stage * stage_bytes;
+        mbar_arrive_expect_tx(full_bar(stage), stage_bytes);
+        tma_load_2d(st, &tmap_x, kb * 64, t0, full_bar(stage));
+#pragma unroll
+        for (int p = 0; p < 3; ++p) tma_load_2d(st + a_bytes + p * b_part, &tmap_w, kb * 64, p * a.E_pad, full_bar(stage));
+        if (++stage == a.stages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // kind::f16, bf16 x bf16 -> fp32, K-major A and B, M = 128, N = E_pad
+      const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t(a.E_pad) >> 3) << 17) | ((128u >> 4) << 24);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!mbar_wait(full_bar(stage), phase, a.err, 211)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t st = base + stage * stage_bytes;
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+#pragma unroll
+          for (int p = 0; p < 3; ++p)
+            tc_mma_f16(tmem_base, smem_desc(st + 32 * ks, 16, 1024, 2),
+                       smem_desc(st + a_bytes + p * b_part + 32 * ks, 16, 1024, 2), idesc,
+                       (kb | ks | p) != 0 ? 1u : 0u);
+        tc_commit(empty_bar(stage));
+        if (++stage == a.stages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (ok) tc_commit(tfull_bar);
+    }
+    __syncwarp();
+  } else {
+    // tail warps: TMEM logits -> shared memory (+ bias), then softmax / top-k / ranks
+    const int g = tid - 64;
+    const int q = warp & 3, half = (warp - 2) >> 2;
+    const TailSmem s = carve_tail(smem, a.E, a.k);
+    const bool ok = mbar_wait(tfull_bar, 0, a.err, 311);
+    tc_fence_after();
+    const int cols = a.E_pad / 2;  // a multiple of 8
+    const int row = q * 32 + lane;
+    const uint32_t lane_addr = tmem_base + (uint32_t(q * 32) << 16);
+    for (int c0 = half * cols; c0 < (half + 1) * cols; c0 += 8) {
+      uint32_t v[8];
+      if (ok) {
+        asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                     : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+                       "=r"(v[7])
+                     : "r"(lane_addr + c0)
+                     : "memory");
+        tmem_wait_ld();
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int e = c0 + j;
+        if (e < a.E) {
+          const float lv = ok ? __uint_as_float(v[j]) : 0.f;
+          s.logits[row * s.lds + e] = a.bias ? __fadd_rn(lv, a.bias[e]) : lv;
+        }
+      }
+    }
+    tc_fence_before();
+    TailBarrier()();
+    route_tail<EW>(s, g, chunk, a.T, a.E, a.k, a.norm_topk, a.valid, a.topk_idx, a.topk_w, a.logits_out, a.sel_mask,
+                   ws, TailBarrier());
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, a.tmem_cols);
+  }
+}
+
+// Router tail on given logits (parity checks against recorded reference logits).
+template <int EW>
+__global__ void __launch_bounds__(kTailThreads) router_logits_kernel(const float* __restrict__ logits_in,
+                                                                     const float* __restrict__ bias, RouterTcArgs a,
+                                                                     RouteWorkspace ws) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const TailSmem s = carve_tail(smem_raw, a.E, a.k);
+  const int chunk = blockIdx.x;
+  const int t0 = chunk * kRouteTokens;
+  if (chunk == 0 && threadIdx.x == 0) *ws.done = 0u;
+  for (int i = threadIdx.x; i < kRouteTokens * a.E; i += blockDim.x) {
+    const int tok = i / a.E, e = i - tok * a.E;
+    const float lv = (t0 + tok < a.T) ? logits_in[int64_t(t0 + tok) * a.E + e] : 0.f;
+    s.logits[tok * s.lds + e] = bias ? __fadd_rn(lv, bias[e]) : lv;
+  }
+  __syncthreads();
+  route_tail<EW>(s, threadIdx.x, chunk, a.T, a.E, a.k, a.norm_topk, a.valid, a.topk_idx, a.topk_w, a.logits_out,
+                 a.sel_mask, ws, BlockSync());
+}
+
+// ---------------------------------------------------------------- scan
+
+namespace {
+
+__device__ __forceinline__ int32_t block_exclusive_scan(int32_t v, int32_t* tmp, int32_t& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int32_t x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int32_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) tmp[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int32_t w = lane < nw ? tmp[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < nw) tmp[32 + lane] = w;
+  }
+  __syncthreads();
+  total = tmp[32 + nw - 1];
+  const int32_t before = warp ? tmp[32 + warp - 1] : 0;
+  __syncthreads();
+  return before + x - v;
+}
+
+// Deterministic block sum: fixed xor tree in each warp, warps added in order.
+__device__ __forceinline__ float block_sum(float v, float* tmp) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if (lane == 0) tmp[warp] = v;
+  __syncthreads();
+  float s = 0.f;
+  for (int w = 0; w < nw; ++w) s = __fadd_rn(s, tmp[w]);
+  __syncthreads();
+  return s;
+}
+
+}  // namespace
+
+// One CTA per expert: exclusive prefix of the expert's per-chunk slot counts
+// and its probability sum.  The last CTA to finish (counted with an atomic
+// after a memory fence; no CTA waits on another) lays out the expert segments
+// and finalises the statistics.
+__global__ void __launch_bounds__(256) route_scan_kernel(int C, int E, int k, RouteWorkspace ws, int32_t* counts_out,
+                                                         float* stats, int32_t* offs_out) {
+  __shared__ int32_t itmp[64];
+  __shared__ float ftmp[32];
+  __shared__ bool is_last;
+  const int tid = threadIdx.x;
+  const int e = blockIdx.x;
+  const int per = (C + blockDim.x - 1) / blockDim.x;
+  const int c0 = tid * per, c1 = min(C, c0 + per);
+  int32_t mine = 0;
+  float ps = 0.f;
+  for (int c = c0; c < c1; ++c) {
+    mine += ws.chunk_excl[int64_t(c) * E + e];
+    ps = __fadd_rn(ps, ws.part_probs[int64_t(c) * E + e]);
+  }
+  int32_t total;
+  int32_t run = block_exclusive_scan(mine, itmp, total);
+  for (int c = c0; c < c1; ++c) {
+    const int32_t v = ws.chunk_excl[int64_t(c) * E + e];
+    ws.chunk_excl[int64_t(c) * E + e] = run;
+    run += v;
+  }
+  const float psum = block_sum(ps, ftmp);
+  if (tid == 0) {
+    ws.counts[e] = total;
+    ws.probs_sum[e] = psum;
+    __threadfence();
+    is_last = atomicAdd(ws.done, 1u) == uint32_t(E - 1);
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+
+  float l2 = 0.f, nv = 0.f;
+  for (int c = c0; c < c1; ++c) {
+    l2 = __fadd_rn(l2, ws.part_misc[2 * c]);
+    nv = __fadd_rn(nv, ws.part_misc[2 * c + 1]);
+  }
+  const float lse2 = block_sum(l2, ftmp);
+  const float n = block_sum(nv, ftmp);
+  // each thread takes one expert (E <= 256): counts -> segment starts by block scans
+  const int32_t cnt = tid < E ? __ldcg(ws.counts + tid) : 0;
+  int32_t ignore;
+  const int32_t ustart = block_exclusive_scan(cnt, itmp, ignore);
+  const int32_t pstart = block_exclusive_scan((cnt + 127) / 128 * 128, itmp, ignore);
+  float term = 0.f;
+  if (tid < E) {
+    ws.offs_start[tid] = ustart;
+    ws.pad_start[tid] = pstart;
+    if (tid == E - 1) ws.pad_start[E] = pstart + (cnt + 127) / 128 * 128;
+    if (offs_out) offs_out[tid] = ustart + cnt;
+    if (counts_out) counts_out[tid] = cnt;
+    if (stats) {
+      const float cf = n > 0.f ? __fdiv_rn(float(cnt), n * float(k)) : 0.f;
+      stats[3 + tid] = cf;
+      term = n > 0.f ? __fmul_rn(cf, __fdiv_rn(__ldcg(ws.probs_sum + tid), n)) : 0.f;
+    }
+  }
+  const float aux = block_sum(term, ftmp);
+  if (tid == 0 && stats) {
+    stats[0] = n > 0.f ? __fmul_rn(float(E), aux) : 0.f;
+    stats[1] = n > 0.f ? __fdiv_rn(lse2, n) : 0.f;
+    stats[2] = n;
+  }
+}
+
+// ---------------------------------------------------------------- host side
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D map over a bf16 [rows, cols] matrix, box 64 x box_rows, 128-byte swizzle; rows
+// outside the matrix read as zero.
+bool make_tmap_bf16(CUtensorMap* m, const void* ptr, uint64_t cols, uint64_t rows, uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int EW>
+int launch_router_t(const uint16_t* x, const float* wr, const float* bias, const float* logits_in, RouterTcArgs a,
+                    const RouteWorkspace& ws, cudaStream_t stream) {
+  const int C = (a.T + kRouteTokens - 1) / kRouteTokens;
+  if (logits_in != nullptr) {
+    const size_t smem = tail_smem_bytes(a.E, a.k);
+    static bool configured = false;
+    if (!configured) {
+      if (cudaFuncSetAttribute(router_logits_kernel<EW>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
+          cudaSuccess)
+        return MCL4MOE_ERR_CUDA;
+      configured = true;
+    }
+    router_logits_kernel<EW><<<C, kTailThreads, smem, stream>>>(logits_in, nullptr, a, ws);  // final logits
+    return cudaGetLastError() == cudaSuccess ? MCL4MOE_OK : MCL4MOE_ERR_CUDA;
+  }
+  // split the router weight into three bf16 parts, then the tensor-core router
+  const int64_t n = int64_t(a.E_pad) * a.d;
+  int blocks = int((n + 255) / 256);
+  if (blocks > 1024) blocks = 1024;
+  router_split_kernel<<<blocks, 256, 0, stream>>>(wr, a.E, a.E_pad, a.d, ws.wsplit);
+  CUtensorMap tx, tw;
+  if (!make_tmap_bf16(&tx, x, uint64_t(a.d), uint64_t(a.T), kRouteTokens)) return MCL4MOE_ERR_CUDA;
+  if (!make_tmap_bf16(&tw, ws.wsplit, uint64_t(a.d), uint64_t(3) * a.E_pad, uint32_t(a.E_pad))) return MCL4MOE_ERR_CUDA;
+  const size_t stage_bytes = size_t(kRouteTokens) * 128 + 3 * size_t(a.E_pad) * 128;
+  int stages = int((110 * 1024) / stage_bytes);
+  stages = stages < 2 ? 2 : (stages > 4 ? 4 : stages);
+  a.stages = stages;
+  const size_t region = size_t(stages) * stage_bytes;
+  const size_t tail = tail_smem_bytes(a.E, a.k);
+  const size_t smem = 1024 + ((region > tail ? region : tail) + 15) / 16 * 16 + 128;
+  uint32_t cols = 32;
+  while (cols < uint32_t(a.E_pad)) cols <<= 1;
+  a.tmem_cols = cols;
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(router_tc_kernel<EW>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) !=
+        cudaSuccess)
+      return MCL4MOE_ERR_CUDA;
+    configured = true;
+  }
+  if (smem > 227 * 1024) return MCL4MOE_ERR_UNSUPPORTED;
+  router_tc_kernel<EW><<<C, kTcThreads, smem, stream>>>(tx, tw, a, ws);
+  return cudaGetLastError() == cudaSuccess ? MCL4MOE_OK : MCL4MOE_ERR_CUDA;
+}
+
+}  // namespace
+
+int launch_route(const uint16_t* x, const float* wr, const float* bias, const float* logits_in, const uint8_t* valid,
+                 int T, int d, int E, int k, int norm_topk, int32_t* topk_idx, float* topk_w, float* logits_out,
+                 float* sel_mask, int32_t* counts_out, float* stats, int32_t* offs_out, int32_t* err,
+                 const RouteWorkspace& ws, cudaStream_t stream) {
+  if (T > 0) {
+    RouterTcArgs a{};
+    a.bias = bias;
+    a.valid = valid;
+    a.T = T;
+    a.d = d;
+    a.E = E;
+    a.E_pad = (E + 15) / 16 * 16;
+    a.k = k;
+    a.norm_topk = norm_topk;
+    a.topk_idx = topk_idx;
+    a.topk_w = topk_w;
+    a.logits_out = logits_out;
+    a.sel_mask = sel_mask;
+    a.err = err;
+    int st;
+    if (E <= 32) st = launch_router_t<1>(x, wr, bias, logits_in, a, ws, stream);
+    else if (E <= 64) st = launch_router_t<2>(x, wr, bias, logits_in, a, ws, stream);
+    else if (E <= 128) st = launch_router_t<4>(x, wr, bias, logits_in, a, ws, stream);
+    else st = launch_router_t<8>(x, wr, bias, logits_in, a, ws, stream);
+    if (st != MCL4MOE_OK) return st;
+  } else if (cudaMemsetAsync(ws.done, 0, sizeof(uint32_t), stream) != cudaSuccess) {
+    return MCL4MOE_ERR_CUDA;  // no router CTA ran: reset the finished-expert counter here
+  }
+  const int C = (T + kRouteTokens - 1) / kRouteTokens;
+  route_scan_kernel<<<E, 256, 0, stream>>>(C, E, k, ws, counts_out, stats, offs_out);
+  return cudaGetLastError() == cudaSuccess ? MCL4MOE_OK : MCL4MOE_ERR_CUDA;
+}
+
+}  // namespace mcl4

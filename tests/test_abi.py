@@ -40,7 +40,7 @@ def test_workspace_sizes_are_host_only(moe_pkg):
     # y (bf16) dominates: mcap * d * 2 bytes
     assert ws >= mcap * d * 2 + mcap * (d // 2 + d // 16 + F // 2 + F // 16)
     assert lib.mcl4moe_moe_workspace_size(T, 2000, E, k, F) == 0  # d % 256 != 0 -> unsupported
-    assert lib.mcl4moe_route_workspace_size(T, E, k) > 0
+    assert lib.mcl4moe_route_workspace_size(T, E, k, d) > 0
 
 
 def test_forward_rejects_bad_arguments_without_touching_the_device(moe_pkg):

@@ -25,7 +25,7 @@ def _route(pkg, case, logits_in=None):
     sel = torch.empty((T, E), dtype=torch.float32, device=DEV)
     counts = torch.empty((E,), dtype=torch.int32, device=DEV)
     stats = torch.empty((3 + E,), dtype=torch.float32, device=DEV)
-    ws_bytes = lib.mcl4moe_route_workspace_size(T, E, k)
+    ws_bytes = lib.mcl4moe_route_workspace_size(T, E, k, d)
     ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=DEV)
     p = lambda t: None if t is None else t.data_ptr()  # noqa: E731
     st = lib.mcl4moe_route(x.data_ptr(), wr.data_ptr(), p(bias), p(lg_in), p(valid), T, d, E, k,
