@@ -10,19 +10,26 @@
 // belongs to exactly one expert and its scales are whole 128x4 atoms.
 // Tile 128 x 256, K step 256 (one 128-byte swizzle row of packed FP4).
 //
-// Warp roles (576 threads, one CTA per SM):
-//   warp 0      TMA producer: A tile, two 128-row B halves, 3 scale bulk copies
-//   warp 1      TMEM owner + single-thread MMA issuer (scales smem -> TMEM, 4 MMAs)
-//   warps 2..17 epilogue: TMEM -> registers, then
-//               mode 0 (gate/up): SwiGLU in bf16 and NVFP4 re-quantisation of h
-//                                 (src/mcl4_coe/backbone.py:572-574)
-//               mode 1 (down):    bf16(acc*g) [* bf16(routing weight)] to bf16 rows
-//                                 (src/mcl4_coe/backbone.py:903)
-// Pipelines: 4 smem stages (full/empty mbarriers); one 256-column fp32
-// accumulator released by the epilogue right after it is read, so the next
-// tile's MMAs overlap the epilogue math.  Scale factors live in a per-stage
-// TMEM ring so a stage's scales are only overwritten after the MMAs that read
-// them completed.  Every wait is bounded (error word instead of a hang).
+// Warp roles (704 threads, one CTA per SM):
+//   warp 0       TMA producer: A tile, two 128-row B halves, 3 scale bulk copies
+//   warp 1       TMEM owner + single-thread MMA issuer (4 MMAs per stage)
+//   warps 2..5   scale-factor writers, one per TMEM lane quarter: each scale
+//                atom (128 rows x 4 scales, 512 B) is read from shared memory
+//                into registers and written to its 4 TMEM columns with
+//                tcgen05.st.  Every lane quarter writes the same 32-row data,
+//                which is the 4x replicated layout the block-scaled MMA reads.
+//                (tcgen05.cp would do the same but costs tensor-pipe time per
+//                instruction comparable to an MMA, serialised with the MMAs.)
+//   warps 6..21  epilogue: TMEM -> registers, then
+//                mode 0 (gate/up): SwiGLU in bf16 and NVFP4 re-quantisation of h
+//                                  (src/mcl4_coe/backbone.py:572-574)
+//                mode 1 (down):    bf16(acc*g) [* bf16(routing weight)] to bf16 rows
+//                                  (src/mcl4_coe/backbone.py:903)
+// Pipelines: 4 smem stages (full / scales-full / empty mbarriers); one
+// 256-column fp32 accumulator released by the epilogue right after it is
+// read, so the next tile's MMAs overlap the epilogue math.  Scale factors live
+// in a per-stage TMEM ring, overwritten only after the MMAs that read them
+// completed.  Every wait is bounded (error word instead of a hang).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -38,17 +45,20 @@ constexpr int kBM = 128, kBN = 256, kBK = 256;
 constexpr int kStages = 4;
 constexpr uint32_t kATile = kBM * kBK / 2;   // 16384
 constexpr uint32_t kBHalf = 128 * kBK / 2;    // 16384 (128 rows)
-constexpr uint32_t kSFA = kBM * kBK / 16;     // 2048
+constexpr uint32_t kSFA = kBM * kBK / 16;      // 2048
 constexpr uint32_t kSFBHalf = 128 * kBK / 16;  // 2048
 constexpr uint32_t kStageBytes = kATile + 2 * kBHalf + kSFA + 2 * kSFBHalf;  // 55296
 constexpr uint32_t kOffB = kATile, kOffSFA = kATile + 2 * kBHalf, kOffSFB = kOffSFA + kSFA;
+constexpr int kSfWarps = 4;
 constexpr int kEpiWarps = 16;
-constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kEpiWarp0 = 2 + kSfWarps;
+constexpr int kThreads = 32 * (kEpiWarp0 + kEpiWarps);
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kSfCol0 = 256;          // accumulator uses columns [0, 256)
 constexpr uint32_t kSfColsPerStage = 48;   // SFA 4 x 4 + SFB 4 x 8
 constexpr uint32_t kIdesc = idesc_nvf4(128, 256);
-constexpr size_t kSmemBytes = size_t(kStages) * kStageBytes + 1024 /*align*/ + 256 /*barriers*/ +
+constexpr uint32_t kBarBytes = 256;
+constexpr size_t kSmemBytes = size_t(kStages) * kStageBytes + 1024 /*align*/ + kBarBytes +
                               sizeof(int32_t) * (kMaxExperts + 1);
 
 static_assert(kSfCol0 + kStages * kSfColsPerStage <= kTmemCols, "TMEM budget");
@@ -80,10 +90,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t bar_base = base + kStages * kStageBytes;
   auto full_bar = [&](int s) { return bar_base + 8u * s; };
   auto empty_bar = [&](int s) { return bar_base + 8u * (kStages + s); };
-  const uint32_t tfull_bar = bar_base + 8u * (2 * kStages);
-  const uint32_t tempty_bar = bar_base + 8u * (2 * kStages + 1);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kStages * kStageBytes + 8 * (2 * kStages + 2));
-  int32_t* pad_s = reinterpret_cast<int32_t*>(smem + kStages * kStageBytes + 256);
+  auto sf_bar = [&](int s) { return bar_base + 8u * (2 * kStages + s); };
+  const uint32_t tfull_bar = bar_base + 8u * (3 * kStages);
+  const uint32_t tempty_bar = bar_base + 8u * (3 * kStages + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kStages * kStageBytes + 8 * (3 * kStages + 2));
+  int32_t* pad_s = reinterpret_cast<int32_t*>(smem + kStages * kStageBytes + kBarBytes);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int E = args.E;
@@ -93,6 +104,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < kStages; ++s) {
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
+      mbar_init(sf_bar(s), kSfWarps);
     }
     mbar_init(tfull_bar, 1);
     mbar_init(tempty_bar, kEpiWarps);
@@ -123,6 +135,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     c.e = find_expert(pad_s, E, c.mb * kBM);
     return c;
   };
+  auto b_rows = [&](const TileCoord& c, int& lr0, int& lr1) {  // local B rows of the two 128-row halves
+    if (args.mode == 0) {
+      lr0 = c.nt * 128;
+      lr1 = args.F + c.nt * 128;
+    } else {
+      lr0 = c.nt * kBN;
+      lr1 = lr0 + 128;
+    }
+  };
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -132,14 +153,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
         const TileCoord c = coord(t);
-        int lr0, lr1;  // local B rows of the two 128-row halves
-        if (args.mode == 0) {
-          lr0 = c.nt * 128;
-          lr1 = args.F + c.nt * 128;
-        } else {
-          lr0 = c.nt * kBN;
-          lr1 = lr0 + 128;
-        }
+        int lr0, lr1;
+        b_rows(c, lr0, lr1);
         const int brow = c.e * args.N_total;
         const uint8_t* bsc = args.b_scales + size_t(c.e) * (size_t(args.N_total) * args.K / 16);
         const uint8_t* asc = args.a_scales + size_t(c.mb) * sf_row_stride;
@@ -175,19 +190,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(tempty_bar, acc_phase ^ 1u, args.err, 201)) break;
         tc_fence_after();
         for (int kb = 0; kb < kblocks; ++kb) {
-          if (!mbar_wait(full_bar(stage), phase, args.err, 202)) {
+          if (!mbar_wait(full_bar(stage), phase, args.err, 202) || !mbar_wait(sf_bar(stage), phase, args.err, 203)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t st = base + stage * kStageBytes;
           const uint32_t sf_col = tmem_base + kSfCol0 + stage * kSfColsPerStage;
-#pragma unroll
-          for (int ks = 0; ks < 4; ++ks) {
-            tc_copy_scales(sf_col + 4 * ks, smem_desc(st + kOffSFA + 512 * ks, 0, 128, 0));
-            tc_copy_scales(sf_col + 16 + 8 * ks, smem_desc(st + kOffSFB + 512 * ks, 0, 128, 0));
-            tc_copy_scales(sf_col + 16 + 8 * ks + 4, smem_desc(st + kOffSFB + kSFBHalf + 512 * ks, 0, 128, 0));
-          }
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks) {
             const uint64_t adesc = smem_desc(st + 32 * ks, 16, 1024, 2);
@@ -207,12 +216,49 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     __syncwarp();
+  } else if (warp < kEpiWarp0) {
+    // ------------------------------------------------------------ scale-factor writers
+    // Lane l of quarter q copies bytes [16 l, 16 l + 16) of each 512-byte atom
+    // (the 4 scales of rows l, l+32, l+64, l+96) to TMEM lane 32q + l, 4 columns.
+    // A stage's TMEM slot is free once the stage is full again: the producer
+    // only refills a stage after the MMAs that read it (and its scales) completed.
+    const int q = warp & 3;
+    const uint32_t lane_base = uint32_t(q * 32) << 16;
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!mbar_wait(full_bar(stage), phase, args.err, 121)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint8_t* st = smem + stage * kStageBytes;
+        const uint32_t sf_col = tmem_base + lane_base + kSfCol0 + stage * kSfColsPerStage;
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          tmem_st4(sf_col + 4 * ks, *reinterpret_cast<const uint4*>(st + kOffSFA + ks * 512 + lane * 16));
+          tmem_st4(sf_col + 16 + 8 * ks, *reinterpret_cast<const uint4*>(st + kOffSFB + ks * 512 + lane * 16));
+          tmem_st4(sf_col + 16 + 8 * ks + 4,
+                   *reinterpret_cast<const uint4*>(st + kOffSFB + kSFBHalf + ks * 512 + lane * 16));
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sf_bar(stage));
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
   } else {
     // ------------------------------------------------------------ epilogue
     // 16 warps: lane quarter q = warp % 4 (the TMEM lanes a warp may read),
     // column group sub = 0..3 (32 h columns in mode 0, 64 output columns in mode 1).
     const int q = warp & 3;
-    const int sub = (warp - 2) >> 2;
+    const int sub = (warp - kEpiWarp0) >> 2;
     const int row_in_tile = q * 32 + lane;
     const uint32_t lane_addr = tmem_base + (uint32_t(q * 32) << 16);
     uint32_t acc_phase = 0;
