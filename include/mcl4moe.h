@@ -116,6 +116,26 @@ int mcl4moe_route(const uint16_t* x, const float* wr, const float* logit_bias, c
                   void* workspace, size_t workspace_bytes, mcl4moe_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Routing without a caller workspace.  No counterpart in the reference: it
+ * serves callers that cannot allocate device scratch (a C/cgo/JNI client
+ * that owns only its input and output buffers, or a serving loop with a
+ * fixed memory pool).  Same arguments, checks and results as mcl4moe_route,
+ * but the scratch is a fixed device array inside this library of
+ * mcl4moe_route_noalloc_scratch_bytes() bytes (8 MiB: enough for T = 131072
+ * at E = 64, k = 8, d = 2048); a shape whose mcl4moe_route_workspace_size
+ * exceeds it returns MCL4MOE_ERR_WORKSPACE.  The first call on a device (that
+ * device current) does the set-up — it looks up the array's device address,
+ * which may load the module — so make it before any stream capture; later
+ * calls allocate nothing.  There is one array per device: calls on one
+ * device must not overlap in time, or they race on the scratch.
+ * ------------------------------------------------------------------------ */
+size_t mcl4moe_route_noalloc_scratch_bytes(void);
+int mcl4moe_route_noalloc(const uint16_t* x, const float* wr, const float* logit_bias, const float* logits_in,
+                          const uint8_t* valid, int T, int d, int E, int k, int norm_topk_prob, int32_t* topk_idx,
+                          float* topk_w, float* logits_out, float* sel_mask, int32_t* counts, float* stats,
+                          mcl4moe_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Full MoE layer forward.
  * Replaces SparseMoE.forward for the routing configuration without mitotic
  * pairs / lineage / coverage penalty / dense subset

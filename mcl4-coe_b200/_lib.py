@@ -26,6 +26,8 @@ EXPORTS = (
     "mcl4moe_quantize_activations",
     "mcl4moe_route_workspace_size",
     "mcl4moe_route",
+    "mcl4moe_route_noalloc_scratch_bytes",
+    "mcl4moe_route_noalloc",
     "mcl4moe_moe_workspace_size",
     "mcl4moe_moe_forward",
     "mcl4moe_padded_rows",
@@ -106,6 +108,12 @@ def load() -> ctypes.CDLL:
     lib.mcl4moe_route.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
                                   c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
                                   c_void_p]
+    lib.mcl4moe_route_noalloc_scratch_bytes.restype = c_size_t
+    lib.mcl4moe_route_noalloc_scratch_bytes.argtypes = []
+    lib.mcl4moe_route_noalloc.restype = c_int
+    lib.mcl4moe_route_noalloc.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                                          c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                          c_void_p]
     lib.mcl4moe_moe_workspace_size.restype = c_size_t
     lib.mcl4moe_moe_workspace_size.argtypes = [c_int, c_int, c_int, c_int, c_int]
     lib.mcl4moe_moe_forward.restype = c_int
