@@ -45,7 +45,7 @@ CONFIGS = {
     "c3": dict(name="c3_granite_zipf", seed=3, t=65536, d=1536, e=32, k=8, f=512, zipf=True),
     "c4": dict(name="c4_decode", seed=4, t=64, d=2048, e=64, k=8, f=1024),
 }
-KERNELS_PER_FORWARD = 6  # router, route-scan, permute+quantise, gate/up GEMM, down GEMM, combine
+KERNELS_PER_FORWARD = 7  # router-weight split, router, route-scan, permute+quantise, gate/up GEMM, down GEMM, combine
 
 
 def load_peaks() -> dict:
