@@ -182,7 +182,7 @@ size_t mcl4moe_moe_workspace_size(int T, int d, int E, int k, int F);
 int mcl4moe_moe_forward(const mcl4moe_moe_args* args, mcl4moe_stream_t stream);
 
 /* Capacity in rows of the padded, expert-major activation buffers
- * (sum over experts of count rounded up to 128, bounded by T*k + 127*E). */
+ * (sum over experts of count rounded up to 256, bounded by T*k + 255*E). */
 int64_t mcl4moe_padded_rows(int T, int E, int k);
 
 /* Device pointer of a named region inside a forward workspace (for tests and

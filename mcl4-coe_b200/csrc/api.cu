@@ -258,7 +258,7 @@ int mcl4moe_moe_forward(const mcl4moe_moe_args* a, mcl4moe_stream_t stream) {
 
 size_t mcl4moe_grouped_linear_workspace_size(int64_t M, int K, int E) {
   if (M < 0 || K <= 0 || E <= 0) return 0;
-  const int64_t mcap = ((M + int64_t(127) * E) + 127) / 128 * 128;
+  const int64_t mcap = padded_rows_cap(M, E, 1);
   size_t off = 0;
   off += align256(sizeof(int32_t) * (E + 1));  // pad_start
   off += align256(sizeof(int32_t) * E);        // offs_start
@@ -280,7 +280,7 @@ int mcl4moe_grouped_linear(const uint16_t* x, int64_t M, int K, const int32_t* o
   if (!aligned16(x) || !aligned16(out) || !aligned16(w) || !aligned16(w_scales)) return MCL4MOE_ERR_INVALID;
   if (workspace_bytes < mcl4moe_grouped_linear_workspace_size(M, K, E)) return MCL4MOE_ERR_WORKSPACE;
   if (M == 0) return MCL4MOE_OK;
-  const int64_t mcap = ((M + int64_t(127) * E) + 127) / 128 * 128;
+  const int64_t mcap = padded_rows_cap(M, E, 1);
   uint8_t* p = static_cast<uint8_t*>(workspace);
   size_t off = 0;
   auto take = [&](size_t bytes) {

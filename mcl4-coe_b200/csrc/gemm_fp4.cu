@@ -6,13 +6,23 @@
 // for the rows m of expert e, with g_a = 1 (activations).
 //
 // Layout: A rows are grouped by expert and each expert segment is padded to a
-// multiple of 128 rows (pad_start[E+1]); every 128-row M block therefore
-// belongs to exactly one expert and its scales are whole 128x4 atoms.
-// Tile 128 x 256, K step 256 (one 128-byte swizzle row of packed FP4).
+// multiple of kSegRows = 256 rows (pad_start[E+1]); every 256-row block
+// therefore belongs to exactly one expert and its scales are whole 128x4 atoms.
 //
-// Warp roles (704 threads, one CTA per SM):
-//   warp 0       TMA producer: A tile, two 128-row B halves, 3 scale bulk copies
-//   warp 1       TMEM owner + single-thread MMA issuer (4 MMAs per stage)
+// CTA pairs.  The kernel runs as clusters of two CTAs on two SMs.  A pair
+// computes a 256 x 256 output tile with one tcgen05.mma.cta_group::2 per K step
+// of 64: each CTA stages its own 128 A rows and one 128-row half of the tile's
+// 256 B rows, so a CTA streams 32 KB of operands per 256-deep K block instead
+// of 48 KB for a single-SM 128 x 256 tile (the L2 -> SM traffic is what bounds
+// the single-SM kernel).  Each CTA's TMEM receives its 128 accumulator rows,
+// its own A scales and the full-N B scales (the layout the pair MMA reads).
+// K step 256 per stage (one 128-byte swizzle row of packed FP4).
+//
+// Warp roles (704 threads per CTA, one CTA per SM):
+//   warp 0       TMA producer: A tile and B half (completion counted on the
+//                even CTA's barrier), 3 scale bulk copies (own barrier)
+//   warp 1       TMEM owner; in the even CTA also the single-thread issuer of
+//                the pair MMAs (4 per stage), committing to both CTAs' barriers
 //   warps 2..5   scale-factor writers, one per TMEM lane quarter: each scale
 //                atom (128 rows x 4 scales, 512 B) is read from shared memory
 //                into registers and written to its 4 TMEM columns with
@@ -21,18 +31,25 @@
 //                (tcgen05.cp would do the same but costs tensor-pipe time per
 //                instruction comparable to an MMA, serialised with the MMAs.)
 //   warps 6..21  epilogue: TMEM -> registers, then
-//                mode 0 (gate/up): SwiGLU in bf16 and NVFP4 re-quantisation of h
+//                MODE 0 (gate/up): SwiGLU in bf16 and NVFP4 re-quantisation of h
 //                                  (src/mcl4_coe/backbone.py:572-574)
-//                mode 1 (down):    bf16(acc*g) [* bf16(routing weight)] to bf16 rows
+//                MODE 1 (down):    bf16(acc*g) [* bf16(routing weight)] rows,
+//                                  staged in 128B-swizzled shared memory and
+//                                  written with TMA tile stores (full lines)
 //                                  (src/mcl4_coe/backbone.py:903)
-// Pipelines: 4 smem stages (full / scales-full / empty mbarriers); one
-// 256-column fp32 accumulator released by the epilogue right after it is
-// read, so the next tile's MMAs overlap the epilogue math.  Scale factors live
-// in a per-stage TMEM ring, overwritten only after the MMAs that read them
-// completed.  Every wait is bounded (error word instead of a hang).
+//                MODE 2 (grouped linear): as MODE 1 into unpadded destination
+//                                  rows with per-row stores of valid rows only
+// Pipelines: smem stages with full (A/B bytes and TMEM scales of both CTAs,
+// on the even CTA), scales-landed and empty mbarriers; one 256-column fp32
+// accumulator released by both CTAs' epilogues right after it is read, so the
+// next tile's MMAs overlap the epilogue math.  Scale factors live in a
+// per-stage TMEM ring, overwritten only after the MMAs that read them
+// completed.  Every mbarrier wait is bounded (error word instead of a hang).
+// No TMA load uses multicast: every CTA fetches its own operand tiles.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstring>
 #include <mutex>
 
 #include "kernels.cuh"
@@ -41,31 +58,43 @@ namespace mcl4 {
 
 namespace {
 
-constexpr int kBM = 128, kBN = 256, kBK = 256;
-constexpr int kStages = 4;
-constexpr uint32_t kATile = kBM * kBK / 2;   // 16384
-constexpr uint32_t kBHalf = 128 * kBK / 2;    // 16384 (128 rows)
-constexpr uint32_t kSFA = kBM * kBK / 16;      // 2048
-constexpr uint32_t kSFBHalf = 128 * kBK / 16;  // 2048
-constexpr uint32_t kStageBytes = kATile + 2 * kBHalf + kSFA + 2 * kSFBHalf;  // 55296
-constexpr uint32_t kOffB = kATile, kOffSFA = kATile + 2 * kBHalf, kOffSFB = kOffSFA + kSFA;
+constexpr int kBM = 128;  // rows per CTA; a pair covers kSegRows = 256
+constexpr int kBN = 256, kBK = 256;
+constexpr uint32_t kATile = kBM * kBK / 2;          // 16384
+constexpr uint32_t kBHalf = 128 * kBK / 2;          // 16384: this CTA's 128 of the tile's 256 B rows
+constexpr uint32_t kSFA = kBM * kBK / 16;           // 2048
+constexpr uint32_t kSFBHalf = 128 * kBK / 16;       // 2048
+constexpr uint32_t kABBytes = kATile + kBHalf;      // 32768 per CTA and stage
+constexpr uint32_t kSFBytes = kSFA + 2 * kSFBHalf;  // 6144 per CTA and stage (full-N B scales)
+constexpr uint32_t kStageBytes = kABBytes + kSFBytes;  // 38912
+constexpr uint32_t kOffB = kATile, kOffSFA = kABBytes, kOffSFB = kABBytes + kSFA;
 constexpr int kSfWarps = 4;
 constexpr int kEpiWarps = 16;
 constexpr int kEpiWarp0 = 2 + kSfWarps;
 constexpr int kThreads = 32 * (kEpiWarp0 + kEpiWarps);
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kSfCol0 = 256;          // accumulator uses columns [0, 256)
-constexpr uint32_t kSfColsPerStage = 48;   // SFA 4 x 4 + SFB 4 x 8
-constexpr uint32_t kIdesc = idesc_nvf4(128, 256);
+constexpr uint32_t kSfCol0 = 256;         // accumulator uses columns [0, 256)
+constexpr uint32_t kSfColsPerStage = 48;  // SFA 4 x 4 + SFB 4 x 8
+constexpr uint32_t kIdesc = idesc_nvf4(256, 256);
 constexpr uint32_t kBarBytes = 256;
-constexpr size_t kSmemBytes = size_t(kStages) * kStageBytes + 1024 /*align*/ + kBarBytes +
-                              sizeof(int32_t) * (kMaxExperts + 1);
+constexpr uint32_t kWarpStoreBytes = 32 * 64 * 2;  // one epilogue warp's 32 rows x 64 bf16 (MODE 1)
 
-static_assert(kSfCol0 + kStages * kSfColsPerStage <= kTmemCols, "TMEM budget");
+template <int MODE>
+struct Cfg {
+  static constexpr int kStages = MODE == 0 ? 5 : 4;
+  static constexpr uint32_t kStoreBytes = MODE == 1 ? kEpiWarps * kWarpStoreBytes : 0;
+  static constexpr size_t kSmem = 1024 /*align*/ + size_t(kStages) * kStageBytes + kStoreBytes + kBarBytes +
+                                  sizeof(int32_t) * (kMaxExperts + 1);
+};
+
 static_assert(kStageBytes % 1024 == 0, "stage must keep 1024-byte alignment for 128B swizzle");
+static_assert(Cfg<0>::kSmem <= 232448 && Cfg<1>::kSmem <= 232448 && Cfg<2>::kSmem <= 232448, "shared memory");
+static_assert(kSfCol0 + Cfg<0>::kStages * kSfColsPerStage <= kTmemCols, "TMEM budget");
+static_assert(8 * (3 * Cfg<0>::kStages + 2) + 4 <= kBarBytes, "barrier area");
+static_assert(kSegRows == 2 * kBM, "a CTA pair covers one 256-row segment block");
 
 struct TileCoord {
-  int e, mb, nt;
+  int e, pm, nt;
 };
 
 __device__ __forceinline__ int find_expert(const int32_t* pad_s, int E, int row) {
@@ -80,65 +109,75 @@ __device__ __forceinline__ int find_expert(const int32_t* pad_s, int E, int row)
 
 }  // namespace
 
-__global__ void __launch_bounds__(kThreads, 1)
+template <int MODE>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     grouped_gemm_fp4_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                            GemmArgs args) {
+                            const __grid_constant__ CUtensorMap tmap_y, GemmArgs args) {
+  constexpr int S = Cfg<MODE>::kStages;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
   uint8_t* smem = smem_raw + (base - raw_addr);
-  const uint32_t bar_base = base + kStages * kStageBytes;
+  const uint32_t store_base = base + S * kStageBytes;  // MODE 1 output staging (1024-aligned)
+  const uint32_t bar_base = store_base + Cfg<MODE>::kStoreBytes;
+  // full: even CTA only; A/B bytes of both CTAs plus the scale writers of both
+  // CTAs (their TMEM scales are in place), so the MMA issuer waits once per stage.
   auto full_bar = [&](int s) { return bar_base + 8u * s; };
-  auto empty_bar = [&](int s) { return bar_base + 8u * (kStages + s); };
-  auto sf_bar = [&](int s) { return bar_base + 8u * (2 * kStages + s); };
-  const uint32_t tfull_bar = bar_base + 8u * (3 * kStages);
-  const uint32_t tempty_bar = bar_base + 8u * (3 * kStages + 1);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kStages * kStageBytes + 8 * (3 * kStages + 2));
-  int32_t* pad_s = reinterpret_cast<int32_t*>(smem + kStages * kStageBytes + kBarBytes);
+  auto sfull_bar = [&](int s) { return bar_base + 8u * (S + s); };       // own scale bytes landed
+  auto empty_bar = [&](int s) { return bar_base + 8u * (2 * S + s); };   // stage consumed by the pair MMA
+  const uint32_t tfull_bar = bar_base + 8u * (3 * S);       // accumulator ready (both CTAs)
+  const uint32_t tempty_bar = bar_base + 8u * (3 * S + 1);  // even CTA: both epilogues read it
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + (bar_base - base) + 8 * (3 * S + 2));
+  int32_t* pad_s = reinterpret_cast<int32_t*>(smem + (bar_base - base) + kBarBytes);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int E = args.E;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = int(cluster_id_x()), npairs = int(cluster_count_x());
 
   for (int i = tid; i <= E; i += kThreads) pad_s[i] = args.pad_start[i];
   if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(full_bar(s), 1);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full_bar(s), 1 + 2 * kSfWarps);
+      mbar_init(sfull_bar(s), 1);
       mbar_init(empty_bar(s), 1);
-      mbar_init(sf_bar(s), kSfWarps);
     }
     mbar_init(tfull_bar, 1);
-    mbar_init(tempty_bar, kEpiWarps);
+    mbar_init(tempty_bar, 2 * kEpiWarps);
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmap_a);
     prefetch_tmap(&tmap_b);
+    if (MODE == 1) prefetch_tmap(&tmap_y);
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
-    tmem_relinquish();
+    tmem_alloc_pair(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
   __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers exist before any cross-CTA arrive or transfer
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int total_mb = pad_s[E] / kBM;
+  const int total_pm = pad_s[E] / kSegRows;
   const int n_tiles = args.n_tiles;
-  const int total_tiles = total_mb * n_tiles;
+  const int total_tiles = total_pm * n_tiles;
   const int kblocks = args.K / kBK;
   const uint32_t sf_row_stride = uint32_t(args.K / 64) * 512u;  // bytes per 128-row scale block
   auto coord = [&](int t) {
     TileCoord c;
-    c.mb = t / n_tiles;
-    c.nt = t - c.mb * n_tiles;
-    c.e = find_expert(pad_s, E, c.mb * kBM);
+    c.pm = t / n_tiles;
+    c.nt = t - c.pm * n_tiles;
+    c.e = find_expert(pad_s, E, c.pm * kSegRows);
     return c;
   };
-  auto b_rows = [&](const TileCoord& c, int& lr0, int& lr1) {  // local B rows of the two 128-row halves
-    if (args.mode == 0) {
-      lr0 = c.nt * 128;
-      lr1 = args.F + c.nt * 128;
+  auto b_rows = [&](const TileCoord& c, int& lr0, int& lr1) {  // local B rows of the tile's two 128-row halves
+    if (MODE == 0) {
+      lr0 = c.nt * 128;           // gate rows
+      lr1 = args.F + c.nt * 128;  // value rows
     } else {
       lr0 = c.nt * kBN;
       lr1 = lr0 + 128;
@@ -146,51 +185,63 @@ __global__ void __launch_bounds__(kThreads, 1)
   };
 
   if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------ TMA producer (both CTAs)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+      for (int t = pair; t < total_tiles && ok; t += npairs) {
         const TileCoord c = coord(t);
         int lr0, lr1;
         b_rows(c, lr0, lr1);
-        const int brow = c.e * args.N_total;
+        const int row0 = c.pm * kSegRows + int(rank) * kBM;
+        const int brow = c.e * args.N_total + (rank == 0 ? lr0 : lr1);
         const uint8_t* bsc = args.b_scales + size_t(c.e) * (size_t(args.N_total) * args.K / 16);
-        const uint8_t* asc = args.a_scales + size_t(c.mb) * sf_row_stride;
+        const uint8_t* bsc0 = bsc + size_t(lr0 / 128) * sf_row_stride;
+        const uint8_t* bsc1 = bsc + size_t(lr1 / 128) * sf_row_stride;
+        const uint8_t* asc = args.a_scales + size_t(row0 / 128) * sf_row_stride;
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, args.err, 101)) {
             ok = false;
             break;
           }
           const uint32_t st = base + stage * kStageBytes;
-          mbar_arrive_expect_tx(full_bar(stage), kStageBytes);
-          tma_load_2d(st, &tmap_a, kb * (kBK / 2), c.mb * kBM, full_bar(stage));
-          tma_load_2d(st + kOffB, &tmap_b, kb * (kBK / 2), brow + lr0, full_bar(stage));
-          tma_load_2d(st + kOffB + kBHalf, &tmap_b, kb * (kBK / 2), brow + lr1, full_bar(stage));
-          bulk_load(st + kOffSFA, asc + kb * 2048, kSFA, full_bar(stage));
-          bulk_load(st + kOffSFB, bsc + size_t(lr0 / 128) * sf_row_stride + kb * 2048, kSFBHalf, full_bar(stage));
-          bulk_load(st + kOffSFB + kSFBHalf, bsc + size_t(lr1 / 128) * sf_row_stride + kb * 2048, kSFBHalf,
-                    full_bar(stage));
-          if (++stage == kStages) {
+          if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * kABBytes);
+          mbar_arrive_expect_tx(sfull_bar(stage), kSFBytes);
+          const uint32_t fb = map_shared_rank(full_bar(stage), 0);
+          tma_load_2d_pair(st, &tmap_a, kb * (kBK / 2), row0, fb);
+          tma_load_2d_pair(st + kOffB, &tmap_b, kb * (kBK / 2), brow, fb);
+          bulk_load(st + kOffSFA, asc + kb * 2048, kSFA, sfull_bar(stage));
+          bulk_load(st + kOffSFB, bsc0 + kb * 2048, kSFBHalf, sfull_bar(stage));
+          bulk_load(st + kOffSFB + kSFBHalf, bsc1 + kb * 2048, kSFBHalf, sfull_bar(stage));
+          if (++stage == S) {
             stage = 0;
             phase ^= 1u;
           }
         }
       }
+      // Drain: wait until the pair MMA released every stage, so that no MMA
+      // completion is still on its way to this CTA's barriers at exit.
+      for (int i = 0; i < S && ok; ++i) {
+        ok = mbar_wait(empty_bar(stage), phase ^ 1u, args.err, 102);
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // ------------------------------------------------------------ pair MMA issuer (even CTA)
+    if (leader && lane == 0) {
       int stage = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+      for (int t = pair; t < total_tiles && ok; t += npairs) {
         if (!mbar_wait(tempty_bar, acc_phase ^ 1u, args.err, 201)) break;
         tc_fence_after();
         for (int kb = 0; kb < kblocks; ++kb) {
-          if (!mbar_wait(full_bar(stage), phase, args.err, 202) || !mbar_wait(sf_bar(stage), phase, args.err, 203)) {
+          if (!mbar_wait(full_bar(stage), phase, args.err, 202)) {
             ok = false;
             break;
           }
@@ -201,80 +252,91 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int ks = 0; ks < 4; ++ks) {
             const uint64_t adesc = smem_desc(st + 32 * ks, 16, 1024, 2);
             const uint64_t bdesc = smem_desc(st + kOffB + 32 * ks, 16, 1024, 2);
-            tc_mma_nvf4(tmem_base, adesc, bdesc, kIdesc, sf_col + 4 * ks, sf_col + 16 + 8 * ks,
-                        (kb | ks) != 0 ? 1u : 0u);
+            tc_mma_nvf4_pair(tmem_base, adesc, bdesc, kIdesc, sf_col + 4 * ks, sf_col + 16 + 8 * ks,
+                             (kb | ks) != 0 ? 1u : 0u);
           }
-          tc_commit(empty_bar(stage));
-          if (++stage == kStages) {
+          tc_commit_pair(map_shared_rank(empty_bar(stage), 0));
+          tc_commit_pair(map_shared_rank(empty_bar(stage), 1));
+          if (++stage == S) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        tc_commit(tfull_bar);
+        tc_commit_pair(map_shared_rank(tfull_bar, 0));
+        tc_commit_pair(map_shared_rank(tfull_bar, 1));
         acc_phase ^= 1u;
       }
     }
     __syncwarp();
   } else if (warp < kEpiWarp0) {
-    // ------------------------------------------------------------ scale-factor writers
+    // ------------------------------------------------------------ scale-factor writers (both CTAs)
     // Lane l of quarter q copies bytes [16 l, 16 l + 16) of each 512-byte atom
     // (the 4 scales of rows l, l+32, l+64, l+96) to TMEM lane 32q + l, 4 columns.
-    // A stage's TMEM slot is free once the stage is full again: the producer
-    // only refills a stage after the MMAs that read it (and its scales) completed.
+    // A stage's TMEM slot is free once the stage's scales have landed again:
+    // the producer refills a stage only after the pair MMAs that read it (and
+    // its scales in both CTAs) completed.
     const int q = warp & 3;
     const uint32_t lane_base = uint32_t(q * 32) << 16;
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+    for (int t = pair; t < total_tiles && ok; t += npairs) {
       for (int kb = 0; kb < kblocks; ++kb) {
-        if (!mbar_wait(full_bar(stage), phase, args.err, 121)) {
+        if (!mbar_wait(sfull_bar(stage), phase, args.err, 121)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint8_t* st = smem + stage * kStageBytes;
         const uint32_t sf_col = tmem_base + lane_base + kSfCol0 + stage * kSfColsPerStage;
+        // columns [0,16): SFA of K steps 0..3; [16,48): per K step, SFB half 0 then half 1
+        uint32_t va[16], vb[32];
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks) {
-          tmem_st4(sf_col + 4 * ks, *reinterpret_cast<const uint4*>(st + kOffSFA + ks * 512 + lane * 16));
-          tmem_st4(sf_col + 16 + 8 * ks, *reinterpret_cast<const uint4*>(st + kOffSFB + ks * 512 + lane * 16));
-          tmem_st4(sf_col + 16 + 8 * ks + 4,
-                   *reinterpret_cast<const uint4*>(st + kOffSFB + kSFBHalf + ks * 512 + lane * 16));
+          const uint4 a = *reinterpret_cast<const uint4*>(st + kOffSFA + ks * 512 + lane * 16);
+          const uint4 b0 = *reinterpret_cast<const uint4*>(st + kOffSFB + ks * 512 + lane * 16);
+          const uint4 b1 = *reinterpret_cast<const uint4*>(st + kOffSFB + kSFBHalf + ks * 512 + lane * 16);
+          va[4 * ks] = a.x, va[4 * ks + 1] = a.y, va[4 * ks + 2] = a.z, va[4 * ks + 3] = a.w;
+          vb[8 * ks] = b0.x, vb[8 * ks + 1] = b0.y, vb[8 * ks + 2] = b0.z, vb[8 * ks + 3] = b0.w;
+          vb[8 * ks + 4] = b1.x, vb[8 * ks + 5] = b1.y, vb[8 * ks + 6] = b1.z, vb[8 * ks + 7] = b1.w;
         }
+        tmem_st16(sf_col, va);
+        tmem_st32(sf_col + 16, vb);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(sf_bar(stage));
-        if (++stage == kStages) {
+        if (lane == 0) mbar_arrive_cluster(map_shared_rank(full_bar(stage), 0));
+        if (++stage == S) {
           stage = 0;
           phase ^= 1u;
         }
       }
     }
   } else {
-    // ------------------------------------------------------------ epilogue
+    // ------------------------------------------------------------ epilogue (both CTAs)
     // 16 warps: lane quarter q = warp % 4 (the TMEM lanes a warp may read),
-    // column group sub = 0..3 (32 h columns in mode 0, 64 output columns in mode 1).
+    // column group sub = 0..3 (32 h columns in MODE 0, 64 output columns otherwise).
     const int q = warp & 3;
     const int sub = (warp - kEpiWarp0) >> 2;
     const int row_in_tile = q * 32 + lane;
     const uint32_t lane_addr = tmem_base + (uint32_t(q * 32) << 16);
+    const uint32_t tempty_leader = map_shared_rank(tempty_bar, 0);
+    const uint32_t my_buf = store_base + uint32_t(warp - kEpiWarp0) * kWarpStoreBytes;
     uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+    for (int t = pair; t < total_tiles; t += npairs) {
       const TileCoord c = coord(t);
       // per-tile scalars first: their load latency overlaps the MMAs of this tile
-      const int64_t p = int64_t(c.mb) * kBM + row_in_tile;  // padded row
+      const int64_t p = int64_t(c.pm) * kSegRows + int64_t(rank) * kBM + row_in_tile;  // padded row
       const int local = int(p - pad_s[c.e]);
       const float gb = __ldg(args.b_g + c.e);
       const int rows_e = args.row_count ? __ldg(args.row_count + c.e) : (1 << 30);
-      const float wrow = (args.mode == 1 && args.row_w && local < rows_e) ? __ldg(args.row_w + p) : 0.f;
+      const float wrow = (MODE != 0 && args.row_w && local < rows_e) ? __ldg(args.row_w + p) : 0.f;
       if (!mbar_wait(tfull_bar, acc_phase, args.err, 301)) break;
       acc_phase ^= 1u;
       tc_fence_after();
       uint32_t va[32], vb[32];
-      if (args.mode == 0) {
+      if (MODE == 0) {
         tmem_ld32(lane_addr + sub * 32, va);        // gate columns
         tmem_ld32(lane_addr + 128 + sub * 32, vb);  // value columns
       } else {
@@ -284,10 +346,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(tempty_bar);  // accumulator may be overwritten now
+      if (lane == 0) mbar_arrive_cluster(tempty_leader);  // accumulator may be overwritten now
 
-      const bool row_valid = local < rows_e;
-      if (args.mode == 0) {
+      if (MODE == 0) {
         // up = bf16(acc * g); h = bf16(bf16(silu(gate)) * value) (src/mcl4_coe/backbone.py:572-574),
         // then NVFP4 with 1x16 row scales (src/mcl4_coe/nvfp4.py:197-225).
         const int F = args.F;
@@ -330,8 +391,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         *reinterpret_cast<uint16_t*>(args.hs +
                                      swizzled_scale_offset(uint64_t(p), uint32_t(hb0), uint32_t(F / 16))) =
             uint16_t(sword);
-      } else if (row_valid) {
-        // y = bf16(acc * g) [* bf16(routing weight), rounded to bf16] (src/mcl4_coe/backbone.py:903)
+      } else if (MODE == 1) {
+        // y = bf16(acc * g) [* bf16(routing weight), rounded to bf16] (src/mcl4_coe/backbone.py:903),
+        // every padded row (padding rows hold zeros), through a 32 x 64 swizzled smem tile.
+        const uint32_t ww = pack_bf16x2(wrow, wrow);
+        if (lane == 0) bulk_wait_read_all();  // the previous tile's store has read this buffer
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint32_t* src = i < 4 ? va + 8 * i : vb + 8 * (i - 4);
+          uint32_t o[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t yy = pack_bf16x2(__uint_as_float(src[2 * j]) * gb, __uint_as_float(src[2 * j + 1]) * gb);
+            o[j] = args.row_w ? bf16x2_mul(yy, ww) : yy;
+          }
+          st_shared_v4(my_buf + uint32_t(lane) * 128u + (uint32_t(i ^ (lane & 7)) << 4),
+                       make_uint4(o[0], o[1], o[2], o[3]));
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmap_y, my_buf, c.nt * kBN + sub * 64, int(p));  // lane 0 holds the warp's first row
+          bulk_commit_group();
+        }
+      } else if (local < rows_e) {
+        // y rows into unpadded destination rows, valid rows only
         const int64_t dst_row = args.out_row_base ? int64_t(args.out_row_base[c.e]) + local : p;
         const uint32_t ww = pack_bf16x2(wrow, wrow);
         uint4* dst = reinterpret_cast<uint4*>(args.y + dst_row * args.ldy + c.nt * kBN + sub * 64);
@@ -348,13 +433,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    if (MODE == 1 && lane == 0) bulk_wait_all();
   }
 
   tc_fence_before();
   __syncthreads();
+  cluster_sync_all();  // no pair MMA or peer access is outstanding past this point
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    tmem_dealloc_pair(tmem_base, kTmemCols);
   }
 }
 
@@ -388,6 +475,54 @@ bool make_tmap(CUtensorMap* m, const void* base, uint64_t row_bytes, uint64_t ro
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 2-D map over a bf16 [rows, ld] matrix, box 64 columns (128 bytes) x 32 rows, 128B swizzle (tile stores).
+bool make_tmap_store(CUtensorMap* m, const void* base, uint64_t ld, uint64_t rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {ld, rows};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {64, 32};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Number of CTA pairs that can be resident at once (one CTA per SM).
+template <int MODE>
+int resident_pairs() {
+  static int n = 0;
+  if (n == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * 74);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = Cfg<MODE>::kSmem;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, grouped_gemm_fp4_kernel<MODE>, &cfg) != cudaSuccess ||
+        clusters <= 0) {
+      (void)cudaGetLastError();
+      clusters = num_sms() / 2;
+    }
+    n = clusters;
+  }
+  return n;
+}
+
+template <int MODE>
+int launch_mode(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ty, const GemmArgs& args,
+                cudaStream_t stream) {
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(grouped_gemm_fp4_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             int(Cfg<MODE>::kSmem)) != cudaSuccess)
+      return MCL4MOE_ERR_CUDA;
+    configured = true;
+  }
+  const int pairs = resident_pairs<MODE>();
+  grouped_gemm_fp4_kernel<MODE><<<2 * pairs, kThreads, Cfg<MODE>::kSmem, stream>>>(ta, tb, ty, args);
+  return cudaGetLastError() == cudaSuccess ? MCL4MOE_OK : MCL4MOE_ERR_CUDA;
+}
+
 }  // namespace
 
 int num_sms() {
@@ -404,21 +539,25 @@ int num_sms() {
 int launch_grouped_gemm(const uint8_t* a, int64_t a_rows, const uint8_t* b, const GemmArgs& args,
                         cudaStream_t stream) {
   if (args.K % kBK != 0 || args.E < 1 || args.E > kMaxExperts) return MCL4MOE_ERR_UNSUPPORTED;
+  if (a_rows % kSegRows != 0) return MCL4MOE_ERR_INVALID;
   if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) | reinterpret_cast<uintptr_t>(args.a_scales) |
        reinterpret_cast<uintptr_t>(args.b_scales)) & 15)
     return MCL4MOE_ERR_INVALID;
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, ty;
   if (!make_tmap(&ta, a, uint64_t(args.K) / 2, uint64_t(a_rows))) return MCL4MOE_ERR_CUDA;
   if (!make_tmap(&tb, b, uint64_t(args.K) / 2, uint64_t(args.E) * args.N_total)) return MCL4MOE_ERR_CUDA;
-  static bool configured = false;
-  if (!configured) {
-    if (cudaFuncSetAttribute(grouped_gemm_fp4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes)) !=
-        cudaSuccess)
-      return MCL4MOE_ERR_CUDA;
-    configured = true;
+  if (args.mode == 0) {
+    memset(&ty, 0, sizeof(ty));
+    return launch_mode<0>(ta, tb, ty, args, stream);
   }
-  grouped_gemm_fp4_kernel<<<num_sms(), kThreads, kSmemBytes, stream>>>(ta, tb, args);
-  return cudaGetLastError() == cudaSuccess ? MCL4MOE_OK : MCL4MOE_ERR_CUDA;
+  if (args.out_row_base == nullptr) {
+    // Tile stores write every padded row: y holds a_rows rows of ldy elements.
+    if ((reinterpret_cast<uintptr_t>(args.y) & 15) || (args.ldy * 2) % 16 != 0) return MCL4MOE_ERR_INVALID;
+    if (!make_tmap_store(&ty, args.y, uint64_t(args.ldy), uint64_t(a_rows))) return MCL4MOE_ERR_CUDA;
+    return launch_mode<1>(ta, tb, ty, args, stream);
+  }
+  memset(&ty, 0, sizeof(ty));
+  return launch_mode<2>(ta, tb, ty, args, stream);
 }
 
 }  // namespace mcl4

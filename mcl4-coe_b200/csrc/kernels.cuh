@@ -51,9 +51,13 @@ inline RouteWorkspace route_workspace(void* base, int T, int E, int k, int d) {
   return w;
 }
 
+// Expert segments of the grouped GEMMs start on multiples of kSegRows rows: a
+// CTA pair computes 256-row tiles that must not straddle two experts.
+constexpr int kSegRows = 256;
+
 inline int64_t padded_rows_cap(int64_t T, int E, int k) {
-  const int64_t m = T * k + int64_t(127) * E;
-  return (m + 127) / 128 * 128;
+  const int64_t m = T * k + int64_t(kSegRows - 1) * E;
+  return (m + kSegRows - 1) / kSegRows * kSegRows;
 }
 
 // ---- launchers (return MCL4MOE_* status)

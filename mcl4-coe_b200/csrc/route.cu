@@ -9,7 +9,7 @@
 // chunk's slots per expert (router.cu), the scan turns per-chunk counts into
 // offsets, and the scatter kernel writes every slot at
 // pad_start[e] + (slots of e in earlier chunks) + rank.  Expert segments are
-// padded to multiples of 128 rows (the GEMM M tile).
+// padded to multiples of kSegRows rows (the GEMM's CTA-pair M tile).
 #include "kernels.cuh"
 
 namespace mcl4 {
@@ -100,7 +100,7 @@ __global__ void pad_from_offs_kernel(const int32_t* offs, int E, int32_t* pad_st
     offs_start[e] = prev;
     counts[e] = c;
     pad_start[e] = prun;
-    prun += (c + 127) / 128 * 128;
+    prun += (c + kSegRows - 1) / kSegRows * kSegRows;
     prev = end > prev ? end : prev;
   }
   pad_start[E] = prun;

@@ -529,12 +529,12 @@ __global__ void __launch_bounds__(256) route_scan_kernel(int C, int E, int k, Ro
   const int32_t cnt = tid < E ? __ldcg(ws.counts + tid) : 0;
   int32_t ignore;
   const int32_t ustart = block_exclusive_scan(cnt, itmp, ignore);
-  const int32_t pstart = block_exclusive_scan((cnt + 127) / 128 * 128, itmp, ignore);
+  const int32_t pstart = block_exclusive_scan((cnt + kSegRows - 1) / kSegRows * kSegRows, itmp, ignore);
   float term = 0.f;
   if (tid < E) {
     ws.offs_start[tid] = ustart;
     ws.pad_start[tid] = pstart;
-    if (tid == E - 1) ws.pad_start[E] = pstart + (cnt + 127) / 128 * 128;
+    if (tid == E - 1) ws.pad_start[E] = pstart + (cnt + kSegRows - 1) / kSegRows * kSegRows;
     if (offs_out) offs_out[tid] = ustart + cnt;
     if (counts_out) counts_out[tid] = cnt;
     if (stats) {
