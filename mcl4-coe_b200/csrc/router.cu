@@ -33,37 +33,19 @@ namespace {
 constexpr int kTailThreads = 256;  // 8 warps run the tail
 constexpr int kTcThreads = 64 + kTailThreads;
 
-__device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    unsigned long long w = __shfl_xor_sync(0xffffffffu, v, o);
-    v = w > v ? w : v;
-  }
-  return v;
-}
-__device__ __forceinline__ float warp_max_f(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
-__device__ __forceinline__ float warp_sum_f(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
-
 struct TailSmem {
-  float* logits;  // [128][E + 1]
-  int32_t* sel;   // [128][k]
-  int32_t* rank;  // [128][k]
-  int32_t* gcount;  // [4][E]
-  float* red;     // [8][E + 2]
+  float* logits;   // [128][E + 1] logits (bias included), overwritten with the routed probabilities
+  int32_t* sel;    // [128][k] selected experts (-1 for tokens that are not routed)
+  float* selp;     // [128][k] their probabilities
+  float* lse2;     // [128] lse^2 of routed tokens (0 otherwise)
+  float* nval;     // [128] 1 for routed tokens
+  uint32_t* bal;   // [4][E] per 32-token group: ballot of the tokens that selected expert e
   int lds;
 };
 
 __host__ __device__ inline size_t tail_smem_bytes(int E, int k) {
   return sizeof(float) * kRouteTokens * (E + 1) + 2 * sizeof(int32_t) * kRouteTokens * k +
-         sizeof(int32_t) * 4 * E + sizeof(float) * 8 * (E + 2) + 64;
+         2 * sizeof(float) * kRouteTokens + sizeof(uint32_t) * 4 * E + 64;
 }
 
 __device__ inline TailSmem carve_tail(uint8_t* base, int E, int k) {
@@ -71,129 +53,133 @@ __device__ inline TailSmem carve_tail(uint8_t* base, int E, int k) {
   t.lds = E + 1;
   t.logits = reinterpret_cast<float*>(base);
   t.sel = reinterpret_cast<int32_t*>(t.logits + kRouteTokens * t.lds);
-  t.rank = t.sel + kRouteTokens * k;
-  t.gcount = t.rank + kRouteTokens * k;
-  t.red = reinterpret_cast<float*>(t.gcount + 4 * E);
+  t.selp = reinterpret_cast<float*>(t.sel + kRouteTokens * k);
+  t.lse2 = t.selp + kRouteTokens * k;
+  t.nval = t.lse2 + kRouteTokens;
+  t.bal = reinterpret_cast<uint32_t*>(t.nval + kRouteTokens);
   return t;
 }
 
 // Softmax / top-k / statistics / stable ranks of one 128-token chunk whose
 // logits (bias included) are in ``s.logits``.  Runs on 256 threads with ids
 // ``g`` 0..255; ``sync()`` is a barrier over exactly those threads.
+//
+// Token-parallel: a group of TPT = max(2, EW) adjacent threads owns one token
+// and holds 32 of its logits each (experts h*32 .. h*32+31 for member h), so a
+// pass covers 256/TPT tokens and the chunk takes TPT/2 passes.  Softmax and
+// top-k (largest probability first, ties to the lower expert index, as
+// torch.topk on the reference's probabilities) combine across the group with
+// xor shuffles.  Per-expert probability sums are column sums over the chunk's
+// tokens in token order; stable ranks come from one ballot per expert and
+// 32-token group.  Semantics: src/mcl4_coe/backbone.py:787-883.
 template <int EW, class Sync>
 __device__ void route_tail(const TailSmem& s, int g, int chunk, int T, int E, int k, int norm_topk,
                            const uint8_t* __restrict__ valid, int32_t* __restrict__ topk_idx,
                            float* __restrict__ topk_w, float* __restrict__ logits_out, float* __restrict__ sel_mask,
                            const RouteWorkspace& ws, Sync sync) {
-  const int lane = g & 31, warp = g >> 5;
+  constexpr int TPT = EW < 2 ? 2 : EW;  // threads per token
+  constexpr int VPT = 32;               // logits per thread (E <= 32 * TPT)
+  constexpr int kPass = kTailThreads / TPT;
+  const int h = g % TPT;
   const int t0 = chunk * kRouteTokens;
-  float prob_acc[EW];
-#pragma unroll
-  for (int i = 0; i < EW; ++i) prob_acc[i] = 0.f;
-  float lse2_acc = 0.f, nval_acc = 0.f;
-  for (int tok = warp * 16; tok < warp * 16 + 16; ++tok) {
+  for (int pass = 0; pass < kRouteTokens / kPass; ++pass) {
+    const int tok = pass * kPass + g / TPT;
     const int t = t0 + tok;
-    if (t >= T) {
-      if (lane < k) s.sel[tok * k + lane] = -1;
-      continue;
-    }
-    float l[EW];
+    const bool in_range = t < T;
+    const bool routed = in_range && (valid == nullptr || valid[t] != 0);
+    float v[VPT];
 #pragma unroll
-    for (int i = 0; i < EW; ++i) {
-      const int e = lane + 32 * i;
-      l[i] = e < E ? s.logits[tok * s.lds + e] : -INFINITY;
-      if (logits_out != nullptr && e < E) logits_out[int64_t(t) * E + e] = l[i];
-    }
-    const bool routed = valid == nullptr || valid[t] != 0;
-    if (!routed) {
-      if (lane < k) {
-        topk_idx[int64_t(t) * k + lane] = -1;
-        topk_w[int64_t(t) * k + lane] = 0.f;
-        s.sel[tok * k + lane] = -1;
-      }
-      if (sel_mask != nullptr)
-#pragma unroll
-        for (int i = 0; i < EW; ++i)
-          if (lane + 32 * i < E) sel_mask[int64_t(t) * E + lane + 32 * i] = 0.f;
-      continue;
+    for (int i = 0; i < VPT; ++i) {
+      const int e = h * VPT + i;
+      v[i] = (e < E && in_range) ? s.logits[tok * s.lds + e] : -INFINITY;
+      if (logits_out != nullptr && e < E && in_range) logits_out[int64_t(t) * E + e] = v[i];
     }
     float m = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < EW; ++i) m = fmaxf(m, l[i]);
-    m = warp_max_f(m);
-    float p[EW], sum = 0.f;
+    for (int i = 0; i < VPT; ++i) m = fmaxf(m, v[i]);
 #pragma unroll
-    for (int i = 0; i < EW; ++i) {
-      p[i] = (lane + 32 * i < E) ? expf(__fsub_rn(l[i], m)) : 0.f;
-      sum = __fadd_rn(sum, p[i]);
-    }
-    sum = warp_sum_f(sum);
-    const float inv_s = __frcp_rn(sum);
-    const float lse = __fadd_rn(m, logf(sum));
-    lse2_acc = __fadd_rn(lse2_acc, __fmul_rn(lse, lse));
-    nval_acc += 1.f;
+    for (int o = 1; o < TPT; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (!in_range) m = 0.f;  // all -inf: keep the arithmetic finite, nothing is written
+    float sum = 0.f;
 #pragma unroll
-    for (int i = 0; i < EW; ++i) {
-      p[i] = __fmul_rn(p[i], inv_s);
-      prob_acc[i] = __fadd_rn(prob_acc[i], p[i]);
+    for (int i = 0; i < VPT; ++i) {
+      v[i] = (h * VPT + i < E && in_range) ? expf(__fsub_rn(v[i], m)) : 0.f;
+      sum = __fadd_rn(sum, v[i]);
     }
-    // top-k: largest probability first, ties to the lower expert index
+#pragma unroll
+    for (int o = 1; o < TPT; o <<= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+    const float inv_s = in_range ? __frcp_rn(sum) : 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      v[i] = __fmul_rn(v[i], inv_s);
+      const int e = h * VPT + i;
+      if (e < E) s.logits[tok * s.lds + e] = routed ? v[i] : 0.f;  // column sums below
+    }
+    if (h == 0) {
+      const float lse = routed ? __fadd_rn(m, logf(sum)) : 0.f;
+      s.lse2[tok] = __fmul_rn(lse, lse);
+      s.nval[tok] = routed ? 1.f : 0.f;
+    }
+    // top-k over the group: each member offers its best remaining candidate
     uint32_t taken = 0;
-    int my_e = -1;
-    float my_p = 0.f;
+    float total = 0.f;
     for (int j = 0; j < k; ++j) {
-      unsigned long long best = 0;
+      float bp = -1.f;
+      int bi = 0;
 #pragma unroll
-      for (int i = 0; i < EW; ++i) {
-        const int e = lane + 32 * i;
-        if (e < E && !((taken >> i) & 1u)) {
-          const unsigned long long key =
-              (static_cast<unsigned long long>(__float_as_uint(p[i])) << 32) | (0xFFFFFFFFu - uint32_t(e));
-          best = key > best ? key : best;
+      for (int i = 0; i < VPT; ++i)
+        if (h * VPT + i < E && !((taken >> i) & 1u) && v[i] > bp) {
+          bp = v[i];
+          bi = i;
         }
+      const uint32_t be = uint32_t(h * VPT + bi);
+      unsigned long long best =
+          bp >= 0.f ? (static_cast<unsigned long long>(__float_as_uint(bp)) << 32) | (0xFFFFFFFFu - be) : 0ull;
+#pragma unroll
+      for (int o = 1; o < TPT; o <<= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+        best = other > best ? other : best;
       }
-      best = warp_max_u64(best);
       const int e_star = int(0xFFFFFFFFu - uint32_t(best & 0xFFFFFFFFull));
-      if ((e_star & 31) == lane) taken |= 1u << (e_star >> 5);
-      if (lane == j) {
-        my_e = e_star;
-        my_p = __uint_as_float(uint32_t(best >> 32));
+      const float p_star = __uint_as_float(uint32_t(best >> 32));
+      if (e_star / VPT == h) taken |= 1u << (e_star % VPT);
+      total = __fadd_rn(total, p_star);
+      if (j % TPT == h) {
+        s.sel[tok * k + j] = routed ? e_star : -1;
+        s.selp[tok * k + j] = p_star;
       }
     }
-    float w = my_p;
-    if (norm_topk) {
-      float total = 0.f;
-      for (int j = 0; j < k; ++j) total = __fadd_rn(total, __shfl_sync(0xffffffffu, my_p, j));
-      w = __fdiv_rn(my_p, fmaxf(total, 1e-9f));
-    }
-    if (lane < k) {
-      topk_idx[int64_t(t) * k + lane] = my_e;
-      topk_w[int64_t(t) * k + lane] = w;
-      s.sel[tok * k + lane] = my_e;
-    }
-    if (sel_mask != nullptr)
+    if (in_range) {
+      for (int j = h; j < k; j += TPT) {
+        const float w = norm_topk ? __fdiv_rn(s.selp[tok * k + j], fmaxf(total, 1e-9f)) : s.selp[tok * k + j];
+        topk_idx[int64_t(t) * k + j] = routed ? s.sel[tok * k + j] : -1;
+        topk_w[int64_t(t) * k + j] = routed ? w : 0.f;
+      }
+      if (sel_mask != nullptr)
 #pragma unroll
-      for (int i = 0; i < EW; ++i)
-        if (lane + 32 * i < E) sel_mask[int64_t(t) * E + lane + 32 * i] = ((taken >> i) & 1u) ? 1.f : 0.f;
-  }
-#pragma unroll
-  for (int i = 0; i < EW; ++i)
-    if (lane + 32 * i < E) s.red[warp * (E + 2) + lane + 32 * i] = prob_acc[i];
-  if (lane == 0) {
-    s.red[warp * (E + 2) + E] = lse2_acc;
-    s.red[warp * (E + 2) + E + 1] = nval_acc;
+        for (int i = 0; i < VPT; ++i) {
+          const int e = h * VPT + i;
+          if (e < E) sel_mask[int64_t(t) * E + e] = (routed && ((taken >> i) & 1u)) ? 1.f : 0.f;
+        }
+    }
   }
   sync();
 
-  // per-chunk statistics, warps added in a fixed order
-  for (int e = g; e < E + 2; e += kTailThreads) {
-    float a = 0.f;
-    for (int w8 = 0; w8 < 8; ++w8) a = __fadd_rn(a, s.red[w8 * (E + 2) + e]);
-    if (e < E) ws.part_probs[int64_t(chunk) * E + e] = a;
-    else ws.part_misc[int64_t(chunk) * 2 + (e - E)] = a;
+  // per-chunk statistics: column sums in token order
+  for (int c = g; c < E + 2; c += kTailThreads) {
+    float acc = 0.f;
+    if (c < E) {
+      for (int tok = 0; tok < kRouteTokens; ++tok) acc = __fadd_rn(acc, s.logits[tok * s.lds + c]);
+      ws.part_probs[int64_t(chunk) * E + c] = acc;
+    } else {
+      const float* col = c == E ? s.lse2 : s.nval;
+      for (int tok = 0; tok < kRouteTokens; ++tok) acc = __fadd_rn(acc, col[tok]);
+      ws.part_misc[int64_t(chunk) * 2 + (c - E)] = acc;
+    }
   }
 
-  // stable ranks: warps 0..3 rank 32 tokens each with ballots, in token order
+  // stable ranks: warps 0..3 own 32 tokens each (lane = token); one ballot per expert
+  const int lane = g & 31, warp = g >> 5;
   if (warp < 4) {
     const int tok = warp * 32 + lane;
     uint32_t mw[EW];
@@ -201,43 +187,32 @@ __device__ void route_tail(const TailSmem& s, int g, int chunk, int T, int E, in
     for (int i = 0; i < EW; ++i) mw[i] = 0;
     for (int j = 0; j < k; ++j) {
       const int e = s.sel[tok * k + j];
-      if (e >= 0) {
 #pragma unroll
-        for (int i = 0; i < EW; ++i)
-          if ((e >> 5) == i) mw[i] |= 1u << (e & 31);
-      }
+      for (int i = 0; i < EW; ++i)
+        if (e >= 0 && (e >> 5) == i) mw[i] |= 1u << (e & 31);
     }
-    const uint32_t lt = (1u << lane) - 1u;
 #pragma unroll
-    for (int i = 0; i < EW; ++i) {
+    for (int i = 0; i < EW; ++i)
       for (int b = 0; b < 32; ++b) {
-        const int e = i * 32 + b;
-        if (e >= E) break;
-        const bool has = (mw[i] >> b) & 1u;
-        const uint32_t bal = __ballot_sync(0xffffffffu, has);
-        if (has) {
-          const int r = __popc(bal & lt);
-          for (int j = 0; j < k; ++j)
-            if (s.sel[tok * k + j] == e) s.rank[tok * k + j] = r;
-        }
-        if (lane == 0) s.gcount[warp * E + e] = __popc(bal);
+        const uint32_t bal = __ballot_sync(0xffffffffu, (mw[i] >> b) & 1u);
+        if (lane == b && i * 32 + b < E) s.bal[warp * E + i * 32 + b] = bal;
       }
-    }
   }
   sync();
   for (int e = g; e < E; e += kTailThreads)
-    ws.chunk_excl[int64_t(chunk) * E + e] = s.gcount[e] + s.gcount[E + e] + s.gcount[2 * E + e] + s.gcount[3 * E + e];
+    ws.chunk_excl[int64_t(chunk) * E + e] =
+        __popc(s.bal[e]) + __popc(s.bal[E + e]) + __popc(s.bal[2 * E + e]) + __popc(s.bal[3 * E + e]);
   for (int i = g; i < kRouteTokens * k; i += kTailThreads) {
     const int tok = i / k;
+    if (t0 + tok >= T) continue;
     const int e = s.sel[i];
-    if (t0 + tok < T) {
-      int r = 0;
-      if (e >= 0) {
-        r = s.rank[i];
-        for (int gi = 0; gi < (tok >> 5); ++gi) r += s.gcount[gi * E + e];
-      }
-      ws.local_rank[int64_t(t0) * k + i] = r;
+    int r = 0;
+    if (e >= 0) {
+      const int grp = tok >> 5;
+      r = __popc(s.bal[grp * E + e] & ((1u << (tok & 31)) - 1u));
+      for (int gi = 0; gi < grp; ++gi) r += __popc(s.bal[gi * E + e]);
     }
+    ws.local_rank[int64_t(t0) * k + i] = r;
   }
 }
 
