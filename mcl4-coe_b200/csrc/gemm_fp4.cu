@@ -234,6 +234,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ pair MMA issuer (even CTA)
     if (leader && lane == 0) {
+      // Four epilogue warps share this warp's scheduler, so the issue loop is
+      // kept short: descriptors, scale columns and barrier addresses of a stage
+      // advance by fixed strides from precomputed stage-0 values.
+      const uint64_t adesc0 = smem_desc(base, 16, 1024, 2);
+      const uint64_t bdesc0 = smem_desc(base + kOffB, 16, 1024, 2);
+      const uint32_t sf0 = tmem_base + kSfCol0;
+      const uint32_t empty0_own = map_shared_rank(empty_bar(0), 0), empty0_peer = map_shared_rank(empty_bar(0), 1);
+      const uint32_t tfull_own = map_shared_rank(tfull_bar, 0), tfull_peer = map_shared_rank(tfull_bar, 1);
       int stage = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
@@ -246,25 +254,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t st = base + stage * kStageBytes;
-          const uint32_t sf_col = tmem_base + kSfCol0 + stage * kSfColsPerStage;
+          const uint64_t adesc = adesc0 + uint64_t(stage) * (kStageBytes >> 4);
+          const uint64_t bdesc = bdesc0 + uint64_t(stage) * (kStageBytes >> 4);
+          const uint32_t sf_col = sf0 + uint32_t(stage) * kSfColsPerStage;
 #pragma unroll
-          for (int ks = 0; ks < 4; ++ks) {
-            const uint64_t adesc = smem_desc(st + 32 * ks, 16, 1024, 2);
-            const uint64_t bdesc = smem_desc(st + kOffB + 32 * ks, 16, 1024, 2);
-            tc_mma_nvf4_pair(tmem_base, adesc, bdesc, kIdesc, sf_col + 4 * ks, sf_col + 16 + 8 * ks,
-                             (kb | ks) != 0 ? 1u : 0u);
-          }
-          tc_commit_pair(map_shared_rank(empty_bar(stage), 0));
-          tc_commit_pair(map_shared_rank(empty_bar(stage), 1));
+          for (int ks = 0; ks < 4; ++ks)
+            tc_mma_nvf4_pair(tmem_base, adesc + 2 * ks, bdesc + 2 * ks, kIdesc, sf_col + 4 * ks,
+                             sf_col + 16 + 8 * ks, (kb | ks) != 0 ? 1u : 0u);
+          tc_commit_pair(empty0_own + 8u * stage);
+          tc_commit_pair(empty0_peer + 8u * stage);
           if (++stage == S) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        tc_commit_pair(map_shared_rank(tfull_bar, 0));
-        tc_commit_pair(map_shared_rank(tfull_bar, 1));
+        tc_commit_pair(tfull_own);
+        tc_commit_pair(tfull_peer);
         acc_phase ^= 1u;
       }
     }
