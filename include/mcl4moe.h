@@ -204,6 +204,44 @@ int mcl4moe_grouped_linear(const uint16_t* x, int64_t M, int K, const int32_t* o
                            const uint8_t* w_scales, const float* w_g, int N, uint16_t* out, int32_t* error_word,
                            void* workspace, size_t workspace_bytes, mcl4moe_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * Expert parallelism (G ranks, rank g owns experts [g*E_loc, (g+1)*E_loc)).
+ * No counterpart in the reference, which runs the layer on one device: these
+ * are the dispatch and combine steps around the grouped GEMMs when the experts
+ * of SparseMoE (src/mcl4_coe/backbone.py:887-910) are sharded across GPUs.
+ * The exchange between ranks (all-to-all of rows, then of partial sums) is
+ * the caller's, e.g. NCCL through torch.distributed.
+ *
+ * Dispatch row (mcl4moe_ep_row_bytes(d, k) bytes): NVFP4 codes [d/2], 1x16
+ * E4M3 scales row-major [d/16], k int8 expert ids local to the destination
+ * (-1: expert on another rank) padded to 16, k fp32 routing weights padded to
+ * 16.  Requires d % 256 == 0, G <= 8, E == G * E_loc.
+ *
+ * mcl4moe_ep_dispatch: from routing (topk_idx/topk_w of mcl4moe_route) builds
+ * one row per (token, destination holding any of its experts), destinations
+ * concatenated in rank order, tokens in index order within a destination.
+ * send_counts (device int32 [2G]): rows then expert slots per destination;
+ * send_pos (int32 [T, G]): row of (t, g) in send_buf or -1.  send_buf must hold
+ * T * G rows (the worst case).
+ * mcl4moe_ep_experts: on the receiving rank, R received rows holding `slots`
+ * local expert slots in total -> partial (bf16 [R, d]): per row, the sum over
+ * its local experts of bf16(bf16(acc * g) * bf16(w)), summed in fp32.
+ * mcl4moe_ep_combine: out[t] = bf16(sum over g of back_buf[send_pos[t, g]]),
+ * back_buf holding the partials returned in send order.
+ * ------------------------------------------------------------------------ */
+int mcl4moe_ep_row_bytes(int d, int k);
+size_t mcl4moe_ep_dispatch_workspace_size(int T, int G);
+int mcl4moe_ep_dispatch(const uint16_t* x, const int32_t* topk_idx, const float* topk_w, const uint8_t* valid, int T,
+                        int d, int k, int G, int E_loc, int32_t* send_counts, int32_t* send_pos, uint8_t* send_buf,
+                        void* workspace, size_t workspace_bytes, mcl4moe_stream_t stream);
+size_t mcl4moe_ep_experts_workspace_size(int R, int slots, int d, int k, int E_loc, int F);
+int mcl4moe_ep_experts(const uint8_t* recv_buf, int R, int slots, int d, int k, int E_loc, int F,
+                       const uint8_t* w_up, const uint8_t* w_up_scales, const float* w_up_g, const uint8_t* w_dn,
+                       const uint8_t* w_dn_scales, const float* w_dn_g, uint16_t* partial, int32_t* error_word,
+                       void* workspace, size_t workspace_bytes, mcl4moe_stream_t stream);
+int mcl4moe_ep_combine(const uint16_t* back_buf, const int32_t* send_pos, int T, int d, int G, uint16_t* out,
+                       mcl4moe_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -9,6 +9,7 @@ through ``__graft_entry__.load_package()`` (registered as ``mcl4coe_b200``).
 """
 
 from . import _lib
+from .expert_parallel import CudaEPOps, ExpertParallelMoE
 from .moe import MoEConfig, SparseMoE, SwiGLUExpert
 from .nvfp4 import (
     GroupedNVFP4Cache,
@@ -21,6 +22,8 @@ from .nvfp4 import (
 )
 
 __all__ = [
+    "CudaEPOps",
+    "ExpertParallelMoE",
     "MoEConfig",
     "SparseMoE",
     "SwiGLUExpert",

@@ -34,6 +34,12 @@ EXPORTS = (
     "mcl4moe_workspace_region",
     "mcl4moe_grouped_linear_workspace_size",
     "mcl4moe_grouped_linear",
+    "mcl4moe_ep_row_bytes",
+    "mcl4moe_ep_dispatch_workspace_size",
+    "mcl4moe_ep_dispatch",
+    "mcl4moe_ep_experts_workspace_size",
+    "mcl4moe_ep_experts",
+    "mcl4moe_ep_combine",
 )
 
 
@@ -127,6 +133,21 @@ def load() -> ctypes.CDLL:
     lib.mcl4moe_grouped_linear.restype = c_int
     lib.mcl4moe_grouped_linear.argtypes = [c_void_p, c_int64, c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p,
                                            c_int, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]
+    lib.mcl4moe_ep_row_bytes.restype = c_int
+    lib.mcl4moe_ep_row_bytes.argtypes = [c_int, c_int]
+    lib.mcl4moe_ep_dispatch_workspace_size.restype = c_size_t
+    lib.mcl4moe_ep_dispatch_workspace_size.argtypes = [c_int, c_int]
+    lib.mcl4moe_ep_dispatch.restype = c_int
+    lib.mcl4moe_ep_dispatch.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
+                                        c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]
+    lib.mcl4moe_ep_experts_workspace_size.restype = c_size_t
+    lib.mcl4moe_ep_experts_workspace_size.argtypes = [c_int, c_int, c_int, c_int, c_int, c_int]
+    lib.mcl4moe_ep_experts.restype = c_int
+    lib.mcl4moe_ep_experts.argtypes = [c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
+                                       c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                       c_size_t, c_void_p]
+    lib.mcl4moe_ep_combine.restype = c_int
+    lib.mcl4moe_ep_combine.argtypes = [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]
     _lib = lib
     return lib
 

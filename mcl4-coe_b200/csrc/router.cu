@@ -413,48 +413,6 @@ __global__ void __launch_bounds__(kTailThreads) router_logits_kernel(const float
 
 // ---------------------------------------------------------------- scan
 
-namespace {
-
-__device__ __forceinline__ int32_t block_exclusive_scan(int32_t v, int32_t* tmp, int32_t& total) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  int32_t x = v;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int32_t y = __shfl_up_sync(0xffffffffu, x, o);
-    if (lane >= o) x += y;
-  }
-  if (lane == 31) tmp[warp] = x;
-  __syncthreads();
-  if (warp == 0) {
-    int32_t w = lane < nw ? tmp[lane] : 0;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int32_t y = __shfl_up_sync(0xffffffffu, w, o);
-      if (lane >= o) w += y;
-    }
-    if (lane < nw) tmp[32 + lane] = w;
-  }
-  __syncthreads();
-  total = tmp[32 + nw - 1];
-  const int32_t before = warp ? tmp[32 + warp - 1] : 0;
-  __syncthreads();
-  return before + x - v;
-}
-
-// Deterministic block sum: fixed xor tree in each warp, warps added in order.
-__device__ __forceinline__ float block_sum(float v, float* tmp) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
-  if (lane == 0) tmp[warp] = v;
-  __syncthreads();
-  float s = 0.f;
-  for (int w = 0; w < nw; ++w) s = __fadd_rn(s, tmp[w]);
-  __syncthreads();
-  return s;
-}
-
-}  // namespace
 
 // One CTA per expert: exclusive prefix of the expert's per-chunk slot counts
 // and its probability sum.  The last CTA to finish (counted with an atomic

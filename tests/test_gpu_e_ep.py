@@ -1,0 +1,114 @@
+"""Expert-parallel kernels on one GPU: G ranks emulated with a single source.
+
+With one source rank, what destination g receives is exactly the slice of the
+send buffer addressed to g, so dispatch -> per-rank experts -> combine can run
+in one process without a collective.  The output must match the single-GPU
+layer (up to the bf16 rounding of per-rank partial sums), the dispatched rows
+must carry the reference quantiser's bytes, and routing is shared bit for bit.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_ref import build_module, x_tensor
+from inputs import moe_case
+from oracle import nvfp4_ref as nr
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _emulate(pkg, moe, x, G, valid=None):
+    ops = pkg.CudaEPOps()
+    T, d = x.shape
+    E, k = len(moe.experts), moe.top_k
+    E_loc = E // G
+    wr = moe.router.weight.detach().float().contiguous()
+    idx, w, stats = ops.route(x, wr, None, valid, k, moe.norm_topk_prob)
+    send, counts, pos = ops.dispatch(x, idx, w, valid, G, E_loc)
+    c = counts.cpu().tolist()
+    rows, slots = c[:G], c[G:]
+    parts, start = [], 0
+    for g in range(G):
+        recv = send[start:start + rows[g]]
+        parts.append(ops.experts(recv, rows[g], slots[g], d, k, moe.experts[g * E_loc:(g + 1) * E_loc]))
+        start += rows[g]
+    back = torch.cat(parts, dim=0)
+    out = ops.combine(back, pos, T, d, G)
+    torch.cuda.synchronize()
+    return out, dict(idx=idx, w=w, send=send, rows=rows, slots=slots, pos=pos, stats=stats)
+
+
+@pytest.mark.parametrize("G", [2, 4])
+def test_emulated_ranks_match_single_gpu_layer(moe_pkg, G):
+    c = moe_case(31, 1024, 512, 16, 4, 512)
+    moe = build_module(moe_pkg, c, DEV)
+    x = x_tensor(c, DEV)
+    with torch.no_grad():
+        ref = moe.forward_details(x)
+    out, info = _emulate(moe_pkg, moe, x, G)
+    np.testing.assert_array_equal(info["idx"].cpu().numpy(), ref["topk_idx"].cpu().numpy())
+    a, b = out.float(), ref["out"].float()
+    rel = (torch.linalg.norm(a - b) / torch.linalg.norm(b)).item()
+    assert rel < 5e-3, rel
+    assert (a - b).abs().max().item() < 1e-1
+    # every (token, destination) row exists exactly when the token has an expert there
+    idx = info["idx"].cpu().numpy()
+    has = np.stack([np.any(idx // (16 // G) == g, axis=1) for g in range(G)], axis=1)
+    pos = info["pos"].cpu().numpy()
+    assert np.array_equal(pos >= 0, has)
+    assert info["rows"] == has.sum(axis=0).tolist()
+    assert sum(info["slots"]) == idx.size
+
+
+def test_dispatched_rows_carry_reference_quantiser_bytes(moe_pkg):
+    c = moe_case(32, 256, 512, 8, 2, 512)
+    moe = build_module(moe_pkg, c, DEV)
+    x = x_tensor(c, DEV)
+    G, d, k = 2, 512, 2
+    _, info = _emulate(moe_pkg, moe, x, G)
+    packed, scales = nr.quantize_activations(x.float().cpu().numpy())
+    send = info["send"].cpu().numpy()
+    pos = info["pos"].cpu().numpy()
+    idx = info["idx"].cpu().numpy()
+    w = info["w"].cpu().numpy()
+    for t in range(x.shape[0]):
+        for g in range(G):
+            p = pos[t, g]
+            if p < 0:
+                continue
+            row = send[p]
+            np.testing.assert_array_equal(row[:d // 2], packed[t])
+            np.testing.assert_array_equal(row[d // 2:d // 2 + d // 16], scales[t])
+            ids = row[d // 2 + d // 16:d // 2 + d // 16 + k].view(np.int8)
+            want = np.where(idx[t] // (8 // G) == g, idx[t] - g * (8 // G), -1)
+            np.testing.assert_array_equal(ids, want)
+            wts = row[d // 2 + d // 16 + 16:d // 2 + d // 16 + 16 + 4 * k].view(np.float32)
+            np.testing.assert_array_equal(wts, w[t])
+
+
+def test_masked_tokens_and_a_rank_without_rows(moe_pkg):
+    c = moe_case(33, 512, 512, 8, 2, 512, valid_frac=0.7)
+    moe = build_module(moe_pkg, c, DEV)
+    # route every token to experts 0..3 (rank 0 of 2): rank 1 receives nothing
+    bias = torch.zeros(8, device=DEV)
+    bias[4:] = -1e4
+    moe.router_logit_bias = bias
+    x = x_tensor(c, DEV)
+    valid = torch.from_numpy(c["valid"]).to(DEV)
+    with torch.no_grad():
+        ref = moe.forward_details(x, valid)
+    ops = moe_pkg.CudaEPOps()
+    wr = moe.router.weight.detach().float().contiguous()
+    idx, w, _ = ops.route(x, wr, bias, valid, 2, moe.norm_topk_prob)
+    send, counts, pos = ops.dispatch(x, idx, w, valid, 2, 4)
+    rows = counts.cpu().tolist()
+    assert rows[1] == 0 and rows[3] == 0
+    p0 = ops.experts(send[:rows[0]], rows[0], rows[2], 512, 2, moe.experts[:4])
+    p1 = ops.experts(send[rows[0]:rows[0]], 0, 0, 512, 2, moe.experts[4:])
+    out = ops.combine(torch.cat([p0, p1]), pos, x.shape[0], 512, 2)
+    torch.cuda.synchronize()
+    a, b = out.float(), ref["out"].float()
+    assert (torch.linalg.norm(a - b) / torch.linalg.norm(b)).item() < 5e-3
+    assert torch.all(a[valid == 0] == 0)
