@@ -46,6 +46,9 @@ CONFIGS = {
     "c4": dict(name="c4_decode", seed=4, t=64, d=2048, e=64, k=8, f=1024),
 }
 KERNELS_PER_FORWARD = 7  # router-weight split, router, route-scan, permute+quantise, gate/up GEMM, down GEMM, combine
+# expert parallel: route (3) + dispatch count/scan/pack (3) + receive count/scan/pad/scatter (4) + 2 GEMMs + partial
+# sums (1) + combine (1)
+KERNELS_PER_EP_FORWARD = 14
 
 
 def load_peaks() -> dict:
@@ -183,6 +186,11 @@ def run_ours(args) -> None:
     cfg = CONFIGS[args.config]
     T, d, E, k, F = cfg["t"], cfg["d"], cfg["e"], cfg["k"], cfg["f"]
     moe, x = build_layer(pkg, cfg, dev, rank)
+    ep = world > 1
+    n_stages = 6 if ep else 5
+    if ep:
+        # expert parallel: the same layer on every rank, each keeps its E / N experts
+        moe = pkg.ExpertParallelMoE.from_dense(moe)
 
     def barrier():
         if world > 1:
@@ -201,7 +209,7 @@ def run_ours(args) -> None:
             moe(x)
         torch.cuda.synchronize()
         # stage events: 6 per step, recorded once beforehand so their handles exist
-        stage_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(K)]
+        stage_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(n_stages + 1)] for _ in range(K)]
         for evs in stage_ev:
             for ev in evs:
                 ev.record()
@@ -222,7 +230,7 @@ def run_ours(args) -> None:
         moe.stage_events = None
         clocks = sampler.stop()
         elapsed_ms = max_over_ranks(start.elapsed_time(end))
-        stage_ms = [statistics.mean(evs[j].elapsed_time(evs[j + 1]) for evs in stage_ev) for j in range(5)]
+        stage_ms = [statistics.mean(evs[j].elapsed_time(evs[j + 1]) for evs in stage_ev) for j in range(n_stages)]
 
         # end to end through the public API with host buffers
         x_host = x.cpu().pin_memory()
@@ -253,8 +261,15 @@ def run_ours(args) -> None:
     value = T * world / (ms_per_step / 1e3)
     peaks = load_peaks()
     fp4_peak = 4.0 * peaks["bf16"]  # dense FP4 = 4x dense BF16 on Blackwell (9 vs 2.25 PFLOP/s nominal)
-    gemm1_flops = 4.0 * T * k * d * F
-    achieved = gemm1_flops / (stage_ms[2] / 1e3) / 1e12
+    if ep:
+        # the rank's experts step (receive layout, both grouped GEMMs, partial sums) on its own slots
+        slots_here = moe.last_exchange["slots"][0]
+        roof_flops, roof_ms = 6.0 * slots_here * d * F, stage_ms[3]
+        roof_kernel = "grouped_gemm_fp4 gate/up + down (expert-parallel experts step of rank 0, incl. row layout)"
+    else:
+        roof_flops, roof_ms = 4.0 * T * k * d * F, stage_ms[2]
+        roof_kernel = "grouped_gemm_fp4 (gate/up, SwiGLU+requant epilogue)"
+    achieved = roof_flops / (roof_ms / 1e3) / 1e12
     traffic = None
     tp = ROOT / "profiles" / "traffic.json"
     if tp.exists():
@@ -266,20 +281,21 @@ def run_ours(args) -> None:
         "dtype": "nvfp4 (e2m1 + e4m3/16) x nvfp4 -> fp32 accumulate, bf16 I/O, fp32 router",
         "data": "synthetic (x~N(0,1) bf16, weights~N(0,0.02) fp32 quantised to NVFP4, seeded torch RNG on device)",
         "config": {"workload": cfg["name"], "tokens_per_gpu": T, "d_model": d, "num_experts": E, "top_k": k,
-                   "expert_ffn": F, "parallelism": "replicas" if world > 1 else "single",
+                   "expert_ffn": F, "parallelism": f"ep{world}" if ep else "single",
                    "l2": "no flush: x (%.0f MB) and NVFP4 weights (%.0f MB) exceed the 126 MB L2" % (
                        T * d * 2 / 1e6, E * 3 * d * F * (0.5 + 1 / 16) / 1e6)},
-        "stages_ms": dict(zip(("route", "permute_quant", "gateup_gemm", "down_gemm", "combine"),
+        "stages_ms": dict(zip(("route", "dispatch", "exchange_rows", "experts", "exchange_partials", "combine")
+                              if ep else ("route", "permute_quant", "gateup_gemm", "down_gemm", "combine"),
                               [round(s, 4) for s in stage_ms])),
         "layer_fp4_tflops": layer_tflops,
-        "roofline": {"bound": "tensor", "kernel": "grouped_gemm_fp4 (gate/up, SwiGLU+requant epilogue)",
+        "roofline": {"bound": "tensor", "kernel": roof_kernel,
                      "achieved": achieved, "peak": fp4_peak, "unit": "TFLOP/s", "frac": achieved / fp4_peak,
                      "traffic": traffic,
                      "peak_source": f"4 x {peaks['source']} dense bf16 {peaks['bf16']} TFLOP/s "
                                     "(MEASURED_PEAKS.json; FP4 dense = 4x BF16 dense)"},
         "e2e": {"value": T * world / (e2e_ms / K / 1e3), "unit": UNIT, "h2d_bytes_per_step": T * d * 2,
                 "d2h_bytes_per_step": T * d * 2 + 8},
-        "gpu_launches": KERNELS_PER_FORWARD * K,
+        "gpu_launches": (KERNELS_PER_EP_FORWARD if ep else KERNELS_PER_FORWARD) * K,
         "clocks": clocks,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

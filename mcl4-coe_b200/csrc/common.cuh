@@ -234,7 +234,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int32_t
   }
 }
 
-// 2-D TMA tile load into shared memory, completion counted on ``bar`` (no multicast).
+// 2-D TMA tile load into this CTA's shared memory, completion counted on ``bar``.
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int32_t x, int32_t y, uint32_t bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
@@ -395,7 +395,7 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
 }
 // 2-D TMA tile load into this CTA's shared memory whose completion is counted
 // on an mbarrier of either CTA of the pair (``bar`` is a cluster address).
-// No multicast: every CTA fetches its own tile.
+// Each CTA fetches its own tile.
 __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const void* tmap, int32_t x, int32_t y,
                                                  uint32_t bar) {
   asm volatile(

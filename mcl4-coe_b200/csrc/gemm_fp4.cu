@@ -45,7 +45,7 @@
 // next tile's MMAs overlap the epilogue math.  Scale factors live in a
 // per-stage TMEM ring, overwritten only after the MMAs that read them
 // completed.  Every mbarrier wait is bounded (error word instead of a hang).
-// No TMA load uses multicast: every CTA fetches its own operand tiles.
+// Every CTA fetches its own operand tiles with plain TMA loads (nothing is shared across the pair).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 

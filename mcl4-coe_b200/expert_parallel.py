@@ -144,6 +144,9 @@ class ExpertParallelMoE(nn.Module):
         self.last_selected_mask: Tensor | None = None
         self.ops = ops if ops is not None else CudaEPOps()
         self.last_exchange: dict[str, list[int]] = {}
+        # optional 7 CUDA events recorded around the six steps (route, dispatch,
+        # row exchange, experts, partial exchange, combine), for stage timing
+        self.stage_events: list | None = None
 
     @classmethod
     def from_dense(cls, moe: nn.Module, group: dist.ProcessGroup | None = None, ops: Any = None) -> "ExpertParallelMoE":
@@ -177,8 +180,13 @@ class ExpertParallelMoE(nn.Module):
         if valid is not None:
             vmask = valid.reshape(-1).to(device=xb.device, dtype=torch.uint8).contiguous()
 
+        ev = self.stage_events
+        mark = (lambda i: ev[i].record()) if ev is not None else (lambda i: None)
+        mark(0)
         idx, w, stats = self.ops.route(xb, wr, bias, vmask, k, self.norm_topk_prob)
+        mark(1)
         send, counts, pos = self.ops.dispatch(xb, idx, w, vmask, G, E_loc)
+        mark(2)
 
         # row and slot counts: [G, 2] per rank, one entry pair per destination
         send_tab = torch.stack([counts[:G], counts[G:]], dim=1).contiguous()
@@ -194,8 +202,12 @@ class ExpertParallelMoE(nn.Module):
         sent = sum(rows_to)
         recv = torch.empty((R, send.shape[1]), dtype=torch.uint8, device=send.device)
         self._all_to_all(recv, send[:sent], rows_from, rows_to)
+        mark(3)
         partial = self.ops.experts(recv, R, slots_here, d, k, self.experts)
+        mark(4)
         back = torch.empty((sent, d), dtype=torch.bfloat16, device=partial.device)
         self._all_to_all(back, partial, rows_to, rows_from)
+        mark(5)
         out = self.ops.combine(back, pos, T, d, G)
+        mark(6)
         return out.to(x.dtype).view_as(x), stats[0], stats[1], stats[3:3 + self.num_experts]
