@@ -232,26 +232,47 @@ def run_ours(args) -> None:
         elapsed_ms = max_over_ranks(start.elapsed_time(end))
         stage_ms = [statistics.mean(evs[j].elapsed_time(evs[j + 1]) for evs in stage_ev) for j in range(n_stages)]
 
-        # end to end through the public API with host buffers
+        # end to end through the public API with host buffers: every step copies its x from
+        # pinned host memory and its output (plus aux / z) back; uploads, layer and downloads
+        # run on three streams, double-buffered, the way a serving loop overlaps them
         x_host = x.cpu().pin_memory()
-        out_host = torch.empty((T, d), dtype=torch.bfloat16).pin_memory()
-        stats_host = torch.empty((3,), dtype=torch.float32).pin_memory()
-        x_dev = torch.empty_like(x)
-        for _ in range(max(1, W)):
-            x_dev.copy_(x_host, non_blocking=True)
-            o, aux, z, _ = moe(x_dev)
-            out_host.copy_(o, non_blocking=True)
+        out_host = [torch.empty((T, d), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+        stats_host = [torch.empty((2,), dtype=torch.float32).pin_memory() for _ in range(2)]
+        x_dev = [torch.empty_like(x) for _ in range(2)]
+        h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        comp = torch.cuda.current_stream(dev)
+
+        def e2e_steps(n, start_event=None):
+            if start_event is not None:
+                h2d.wait_event(start_event)  # no upload starts before the timed region
+            up_done = [torch.cuda.Event() for _ in range(n)]
+            used = [torch.cuda.Event() for _ in range(n)]
+            for i in range(n):
+                b = i % 2
+                with torch.cuda.stream(h2d):
+                    if i >= 2:
+                        h2d.wait_event(used[i - 2])  # the layer of step i-2 has read x_dev[b]
+                    x_dev[b].copy_(x_host, non_blocking=True)
+                    up_done[i].record(h2d)
+                comp.wait_event(up_done[i])
+                o, aux, z, _ = moe(x_dev[b])
+                st = torch.stack([aux.reshape(()), z.reshape(())])
+                used[i].record(comp)
+                d2h.wait_event(used[i])
+                with torch.cuda.stream(d2h):
+                    o.record_stream(d2h)
+                    st.record_stream(d2h)
+                    out_host[b].copy_(o, non_blocking=True)
+                    stats_host[b].copy_(st, non_blocking=True)
+            comp.wait_stream(d2h)
+
+        e2e_steps(max(2, W))
         torch.cuda.synchronize()
         e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         barrier()
         torch.cuda.synchronize()
         e_start.record()
-        for _ in range(K):
-            x_dev.copy_(x_host, non_blocking=True)
-            o, aux, z, _ = moe(x_dev)
-            out_host.copy_(o, non_blocking=True)
-            stats_host[0:1].copy_(aux.reshape(1), non_blocking=True)
-            stats_host[1:2].copy_(z.reshape(1), non_blocking=True)
+        e2e_steps(K, e_start)
         e_end.record()
         torch.cuda.synchronize()
         barrier()

@@ -242,6 +242,20 @@ int mcl4moe_ep_experts(const uint8_t* recv_buf, int R, int slots, int d, int k, 
 int mcl4moe_ep_combine(const uint16_t* back_buf, const int32_t* send_pos, int T, int d, int G, uint16_t* out,
                        mcl4moe_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * Peer-memory transport for the expert-parallel exchange (no counterpart in
+ * the reference).  mcl4moe_ipc_export: CUDA IPC handle (64 bytes) of the
+ * allocation holding ptr, and ptr's offset in it.  mcl4moe_ipc_import (another
+ * process on the same node, any device with peer access): map that allocation,
+ * returning its base; add the offset.  mcl4moe_ipc_close: unmap a base returned
+ * by mcl4moe_ipc_import.  mcl4moe_copy_async: device-to-device copy on `stream`
+ * (to a peer mapping it runs on the copy engines over NVLink).
+ * ------------------------------------------------------------------------ */
+int mcl4moe_ipc_export(const void* ptr, uint8_t* handle_out, uint64_t* offset_out);
+int mcl4moe_ipc_import(const uint8_t* handle, void** base_out);
+int mcl4moe_ipc_close(void* base);
+int mcl4moe_copy_async(void* dst, const void* src, size_t bytes, mcl4moe_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -40,6 +40,10 @@ EXPORTS = (
     "mcl4moe_ep_experts_workspace_size",
     "mcl4moe_ep_experts",
     "mcl4moe_ep_combine",
+    "mcl4moe_ipc_export",
+    "mcl4moe_ipc_import",
+    "mcl4moe_ipc_close",
+    "mcl4moe_copy_async",
 )
 
 
@@ -148,6 +152,14 @@ def load() -> ctypes.CDLL:
                                        c_size_t, c_void_p]
     lib.mcl4moe_ep_combine.restype = c_int
     lib.mcl4moe_ep_combine.argtypes = [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]
+    lib.mcl4moe_ipc_export.restype = c_int
+    lib.mcl4moe_ipc_export.argtypes = [c_void_p, c_void_p, POINTER(ctypes.c_uint64)]
+    lib.mcl4moe_ipc_import.restype = c_int
+    lib.mcl4moe_ipc_import.argtypes = [c_void_p, POINTER(c_void_p)]
+    lib.mcl4moe_ipc_close.restype = c_int
+    lib.mcl4moe_ipc_close.argtypes = [c_void_p]
+    lib.mcl4moe_copy_async.restype = c_int
+    lib.mcl4moe_copy_async.argtypes = [c_void_p, c_void_p, c_size_t, c_void_p]
     _lib = lib
     return lib
 

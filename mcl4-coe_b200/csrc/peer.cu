@@ -1,0 +1,87 @@
+// Peer-memory transport for the expert-parallel exchange: CUDA IPC handles of
+// buffers owned by other ranks (processes) on the same node, and asynchronous
+// device-to-device copies into them.  A copy whose destination is another
+// GPU's memory runs on this GPU's copy engines over NVLink and uses no SMs, so
+// it can overlap the grouped GEMMs; NVLink peer copies measured ~660 GB/s per
+// direction on B200 against ~300 GB/s per GPU for an NCCL all-to-all of the
+// same sizes.  Nothing here allocates device memory: the buffers belong to the
+// caller (PyTorch); importing a handle maps the peer's allocation.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "kernels.cuh"
+
+namespace mcl4 {
+namespace {
+
+PFN_cuMemGetAddressRange_v3020 address_range_fn() {
+  static PFN_cuMemGetAddressRange_v3020 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(p);
+  });
+  return fn;
+}
+
+}  // namespace
+}  // namespace mcl4
+
+using namespace mcl4;
+
+extern "C" {
+
+int mcl4moe_ipc_export(const void* ptr, uint8_t* handle_out, uint64_t* offset_out) {
+  if (!ptr || !handle_out || !offset_out) return MCL4MOE_ERR_INVALID;
+  auto range = address_range_fn();
+  if (!range) return MCL4MOE_ERR_CUDA;
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS) return MCL4MOE_ERR_CUDA;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return MCL4MOE_ERR_CUDA;
+  }
+  static_assert(sizeof(h) == 64, "cudaIpcMemHandle_t is 64 bytes");
+  std::memcpy(handle_out, &h, sizeof(h));
+  *offset_out = uint64_t(reinterpret_cast<uintptr_t>(ptr) - uintptr_t(base));
+  return MCL4MOE_OK;
+}
+
+int mcl4moe_ipc_import(const uint8_t* handle, void** base_out) {
+  if (!handle || !base_out) return MCL4MOE_ERR_INVALID;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return MCL4MOE_ERR_CUDA;
+  }
+  *base_out = p;
+  return MCL4MOE_OK;
+}
+
+int mcl4moe_ipc_close(void* base) {
+  if (!base) return MCL4MOE_ERR_INVALID;
+  if (cudaIpcCloseMemHandle(base) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return MCL4MOE_ERR_CUDA;
+  }
+  return MCL4MOE_OK;
+}
+
+int mcl4moe_copy_async(void* dst, const void* src, size_t bytes, mcl4moe_stream_t stream) {
+  if (bytes == 0) return MCL4MOE_OK;
+  if (!dst || !src) return MCL4MOE_ERR_INVALID;
+  return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, stream) == cudaSuccess ? MCL4MOE_OK
+                                                                                           : MCL4MOE_ERR_CUDA;
+}
+
+}  // extern "C"
