@@ -190,7 +190,7 @@ def run_ours(args) -> None:
     n_stages = 6 if ep else 5
     if ep:
         # expert parallel: the same layer on every rank, each keeps its E / N experts
-        moe = pkg.ExpertParallelMoE.from_dense(moe)
+        moe = pkg.ExpertParallelMoE.from_dense(moe, chunks=args.ep_chunks)
 
     def barrier():
         if world > 1:
@@ -247,13 +247,19 @@ def run_ours(args) -> None:
                 h2d.wait_event(start_event)  # no upload starts before the timed region
             up_done = [torch.cuda.Event() for _ in range(n)]
             used = [torch.cuda.Event() for _ in range(n)]
-            for i in range(n):
-                b = i % 2
+
+            def upload(i):  # issued one step ahead, so the host never waits to start a copy
                 with torch.cuda.stream(h2d):
                     if i >= 2:
-                        h2d.wait_event(used[i - 2])  # the layer of step i-2 has read x_dev[b]
-                    x_dev[b].copy_(x_host, non_blocking=True)
+                        h2d.wait_event(used[i - 2])  # the layer of step i-2 has read x_dev[i % 2]
+                    x_dev[i % 2].copy_(x_host, non_blocking=True)
                     up_done[i].record(h2d)
+
+            upload(0)
+            for i in range(n):
+                if i + 1 < n:
+                    upload(i + 1)
+                b = i % 2
                 comp.wait_event(up_done[i])
                 o, aux, z, _ = moe(x_dev[b])
                 st = torch.stack([aux.reshape(()), z.reshape(())])
@@ -291,6 +297,14 @@ def run_ours(args) -> None:
         roof_flops, roof_ms = 4.0 * T * k * d * F, stage_ms[2]
         roof_kernel = "grouped_gemm_fp4 (gate/up, SwiGLU+requant epilogue)"
     achieved = roof_flops / (roof_ms / 1e3) / 1e12
+    decode = cfg["name"].startswith("c4")
+    if decode and not ep:
+        # decode: weight streaming; algorithmic bytes = NVFP4 bytes of every expert that received a
+        # token (codes + 16-element scales + global scales) + x and out in bf16 + the fp32 router
+        with torch.inference_mode():
+            touched = int((moe.forward_details(x)["offs"].diff(prepend=torch.zeros(1, dtype=torch.int32,
+                                                                                     device=dev)) > 0).sum())
+        dec_bytes = touched * (3 * d * F * (0.5 + 1 / 16) + 8) + 4 * T * d + 4 * E * d
     traffic = None
     tp = ROOT / "profiles" / "traffic.json"
     if tp.exists():
@@ -303,17 +317,24 @@ def run_ours(args) -> None:
         "data": "synthetic (x~N(0,1) bf16, weights~N(0,0.02) fp32 quantised to NVFP4, seeded torch RNG on device)",
         "config": {"workload": cfg["name"], "tokens_per_gpu": T, "d_model": d, "num_experts": E, "top_k": k,
                    "expert_ffn": F, "parallelism": f"ep{world}" if ep else "single",
+                   **({"ep_chunks": args.ep_chunks} if ep else {}),
                    "l2": "no flush: x (%.0f MB) and NVFP4 weights (%.0f MB) exceed the 126 MB L2" % (
                        T * d * 2 / 1e6, E * 3 * d * F * (0.5 + 1 / 16) / 1e6)},
         "stages_ms": dict(zip(("route", "dispatch", "exchange_rows", "experts", "exchange_partials", "combine")
                               if ep else ("route", "permute_quant", "gateup_gemm", "down_gemm", "combine"),
                               [round(s, 4) for s in stage_ms])),
         "layer_fp4_tflops": layer_tflops,
-        "roofline": {"bound": "tensor", "kernel": roof_kernel,
-                     "achieved": achieved, "peak": fp4_peak, "unit": "TFLOP/s", "frac": achieved / fp4_peak,
-                     "traffic": traffic,
-                     "peak_source": f"4 x {peaks['source']} dense bf16 {peaks['bf16']} TFLOP/s "
-                                    "(MEASURED_PEAKS.json; FP4 dense = 4x BF16 dense)"},
+        "roofline": ({"bound": "hbm", "kernel": "whole layer forward (decode: grouped GEMMs stream the touched experts)",
+                      "achieved": dec_bytes / (ms_per_step / 1e3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                      "frac": dec_bytes / (ms_per_step / 1e3) / 1e9 / peaks["hbm_gbs"], "traffic": traffic,
+                      "experts_touched": touched, "algorithmic_bytes": dec_bytes,
+                      "peak_source": f"{peaks['source']} copy bandwidth (MEASURED_PEAKS.json)"}
+                     if decode and not ep else
+                     {"bound": "tensor", "kernel": roof_kernel,
+                      "achieved": achieved, "peak": fp4_peak, "unit": "TFLOP/s", "frac": achieved / fp4_peak,
+                      "traffic": traffic,
+                      "peak_source": f"4 x {peaks['source']} dense bf16 {peaks['bf16']} TFLOP/s "
+                                     "(MEASURED_PEAKS.json; FP4 dense = 4x BF16 dense)"}),
         "e2e": {"value": T * world / (e2e_ms / K / 1e3), "unit": UNIT, "h2d_bytes_per_step": T * d * 2,
                 "d2h_bytes_per_step": T * d * 2 + 8},
         "gpu_launches": (KERNELS_PER_EP_FORWARD if ep else KERNELS_PER_FORWARD) * K,
@@ -382,6 +403,8 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--cpu-sample", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ep-chunks", type=int, default=1,
+                    help="expert parallel (N > 1): token chunks whose exchange overlaps another chunk's experts")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -241,6 +241,18 @@ int mcl4moe_ep_experts(const uint8_t* recv_buf, int R, int slots, int d, int k, 
                        void* workspace, size_t workspace_bytes, mcl4moe_stream_t stream);
 int mcl4moe_ep_combine(const uint16_t* back_buf, const int32_t* send_pos, int T, int d, int G, uint16_t* out,
                        mcl4moe_stream_t stream);
+/* mcl4moe_ep_experts with the partial sums stored straight into their sources'
+ * buffers (one kernel does the sums and the return transfer): received rows of
+ * source s are [seg_start[s], seg_start[s+1]) (host int32 [G+1], seg_start[G]
+ * == R) and row r of source s goes to dst[s] + (r - seg_start[s]) * d bf16
+ * elements; dst[s] (host array of device pointers) may map another GPU's memory
+ * (mcl4moe_ipc_import).  The stores are complete when the stream reaches the
+ * end of the call. */
+int mcl4moe_ep_experts_to_peers(const uint8_t* recv_buf, int R, int slots, int d, int k, int E_loc, int F,
+                                const uint8_t* w_up, const uint8_t* w_up_scales, const float* w_up_g,
+                                const uint8_t* w_dn, const uint8_t* w_dn_scales, const float* w_dn_g, int G,
+                                const int32_t* seg_start, void* const* dst, int32_t* error_word, void* workspace,
+                                size_t workspace_bytes, mcl4moe_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Peer-memory transport for the expert-parallel exchange (no counterpart in

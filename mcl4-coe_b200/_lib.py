@@ -40,6 +40,7 @@ EXPORTS = (
     "mcl4moe_ep_experts_workspace_size",
     "mcl4moe_ep_experts",
     "mcl4moe_ep_combine",
+    "mcl4moe_ep_experts_to_peers",
     "mcl4moe_ipc_export",
     "mcl4moe_ipc_import",
     "mcl4moe_ipc_close",
@@ -150,6 +151,10 @@ def load() -> ctypes.CDLL:
     lib.mcl4moe_ep_experts.argtypes = [c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
                                        c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                        c_size_t, c_void_p]
+    lib.mcl4moe_ep_experts_to_peers.restype = c_int
+    lib.mcl4moe_ep_experts_to_peers.argtypes = [c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p,
+                                                c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p,
+                                                c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]
     lib.mcl4moe_ep_combine.restype = c_int
     lib.mcl4moe_ep_combine.argtypes = [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]
     lib.mcl4moe_ipc_export.restype = c_int

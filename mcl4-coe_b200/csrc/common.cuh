@@ -100,6 +100,52 @@ __device__ __forceinline__ uint32_t bf16x2_max(uint32_t a, uint32_t b) {
   return r;
 }
 
+// ---- packed float32 pairs (sm_100 f32x2: two independent IEEE round-to-nearest ops)
+__device__ __forceinline__ uint64_t f2pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+// amax / 6 correctly rounded to float32 for any non-negative finite bfloat16
+// amax: product with RN(1/6) followed by one Markstein correction step
+// (remainder by fma, then fma with the reciprocal).  Checked exhaustively against
+// the exact quotient over all 32640 such inputs.
+__device__ __forceinline__ float div6_bf16_amax(float a) {
+  const float r = 0.16666667163372039794921875f;  // RN(1/6)
+  const float q0 = __fmul_rn(a, r);
+  const float e = __fmaf_rn(-6.0f, q0, a);
+  return __fmaf_rn(e, r, q0);
+}
+
+// SiLU of two bf16-rounded gate values, g / (1 + 2^(-g log2 e)), with the hardware
+// exp2 and reciprocal approximations (a few float32 ulps); the multiplies and adds
+// run as packed pairs.
+__device__ __forceinline__ void silu_f32x2(float g0, float g1, float& s0, float& s1) {
+  const uint64_t gg = f2pack(g0, g1);
+  float t0, t1, e0, e1, d0, d1, r0, r1;
+  f2unpack(fmul2(gg, f2pack(-1.4426950408889634f, -1.4426950408889634f)), t0, t1);
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(t0));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(t1));
+  f2unpack(fadd2(f2pack(e0, e1), f2pack(1.0f, 1.0f)), d0, d1);
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r0) : "f"(d0));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r1) : "f"(d1));
+  f2unpack(fmul2(gg, f2pack(r0, r1)), s0, s1);
+}
+
 // 8 float32 values -> 8 E2M1 nibbles (element 0 in the low nibble) with the
 // reference's rounding, for products of a bfloat16 value and a global-scale-1
 // inverse block scale.  The hardware conversion rounds to nearest-even on the
@@ -118,51 +164,48 @@ __device__ __forceinline__ uint32_t e2m1x8_act(const float (&n)[8]) {
       "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
       : "=r"(w)
       : "f"(n[0]), "f"(n[1]), "f"(n[2]), "f"(n[3]), "f"(n[4]), "f"(n[5]), "f"(n[6]), "f"(n[7]));
+  // One test for all eight values first (the fix-up is rare): min over the XOR
+  // with the pattern is zero exactly when some value matches.
+  uint32_t hit = 0xFFFFFFFFu;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) hit = min(hit, (__float_as_uint(n[i]) & 0x7F7FFFFFu) ^ 0x40200001u);
+  if (hit != 0u) return w;
   uint32_t fix = 0;
 #pragma unroll
   for (int i = 0; i < 8; ++i) fix |= ((__float_as_uint(n[i]) & 0x7F7FFFFFu) == 0x40200001u ? 1u : 0u) << (4 * i);
   return w - fix;
 }
 
-// Scale of one 16-element activation block (g = 1) and its inverse:
-// s = e4m3(min(amax/6, 448)), inv = min(1/dec, FLT_MAX) (src/mcl4_coe/nvfp4.py:215-221).
-__device__ __forceinline__ uint32_t act_block_scale(float amax, float& inv) {
-  const uint32_t s = f32_to_e4m3(fminf(__fdiv_rn(amax, 6.0f), 448.0f));
-  inv = inverse_decoding(e4m3_to_f32(s));
-  return s;
+// 1 / decoded value of every non-negative E4M3 code (inverse_decoding of
+// e4m3_to_f32), filled by the block's threads; callers sync before use.
+__device__ __forceinline__ void fill_inverse_scale_table(float* t) {
+  for (int i = threadIdx.x; i < 128; i += blockDim.x) t[i] = inverse_decoding(e4m3_to_f32(uint32_t(i)));
 }
 
-// Quantise 16 bf16 values (8 packed words) of one activation block.
-__device__ __forceinline__ uint32_t quantize_block16_bf16(const uint32_t (&w)[8], uint2& packed) {
+// Quantise 16 bf16 values (8 packed words) of one activation block; ``inv_tab``
+// is a table from fill_inverse_scale_table.  Bytes of src/mcl4_coe/nvfp4.py:215-224
+// (s = e4m3(min(amax/6, 448)), inv = min(1/dec, FLT_MAX), codes of x*inv): amax of
+// bf16 values is itself a bf16 value, so div6_bf16_amax is the exact quotient, and
+// the table holds the exact inverses.
+__device__ __forceinline__ uint32_t quantize_block16_bf16(const uint32_t (&w)[8], uint2& packed,
+                                                          const float* inv_tab) {
   uint32_t mx = 0;
 #pragma unroll
   for (int i = 0; i < 8; ++i) mx = bf16x2_max(mx, w[i] & 0x7FFF7FFFu);
-  float inv;
-  const uint32_t s = act_block_scale(fmaxf(bf16x2_lo(mx), bf16x2_hi(mx)), inv);
+  const uint32_t s = f32_to_e4m3(fminf(div6_bf16_amax(fmaxf(bf16x2_lo(mx), bf16x2_hi(mx))), 448.0f));
+  const float inv = inv_tab[s];
+  const uint64_t inv2 = f2pack(inv, inv);
   float n[8];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    n[2 * i] = __fmul_rn(bf16x2_lo(w[i]), inv);
-    n[2 * i + 1] = __fmul_rn(bf16x2_hi(w[i]), inv);
-  }
+  for (int i = 0; i < 4; ++i) f2unpack(fmul2(f2pack(bf16x2_lo(w[i]), bf16x2_hi(w[i])), inv2), n[2 * i], n[2 * i + 1]);
   packed.x = e2m1x8_act(n);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    n[2 * i] = __fmul_rn(bf16x2_lo(w[4 + i]), inv);
-    n[2 * i + 1] = __fmul_rn(bf16x2_hi(w[4 + i]), inv);
-  }
+  for (int i = 0; i < 4; ++i)
+    f2unpack(fmul2(f2pack(bf16x2_lo(w[4 + i]), bf16x2_hi(w[4 + i])), inv2), n[2 * i], n[2 * i + 1]);
   packed.y = e2m1x8_act(n);
   return s;
 }
 
-// SiLU of a bf16-rounded gate value: g / (1 + 2^(-g log2 e)) with the
-// hardware exp2 and reciprocal approximations (a few float32 ulps).
-__device__ __forceinline__ float silu_f32(float g) {
-  float e, r;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(g * -1.4426950408889634f));
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + e));
-  return g * r;
-}
 
 // Byte offset of scale (row r, 16-block c) in the 128x4 scale atoms
 // (src/mcl4_coe/nvfp4.py:131-144; the layout tcgen05 block-scaled MMA reads).

@@ -121,6 +121,8 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const uint16_t* __restrict
                                                       int32_t* __restrict__ send_pos) {
   __shared__ int32_t s_pos[32][kMaxRanks];
   __shared__ int32_t s_start[kMaxRanks];
+  __shared__ float inv_tab[128];
+  fill_inverse_scale_table(inv_tab);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int w = blockIdx.x;
   const EpRow L = ep_row(d, k);
@@ -173,7 +175,7 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const uint16_t* __restrict
         const uint4* src = reinterpret_cast<const uint4*>(x + int64_t(t) * d + b * 16);
         const uint4 u0 = __ldg(src), u1 = __ldg(src + 1);
         const uint32_t wds[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-        s = quantize_block16_bf16(wds, pk);
+        s = quantize_block16_bf16(wds, pk, inv_tab);
       }
       const int base_lane = lane & ~3;
       uint32_t word = 0;
@@ -343,6 +345,50 @@ __global__ void __launch_bounds__(256) ep_partial_kernel(const uint16_t* __restr
   }
 }
 
+// Where the partial of received row r goes: rows of source s are
+// [start[s], start[s+1]); row r of source s lands at addr[s] + (r - start[s]) * d
+// bf16 elements.  addr[s] may map another GPU's memory (peer / IPC mapping).
+struct EpDest {
+  int G;
+  int32_t start[kMaxRanks + 1];
+  uint16_t* addr[kMaxRanks];
+};
+
+// ep_partial_kernel with the partial sums stored straight into their sources'
+// receive buffers: over NVLink for other GPUs, so the return transfer overlaps
+// this kernel's reads of y.
+__global__ void __launch_bounds__(256) ep_partial_remote_kernel(const uint16_t* __restrict__ y,
+                                                                const int32_t* __restrict__ slot_pos, int R, int k,
+                                                                int d, EpDest dst) {
+  const int lane = threadIdx.x & 31;
+  const int r = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (r >= R) return;
+  int s = 0;
+  while (s + 1 < dst.G && r >= dst.start[s + 1]) ++s;
+  uint16_t* out_row = dst.addr[s] + int64_t(r - dst.start[s]) * d;
+  const int my_pos = lane < k ? slot_pos[int64_t(r) * k + lane] : -1;
+  for (int c = lane * 8; c < d; c += 256) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < k; ++j) {
+      const int p = __shfl_sync(0xffffffffu, my_pos, j);
+      if (p < 0) continue;
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(y + int64_t(p) * d + c));
+      const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        acc[2 * i] = __fadd_rn(acc[2 * i], bf16_to_f32(uint16_t(w4[i] & 0xFFFFu)));
+        acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], bf16_to_f32(uint16_t(w4[i] >> 16)));
+      }
+    }
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      o[i] = uint32_t(f32_to_bf16(acc[2 * i])) | (uint32_t(f32_to_bf16(acc[2 * i + 1])) << 16);
+    *reinterpret_cast<uint4*>(out_row + c) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  __threadfence_system();  // the stores reach the peers before anyone is told the kernel is done
+}
+
 // out[t] = bf16(sum over destinations g = 0..G-1 of the partial returned for (t, g)).
 __global__ void __launch_bounds__(256) ep_final_kernel(const uint16_t* __restrict__ back,
                                                        const int32_t* __restrict__ send_pos, int T, int d, int G,
@@ -479,13 +525,17 @@ size_t mcl4moe_ep_experts_workspace_size(int R, int slots, int d, int k, int E_l
   return experts_ws(nullptr, R, slots, d, k, E_loc, F).bytes;
 }
 
-int mcl4moe_ep_experts(const uint8_t* recv_buf, int R, int slots, int d, int k, int E_loc, int F,
-                       const uint8_t* w_up, const uint8_t* w_up_scales, const float* w_up_g, const uint8_t* w_dn,
-                       const uint8_t* w_dn_scales, const float* w_dn_g, uint16_t* partial, int32_t* error_word,
-                       void* workspace, size_t workspace_bytes, mcl4moe_stream_t stream) {
+}  // extern "C"
+
+namespace {
+
+int ep_experts_impl(const uint8_t* recv_buf, int R, int slots, int d, int k, int E_loc, int F, const uint8_t* w_up,
+                    const uint8_t* w_up_scales, const float* w_up_g, const uint8_t* w_dn, const uint8_t* w_dn_scales,
+                    const float* w_dn_g, uint16_t* partial, const EpDest* remote, int32_t* error_word,
+                    void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   int st = check_ep_shape(d, k, 1, E_loc, F);
   if (st != MCL4MOE_OK) return st;
-  if (R < 0 || slots < 0 || !workspace || (R > 0 && (!recv_buf || !partial))) return MCL4MOE_ERR_INVALID;
+  if (R < 0 || slots < 0 || !workspace || (R > 0 && (!recv_buf || (!partial && !remote)))) return MCL4MOE_ERR_INVALID;
   if (!w_up || !w_up_scales || !w_up_g || !w_dn || !w_dn_scales || !w_dn_g) return MCL4MOE_ERR_INVALID;
   if (!aligned16(recv_buf) || !aligned16(partial) || !aligned16(w_up) || !aligned16(w_dn) ||
       !aligned16(w_up_scales) || !aligned16(w_dn_scales))
@@ -534,8 +584,42 @@ int mcl4moe_ep_experts(const uint8_t* recv_buf, int R, int slots, int d, int k, 
   g2.ldy = d;
   g2.err = err;
   if ((st = launch_grouped_gemm(w.hq, w.mcap, w_dn, g2, s)) != MCL4MOE_OK) return st;
-  ep_partial_kernel<<<(R + 7) / 8, 256, 0, s>>>(w.y, w.slot_pos, R, k, d, partial);
+  if (remote)
+    ep_partial_remote_kernel<<<(R + 7) / 8, 256, 0, s>>>(w.y, w.slot_pos, R, k, d, *remote);
+  else
+    ep_partial_kernel<<<(R + 7) / 8, 256, 0, s>>>(w.y, w.slot_pos, R, k, d, partial);
   return cudaGetLastError() == cudaSuccess ? MCL4MOE_OK : MCL4MOE_ERR_CUDA;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mcl4moe_ep_experts(const uint8_t* recv_buf, int R, int slots, int d, int k, int E_loc, int F,
+                       const uint8_t* w_up, const uint8_t* w_up_scales, const float* w_up_g, const uint8_t* w_dn,
+                       const uint8_t* w_dn_scales, const float* w_dn_g, uint16_t* partial, int32_t* error_word,
+                       void* workspace, size_t workspace_bytes, mcl4moe_stream_t stream) {
+  return ep_experts_impl(recv_buf, R, slots, d, k, E_loc, F, w_up, w_up_scales, w_up_g, w_dn, w_dn_scales, w_dn_g,
+                         partial, nullptr, error_word, workspace, workspace_bytes, stream);
+}
+
+int mcl4moe_ep_experts_to_peers(const uint8_t* recv_buf, int R, int slots, int d, int k, int E_loc, int F,
+                                const uint8_t* w_up, const uint8_t* w_up_scales, const float* w_up_g,
+                                const uint8_t* w_dn, const uint8_t* w_dn_scales, const float* w_dn_g, int G,
+                                const int32_t* seg_start, void* const* dst, int32_t* error_word, void* workspace,
+                                size_t workspace_bytes, mcl4moe_stream_t stream) {
+  if (G <= 0 || G > kMaxRanks || !seg_start || !dst) return MCL4MOE_ERR_INVALID;
+  EpDest e{};
+  e.G = G;
+  for (int s = 0; s <= G; ++s) e.start[s] = seg_start[s];
+  if (e.start[0] != 0 || e.start[G] != R) return MCL4MOE_ERR_INVALID;
+  for (int s = 0; s < G; ++s) {
+    if (e.start[s + 1] < e.start[s]) return MCL4MOE_ERR_INVALID;
+    if (e.start[s + 1] > e.start[s] && (!dst[s] || !aligned16(dst[s]))) return MCL4MOE_ERR_INVALID;
+    e.addr[s] = static_cast<uint16_t*>(dst[s]);
+  }
+  return ep_experts_impl(recv_buf, R, slots, d, k, E_loc, F, w_up, w_up_scales, w_up_g, w_dn, w_dn_scales, w_dn_g,
+                         nullptr, &e, error_word, workspace, workspace_bytes, stream);
 }
 
 int mcl4moe_ep_combine(const uint16_t* back_buf, const int32_t* send_pos, int T, int d, int G, uint16_t* out,

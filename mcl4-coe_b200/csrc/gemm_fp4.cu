@@ -84,7 +84,7 @@ struct Cfg {
   static constexpr int kStages = MODE == 0 ? 5 : 4;
   static constexpr uint32_t kStoreBytes = MODE == 1 ? kEpiWarps * kWarpStoreBytes : 0;
   static constexpr size_t kSmem = 1024 /*align*/ + size_t(kStages) * kStageBytes + kStoreBytes + kBarBytes +
-                                  sizeof(int32_t) * (kMaxExperts + 1);
+                                  sizeof(int32_t) * (kMaxExperts + 1) + sizeof(float) * 128;
 };
 
 static_assert(kStageBytes % 1024 == 0, "stage must keep 1024-byte alignment for 128B swizzle");
@@ -129,6 +129,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const uint32_t tempty_bar = bar_base + 8u * (3 * S + 1);  // even CTA: both epilogues read it
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + (bar_base - base) + 8 * (3 * S + 2));
   int32_t* pad_s = reinterpret_cast<int32_t*>(smem + (bar_base - base) + kBarBytes);
+  float* s_inv = reinterpret_cast<float*>(pad_s + kMaxExperts + 1);  // 1/decoded scale per E4M3 code
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int E = args.E;
@@ -137,6 +138,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int pair = int(cluster_id_x()), npairs = int(cluster_count_x());
 
   for (int i = tid; i <= E; i += kThreads) pad_s[i] = args.pad_start[i];
+  if (MODE == 0 && tid < 128) s_inv[tid] = inverse_decoding(e4m3_to_f32(uint32_t(tid)));
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(full_bar(s), 1 + 2 * kSfWarps);
@@ -365,24 +367,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         for (int blk = 0; blk < 2; ++blk) {
           uint32_t hh[8];
           uint32_t mx = 0;
+          const uint64_t gb2 = f2pack(gb, gb);
 #pragma unroll
           for (int pr = 0; pr < 8; ++pr) {
             const int j = blk * 16 + 2 * pr;
-            const uint32_t gg = pack_bf16x2(__uint_as_float(va[j]) * gb, __uint_as_float(va[j + 1]) * gb);
-            const uint32_t uu = pack_bf16x2(__uint_as_float(vb[j]) * gb, __uint_as_float(vb[j + 1]) * gb);
-            const uint32_t ss = pack_bf16x2(silu_f32(bf16x2_lo(gg)), silu_f32(bf16x2_hi(gg)));
-            hh[pr] = bf16x2_mul(ss, uu);
+            float a0, a1, b0, b1, s0, s1;
+            f2unpack(fmul2(f2pack(__uint_as_float(va[j]), __uint_as_float(va[j + 1])), gb2), a0, a1);
+            f2unpack(fmul2(f2pack(__uint_as_float(vb[j]), __uint_as_float(vb[j + 1])), gb2), b0, b1);
+            const uint32_t gg = pack_bf16x2(a0, a1);
+            const uint32_t uu = pack_bf16x2(b0, b1);
+            silu_f32x2(bf16x2_lo(gg), bf16x2_hi(gg), s0, s1);
+            hh[pr] = bf16x2_mul(pack_bf16x2(s0, s1), uu);
             mx = bf16x2_max(mx, hh[pr] & 0x7FFF7FFFu);
           }
-          float inv;
-          sword |= act_block_scale(fmaxf(bf16x2_lo(mx), bf16x2_hi(mx)), inv) << (8 * blk);
+          // scale = e4m3(min(amax/6, 448)), inv = 1/decoded scale (src/mcl4_coe/nvfp4.py:215-221)
+          const uint32_t sc = f32_to_e4m3(fminf(div6_bf16_amax(fmaxf(bf16x2_lo(mx), bf16x2_hi(mx))), 448.0f));
+          const float inv = s_inv[sc];
+          sword |= sc << (8 * blk);
+          const uint64_t inv2 = f2pack(inv, inv);
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
             float n[8];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-              n[2 * i] = __fmul_rn(bf16x2_lo(hh[half * 4 + i]), inv);
-              n[2 * i + 1] = __fmul_rn(bf16x2_hi(hh[half * 4 + i]), inv);
+              const uint32_t w = hh[half * 4 + i];
+              f2unpack(fmul2(f2pack(bf16x2_lo(w), bf16x2_hi(w)), inv2), n[2 * i], n[2 * i + 1]);
             }
             packed[blk * 2 + half] = e2m1x8_act(n);
           }

@@ -156,6 +156,9 @@ int launch_quantize_weights(const float* const* w_ptrs, const int32_t* slots, in
 __global__ void __launch_bounds__(256) act_quant_kernel(const uint16_t* __restrict__ x, int64_t rows, int cols,
                                                         int64_t ld_x, uint8_t* __restrict__ packed,
                                                         uint8_t* __restrict__ scales, int swizzled) {
+  __shared__ float inv_tab[128];
+  fill_inverse_scale_table(inv_tab);
+  __syncthreads();
   const int lane = threadIdx.x & 31;
   const int64_t row = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -168,7 +171,7 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const uint16_t* __restri
       uint4 u0 = __ldg(src), u1 = __ldg(src + 1);
       const uint32_t wds[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
       uint2 pk;
-      s = quantize_block16_bf16(wds, pk);
+      s = quantize_block16_bf16(wds, pk, inv_tab);
       *reinterpret_cast<uint2*>(packed + row * (cols / 2) + b * 8) = pk;
     }
     if (!swizzled) {

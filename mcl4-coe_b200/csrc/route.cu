@@ -23,6 +23,9 @@ __global__ void __launch_bounds__(256) permute_quant_kernel(
     const uint16_t* __restrict__ x, const uint8_t* __restrict__ valid, const int32_t* __restrict__ topk_idx,
     const float* __restrict__ topk_w, int T, int d, int E, int k, RouteWorkspace ws, int32_t* __restrict__ slot_pos,
     float* __restrict__ sorted_w, int32_t* __restrict__ perm, uint8_t* __restrict__ xq, uint8_t* __restrict__ xs) {
+  __shared__ float inv_tab[128];
+  fill_inverse_scale_table(inv_tab);
+  __syncthreads();
   const int lane = threadIdx.x & 31;
   const int nblk = d / 16;
   const int token_blocks = (T + 7) / 8;
@@ -62,7 +65,7 @@ __global__ void __launch_bounds__(256) permute_quant_kernel(
       const uint4* src = reinterpret_cast<const uint4*>(x + int64_t(t) * d + b * 16);
       uint4 u0 = __ldg(src), u1 = __ldg(src + 1);
       const uint32_t wds[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-      s = quantize_block16_bf16(wds, pk);
+      s = quantize_block16_bf16(wds, pk, inv_tab);
     }
     const int base_lane = lane & ~3;
     uint32_t word = 0;
@@ -117,6 +120,9 @@ __global__ void __launch_bounds__(256) quant_grouped_rows_kernel(const uint16_t*
                                                                  const int32_t* __restrict__ pad_start,
                                                                  const int32_t* __restrict__ counts, int E,
                                                                  uint8_t* __restrict__ xq, uint8_t* __restrict__ xs) {
+  __shared__ float inv_tab[128];
+  fill_inverse_scale_table(inv_tab);
+  __syncthreads();
   const int lane = threadIdx.x & 31;
   const int nblk = K / 16;
   const int64_t row_blocks = (M + 7) / 8;
@@ -150,7 +156,7 @@ __global__ void __launch_bounds__(256) quant_grouped_rows_kernel(const uint16_t*
       const uint4* src = reinterpret_cast<const uint4*>(x + m * K + b * 16);
       uint4 u0 = __ldg(src), u1 = __ldg(src + 1);
       const uint32_t wds[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-      s = quantize_block16_bf16(wds, pk);
+      s = quantize_block16_bf16(wds, pk, inv_tab);
       *reinterpret_cast<uint2*>(xq + p * (K / 2) + b * 8) = pk;
     }
     const int base_lane = lane & ~3;

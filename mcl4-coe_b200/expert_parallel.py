@@ -74,13 +74,13 @@ class CudaEPOps:
                                      ws.data_ptr(), ws.numel(), _stream_handle()), "mcl4moe_route")
         return idx, w, stats
 
-    def dispatch(self, x: Tensor, idx: Tensor, w: Tensor, valid: Tensor | None, G: int, E_loc: int):
+    def dispatch(self, x: Tensor, idx: Tensor, w: Tensor, valid: Tensor | None, G: int, E_loc: int, slot: int = 0):
         lib = _lib.load()
         T, d = x.shape
         k = idx.shape[1]
         dev = x.device
         rb = self.row_bytes(d, k)
-        send_buf = self._scratch("send", T * G * rb, dev)
+        send_buf = self._scratch(f"send{slot}", T * G * rb, dev)
         counts = torch.empty((2 * G,), dtype=torch.int32, device=dev)
         pos = torch.empty((T, G), dtype=torch.int32, device=dev)
         ws = self._scratch("dispatch", lib.mcl4moe_ep_dispatch_workspace_size(T, G), dev)
@@ -112,8 +112,30 @@ class CudaEPOps:
                                           ws.data_ptr(), ws.numel(), _stream_handle()), "mcl4moe_ep_experts")
         return partial
 
-    def combine(self, back: Tensor, pos: Tensor, T: int, d: int, G: int) -> Tensor:
-        out = torch.empty((T, d), dtype=torch.bfloat16, device=pos.device)
+    def experts_to_peers(self, recv: Tensor, R: int, slots: int, d: int, k: int, experts: nn.ModuleList,
+                         seg_start: list[int], dst: list[int]) -> None:
+        """The experts step with each partial-sum row stored straight to ``dst[s]``
+        (a peer mapping for rows from another rank)."""
+        lib = _lib.load()
+        dev = recv.device
+        E_loc = len(experts)
+        F = experts[0].down_proj.weight.shape[1]
+        up, dn = getattr(self, "_caches", None) or (get_or_build_grouped_cache(experts, "up_proj"),
+                                                    get_or_build_grouped_cache(experts, "down_proj"))
+        self._caches = None
+        G = len(dst)
+        starts = (ctypes.c_int32 * (G + 1))(*seg_start)
+        ptrs = (ctypes.c_void_p * G)(*dst)
+        ws = self._scratch("experts", lib.mcl4moe_ep_experts_workspace_size(R, slots, d, k, E_loc, F), dev)
+        _lib.check(lib.mcl4moe_ep_experts_to_peers(recv.data_ptr(), R, slots, d, k, E_loc, F, up.packed.data_ptr(),
+                                                   up.scales.data_ptr(), up.g.data_ptr(), dn.packed.data_ptr(),
+                                                   dn.scales.data_ptr(), dn.g.data_ptr(), G, starts, ptrs, None,
+                                                   ws.data_ptr(), ws.numel(), _stream_handle()),
+                   "mcl4moe_ep_experts_to_peers")
+
+    def combine(self, back: Tensor, pos: Tensor, T: int, d: int, G: int, out: Tensor | None = None) -> Tensor:
+        if out is None:
+            out = torch.empty((T, d), dtype=torch.bfloat16, device=pos.device)
         _lib.check(_lib.load().mcl4moe_ep_combine(back.data_ptr() if back.numel() else None, pos.data_ptr(), T, d,
                                                   G, out.data_ptr(), _stream_handle()), "mcl4moe_ep_combine")
         return out
@@ -188,20 +210,25 @@ class PeerExchange:
         dist.barrier(group=self.group)
         self.arena, self.regions, self.peer_base = None, {}, []
 
+    def address(self, rank: int, name: str, byte_offset: int = 0) -> int:
+        """Device address (in this process) of region ``name`` of ``rank`` plus an offset."""
+        return self.peer_base[rank] + self.regions[name][0] + byte_offset
+
     def local(self, name: str, nbytes: int) -> Tensor:
         off, size = self.regions[name]
         assert nbytes <= size
         return self.arena[off:off + nbytes]
 
-    def put(self, name: str, pieces: list[tuple[int, Tensor, int]]) -> None:
-        """Copy each ``(dest, src, byte_offset)`` into region ``name`` of ``dest``,
-        then wait (on the device) until every rank's copies have landed."""
+    def issue(self, name: str, pieces: list[tuple[int, Tensor, int]]) -> list:
+        """Start copying each ``(dest, src, byte_offset)`` into region ``name`` of
+        ``dest`` once the current stream has produced ``src``; returns the events
+        that mark the end of these copies (for ``complete``)."""
         lib = _lib.load()
         cur = torch.cuda.current_stream(self.device)
         ready = torch.cuda.Event()
         ready.record(cur)
         off0, size = self.regions[name]
-        used = set()
+        used: dict[int, torch.cuda.Stream] = {}
         for dest, src, byte_off in pieces:
             n = src.numel() * src.element_size()
             if n == 0:
@@ -210,15 +237,29 @@ class PeerExchange:
             st = self.streams[dest]
             if dest not in used:
                 st.wait_event(ready)
-                used.add(dest)
+                used[dest] = st
             _lib.check(lib.mcl4moe_copy_async(ctypes.c_void_p(self.peer_base[dest] + off0 + byte_off),
                                               ctypes.c_void_p(src.data_ptr()), n, st.cuda_stream),
                        "mcl4moe_copy_async")
             src.record_stream(st)
-        for dest in used:
-            cur.wait_stream(self.streams[dest])
+        done = []
+        for st in used.values():
+            ev = torch.cuda.Event()
+            ev.record(st)
+            done.append(ev)
+        return done
+
+    def complete(self, events: list) -> None:
+        """Order the current stream after this rank's copies (``events``) and, with
+        a one-element all-reduce, after every other rank's copies issued before
+        its matching call."""
+        cur = torch.cuda.current_stream(self.device)
+        for ev in events:
+            cur.wait_event(ev)
         dist.all_reduce(self.token, group=self.group)
 
+    def put(self, name: str, pieces: list[tuple[int, Tensor, int]]) -> None:
+        self.complete(self.issue(name, pieces))
 
 class ExpertParallelMoE(nn.Module):
     """SparseMoE whose experts are sharded over ``group`` (one process per GPU).
@@ -231,7 +272,7 @@ class ExpertParallelMoE(nn.Module):
     """
 
     def __init__(self, config: Any, group: dist.ProcessGroup | None = None, ops: Any = None,
-                 transport: str = "auto") -> None:
+                 transport: str = "auto", chunks: int = 1) -> None:
         super().__init__()
         self.group = group
         self.world = dist.get_world_size(group)
@@ -258,20 +299,24 @@ class ExpertParallelMoE(nn.Module):
         # "collective": all-to-all through torch.distributed (any backend, e.g. gloo)
         self.transport = transport
         self._peer: PeerExchange | None = None
+        # the batch is cut into this many token chunks; with the peer transport the
+        # exchange of one chunk overlaps the experts step of another
+        self.chunks = max(1, int(chunks))
+        self.min_chunk_tokens = 1024
         # optional 7 CUDA events recorded around the six steps (route, dispatch,
         # row exchange, experts, partial exchange, combine), for stage timing
         self.stage_events: list | None = None
 
     @classmethod
     def from_dense(cls, moe: nn.Module, group: dist.ProcessGroup | None = None, ops: Any = None,
-                   transport: str = "auto") -> "ExpertParallelMoE":
+                   transport: str = "auto", chunks: int = 1) -> "ExpertParallelMoE":
         """Shard a single-device layer (this package's or the reference's SparseMoE):
         the router is shared, this rank keeps its block of experts."""
         E = len(moe.experts)
         cfg = type("Cfg", (), dict(d_model=moe.router.in_features, num_experts=E,
                                    expert_hidden_dim=moe.experts[0].down_proj.in_features, top_k=moe.top_k,
                                    norm_topk_prob=moe.norm_topk_prob))()
-        mod = cls(cfg, group, ops, transport)
+        mod = cls(cfg, group, ops, transport, chunks)
         mod.router = moe.router
         lo = mod.expert_offset
         mod.experts = nn.ModuleList(list(moe.experts)[lo:lo + mod.experts_per_rank])
@@ -302,83 +347,124 @@ class ExpertParallelMoE(nn.Module):
             self.ops.prepare(self.experts)
         idx, w, stats = self.ops.route(xb, wr, bias, vmask, k, self.norm_topk_prob)
         mark(1)
-        send, counts, pos = self.ops.dispatch(xb, idx, w, vmask, G, E_loc)
+        n = max(1, min(self.chunks, T // self.min_chunk_tokens)) if T > 0 else 1
+        bounds = [(T * c // n, T * (c + 1) // n) for c in range(n)]
+        disp = []
+        for c, (lo, hi) in enumerate(bounds):
+            vm = None if vmask is None else vmask[lo:hi]
+            disp.append(self.ops.dispatch(xb[lo:hi], idx[lo:hi], w[lo:hi], vm, G, E_loc, c))
         mark(2)
-
+        out = torch.empty((T, d), dtype=torch.bfloat16, device=xb.device)
         use_peer = self.transport == "peer" or (
             self.transport == "auto" and xb.is_cuda and dist.get_backend(self.group) == "nccl")
         if use_peer:
-            back = self._exchange_peer(send, counts, T, d, k, mark)
+            backs = self._exchange_peer(disp, bounds, d, k, mark)
         else:
-            back = self._exchange_collective(send, counts, d, k, mark)
+            backs = self._exchange_collective(disp, d, k, mark)
         mark(5)
-        out = self.ops.combine(back, pos, T, d, G)
+        for c, (lo, hi) in enumerate(bounds):
+            self.ops.combine(backs[c], disp[c][2], hi - lo, d, G, out[lo:hi])
         mark(6)
         return out.to(x.dtype).view_as(x), stats[0], stats[1], stats[3:3 + self.num_experts]
 
-    def _exchange_collective(self, send: Tensor, counts: Tensor, d: int, k: int, mark) -> Tensor:
-        """Rows out and partial sums back through ``all_to_all_single``."""
+    def _exchange_collective(self, disp: list, d: int, k: int, mark) -> list[Tensor]:
+        """Rows out and partial sums back through ``all_to_all_single``, chunk after chunk."""
         G = self.world
-        # row and slot counts: [G, 2] per rank, one entry pair per destination
-        send_tab = torch.stack([counts[:G], counts[G:]], dim=1).contiguous()
-        recv_tab = torch.empty_like(send_tab)
-        self._all_to_all(recv_tab, send_tab, [1] * G, [1] * G)
-        tab = torch.cat([send_tab, recv_tab], dim=0).cpu()  # the split sizes are needed on the host
-        rows_to = tab[:G, 0].tolist()
-        rows_from = tab[G:, 0].tolist()
-        slots_here = int(tab[G:, 1].sum())
-        R = int(sum(rows_from))
-        self.last_exchange = dict(rows_to=rows_to, rows_from=rows_from, slots=[slots_here])
-        sent = sum(rows_to)
-        recv = torch.empty((R, send.shape[1]), dtype=torch.uint8, device=send.device)
-        self._all_to_all(recv, send[:sent], rows_from, rows_to)
+        backs, ex = [], dict(rows_to=[0] * G, rows_from=[0] * G, slots=[0])
+        for send, counts, _ in disp:
+            # row and slot counts: [G, 2] per rank, one entry pair per destination
+            send_tab = torch.stack([counts[:G], counts[G:]], dim=1).contiguous()
+            recv_tab = torch.empty_like(send_tab)
+            self._all_to_all(recv_tab, send_tab, [1] * G, [1] * G)
+            tab = torch.cat([send_tab, recv_tab], dim=0).cpu()  # the split sizes are needed on the host
+            rows_to = tab[:G, 0].tolist()
+            rows_from = tab[G:, 0].tolist()
+            slots_here = int(tab[G:, 1].sum())
+            R = int(sum(rows_from))
+            sent = sum(rows_to)
+            recv = torch.empty((R, send.shape[1]), dtype=torch.uint8, device=send.device)
+            self._all_to_all(recv, send[:sent], rows_from, rows_to)
+            partial = self.ops.experts(recv, R, slots_here, d, k, self.experts)
+            back = torch.empty((sent, d), dtype=torch.bfloat16, device=partial.device)
+            self._all_to_all(back, partial, rows_to, rows_from)
+            backs.append(back)
+            ex = dict(rows_to=[a + b for a, b in zip(ex["rows_to"], rows_to)],
+                      rows_from=[a + b for a, b in zip(ex["rows_from"], rows_from)], slots=[ex["slots"][0] + slots_here])
+        self.last_exchange = ex
         mark(3)
-        partial = self.ops.experts(recv, R, slots_here, d, k, self.experts)
         mark(4)
-        back = torch.empty((sent, d), dtype=torch.bfloat16, device=partial.device)
-        self._all_to_all(back, partial, rows_to, rows_from)
-        return back
+        return backs
 
-    def _exchange_peer(self, send: Tensor, counts: Tensor, T: int, d: int, k: int, mark) -> Tensor:
-        """Rows out and partial sums back through peer memory (copy engines)."""
-        G, me = self.world, self.rank
+    def _exchange_peer(self, disp: list, bounds: list, d: int, k: int, mark) -> list[Tensor]:
+        """Rows out and partial sums back through peer memory (copy engines), the
+        exchange of one chunk overlapping the experts step of another."""
+        G, me, n = self.world, self.rank, len(disp)
+        dev = disp[0][1].device
         if self._peer is None:
-            self._peer = PeerExchange(self.group, send.device)
+            self._peer = PeerExchange(self.group, dev)
         px = self._peer
-        # every rank's per-destination row and slot counts and its token count
-        mine = torch.cat([counts, torch.tensor([T], dtype=torch.int32, device=counts.device)])
-        allc = torch.empty((G, 2 * G + 1), dtype=torch.int32, device=counts.device)
+        # every rank's per-chunk, per-destination row and slot counts and chunk sizes: one gather
+        mine = torch.cat([torch.cat([cnt, torch.tensor([hi - lo], dtype=torch.int32, device=dev)])
+                          for (_, cnt, _), (lo, hi) in zip(disp, bounds)])
+        allc = torch.empty((G, n * (2 * G + 1)), dtype=torch.int32, device=dev)
         dist.all_gather_into_tensor(allc, mine, group=self.group)
-        tab = allc.cpu().tolist()
-        rows = [r[:G] for r in tab]          # rows[s][g]: rows from s to g
-        slots = [r[G:2 * G] for r in tab]
-        t_max = max(r[2 * G] for r in tab)
-        rb = send.shape[1]
-        px.reserve({"rows": G * t_max * rb, "back": G * t_max * d * 2})
-        rows_to, rows_from = rows[me], [rows[s][me] for s in range(G)]
-        R = sum(rows_from)
-        slots_here = sum(slots[s][me] for s in range(G))
-        self.last_exchange = dict(rows_to=rows_to, rows_from=rows_from, slots=[slots_here])
-        # my rows for g go after the rows of lower ranks in g's receive region
-        pieces, start = [], 0
-        for g in range(G):
-            n = rows[me][g]
-            at = sum(rows[s][g] for s in range(me))
-            pieces.append((g, send[start:start + n].reshape(-1), at * rb))
-            start += n
-        px.put("rows", pieces)
-        recv = px.local("rows", R * rb).view(R, rb)
-        mark(3)
-        partial = self.ops.experts(recv, R, slots_here, d, k, self.experts)
-        mark(4)
-        # partials of the rows from s go where s keeps its segment for me
-        pieces, at_here = [], 0
-        for s in range(G):
-            n = rows[s][me]
-            at = sum(rows[s][g] for g in range(me))
-            pieces.append((s, partial[at_here:at_here + n].reshape(-1), at * d * 2))
-            at_here += n
-        px.put("back", pieces)
-        sent = sum(rows_to)
-        return px.local("back", sent * d * 2).view(torch.bfloat16).view(sent, d)
+        tab = allc.cpu().view(G, n, 2 * G + 1).tolist()
+        rb = disp[0][0].shape[1]
+        sizes = {}
+        for c in range(n):
+            t_max = max(tab[s][c][2 * G] for s in range(G))
+            sizes[f"rows{c}"] = G * t_max * rb
+            sizes[f"back{c}"] = G * t_max * d * 2
+        px.reserve(sizes)
+        ex = dict(rows_to=[0] * G, rows_from=[0] * G, slots=[0])
+        for c in range(n):
+            ex["rows_to"] = [a + tab[me][c][g] for a, g in zip(ex["rows_to"], range(G))]
+            ex["rows_from"] = [a + tab[s][c][me] for a, s in zip(ex["rows_from"], range(G))]
+            ex["slots"][0] += sum(tab[s][c][G + me] for s in range(G))
+        self.last_exchange = ex
 
+        def rows_pieces(c):  # my rows for g go after the rows of lower ranks in g's region
+            send, pieces, start = disp[c][0], [], 0
+            for g in range(G):
+                cnt = tab[me][c][g]
+                at = sum(tab[s][c][g] for s in range(me))
+                pieces.append((g, send[start:start + cnt].reshape(-1), at * rb))
+                start += cnt
+            return pieces
+
+        def back_pieces(c, partial):  # partials of the rows from s go where s keeps its segment for me
+            pieces, at_here = [], 0
+            for s in range(G):
+                cnt = tab[s][c][me]
+                at = sum(tab[s][c][g] for g in range(me))
+                pieces.append((s, partial[at_here:at_here + cnt].reshape(-1), at * d * 2))
+                at_here += cnt
+            return pieces
+
+        px.complete(px.issue("rows0", rows_pieces(0)))
+        mark(3)
+        back_events = []
+        for c in range(n):
+            nxt = px.issue(f"rows{c + 1}", rows_pieces(c + 1)) if c + 1 < n else None
+            R = sum(tab[s][c][me] for s in range(G))
+            slots_here = sum(tab[s][c][G + me] for s in range(G))
+            recv = px.local(f"rows{c}", R * rb).view(R, rb)
+            if hasattr(self.ops, "experts_to_peers"):
+                # partial sums stored over NVLink by the kernel that computes them
+                seg = [0]
+                for s in range(G):
+                    seg.append(seg[-1] + tab[s][c][me])
+                dst = [px.address(s, f"back{c}", sum(tab[s][c][g] for g in range(me)) * d * 2) for s in range(G)]
+                self.ops.experts_to_peers(recv, R, slots_here, d, k, self.experts, seg, dst)
+            else:
+                partial = self.ops.experts(recv, R, slots_here, d, k, self.experts)
+                back_events += px.issue(f"back{c}", back_pieces(c, partial))
+            if nxt is not None:
+                px.complete(nxt)
+        mark(4)
+        px.complete(back_events)
+        backs = []
+        for c in range(n):
+            sent = sum(tab[me][c][g] for g in range(G))
+            backs.append(px.local(f"back{c}", sent * d * 2).view(torch.bfloat16).view(sent, d))
+        return backs

@@ -40,7 +40,7 @@ class OracleEPOps:
         stats = np.concatenate([[r.aux_loss, r.z_loss, np.float32(r.active.size)], r.counts]).astype(np.float32)
         return torch.from_numpy(idx), torch.from_numpy(w), torch.from_numpy(stats)
 
-    def dispatch(self, x, idx, w, valid, G, E_loc):
+    def dispatch(self, x, idx, w, valid, G, E_loc, slot=0):
         xs = x.float().numpy()
         T, d = xs.shape
         k = idx.shape[1]
@@ -105,14 +105,18 @@ class OracleEPOps:
         assert n_slots == slots, (n_slots, slots)
         return torch.from_numpy(partial).to(torch.bfloat16)
 
-    def combine(self, back, pos, T, d, G):
+    def combine(self, back, pos, T, d, G, out=None):
         b = back.float().numpy()
         p = pos.numpy()
-        out = np.zeros((T, d), np.float32)
+        res = np.zeros((T, d), np.float32)
         for t in range(T):
             acc = np.zeros(d, np.float32)
             for g in range(G):
                 if p[t, g] >= 0:
                     acc = (acc + b[p[t, g]]).astype(np.float32)
-            out[t] = nr.round_bf16(acc)
-        return torch.from_numpy(out).to(torch.bfloat16)
+            res[t] = nr.round_bf16(acc)
+        res = torch.from_numpy(res).to(torch.bfloat16)
+        if out is not None:
+            out.copy_(res)
+            return out
+        return res

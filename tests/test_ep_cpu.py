@@ -59,7 +59,8 @@ def _worker(rank, world, port, case):
         if case["zipf"]:
             bias = torch.from_numpy((2.0 * np.log(1.0 / np.arange(1, E + 1))).astype(np.float32))
             dense.router_logit_bias = bias
-        ep = pkg.ExpertParallelMoE.from_dense(dense, ops=OracleEPOps())
+        ep = pkg.ExpertParallelMoE.from_dense(dense, ops=OracleEPOps(), chunks=case["chunks"])
+        ep.min_chunk_tokens = 8  # several chunks even for these small batches
         assert ep.experts_per_rank == E // world and ep.expert_offset == rank * (E // world)
 
         r = np.random.default_rng(100 + rank)
@@ -94,8 +95,8 @@ def _worker(rank, world, port, case):
 
 
 CASES = [
-    dict(name="uniform_k2", t=40, d=256, e=8, k=2, f=256, norm=True, zipf=False, valid=False),
-    dict(name="zipf_valid_k3", t=48, d=256, e=8, k=3, f=256, norm=False, zipf=True, valid=True),
+    dict(name="uniform_k2", t=40, d=256, e=8, k=2, f=256, norm=True, zipf=False, valid=False, chunks=1),
+    dict(name="zipf_valid_k3_chunked", t=48, d=256, e=8, k=3, f=256, norm=False, zipf=True, valid=True, chunks=3),
 ]
 
 
