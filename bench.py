@@ -49,6 +49,7 @@ KERNELS_PER_FORWARD = 7  # router-weight split, router, route-scan, permute+quan
 # expert parallel: route (3) + dispatch count/scan/pack (3) + receive count/scan/pad/scatter (4) + 2 GEMMs + partial
 # sums (1) + combine (1)
 KERNELS_PER_EP_FORWARD = 14
+EP_STAGES = ("route", "dispatch", "counts", "exchange_rows", "experts", "exchange_partials", "combine")
 
 
 def load_peaks() -> dict:
@@ -187,10 +188,11 @@ def run_ours(args) -> None:
     T, d, E, k, F = cfg["t"], cfg["d"], cfg["e"], cfg["k"], cfg["f"]
     moe, x = build_layer(pkg, cfg, dev, rank)
     ep = world > 1
-    n_stages = 6 if ep else 5
+    n_stages = 7 if ep else 5
     if ep:
         # expert parallel: the same layer on every rank, each keeps its E / N experts
         moe = pkg.ExpertParallelMoE.from_dense(moe, chunks=args.ep_chunks)
+        moe.partials_via = args.ep_partials
 
     def barrier():
         if world > 1:
@@ -231,6 +233,12 @@ def run_ours(args) -> None:
         clocks = sampler.stop()
         elapsed_ms = max_over_ranks(start.elapsed_time(end))
         stage_ms = [statistics.mean(evs[j].elapsed_time(evs[j + 1]) for evs in stage_ev) for j in range(n_stages)]
+        stage_spread = None
+        if ep:  # every rank's stage times: min / max over ranks show imbalance and waiting
+            allst = [None] * world
+            dist.all_gather_object(allst, stage_ms)
+            stage_spread = {name: [round(min(r[i] for r in allst), 4), round(max(r[i] for r in allst), 4)]
+                            for i, name in enumerate(EP_STAGES)}
 
         # end to end through the public API with host buffers: every step copies its x from
         # pinned host memory and its output (plus aux / z) back; uploads, layer and downloads
@@ -291,7 +299,7 @@ def run_ours(args) -> None:
     if ep:
         # the rank's experts step (receive layout, both grouped GEMMs, partial sums) on its own slots
         slots_here = moe.last_exchange["slots"][0]
-        roof_flops, roof_ms = 6.0 * slots_here * d * F, stage_ms[3]
+        roof_flops, roof_ms = 6.0 * slots_here * d * F, stage_ms[4]
         roof_kernel = "grouped_gemm_fp4 gate/up + down (expert-parallel experts step of rank 0, incl. row layout)"
     else:
         roof_flops, roof_ms = 4.0 * T * k * d * F, stage_ms[2]
@@ -317,12 +325,12 @@ def run_ours(args) -> None:
         "data": "synthetic (x~N(0,1) bf16, weights~N(0,0.02) fp32 quantised to NVFP4, seeded torch RNG on device)",
         "config": {"workload": cfg["name"], "tokens_per_gpu": T, "d_model": d, "num_experts": E, "top_k": k,
                    "expert_ffn": F, "parallelism": f"ep{world}" if ep else "single",
-                   **({"ep_chunks": args.ep_chunks} if ep else {}),
+                   **({"ep_chunks": moe.chunks, "ep_partials": moe.partials_via} if ep else {}),
                    "l2": "no flush: x (%.0f MB) and NVFP4 weights (%.0f MB) exceed the 126 MB L2" % (
                        T * d * 2 / 1e6, E * 3 * d * F * (0.5 + 1 / 16) / 1e6)},
-        "stages_ms": dict(zip(("route", "dispatch", "exchange_rows", "experts", "exchange_partials", "combine")
-                              if ep else ("route", "permute_quant", "gateup_gemm", "down_gemm", "combine"),
+        "stages_ms": dict(zip(EP_STAGES if ep else ("route", "permute_quant", "gateup_gemm", "down_gemm", "combine"),
                               [round(s, 4) for s in stage_ms])),
+        **({"stages_ms_over_ranks": stage_spread} if ep else {}),
         "layer_fp4_tflops": layer_tflops,
         "roofline": ({"bound": "hbm", "kernel": "whole layer forward (decode: grouped GEMMs stream the touched experts)",
                       "achieved": dec_bytes / (ms_per_step / 1e3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -403,7 +411,9 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--cpu-sample", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--ep-chunks", type=int, default=1,
+    ap.add_argument("--ep-partials", default="copy", choices=("kernel", "copy"),
+                    help="expert parallel: partial sums stored to their sources by the summing kernel or copied")
+    ap.add_argument("--ep-chunks", type=int, default=0,
                     help="expert parallel (N > 1): token chunks whose exchange overlaps another chunk's experts")
     args = ap.parse_args()
     if args.warmup < 3:
