@@ -250,6 +250,7 @@ struct RouterTcArgs {
   const float* bias;
   const uint8_t* valid;
   int T, d, E, E_pad, k, norm_topk, stages;
+  int fused;  // 3 * E_pad <= 256: the three weight parts form one N = 3 * E_pad operand
   uint32_t tmem_cols;
   int32_t* topk_idx;
   float* topk_w;
@@ -310,8 +311,13 @@ __global__ void __launch_bounds__(kTcThreads) router_tc_kernel(const __grid_cons
         const uint32_t st = base + stage * stage_bytes;
         mbar_arrive_expect_tx(full_bar(stage), stage_bytes);
         tma_load_2d(st, &tmap_x, kb * 64, t0, full_bar(stage));
+        if (a.fused) {
+          tma_load_2d(st + a_bytes, &tmap_w, kb * 64, 0, full_bar(stage));  // the three parts, stacked
+        } else {
 #pragma unroll
-        for (int p = 0; p < 3; ++p) tma_load_2d(st + a_bytes + p * b_part, &tmap_w, kb * 64, p * a.E_pad, full_bar(stage));
+          for (int p = 0; p < 3; ++p)
+            tma_load_2d(st + a_bytes + p * b_part, &tmap_w, kb * 64, p * a.E_pad, full_bar(stage));
+        }
         if (++stage == a.stages) {
           stage = 0;
           phase ^= 1u;
@@ -321,8 +327,11 @@ __global__ void __launch_bounds__(kTcThreads) router_tc_kernel(const __grid_cons
     __syncwarp();
   } else if (warp == 1) {
     if (lane == 0) {
-      // kind::f16, bf16 x bf16 -> fp32, K-major A and B, M = 128, N = E_pad
-      const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t(a.E_pad) >> 3) << 17) | ((128u >> 4) << 24);
+      // kind::f16, bf16 x bf16 -> fp32, K-major A and B, M = 128, N = E_pad (or 3 * E_pad
+      // when fused: one MMA per K step writes the three parts' products to columns
+      // [0, E_pad), [E_pad, 2 E_pad), [2 E_pad, 3 E_pad))
+      const uint32_t n_mma = a.fused ? 3u * uint32_t(a.E_pad) : uint32_t(a.E_pad);
+      const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((n_mma >> 3) << 17) | ((128u >> 4) << 24);
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -333,13 +342,20 @@ __global__ void __launch_bounds__(kTcThreads) router_tc_kernel(const __grid_cons
         }
         tc_fence_after();
         const uint32_t st = base + stage * stage_bytes;
+        if (a.fused) {
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks)
+          for (int ks = 0; ks < 4; ++ks)
+            tc_mma_f16(tmem_base, smem_desc(st + 32 * ks, 16, 1024, 2), smem_desc(st + a_bytes + 32 * ks, 16, 1024, 2),
+                       idesc, (kb | ks) != 0 ? 1u : 0u);
+        } else {
 #pragma unroll
-          for (int p = 0; p < 3; ++p)
-            tc_mma_f16(tmem_base, smem_desc(st + 32 * ks, 16, 1024, 2),
-                       smem_desc(st + a_bytes + p * b_part + 32 * ks, 16, 1024, 2), idesc,
-                       (kb | ks | p) != 0 ? 1u : 0u);
+          for (int ks = 0; ks < 4; ++ks)
+#pragma unroll
+            for (int p = 0; p < 3; ++p)
+              tc_mma_f16(tmem_base, smem_desc(st + 32 * ks, 16, 1024, 2),
+                         smem_desc(st + a_bytes + p * b_part + 32 * ks, 16, 1024, 2), idesc,
+                         (kb | ks | p) != 0 ? 1u : 0u);
+        }
         tc_commit(empty_bar(stage));
         if (++stage == a.stages) {
           stage = 0;
@@ -359,21 +375,29 @@ __global__ void __launch_bounds__(kTcThreads) router_tc_kernel(const __grid_cons
     const int cols = a.E_pad / 2;  // a multiple of 8
     const int row = q * 32 + lane;
     const uint32_t lane_addr = tmem_base + (uint32_t(q * 32) << 16);
+    auto ld8 = [&](uint32_t col, uint32_t (&v)[8]) {
+      asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                   : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                   : "r"(lane_addr + col)
+                   : "memory");
+    };
     for (int c0 = half * cols; c0 < (half + 1) * cols; c0 += 8) {
-      uint32_t v[8];
+      uint32_t v[8], vm[8], vl[8];
       if (ok) {
-        asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                     : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
-                       "=r"(v[7])
-                     : "r"(lane_addr + c0)
-                     : "memory");
+        ld8(c0, v);
+        if (a.fused) {
+          ld8(c0 + a.E_pad, vm);
+          ld8(c0 + 2 * a.E_pad, vl);
+        }
         tmem_wait_ld();
       }
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int e = c0 + j;
         if (e < a.E) {
-          const float lv = ok ? __uint_as_float(v[j]) : 0.f;
+          float lv = ok ? __uint_as_float(v[j]) : 0.f;
+          // fused: hi + (mid + lo), the two small parts first
+          if (ok && a.fused) lv = __fadd_rn(lv, __fadd_rn(__uint_as_float(vm[j]), __uint_as_float(vl[j])));
           s.logits[row * s.lds + e] = a.bias ? __fadd_rn(lv, a.bias[e]) : lv;
         }
       }
@@ -538,7 +562,9 @@ int launch_router_t(const uint16_t* x, const float* wr, const float* bias, const
   router_split_kernel<<<blocks, 256, 0, stream>>>(wr, a.E, a.E_pad, a.d, ws.wsplit);
   CUtensorMap tx, tw;
   if (!make_tmap_bf16(&tx, x, uint64_t(a.d), uint64_t(a.T), kRouteTokens)) return MCL4MOE_ERR_CUDA;
-  if (!make_tmap_bf16(&tw, ws.wsplit, uint64_t(a.d), uint64_t(3) * a.E_pad, uint32_t(a.E_pad))) return MCL4MOE_ERR_CUDA;
+  a.fused = 3 * a.E_pad <= 256 ? 1 : 0;
+  if (!make_tmap_bf16(&tw, ws.wsplit, uint64_t(a.d), uint64_t(3) * a.E_pad, uint32_t(a.fused ? 3 * a.E_pad : a.E_pad)))
+    return MCL4MOE_ERR_CUDA;
   const size_t stage_bytes = size_t(kRouteTokens) * 128 + 3 * size_t(a.E_pad) * 128;
   int stages = int((110 * 1024) / stage_bytes);
   stages = stages < 2 ? 2 : (stages > 4 ? 4 : stages);
@@ -547,7 +573,7 @@ int launch_router_t(const uint16_t* x, const float* wr, const float* bias, const
   const size_t tail = tail_smem_bytes(a.E, a.k);
   const size_t smem = 1024 + ((region > tail ? region : tail) + 15) / 16 * 16 + 128;
   uint32_t cols = 32;
-  while (cols < uint32_t(a.E_pad)) cols <<= 1;
+  while (cols < uint32_t(a.fused ? 3 * a.E_pad : a.E_pad)) cols <<= 1;
   a.tmem_cols = cols;
   static bool configured = false;
   if (!configured) {
