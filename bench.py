@@ -224,14 +224,19 @@ def run_ours(args) -> None:
         torch.cuda.synchronize()
         start.record()
         for i in range(K):
-            moe.stage_events = stage_ev[i]
             moe(x)
         end.record()
         torch.cuda.synchronize()
         barrier()
-        moe.stage_events = None
         clocks = sampler.stop()
         elapsed_ms = max_over_ranks(start.elapsed_time(end))
+        # stage breakdown in a separate pass: events between the kernels would keep the
+        # timed forwards from overlapping one kernel's start with the previous one's end
+        for i in range(K):
+            moe.stage_events = stage_ev[i]
+            moe(x)
+        torch.cuda.synchronize()
+        moe.stage_events = None
         stage_ms = [statistics.mean(evs[j].elapsed_time(evs[j + 1]) for evs in stage_ev) for j in range(n_stages)]
         stage_spread = None
         if ep:  # every rank's stage times: min / max over ranks show imbalance and waiting

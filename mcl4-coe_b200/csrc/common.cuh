@@ -403,6 +403,13 @@ __device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
   return v;
 }
 
+// ---- programmatic dependent launch: a kernel launched with launch_pdl may
+// start while the previous kernel on the stream finishes; pdl_wait() blocks the
+// calling thread until that kernel has completed and its writes are visible (a
+// no-op for an ordinary launch); pdl_trigger() lets the next kernel launch early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---- CTA pairs (cluster of 2): two SMs share one 256-row MMA
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;

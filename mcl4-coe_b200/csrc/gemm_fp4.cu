@@ -137,7 +137,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const bool leader = rank == 0;
   const int pair = int(cluster_id_x()), npairs = int(cluster_count_x());
 
-  for (int i = tid; i <= E; i += kThreads) pad_s[i] = args.pad_start[i];
   if (MODE == 0 && tid < 128) s_inv[tid] = inverse_decoding(e4m3_to_f32(uint32_t(tid)));
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
@@ -158,6 +157,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     tmem_alloc_pair(smem_u32(tmem_slot), kTmemCols);
     tmem_relinquish_pair();
   }
+  // Everything above is independent of the previous kernel's output; from here on
+  // its writes (expert layout, A operand) are read.
+  pdl_wait();
+  for (int i = tid; i <= E; i += kThreads) pad_s[i] = args.pad_start[i];
   tc_fence_before();
   __syncthreads();
   cluster_sync_all();  // both CTAs' barriers exist before any cross-CTA arrive or transfer
@@ -451,6 +454,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (MODE == 1 && lane == 0) bulk_wait_all();
   }
 
+  pdl_trigger();  // the next kernel may launch; it waits for this grid's writes
   tc_fence_before();
   __syncthreads();
   cluster_sync_all();  // no pair MMA or peer access is outstanding past this point
@@ -534,8 +538,10 @@ int launch_mode(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
     configured = true;
   }
   const int pairs = resident_pairs<MODE>();
-  grouped_gemm_fp4_kernel<MODE><<<2 * pairs, kThreads, Cfg<MODE>::kSmem, stream>>>(ta, tb, ty, args);
-  return cudaGetLastError() == cudaSuccess ? MCL4MOE_OK : MCL4MOE_ERR_CUDA;
+  return launch_pdl(grouped_gemm_fp4_kernel<MODE>, dim3(2 * pairs), dim3(kThreads), Cfg<MODE>::kSmem, stream, ta, tb,
+                    ty, args) == cudaSuccess
+             ? MCL4MOE_OK
+             : MCL4MOE_ERR_CUDA;
 }
 
 }  // namespace

@@ -1,6 +1,8 @@
 // Internal launch interface shared by the kernel files and the C ABI (api.cu).
 #pragma once
 
+#include <utility>
+
 #include "common.cuh"
 
 namespace mcl4 {
@@ -92,6 +94,25 @@ __device__ __forceinline__ float block_sum(float v, float* tmp) {
   return s;
 }
 
+
+// Launch ``kernel`` with programmatic stream serialization: it may begin while the
+// previous kernel on ``stream`` drains, and must pdl_wait() before reading that
+// kernel's outputs.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Expert segments of the grouped GEMMs start on multiples of kSegRows rows: a
 // CTA pair computes 256-row tiles that must not straddle two experts.

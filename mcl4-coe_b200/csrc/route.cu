@@ -26,6 +26,8 @@ __global__ void __launch_bounds__(256) permute_quant_kernel(
   __shared__ float inv_tab[128];
   fill_inverse_scale_table(inv_tab);
   __syncthreads();
+  pdl_wait();     // routing and the expert layout are complete
+  pdl_trigger();  // the gate/up GEMM may launch (it waits for this grid's writes)
   const int lane = threadIdx.x & 31;
   const int nblk = d / 16;
   const int token_blocks = (T + 7) / 8;
@@ -86,9 +88,10 @@ int launch_permute_quantize(const uint16_t* x, const uint8_t* valid, const int32
                             int T, int d, int E, int k, const RouteWorkspace& ws, int32_t* slot_pos, float* sorted_w,
                             int32_t* perm, uint8_t* xq, uint8_t* xs, cudaStream_t stream) {
   const int blocks = (T + 7) / 8 + E;
-  permute_quant_kernel<<<blocks, 256, 0, stream>>>(x, valid, topk_idx, topk_w, T, d, E, k, ws, slot_pos, sorted_w,
-                                                   perm, xq, xs);
-  return cudaGetLastError() == cudaSuccess ? MCL4MOE_OK : MCL4MOE_ERR_CUDA;
+  return launch_pdl(permute_quant_kernel, dim3(blocks), dim3(256), 0, stream, x, valid, topk_idx, topk_w, T, d, E, k,
+                    ws, slot_pos, sorted_w, perm, xq, xs) == cudaSuccess
+             ? MCL4MOE_OK
+             : MCL4MOE_ERR_CUDA;
 }
 
 // ---------------------------------------------------------------- grouped-linear helpers
@@ -184,6 +187,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const uint16_t* __restrict
                                                       const int32_t* __restrict__ slot_pos,
                                                       const uint8_t* __restrict__ valid, int T, int k, int d,
                                                       uint16_t* __restrict__ out) {
+  pdl_wait();  // the down projection's rows are complete
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (t >= T) return;
@@ -215,8 +219,10 @@ __global__ void __launch_bounds__(256) combine_kernel(const uint16_t* __restrict
 int launch_combine(const uint16_t* y, const int32_t* slot_pos, const uint8_t* valid, int T, int k, int d, uint16_t* out,
                    cudaStream_t stream) {
   if (T == 0) return MCL4MOE_OK;
-  combine_kernel<<<(T + 7) / 8, 256, 0, stream>>>(y, slot_pos, valid, T, k, d, out);
-  return cudaGetLastError() == cudaSuccess ? MCL4MOE_OK : MCL4MOE_ERR_CUDA;
+  return launch_pdl(combine_kernel, dim3((T + 7) / 8), dim3(256), 0, stream, y, slot_pos, valid, T, k, d, out) ==
+                 cudaSuccess
+             ? MCL4MOE_OK
+             : MCL4MOE_ERR_CUDA;
 }
 
 }  // namespace mcl4

@@ -281,7 +281,6 @@ __global__ void __launch_bounds__(kTcThreads) router_tc_kernel(const __grid_cons
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int chunk = blockIdx.x;
   const int t0 = chunk * kRouteTokens;
-  if (chunk == 0 && tid == 0) *ws.done = 0u;  // the scan kernel runs after this one
   if (tid == 0) {
     for (int s = 0; s < a.stages; ++s) {
       mbar_init(full_bar(s), 1);
@@ -299,6 +298,8 @@ __global__ void __launch_bounds__(kTcThreads) router_tc_kernel(const __grid_cons
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int kblocks = a.d / 64;
+  pdl_wait();  // the router-weight split (previous kernel) has finished
+  if (chunk == 0 && tid == 0) *ws.done = 0u;  // the scan kernel runs after this one
 
   if (warp == 0) {
     if (lane == 0) {
@@ -404,6 +405,7 @@ __global__ void __launch_bounds__(kTcThreads) router_tc_kernel(const __grid_cons
     }
     tc_fence_before();
     TailBarrier()();
+    pdl_trigger();  // the scan kernel may launch; it waits for this grid's writes
     route_tail<EW>(s, g, chunk, a.T, a.E, a.k, a.norm_topk, a.valid, a.topk_idx, a.topk_w, a.logits_out, a.sel_mask,
                    ws, TailBarrier());
   }
@@ -447,6 +449,8 @@ __global__ void __launch_bounds__(256) route_scan_kernel(int C, int E, int k, Ro
   __shared__ int32_t itmp[64];
   __shared__ float ftmp[32];
   __shared__ bool is_last;
+  pdl_wait();
+  pdl_trigger();
   const int tid = threadIdx.x;
   const int e = blockIdx.x;
   const int per = (C + blockDim.x - 1) / blockDim.x;
@@ -583,7 +587,8 @@ int launch_router_t(const uint16_t* x, const float* wr, const float* bias, const
     configured = true;
   }
   if (smem > 227 * 1024) return MCL4MOE_ERR_UNSUPPORTED;
-  router_tc_kernel<EW><<<C, kTcThreads, smem, stream>>>(tx, tw, a, ws);
+  if (launch_pdl(router_tc_kernel<EW>, dim3(C), dim3(kTcThreads), smem, stream, tx, tw, a, ws) != cudaSuccess)
+    return MCL4MOE_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? MCL4MOE_OK : MCL4MOE_ERR_CUDA;
 }
 
@@ -618,7 +623,9 @@ int launch_route(const uint16_t* x, const float* wr, const float* bias, const fl
     return MCL4MOE_ERR_CUDA;  // no router CTA ran: reset the finished-expert counter here
   }
   const int C = (T + kRouteTokens - 1) / kRouteTokens;
-  route_scan_kernel<<<E, 256, 0, stream>>>(C, E, k, ws, counts_out, stats, offs_out);
+  if (launch_pdl(route_scan_kernel, dim3(E), dim3(256), 0, stream, C, E, k, ws, counts_out, stats, offs_out) !=
+      cudaSuccess)
+    return MCL4MOE_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? MCL4MOE_OK : MCL4MOE_ERR_CUDA;
 }
 
