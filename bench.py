@@ -206,7 +206,10 @@ def run_ours(args) -> None:
         return float(t.item())
 
     K, W = args.steps, args.warmup
+    graph = args.cuda_graph and not ep
     with torch.inference_mode():
+        if graph:
+            moe.enable_cuda_graph()
         for _ in range(W):
             moe(x)
         torch.cuda.synchronize()
@@ -232,6 +235,8 @@ def run_ours(args) -> None:
         elapsed_ms = max_over_ranks(start.elapsed_time(end))
         # stage breakdown in a separate pass: events between the kernels would keep the
         # timed forwards from overlapping one kernel's start with the previous one's end
+        if graph:
+            moe.enable_cuda_graph(False)
         for i in range(K):
             moe.stage_events = stage_ev[i]
             moe(x)
@@ -331,6 +336,7 @@ def run_ours(args) -> None:
         "config": {"workload": cfg["name"], "tokens_per_gpu": T, "d_model": d, "num_experts": E, "top_k": k,
                    "expert_ffn": F, "parallelism": f"ep{world}" if ep else "single",
                    **({"ep_chunks": moe.chunks, "ep_partials": moe.partials_via} if ep else {}),
+                   **({"cuda_graph": True} if graph else {}),
                    "l2": "no flush: x (%.0f MB) and NVFP4 weights (%.0f MB) exceed the 126 MB L2" % (
                        T * d * 2 / 1e6, E * 3 * d * F * (0.5 + 1 / 16) / 1e6)},
         "stages_ms": dict(zip(EP_STAGES if ep else ("route", "permute_quant", "gateup_gemm", "down_gemm", "combine"),
@@ -416,6 +422,8 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--cpu-sample", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cuda-graph", action="store_true",
+                    help="1 GPU: serve the timed forwards from a captured CUDA graph (SparseMoE.enable_cuda_graph)")
     ap.add_argument("--ep-partials", default="copy", choices=("kernel", "copy"),
                     help="expert parallel: partial sums stored to their sources by the summing kernel or copied")
     ap.add_argument("--ep-chunks", type=int, default=0,

@@ -24,8 +24,13 @@ struct RouteWorkspace {
   float* probs_sum;      // [E]     sum of routed probabilities per expert
   uint32_t* done;        // [1]     finished-expert counter of the scan (zeroed by the router)
   uint16_t* wsplit;      // [3][E_pad][d] bf16 parts of the router weight (hi, mid, lo)
+  float* small_logits;   // [T, E] logits of small batches (T <= kRouteGemvMaxT), else null
   size_t bytes;
 };
+
+// Batches up to this many tokens compute their fp32 router logits on the CUDA cores
+// (a few tokens leave the tensor-core router with one CTA walking d serially).
+constexpr int kRouteGemvMaxT = 1024;
 
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
@@ -49,6 +54,7 @@ inline RouteWorkspace route_workspace(void* base, int T, int E, int k, int d) {
   w.probs_sum = reinterpret_cast<float*>(take(sizeof(float) * E));
   w.done = reinterpret_cast<uint32_t*>(take(sizeof(uint32_t)));
   w.wsplit = reinterpret_cast<uint16_t*>(take(sizeof(uint16_t) * 3 * size_t((E + 15) / 16 * 16) * size_t(d)));
+  w.small_logits = T <= kRouteGemvMaxT ? reinterpret_cast<float*>(take(sizeof(float) * size_t(T) * E)) : nullptr;
   w.bytes = off;
   return w;
 }

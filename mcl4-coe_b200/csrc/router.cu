@@ -244,6 +244,50 @@ __global__ void __launch_bounds__(256) router_split_kernel(const float* __restri
   }
 }
 
+// ---------------------------------------------------------------- small-batch router
+
+// fp32 logits of a small batch on the CUDA cores: CTA (token block of 8, expert
+// block of 8); warp w owns expert e0 + w, lane l accumulates elements l, l+32, ...
+// of d for the 8 tokens with fp32 fma, then a fixed xor tree sums the lanes
+// (deterministic).  logits[t, e] = sum_k x[t, k] * Wr[e, k] (+ bias[e]).
+__global__ void __launch_bounds__(256) router_gemv_kernel(const uint16_t* __restrict__ x,
+                                                          const float* __restrict__ wr,
+                                                          const float* __restrict__ bias, int T, int d, int E,
+                                                          float* __restrict__ logits) {
+  extern __shared__ uint16_t xs[];  // [8][d] bf16
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int t0 = blockIdx.x * 8, e = blockIdx.y * 8 + warp;
+  const int nt = min(8, T - t0);
+  for (int i = threadIdx.x; i < 8 * d / 8; i += blockDim.x) {  // 16-byte chunks
+    const int r = i / (d / 8), c = i - r * (d / 8);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < nt) v = __ldg(reinterpret_cast<const uint4*>(x + int64_t(t0 + r) * d) + c);
+    reinterpret_cast<uint4*>(xs)[i] = v;
+  }
+  __syncthreads();
+  pdl_trigger();
+  if (e >= E) return;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  const float* wrow = wr + int64_t(e) * d;
+  for (int kk = lane; kk < d; kk += 32) {
+    const float wv = __ldg(wrow + kk);
+#pragma unroll
+    for (int r = 0; r < 8; ++r) acc[r] = __fmaf_rn(bf16_to_f32(xs[r * d + kk]), wv, acc[r]);
+  }
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc[r] = __fadd_rn(acc[r], __shfl_xor_sync(0xffffffffu, acc[r], o));
+  }
+  if (lane < nt) {
+    float v = acc[0];
+#pragma unroll
+    for (int r = 1; r < 8; ++r)
+      if (lane == r) v = acc[r];
+    logits[int64_t(t0 + lane) * E + e] = bias ? __fadd_rn(v, bias[e]) : v;
+  }
+}
+
 // ---------------------------------------------------------------- tensor-core router
 
 struct RouterTcArgs {
@@ -613,6 +657,23 @@ int launch_route(const uint16_t* x, const float* wr, const float* bias, const fl
     a.logits_out = logits_out;
     a.sel_mask = sel_mask;
     a.err = err;
+    if (logits_in == nullptr && T <= kRouteGemvMaxT && ws.small_logits != nullptr) {
+      const size_t smem = sizeof(uint16_t) * 8 * size_t(d);
+      if (smem > 48 * 1024) {
+        static bool configured = false;
+        if (!configured) {
+          if (cudaFuncSetAttribute(router_gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
+              cudaSuccess)
+            return MCL4MOE_ERR_CUDA;
+          configured = true;
+        }
+      }
+      if (smem > 200 * 1024) return MCL4MOE_ERR_UNSUPPORTED;
+      router_gemv_kernel<<<dim3((T + 7) / 8, (E + 7) / 8), 256, smem, stream>>>(x, wr, bias, T, d, E,
+                                                                              ws.small_logits);
+      if (cudaGetLastError() != cudaSuccess) return MCL4MOE_ERR_CUDA;
+      logits_in = ws.small_logits;  // final logits: the tail below adds no bias
+    }
     int st;
     if (E <= 32) st = launch_router_t<1>(x, wr, bias, logits_in, a, ws, stream);
     else if (E <= 64) st = launch_router_t<2>(x, wr, bias, logits_in, a, ws, stream);

@@ -119,6 +119,51 @@ class SparseMoE(nn.Module):
         self.last_h: Tensor | None = None
         self._ws: Tensor | None = None
         self._ws_key: tuple | None = None
+        self._graphs: dict | None = None  # CUDA-graph replay (enable_cuda_graph)
+
+    def enable_cuda_graph(self, enabled: bool = True) -> None:
+        """Serve repeated calls of one shape from a captured CUDA graph.
+
+        The first call per (tokens, mask, bias, device) captures the whole layer
+        forward (one library call) with static input and output buffers; later calls
+        copy x in, replay the graph and return copies of the outputs, which removes
+        the per-call host work (weight-cache checks, argument set-up, kernel launches)
+        that dominates small decode batches.  While enabled the weights are not
+        re-checked per call: call ``enable_cuda_graph()`` again after changing them
+        (or growing / pruning experts) to capture afresh.  Forward only; no
+        ``forward_details``.
+        """
+        self._graphs = {} if enabled else None
+
+    def _graph_forward(self, flat: Tensor, valid: Tensor | None, x_shape, x_dtype):
+        T, d = flat.shape
+        dev = flat.device
+        bias = self.router_logit_bias
+        key = (T, d, str(dev), valid is not None, bias is not None)
+        ent = self._graphs.get(key)
+        if ent is None:
+            ent = {"x": torch.empty((T, d), dtype=torch.bfloat16, device=dev),
+                   "valid": None if valid is None else torch.empty((T,), dtype=torch.uint8, device=dev)}
+            ent["x"].copy_(flat)
+            if valid is not None:
+                ent["valid"].copy_(valid.reshape(-1))
+            # eager call first: builds the weight caches and sizes the workspace
+            self._forward_impl(ent["x"], ent["valid"], None, None, None, details=False, static=ent)
+            torch.cuda.synchronize(dev)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self._forward_impl(ent["x"], ent["valid"], None, None, None, details=False, static=ent)
+            ent["graph"] = g
+            self._graphs[key] = ent
+        ent["x"].copy_(flat)
+        if valid is not None:
+            ent["valid"].copy_(valid.reshape(-1).to(torch.uint8))
+        ent["graph"].replay()
+        E = len(self.experts)
+        self.last_selected_mask = ent["sel"].clone().view(*x_shape[:-1], E)
+        stats = ent["stats"].clone()
+        out = ent["out"].to(x_dtype).view(x_shape) if x_dtype != torch.bfloat16 else ent["out"].clone().view(x_shape)
+        return out, stats[0], stats[1], stats[3:3 + E]
 
     @classmethod
     def from_reference(cls, ref: nn.Module) -> "SparseMoE":
@@ -167,6 +212,9 @@ class SparseMoE(nn.Module):
     def forward(self, x: Tensor, valid: Tensor | None = None, *, prior_expert_mask: Tensor | None = None,
                 dense_expert_indices: Sequence[int] | Tensor | None = None,
                 dense_subset_k: int | None = None) -> tuple[Tensor, Tensor, Tensor, Tensor]:
+        if (self._graphs is not None and prior_expert_mask is None and dense_expert_indices is None
+                and dense_subset_k is None and x.is_cuda and not torch.is_grad_enabled()):
+            return self._graph_forward(x.reshape(-1, x.shape[-1]).to(torch.bfloat16), valid, x.shape, x.dtype)
         r = self._forward_impl(x, valid, prior_expert_mask, dense_expert_indices, dense_subset_k, details=False)
         return r["out"], r["aux_loss"], r["router_z_loss"], r["counts"]
 
@@ -179,7 +227,7 @@ class SparseMoE(nn.Module):
         expert-major rows) and ``pad_start`` [E+1]."""
         return self._forward_impl(x, valid, None, None, None, details=True)
 
-    def _forward_impl(self, x, valid, prior_expert_mask, dense_expert_indices, dense_subset_k, details):
+    def _forward_impl(self, x, valid, prior_expert_mask, dense_expert_indices, dense_subset_k, details, static=None):
         flat = x.reshape(-1, x.shape[-1])
         if flat.device.type != "cuda":
             raise ValueError("SparseMoE on B200 requires CUDA tensors (there is no CPU fallback)")
@@ -213,10 +261,19 @@ class SparseMoE(nn.Module):
             if vmask.numel() != T:
                 raise ValueError("valid must have one entry per token")
 
-        out = torch.empty((T, d), dtype=torch.bfloat16, device=dev)
-        stats = torch.empty((3 + E,), dtype=torch.float32, device=dev)
-        sel = torch.empty((T, E), dtype=torch.float32, device=dev)
-        ws = self._workspace(T, d, E, k, F, dev)
+        if static is not None:  # graph capture: fixed output buffers and workspace
+            if "out" not in static:
+                static["out"] = torch.empty((T, d), dtype=torch.bfloat16, device=dev)
+                static["stats"] = torch.empty((3 + E,), dtype=torch.float32, device=dev)
+                static["sel"] = torch.empty((T, E), dtype=torch.float32, device=dev)
+                static["ws"] = torch.empty((max(_lib.load().mcl4moe_moe_workspace_size(T, d, E, k, F), 256),),
+                                           dtype=torch.uint8, device=dev)
+            out, stats, sel, ws = static["out"], static["stats"], static["sel"], static["ws"]
+        else:
+            out = torch.empty((T, d), dtype=torch.bfloat16, device=dev)
+            stats = torch.empty((3 + E,), dtype=torch.float32, device=dev)
+            sel = torch.empty((T, E), dtype=torch.float32, device=dev)
+            ws = self._workspace(T, d, E, k, F, dev)
         extra = {}
         if details:
             extra = dict(topk_idx=torch.empty((T, k), dtype=torch.int32, device=dev),

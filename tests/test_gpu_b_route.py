@@ -77,3 +77,20 @@ def test_router_product_and_selection_vs_reference(moe_pkg, golden, case):
     assert np.all(same | tie), f"{int((~same & ~tie).sum())} non-tie tokens routed differently"
     np.testing.assert_allclose(r["stats"][0], g[f"{name}__aux"], rtol=1e-4)
     np.testing.assert_allclose(r["stats"][1], g[f"{name}__z"], rtol=1e-4)
+
+
+@pytest.mark.parametrize("name", ["r_e64k8", "r_zipf"])
+def test_tensor_core_router_on_tiled_batch(moe_pkg, golden, name):
+    """Batches above the small-batch limit take the tcgen05 router: tile a golden case to
+    2048 tokens (identical rows have identical reference logits) and compare."""
+    c = dict(routing_cases())[name]
+    reps = 2048 // c["t"]
+    big = dict(c, t=c["t"] * reps, x_bf16_bits=np.tile(c["x_bf16_bits"].reshape(c["t"], c["d"]), (reps, 1)))
+    g = golden("routing")
+    r = _route(moe_pkg, big)
+    ref_logits = np.tile(g[f"{name}__logits"], (reps, 1))
+    np.testing.assert_allclose(r["logits"], ref_logits, rtol=1e-5, atol=2e-6)
+    tie = near_tie_tokens(ref_logits, c["k"])
+    ref_idx = np.tile(g[f"{name}__topk_indices"], (reps, 1))
+    same = np.all(np.sort(r["topk_idx"], 1) == np.sort(ref_idx, 1), axis=1)
+    assert np.all(same | tie)

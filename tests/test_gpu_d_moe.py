@@ -237,3 +237,20 @@ def test_garbage_workspace_does_not_leak_into_results(moe_pkg):
     torch.cuda.synchronize()
     assert moe.read_device_error() == 0
     assert torch.equal(ref, got)
+
+
+def test_cuda_graph_replay_matches_eager(moe_pkg):
+    """enable_cuda_graph: repeated same-shape calls replay a captured graph and give the
+    eager outputs bit for bit, for new inputs on every call."""
+    c = moe_case(51, 64, 512, 16, 4, 512)
+    moe = build_module(moe_pkg, c, DEV)
+    xs = [x_tensor(c, DEV) * s for s in (1.0, 0.5, 2.0)]
+    with torch.no_grad():
+        eager = [moe(x) for x in xs]
+        moe.enable_cuda_graph()
+        graphed = [moe(x) for x in xs]
+        moe.enable_cuda_graph(False)
+    torch.cuda.synchronize()
+    for (o1, a1, z1, c1), (o2, a2, z2, c2) in zip(eager, graphed):
+        assert torch.equal(o1, o2) and torch.equal(c1, c2)
+        assert float(a1) == float(a2) and float(z1) == float(z2)
