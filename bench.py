@@ -335,7 +335,8 @@ def run_ours(args) -> None:
         "data": "synthetic (x~N(0,1) bf16, weights~N(0,0.02) fp32 quantised to NVFP4, seeded torch RNG on device)",
         "config": {"workload": cfg["name"], "tokens_per_gpu": T, "d_model": d, "num_experts": E, "top_k": k,
                    "expert_ffn": F, "parallelism": f"ep{world}" if ep else "single",
-                   **({"ep_chunks": moe.chunks, "ep_partials": moe.partials_via} if ep else {}),
+                   **({"ep_chunks": len(moe._chunk_bounds(T)), "ep_chunk_weights": moe.chunk_weights,
+                      "ep_partials": moe.partials_via} if ep else {}),
                    **({"cuda_graph": True} if graph else {}),
                    "l2": "no flush: x (%.0f MB) and NVFP4 weights (%.0f MB) exceed the 126 MB L2" % (
                        T * d * 2 / 1e6, E * 3 * d * F * (0.5 + 1 / 16) / 1e6)},

@@ -234,6 +234,16 @@ size_t mcl4moe_ep_dispatch_workspace_size(int T, int G);
 int mcl4moe_ep_dispatch(const uint16_t* x, const int32_t* topk_idx, const float* topk_w, const uint8_t* valid, int T,
                         int d, int k, int G, int E_loc, int32_t* send_counts, int32_t* send_pos, uint8_t* send_buf,
                         void* workspace, size_t workspace_bytes, mcl4moe_stream_t stream);
+/* mcl4moe_ep_dispatch in two calls on the same stream and workspace: _count
+ * writes send_counts (and the per-group offsets _pack needs, in the workspace);
+ * _pack writes send_pos and send_buf.  A caller exchanges the counts between
+ * the two, so that reading them on the host overlaps the packing. */
+int mcl4moe_ep_dispatch_count(const int32_t* topk_idx, const uint8_t* valid, int T, int k, int G, int E_loc,
+                              int32_t* send_counts, void* workspace, size_t workspace_bytes,
+                              mcl4moe_stream_t stream);
+int mcl4moe_ep_dispatch_pack(const uint16_t* x, const int32_t* topk_idx, const float* topk_w, const uint8_t* valid,
+                             int T, int d, int k, int G, int E_loc, const int32_t* send_counts, int32_t* send_pos,
+                             uint8_t* send_buf, void* workspace, size_t workspace_bytes, mcl4moe_stream_t stream);
 size_t mcl4moe_ep_experts_workspace_size(int R, int slots, int d, int k, int E_loc, int F);
 int mcl4moe_ep_experts(const uint8_t* recv_buf, int R, int slots, int d, int k, int E_loc, int F,
                        const uint8_t* w_up, const uint8_t* w_up_scales, const float* w_up_g, const uint8_t* w_dn,
@@ -267,6 +277,10 @@ int mcl4moe_ipc_export(const void* ptr, uint8_t* handle_out, uint64_t* offset_ou
 int mcl4moe_ipc_import(const uint8_t* handle, void** base_out);
 int mcl4moe_ipc_close(void* base);
 int mcl4moe_copy_async(void* dst, const void* src, size_t bytes, mcl4moe_stream_t stream);
+/* n device-to-device copies, copy i on streams[i % n_streams], in list order
+ * (zero-byte entries are skipped); all arguments are host arrays. */
+int mcl4moe_copy_list_async(void* const* dst, const void* const* src, const uint64_t* bytes, int n,
+                            mcl4moe_stream_t const* streams, int n_streams);
 
 #ifdef __cplusplus
 }

@@ -37,6 +37,8 @@ EXPORTS = (
     "mcl4moe_ep_row_bytes",
     "mcl4moe_ep_dispatch_workspace_size",
     "mcl4moe_ep_dispatch",
+    "mcl4moe_ep_dispatch_count",
+    "mcl4moe_ep_dispatch_pack",
     "mcl4moe_ep_experts_workspace_size",
     "mcl4moe_ep_experts",
     "mcl4moe_ep_combine",
@@ -45,6 +47,7 @@ EXPORTS = (
     "mcl4moe_ipc_import",
     "mcl4moe_ipc_close",
     "mcl4moe_copy_async",
+    "mcl4moe_copy_list_async",
 )
 
 
@@ -145,6 +148,12 @@ def load() -> ctypes.CDLL:
     lib.mcl4moe_ep_dispatch.restype = c_int
     lib.mcl4moe_ep_dispatch.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
                                         c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]
+    lib.mcl4moe_ep_dispatch_count.restype = c_int
+    lib.mcl4moe_ep_dispatch_count.argtypes = [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
+                                              c_size_t, c_void_p]
+    lib.mcl4moe_ep_dispatch_pack.restype = c_int
+    lib.mcl4moe_ep_dispatch_pack.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
+                                             c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]
     lib.mcl4moe_ep_experts_workspace_size.restype = c_size_t
     lib.mcl4moe_ep_experts_workspace_size.argtypes = [c_int, c_int, c_int, c_int, c_int, c_int]
     lib.mcl4moe_ep_experts.restype = c_int
@@ -165,6 +174,8 @@ def load() -> ctypes.CDLL:
     lib.mcl4moe_ipc_close.argtypes = [c_void_p]
     lib.mcl4moe_copy_async.restype = c_int
     lib.mcl4moe_copy_async.argtypes = [c_void_p, c_void_p, c_size_t, c_void_p]
+    lib.mcl4moe_copy_list_async.restype = c_int
+    lib.mcl4moe_copy_list_async.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int]
     _lib = lib
     return lib
 

@@ -60,6 +60,8 @@ __global__ void __launch_bounds__(256) ep_count_kernel(const int32_t* __restrict
                                                        const uint8_t* __restrict__ valid, int T, int k, int G,
                                                        int E_loc, int32_t* __restrict__ grp_rows,
                                                        int32_t* __restrict__ send_slots) {
+  pdl_wait();     // the previous kernel on the stream has completed (PDL launch)
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int w = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (w >= (T + 31) / 32) return;
@@ -92,6 +94,8 @@ __global__ void __launch_bounds__(256) ep_count_kernel(const int32_t* __restrict
 // One CTA per column: exclusive scan over groups in place; column total to ``totals``.
 __global__ void __launch_bounds__(256) ep_column_scan_kernel(int32_t* __restrict__ grp, int W, int cols,
                                                              int32_t* __restrict__ totals) {
+  pdl_wait();     // the previous kernel on the stream has completed (PDL launch)
+  pdl_trigger();
   __shared__ int32_t tmp[64];
   const int c = blockIdx.x, tid = threadIdx.x;
   const int per = (W + blockDim.x - 1) / blockDim.x;
@@ -123,6 +127,8 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const uint16_t* __restrict
   __shared__ int32_t s_start[kMaxRanks];
   __shared__ float inv_tab[128];
   fill_inverse_scale_table(inv_tab);
+  pdl_wait();     // the previous kernel on the stream has completed (PDL launch)
+  pdl_trigger();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int w = blockIdx.x;
   const EpRow L = ep_row(d, k);
@@ -196,6 +202,8 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const uint16_t* __restrict
 template <int EW>
 __global__ void __launch_bounds__(256) ep_recv_count_kernel(const uint8_t* __restrict__ recv, int R, int d, int k,
                                                             int E_loc, int32_t* __restrict__ grp_cnt) {
+  pdl_wait();     // the previous kernel on the stream has completed (PDL launch)
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int w = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (w >= (R + 31) / 32) return;
@@ -225,6 +233,8 @@ __global__ void __launch_bounds__(256) ep_recv_count_kernel(const uint8_t* __res
 // Segment starts of the local experts, each padded to kSegRows rows.
 __global__ void __launch_bounds__(256) ep_pad_kernel(const int32_t* __restrict__ counts, int E_loc,
                                                      int32_t* __restrict__ pad_start) {
+  pdl_wait();     // the previous kernel on the stream has completed (PDL launch)
+  pdl_trigger();
   __shared__ int32_t tmp[64];
   const int e = threadIdx.x;
   const int c = e < E_loc ? counts[e] : 0;
@@ -245,6 +255,8 @@ __global__ void __launch_bounds__(256) ep_scatter_kernel(const uint8_t* __restri
                                                          uint8_t* __restrict__ xq, uint8_t* __restrict__ xs,
                                                          float* __restrict__ sorted_w,
                                                          int32_t* __restrict__ slot_pos) {
+  pdl_wait();     // the previous kernel on the stream has completed (PDL launch)
+  pdl_trigger();
   __shared__ uint32_t s_bal[32 * EW];
   __shared__ int32_t s_pos[32][32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -320,6 +332,8 @@ __global__ void __launch_bounds__(256) ep_scatter_kernel(const uint8_t* __restri
 __global__ void __launch_bounds__(256) ep_partial_kernel(const uint16_t* __restrict__ y,
                                                          const int32_t* __restrict__ slot_pos, int R, int k, int d,
                                                          uint16_t* __restrict__ partial) {
+  pdl_wait();     // the previous kernel on the stream has completed (PDL launch)
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int r = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (r >= R) return;
@@ -360,6 +374,8 @@ struct EpDest {
 __global__ void __launch_bounds__(256) ep_partial_remote_kernel(const uint16_t* __restrict__ y,
                                                                 const int32_t* __restrict__ slot_pos, int R, int k,
                                                                 int d, EpDest dst) {
+  pdl_wait();     // the previous kernel on the stream has completed (PDL launch)
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int r = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (r >= R) return;
@@ -393,6 +409,8 @@ __global__ void __launch_bounds__(256) ep_partial_remote_kernel(const uint16_t* 
 __global__ void __launch_bounds__(256) ep_final_kernel(const uint16_t* __restrict__ back,
                                                        const int32_t* __restrict__ send_pos, int T, int d, int G,
                                                        uint16_t* __restrict__ out) {
+  pdl_wait();     // the previous kernel on the stream has completed (PDL launch)
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (t >= T) return;
@@ -472,13 +490,16 @@ int check_ep_shape(int d, int k, int G, int E_loc, int F) {
 }
 
 template <int EW>
-void launch_recv_layout(const uint8_t* recv, int R, int d, int k, int E_loc, const ExpertsWs& w, cudaStream_t s) {
+cudaError_t launch_recv_layout(const uint8_t* recv, int R, int d, int k, int E_loc, const ExpertsWs& w,
+                               cudaStream_t s) {
   const int W = (R + 31) / 32;
-  ep_recv_count_kernel<EW><<<(W + 7) / 8, 256, 0, s>>>(recv, R, d, k, E_loc, w.grp);
-  ep_column_scan_kernel<<<E_loc, 256, 0, s>>>(w.grp, W, E_loc, w.counts);
-  ep_pad_kernel<<<1, 256, 0, s>>>(w.counts, E_loc, w.pad_start);
-  ep_scatter_kernel<EW><<<W + E_loc, 256, 0, s>>>(recv, R, d, k, E_loc, w.grp, w.counts, w.pad_start, w.xq, w.xs,
-                                                  w.sorted_w, w.slot_pos);
+  cudaError_t e = launch_pdl(ep_recv_count_kernel<EW>, dim3((W + 7) / 8), dim3(256), 0, s, recv, R, d, k, E_loc, w.grp);
+  if (e == cudaSuccess) e = launch_pdl(ep_column_scan_kernel, dim3(E_loc), dim3(256), 0, s, w.grp, W, E_loc, w.counts);
+  if (e == cudaSuccess) e = launch_pdl(ep_pad_kernel, dim3(1), dim3(256), 0, s, w.counts, E_loc, w.pad_start);
+  if (e == cudaSuccess)
+    e = launch_pdl(ep_scatter_kernel<EW>, dim3(W + E_loc), dim3(256), 0, s, recv, R, d, k, E_loc, w.grp, w.counts,
+                   w.pad_start, w.xq, w.xs, w.sorted_w, w.slot_pos);
+  return e;
 }
 
 }  // namespace
@@ -499,6 +520,41 @@ size_t mcl4moe_ep_dispatch_workspace_size(int T, int G) {
   return dispatch_ws_bytes(T, G);
 }
 
+int mcl4moe_ep_dispatch_count(const int32_t* topk_idx, const uint8_t* valid, int T, int k, int G, int E_loc,
+                              int32_t* send_counts, void* workspace, size_t workspace_bytes,
+                              mcl4moe_stream_t stream) {
+  int st = check_ep_shape(256, k, G, E_loc, 256);
+  if (st != MCL4MOE_OK) return st;
+  if (T < 0 || !send_counts || !workspace || (T > 0 && !topk_idx)) return MCL4MOE_ERR_INVALID;
+  if (workspace_bytes < dispatch_ws_bytes(T, G)) return MCL4MOE_ERR_WORKSPACE;
+  cudaStream_t s = stream;
+  if (cudaMemsetAsync(send_counts, 0, sizeof(int32_t) * 2 * G, s) != cudaSuccess) return MCL4MOE_ERR_CUDA;
+  if (T == 0) return MCL4MOE_OK;
+  int32_t* grp = static_cast<int32_t*>(workspace);
+  const int W = (T + 31) / 32;
+  cudaError_t e = launch_pdl(ep_count_kernel, dim3((W + 7) / 8), dim3(256), 0, s, topk_idx, valid, T, k, G, E_loc,
+                             grp, send_counts + G);
+  if (e == cudaSuccess) e = launch_pdl(ep_column_scan_kernel, dim3(G), dim3(256), 0, s, grp, W, G, send_counts);
+  return e == cudaSuccess ? MCL4MOE_OK : MCL4MOE_ERR_CUDA;
+}
+
+int mcl4moe_ep_dispatch_pack(const uint16_t* x, const int32_t* topk_idx, const float* topk_w, const uint8_t* valid,
+                             int T, int d, int k, int G, int E_loc, const int32_t* send_counts, int32_t* send_pos,
+                             uint8_t* send_buf, void* workspace, size_t workspace_bytes, mcl4moe_stream_t stream) {
+  int st = check_ep_shape(d, k, G, E_loc, 256);
+  if (st != MCL4MOE_OK) return st;
+  if (T < 0 || !send_counts || !workspace || (T > 0 && (!x || !topk_idx || !topk_w || !send_pos || !send_buf)))
+    return MCL4MOE_ERR_INVALID;
+  if (!aligned16(x) || !aligned16(send_buf)) return MCL4MOE_ERR_INVALID;
+  if (workspace_bytes < dispatch_ws_bytes(T, G)) return MCL4MOE_ERR_WORKSPACE;
+  if (T == 0) return MCL4MOE_OK;
+  const int W = (T + 31) / 32;
+  return launch_pdl(ep_pack_kernel, dim3(W), dim3(256), 0, stream, x, topk_idx, topk_w, valid, T, d, k, G, E_loc,
+                    static_cast<const int32_t*>(workspace), send_counts, send_buf, send_pos) == cudaSuccess
+             ? MCL4MOE_OK
+             : MCL4MOE_ERR_CUDA;
+}
+
 int mcl4moe_ep_dispatch(const uint16_t* x, const int32_t* topk_idx, const float* topk_w, const uint8_t* valid, int T,
                         int d, int k, int G, int E_loc, int32_t* send_counts, int32_t* send_pos, uint8_t* send_buf,
                         void* workspace, size_t workspace_bytes, mcl4moe_stream_t stream) {
@@ -507,17 +563,11 @@ int mcl4moe_ep_dispatch(const uint16_t* x, const int32_t* topk_idx, const float*
   if (T < 0 || !send_counts || !workspace || (T > 0 && (!x || !topk_idx || !topk_w || !send_pos || !send_buf)))
     return MCL4MOE_ERR_INVALID;
   if (!aligned16(x) || !aligned16(send_buf)) return MCL4MOE_ERR_INVALID;
-  if (workspace_bytes < dispatch_ws_bytes(T, G)) return MCL4MOE_ERR_WORKSPACE;
-  cudaStream_t s = stream;
-  if (cudaMemsetAsync(send_counts, 0, sizeof(int32_t) * 2 * G, s) != cudaSuccess) return MCL4MOE_ERR_CUDA;
-  if (T == 0) return MCL4MOE_OK;
-  int32_t* grp = static_cast<int32_t*>(workspace);
-  const int W = (T + 31) / 32;
-  ep_count_kernel<<<(W + 7) / 8, 256, 0, s>>>(topk_idx, valid, T, k, G, E_loc, grp, send_counts + G);
-  ep_column_scan_kernel<<<G, 256, 0, s>>>(grp, W, G, send_counts);
-  ep_pack_kernel<<<W, 256, 0, s>>>(x, topk_idx, topk_w, valid, T, d, k, G, E_loc, grp, send_counts, send_buf,
-                                   send_pos);
-  return cudaGetLastError() == cudaSuccess ? MCL4MOE_OK : MCL4MOE_ERR_CUDA;
+  if ((st = mcl4moe_ep_dispatch_count(topk_idx, valid, T, k, G, E_loc, send_counts, workspace, workspace_bytes,
+                                      stream)) != MCL4MOE_OK)
+    return st;
+  return mcl4moe_ep_dispatch_pack(x, topk_idx, topk_w, valid, T, d, k, G, E_loc, send_counts, send_pos, send_buf,
+                                  workspace, workspace_bytes, stream);
 }
 
 size_t mcl4moe_ep_experts_workspace_size(int R, int slots, int d, int k, int E_loc, int F) {
@@ -546,10 +596,11 @@ int ep_experts_impl(const uint8_t* recv_buf, int R, int slots, int d, int k, int
   cudaStream_t s = stream;
   int32_t* err = error_word ? error_word : w.err;
   if (!error_word && cudaMemsetAsync(w.err, 0, sizeof(int32_t), s) != cudaSuccess) return MCL4MOE_ERR_CUDA;
-  if (E_loc <= 32) launch_recv_layout<1>(recv_buf, R, d, k, E_loc, w, s);
-  else if (E_loc <= 64) launch_recv_layout<2>(recv_buf, R, d, k, E_loc, w, s);
-  else if (E_loc <= 128) launch_recv_layout<4>(recv_buf, R, d, k, E_loc, w, s);
-  else launch_recv_layout<8>(recv_buf, R, d, k, E_loc, w, s);
+  const cudaError_t le = E_loc <= 32    ? launch_recv_layout<1>(recv_buf, R, d, k, E_loc, w, s)
+                         : E_loc <= 64  ? launch_recv_layout<2>(recv_buf, R, d, k, E_loc, w, s)
+                         : E_loc <= 128 ? launch_recv_layout<4>(recv_buf, R, d, k, E_loc, w, s)
+                                        : launch_recv_layout<8>(recv_buf, R, d, k, E_loc, w, s);
+  if (le != cudaSuccess) return MCL4MOE_ERR_CUDA;
   if (cudaGetLastError() != cudaSuccess) return MCL4MOE_ERR_CUDA;
 
   GemmArgs g1{};
@@ -585,10 +636,14 @@ int ep_experts_impl(const uint8_t* recv_buf, int R, int slots, int d, int k, int
   g2.err = err;
   if ((st = launch_grouped_gemm(w.hq, w.mcap, w_dn, g2, s)) != MCL4MOE_OK) return st;
   if (remote)
-    ep_partial_remote_kernel<<<(R + 7) / 8, 256, 0, s>>>(w.y, w.slot_pos, R, k, d, *remote);
-  else
-    ep_partial_kernel<<<(R + 7) / 8, 256, 0, s>>>(w.y, w.slot_pos, R, k, d, partial);
-  return cudaGetLastError() == cudaSuccess ? MCL4MOE_OK : MCL4MOE_ERR_CUDA;
+    return launch_pdl(ep_partial_remote_kernel, dim3((R + 7) / 8), dim3(256), 0, s, w.y, w.slot_pos, R, k, d,
+                      *remote) == cudaSuccess
+               ? MCL4MOE_OK
+               : MCL4MOE_ERR_CUDA;
+  return launch_pdl(ep_partial_kernel, dim3((R + 7) / 8), dim3(256), 0, s, w.y, w.slot_pos, R, k, d, partial) ==
+                 cudaSuccess
+             ? MCL4MOE_OK
+             : MCL4MOE_ERR_CUDA;
 }
 
 }  // namespace
@@ -627,8 +682,10 @@ int mcl4moe_ep_combine(const uint16_t* back_buf, const int32_t* send_pos, int T,
   if (T < 0 || d <= 0 || d % 256 != 0 || G <= 0 || G > kMaxRanks) return MCL4MOE_ERR_INVALID;
   if (T == 0) return MCL4MOE_OK;
   if (!send_pos || !out || !aligned16(out) || (back_buf && !aligned16(back_buf))) return MCL4MOE_ERR_INVALID;
-  ep_final_kernel<<<(T + 7) / 8, 256, 0, stream>>>(back_buf, send_pos, T, d, G, out);
-  return cudaGetLastError() == cudaSuccess ? MCL4MOE_OK : MCL4MOE_ERR_CUDA;
+  return launch_pdl(ep_final_kernel, dim3((T + 7) / 8), dim3(256), 0, stream, back_buf, send_pos, T, d, G, out) ==
+                 cudaSuccess
+             ? MCL4MOE_OK
+             : MCL4MOE_ERR_CUDA;
 }
 
 }  // extern "C"

@@ -530,13 +530,8 @@ int resident_pairs() {
 template <int MODE>
 int launch_mode(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ty, const GemmArgs& args,
                 cudaStream_t stream) {
-  static bool configured = false;
-  if (!configured) {
-    if (cudaFuncSetAttribute(grouped_gemm_fp4_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             int(Cfg<MODE>::kSmem)) != cudaSuccess)
-      return MCL4MOE_ERR_CUDA;
-    configured = true;
-  }
+  static std::atomic<uint64_t> configured{0};
+  if (!raise_smem_limit(grouped_gemm_fp4_kernel<MODE>, int(Cfg<MODE>::kSmem), configured)) return MCL4MOE_ERR_CUDA;
   const int pairs = resident_pairs<MODE>();
   return launch_pdl(grouped_gemm_fp4_kernel<MODE>, dim3(2 * pairs), dim3(kThreads), Cfg<MODE>::kSmem, stream, ta, tb,
                     ty, args) == cudaSuccess

@@ -1,6 +1,7 @@
 // Internal launch interface shared by the kernel files and the C ABI (api.cu).
 #pragma once
 
+#include <atomic>
 #include <utility>
 
 #include "common.cuh"
@@ -18,7 +19,7 @@ struct RouteWorkspace {
   int32_t* chunk_excl;   // [C, E]  chunk counts, then (after the scan) exclusive prefix over chunks
   float* part_probs;     // [C, E]  per-chunk sum of routed probabilities
   float* part_misc;      // [C, 2]  per-chunk sum of lse^2 and routed-token count
-  int32_t* pad_start;    // [E + 1] padded row start of each expert (multiple of 128)
+  int32_t* pad_start;    // [E + 1] padded row start of each expert (multiple of kSegRows)
   int32_t* offs_start;   // [E]     unpadded row start of each expert
   int32_t* counts;       // [E]     routed slots per expert
   float* probs_sum;      // [E]     sum of routed probabilities per expert
@@ -118,6 +119,21 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// Raise a kernel's dynamic shared-memory limit on the current device, once per
+// device: the attribute belongs to the kernel's instance in each device's
+// context, so a process that drives several GPUs sets it on every one.  ``done``
+// is a bitmask of the devices (ordinal < 64) already configured.
+template <typename... KArgs>
+inline bool raise_smem_limit(void (*kernel)(KArgs...), int bytes, std::atomic<uint64_t>& done) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  const uint64_t bit = dev < 64 ? (uint64_t(1) << dev) : 0;
+  if (bit != 0 && (done.load(std::memory_order_acquire) & bit) != 0) return true;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return false;
+  done.fetch_or(bit, std::memory_order_release);
+  return true;
 }
 
 // Expert segments of the grouped GEMMs start on multiples of kSegRows rows: a

@@ -84,4 +84,18 @@ int mcl4moe_copy_async(void* dst, const void* src, size_t bytes, mcl4moe_stream_
                                                                                            : MCL4MOE_ERR_CUDA;
 }
 
+int mcl4moe_copy_list_async(void* const* dst, const void* const* src, const uint64_t* bytes, int n,
+                            mcl4moe_stream_t const* streams, int n_streams) {
+  if (n < 0 || n_streams <= 0 || (n > 0 && (!dst || !src || !bytes || !streams))) return MCL4MOE_ERR_INVALID;
+  for (int i = 0; i < n; ++i)
+    if (bytes[i] != 0 && (!dst[i] || !src[i])) return MCL4MOE_ERR_INVALID;
+  for (int i = 0; i < n; ++i) {
+    if (bytes[i] == 0) continue;
+    if (cudaMemcpyAsync(dst[i], src[i], size_t(bytes[i]), cudaMemcpyDeviceToDevice, streams[i % n_streams]) !=
+        cudaSuccess)
+      return MCL4MOE_ERR_CUDA;
+  }
+  return MCL4MOE_OK;
+}
+
 }  // extern "C"

@@ -593,13 +593,8 @@ int launch_router_t(const uint16_t* x, const float* wr, const float* bias, const
   const int C = (a.T + kRouteTokens - 1) / kRouteTokens;
   if (logits_in != nullptr) {
     const size_t smem = tail_smem_bytes(a.E, a.k);
-    static bool configured = false;
-    if (!configured) {
-      if (cudaFuncSetAttribute(router_logits_kernel<EW>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
-          cudaSuccess)
-        return MCL4MOE_ERR_CUDA;
-      configured = true;
-    }
+    static std::atomic<uint64_t> configured{0};
+    if (!raise_smem_limit(router_logits_kernel<EW>, 200 * 1024, configured)) return MCL4MOE_ERR_CUDA;
     router_logits_kernel<EW><<<C, kTailThreads, smem, stream>>>(logits_in, nullptr, a, ws);  // final logits
     return cudaGetLastError() == cudaSuccess ? MCL4MOE_OK : MCL4MOE_ERR_CUDA;
   }
@@ -623,13 +618,8 @@ int launch_router_t(const uint16_t* x, const float* wr, const float* bias, const
   uint32_t cols = 32;
   while (cols < uint32_t(a.fused ? 3 * a.E_pad : a.E_pad)) cols <<= 1;
   a.tmem_cols = cols;
-  static bool configured = false;
-  if (!configured) {
-    if (cudaFuncSetAttribute(router_tc_kernel<EW>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) !=
-        cudaSuccess)
-      return MCL4MOE_ERR_CUDA;
-    configured = true;
-  }
+  static std::atomic<uint64_t> configured{0};
+  if (!raise_smem_limit(router_tc_kernel<EW>, 227 * 1024, configured)) return MCL4MOE_ERR_CUDA;
   if (smem > 227 * 1024) return MCL4MOE_ERR_UNSUPPORTED;
   if (launch_pdl(router_tc_kernel<EW>, dim3(C), dim3(kTcThreads), smem, stream, tx, tw, a, ws) != cudaSuccess)
     return MCL4MOE_ERR_CUDA;
@@ -660,13 +650,8 @@ int launch_route(const uint16_t* x, const float* wr, const float* bias, const fl
     if (logits_in == nullptr && T <= kRouteGemvMaxT && ws.small_logits != nullptr) {
       const size_t smem = sizeof(uint16_t) * 8 * size_t(d);
       if (smem > 48 * 1024) {
-        static bool configured = false;
-        if (!configured) {
-          if (cudaFuncSetAttribute(router_gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
-              cudaSuccess)
-            return MCL4MOE_ERR_CUDA;
-          configured = true;
-        }
+        static std::atomic<uint64_t> configured{0};
+        if (!raise_smem_limit(router_gemv_kernel, 200 * 1024, configured)) return MCL4MOE_ERR_CUDA;
       }
       if (smem > 200 * 1024) return MCL4MOE_ERR_UNSUPPORTED;
       router_gemv_kernel<<<dim3((T + 7) / 8, (E + 7) / 8), 256, smem, stream>>>(x, wr, bias, T, d, E,

@@ -90,20 +90,52 @@ class CudaEPOps:
                                            ws.numel(), _stream_handle()), "mcl4moe_ep_dispatch")
         return send_buf[: T * G * rb].view(T * G, rb), counts, pos
 
-    def prepare(self, experts: nn.ModuleList) -> None:
-        """Validate / refresh the NVFP4 weight caches of this rank's experts.  Called
-        before routing, so this host work overlaps the device work instead of
-        following the host synchronisation of the exchange."""
-        self._caches = (get_or_build_grouped_cache(experts, "up_proj"), get_or_build_grouped_cache(experts, "down_proj"))
+    def dispatch_count(self, idx: Tensor, valid: Tensor | None, G: int, E_loc: int, slot: int = 0,
+                       out: Tensor | None = None) -> Tensor:
+        """First half of ``dispatch``: the rows and slots bound for each rank (device int32 [2G],
+        written to ``out`` when given)."""
+        lib = _lib.load()
+        T, k = idx.shape
+        dev = idx.device
+        counts = out if out is not None else torch.empty((2 * G,), dtype=torch.int32, device=dev)
+        assert counts.is_contiguous() and counts.numel() == 2 * G and counts.dtype == torch.int32
+        ws = self._scratch(f"dispatch{slot}", lib.mcl4moe_ep_dispatch_workspace_size(T, G), dev)
+        _lib.check(lib.mcl4moe_ep_dispatch_count(idx.data_ptr(), None if valid is None else valid.data_ptr(), T, k,
+                                                 G, E_loc, counts.data_ptr(), ws.data_ptr(), ws.numel(),
+                                                 _stream_handle()), "mcl4moe_ep_dispatch_count")
+        return counts
 
-    def experts(self, recv: Tensor, R: int, slots: int, d: int, k: int, experts: nn.ModuleList) -> Tensor:
+    def dispatch_pack(self, x: Tensor, idx: Tensor, w: Tensor, valid: Tensor | None, G: int, E_loc: int,
+                      counts: Tensor, slot: int = 0):
+        """Second half of ``dispatch`` (after ``dispatch_count`` with the same ``slot``)."""
+        lib = _lib.load()
+        T, d = x.shape
+        k = idx.shape[1]
+        dev = x.device
+        rb = self.row_bytes(d, k)
+        send_buf = self._scratch(f"send{slot}", T * G * rb, dev)
+        pos = torch.empty((T, G), dtype=torch.int32, device=dev)
+        ws = self._scratch(f"dispatch{slot}", lib.mcl4moe_ep_dispatch_workspace_size(T, G), dev)
+        _lib.check(lib.mcl4moe_ep_dispatch_pack(x.data_ptr(), idx.data_ptr(), w.data_ptr(),
+                                                None if valid is None else valid.data_ptr(), T, d, k, G, E_loc,
+                                                counts.data_ptr(), pos.data_ptr(), send_buf.data_ptr(), ws.data_ptr(),
+                                                ws.numel(), _stream_handle()), "mcl4moe_ep_dispatch_pack")
+        return send_buf[: T * G * rb].view(T * G, rb), counts, pos
+
+    def prepare(self, experts: nn.ModuleList) -> tuple:
+        """Validate / refresh the NVFP4 weight caches of this rank's experts and return
+        them for the ``experts`` calls of one forward.  Called before routing, so this
+        host work overlaps the device work instead of following the host
+        synchronisation of the exchange, and runs once per forward, not per chunk."""
+        return get_or_build_grouped_cache(experts, "up_proj"), get_or_build_grouped_cache(experts, "down_proj")
+
+    def experts(self, recv: Tensor, R: int, slots: int, d: int, k: int, experts: nn.ModuleList,
+                caches: tuple | None = None) -> Tensor:
         lib = _lib.load()
         dev = recv.device
         E_loc = len(experts)
         F = experts[0].down_proj.weight.shape[1]
-        up, dn = getattr(self, "_caches", None) or (get_or_build_grouped_cache(experts, "up_proj"),
-                                                    get_or_build_grouped_cache(experts, "down_proj"))
-        self._caches = None
+        up, dn = caches or self.prepare(experts)
         partial = torch.empty((R, d), dtype=torch.bfloat16, device=dev)
         ws = self._scratch("experts", lib.mcl4moe_ep_experts_workspace_size(R, slots, d, k, E_loc, F), dev)
         _lib.check(lib.mcl4moe_ep_experts(recv.data_ptr(), R, slots, d, k, E_loc, F, up.packed.data_ptr(),
@@ -113,16 +145,14 @@ class CudaEPOps:
         return partial
 
     def experts_to_peers(self, recv: Tensor, R: int, slots: int, d: int, k: int, experts: nn.ModuleList,
-                         seg_start: list[int], dst: list[int]) -> None:
+                         seg_start: list[int], dst: list[int], caches: tuple | None = None) -> None:
         """The experts step with each partial-sum row stored straight to ``dst[s]``
         (a peer mapping for rows from another rank)."""
         lib = _lib.load()
         dev = recv.device
         E_loc = len(experts)
         F = experts[0].down_proj.weight.shape[1]
-        up, dn = getattr(self, "_caches", None) or (get_or_build_grouped_cache(experts, "up_proj"),
-                                                    get_or_build_grouped_cache(experts, "down_proj"))
-        self._caches = None
+        up, dn = caches or self.prepare(experts)
         G = len(dst)
         starts = (ctypes.c_int32 * (G + 1))(*seg_start)
         ptrs = (ctypes.c_void_p * G)(*dst)
@@ -161,7 +191,9 @@ class PeerExchange:
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.device = device
-        self.streams = [torch.cuda.Stream(device=device) for _ in range(2)]
+        # two copy streams per direction (dispatched rows, returned partial sums), so a
+        # chunk's rows never queue behind the previous chunk's partial sums
+        self.streams = [torch.cuda.Stream(device=device) for _ in range(4)]
         self.token = torch.zeros((1,), dtype=torch.float32, device=device)
         self.arena: Tensor | None = None
         self.regions: dict[str, tuple[int, int]] = {}
@@ -219,35 +251,37 @@ class PeerExchange:
         assert nbytes <= size
         return self.arena[off:off + nbytes]
 
-    def issue(self, name: str, pieces: list[tuple[int, Tensor, int]]) -> list:
-        """Start copying each ``(dest, src, byte_offset)`` into region ``name`` of
-        ``dest`` once the current stream has produced ``src``; returns the events
-        that mark the end of these copies (for ``complete``).
+    def issue(self, name: str, pieces: list[tuple[int, int, int, int]], lane: int = 0) -> list:
+        """Start the copies ``(dest, src_address, nbytes, byte_offset)`` into region
+        ``name`` of ``dest`` once the current stream has produced their sources;
+        returns the events that mark the end of these copies (for ``complete``).
+        The caller keeps the source memory alive until ``complete``.
 
         Schedule: destinations in the staggered order me+1, me+2, ... (the local
         copy last), alternating over two streams.  At any moment every rank then
         targets a different rank; issuing all copies at once, or in the same order
         on every rank, piles the traffic onto the same destinations (measured on
-        8 x B200: 200-430 GB/s per GPU against 660 GB/s staggered)."""
-        lib = _lib.load()
+        8 x B200: 200-430 GB/s per GPU against 660 GB/s staggered).  ``lane`` 0 or 1
+        picks the stream pair (one per direction of the exchange).  One library call
+        issues the whole list."""
         cur = torch.cuda.current_stream(self.device)
         ready = torch.cuda.Event()
         ready.record(cur)
         off0, size = self.regions[name]
-        order = sorted(pieces, key=lambda pc: (pc[0] - self.rank - 1) % self.world)
-        lanes = self.streams[:2]
+        order = sorted((pc for pc in pieces if pc[2] > 0), key=lambda pc: (pc[0] - self.rank - 1) % self.world)
+        lanes = self.streams[2 * lane:2 * lane + 2]
         for st in lanes:
             st.wait_event(ready)
-        for i, (dest, src, byte_off) in enumerate(order):
-            n = src.numel() * src.element_size()
-            if n == 0:
-                continue
-            assert byte_off + n <= size, (name, byte_off, n, size)
-            st = lanes[i % len(lanes)]
-            _lib.check(lib.mcl4moe_copy_async(ctypes.c_void_p(self.peer_base[dest] + off0 + byte_off),
-                                              ctypes.c_void_p(src.data_ptr()), n, st.cuda_stream),
-                       "mcl4moe_copy_async")
-            src.record_stream(st)
+        n = len(order)
+        if n:
+            for dest, _, nbytes, byte_off in order:
+                assert byte_off + nbytes <= size, (name, byte_off, nbytes, size)
+            dst = (ctypes.c_void_p * n)(*[self.peer_base[dest] + off0 + off for dest, _, _, off in order])
+            src = (ctypes.c_void_p * n)(*[a for _, a, _, _ in order])
+            nb = (ctypes.c_uint64 * n)(*[b for _, _, b, _ in order])
+            sts = (ctypes.c_void_p * len(lanes))(*[st.cuda_stream for st in lanes])
+            _lib.check(_lib.load().mcl4moe_copy_list_async(dst, src, nb, n, sts, len(lanes)),
+                       "mcl4moe_copy_list_async")
         done = []
         for st in lanes:
             ev = torch.cuda.Event()
@@ -264,8 +298,9 @@ class PeerExchange:
             cur.wait_event(ev)
         dist.all_reduce(self.token, group=self.group)
 
-    def put(self, name: str, pieces: list[tuple[int, Tensor, int]]) -> None:
-        self.complete(self.issue(name, pieces))
+    def put(self, name: str, pieces: list[tuple[int, int, int, int]], lane: int = 0) -> None:
+        self.complete(self.issue(name, pieces, lane))
+
 
 class ExpertParallelMoE(nn.Module):
     """SparseMoE whose experts are sharded over ``group`` (one process per GPU).
@@ -305,11 +340,15 @@ class ExpertParallelMoE(nn.Module):
         # "collective": all-to-all through torch.distributed (any backend, e.g. gloo)
         self.transport = transport
         self._peer: PeerExchange | None = None
-        # the batch is cut into this many token chunks; with the peer transport the
-        # exchange of one chunk overlaps the experts step of another.  0 = automatic:
-        # 1 up to 2 ranks (the exchange is small and smaller GEMMs cost more than the
-        # overlap gains), 2 beyond (measured on B200 at 2 and 8 ranks)
+        # the batch is cut into token chunks; with the peer transport the exchange of one
+        # chunk overlaps the experts step of another.  ``chunks`` > 0: that many equal
+        # chunks; ``chunk_weights`` (relative sizes) overrides it.  0 = automatic: one
+        # chunk up to 2 ranks (the exchange is small and smaller GEMMs cost more than
+        # the overlap gains), two equal chunks beyond (measured on 8 x B200: 2.9-3.2 ms
+        # against 3.5 ms for 1 chunk, 3.1-3.3 ms for 3, 4 or 6, and 3.0-3.3 ms for
+        # uneven splits 0.55:0.45 to 0.65:0.35)
         self.chunks = int(chunks) if chunks > 0 else (1 if self.world <= 2 else 2)
+        self.chunk_weights: list[float] | None = None
         self.min_chunk_tokens = 1024
         # optional 8 CUDA events recorded around the seven steps (route, dispatch,
         # count exchange, row exchange, experts, partial exchange, combine), for stage timing
@@ -355,31 +394,49 @@ class ExpertParallelMoE(nn.Module):
         ev = self.stage_events
         mark = (lambda i: ev[i].record()) if ev is not None else (lambda i: None)
         mark(0)
-        if hasattr(self.ops, "prepare"):
-            self.ops.prepare(self.experts)
+        caches = self.ops.prepare(self.experts) if hasattr(self.ops, "prepare") else None
         idx, w, stats = self.ops.route(xb, wr, bias, vmask, k, self.norm_topk_prob)
         mark(1)
-        n = max(1, min(self.chunks, T // self.min_chunk_tokens)) if T > 0 else 1
-        bounds = [(T * c // n, T * (c + 1) // n) for c in range(n)]
-        disp = []
-        for c, (lo, hi) in enumerate(bounds):
-            vm = None if vmask is None else vmask[lo:hi]
-            disp.append(self.ops.dispatch(xb[lo:hi], idx[lo:hi], w[lo:hi], vm, G, E_loc, c))
-        mark(2)
+        bounds = self._chunk_bounds(T)
         out = torch.empty((T, d), dtype=torch.bfloat16, device=xb.device)
         use_peer = self.transport == "peer" or (
             self.transport == "auto" and xb.is_cuda and dist.get_backend(self.group) == "nccl")
         if use_peer:
-            backs = self._exchange_peer(disp, bounds, d, k, mark)
+            disp, backs = self._exchange_peer(xb, idx, w, vmask, bounds, caches, mark)
         else:
-            backs = self._exchange_collective(disp, d, k, mark)
+            disp = []
+            for c, (lo, hi) in enumerate(bounds):
+                vm = None if vmask is None else vmask[lo:hi]
+                disp.append(self.ops.dispatch(xb[lo:hi], idx[lo:hi], w[lo:hi], vm, G, E_loc, c))
+            mark(2)
+            backs = self._exchange_collective(disp, d, k, caches, mark)
         mark(6)
         for c, (lo, hi) in enumerate(bounds):
             self.ops.combine(backs[c], disp[c][2], hi - lo, d, G, out[lo:hi])
         mark(7)
         return out.to(x.dtype).view_as(x), stats[0], stats[1], stats[3:3 + self.num_experts]
 
-    def _exchange_collective(self, disp: list, d: int, k: int, mark) -> list[Tensor]:
+    def _chunk_bounds(self, T: int) -> list[tuple[int, int]]:
+        """Token ranges of the chunks (``chunk_weights`` or ``chunks`` equal parts); one
+        chunk when a chunk would hold fewer than ``min_chunk_tokens`` tokens."""
+        weights = self.chunk_weights or [1.0] * max(1, self.chunks)
+        if T <= 0 or T < len(weights) * self.min_chunk_tokens:
+            if T <= 0 or T < 2 * self.min_chunk_tokens:
+                return [(0, max(T, 0))]
+            weights = [1.0] * (T // self.min_chunk_tokens)
+        total, acc, cuts = float(sum(weights)), 0.0, [0]
+        for wgt in weights[:-1]:
+            acc += wgt
+            cuts.append(int(round(T * acc / total)))
+        cuts.append(T)
+        return [(lo, hi) for lo, hi in zip(cuts[:-1], cuts[1:])]
+
+    def _experts(self, recv: Tensor, R: int, slots: int, d: int, k: int, caches) -> Tensor:
+        if caches is None:
+            return self.ops.experts(recv, R, slots, d, k, self.experts)
+        return self.ops.experts(recv, R, slots, d, k, self.experts, caches)
+
+    def _exchange_collective(self, disp: list, d: int, k: int, caches, mark) -> list[Tensor]:
         """Rows out and partial sums back through ``all_to_all_single``, chunk after chunk."""
         G = self.world
         backs, ex = [], dict(rows_to=[0] * G, rows_from=[0] * G, slots=[0])
@@ -396,7 +453,7 @@ class ExpertParallelMoE(nn.Module):
             sent = sum(rows_to)
             recv = torch.empty((R, send.shape[1]), dtype=torch.uint8, device=send.device)
             self._all_to_all(recv, send[:sent], rows_from, rows_to)
-            partial = self.ops.experts(recv, R, slots_here, d, k, self.experts)
+            partial = self._experts(recv, R, slots_here, d, k, caches)
             back = torch.empty((sent, d), dtype=torch.bfloat16, device=partial.device)
             self._all_to_all(back, partial, rows_to, rows_from)
             backs.append(back)
@@ -408,20 +465,60 @@ class ExpertParallelMoE(nn.Module):
         mark(5)
         return backs
 
-    def _exchange_peer(self, disp: list, bounds: list, d: int, k: int, mark) -> list[Tensor]:
-        """Rows out and partial sums back through peer memory (copy engines), the
-        exchange of one chunk overlapping the experts step of another."""
-        G, me, n = self.world, self.rank, len(disp)
-        dev = disp[0][1].device
+    def _counts_tab(self, cnts: Tensor, bounds: list) -> tuple[Tensor, Any]:
+        """All-gather every rank's per-chunk counts and chunk sizes and start their
+        copy to pinned host memory; returns the host buffer and the event that marks
+        its arrival, so the rows can be packed while the host waits."""
+        G, n = self.world, len(bounds)
+        dev = cnts.device
+        key = (tuple(bounds), str(dev))
+        if getattr(self, "_sizes_key", None) != key:
+            self._sizes_dev = torch.tensor([hi - lo for lo, hi in bounds], dtype=torch.int32, device=dev)
+            self._sizes_key = key
+        cnts[:, 2 * G].copy_(self._sizes_dev)
+        allc = torch.empty((G * n * (2 * G + 1),), dtype=torch.int32, device=dev)
+        dist.all_gather_into_tensor(allc, cnts.view(-1), group=self.group)
+        host = getattr(self, "_tab_host", None)
+        if host is None or host.numel() < allc.numel():
+            host = torch.empty((allc.numel(),), dtype=torch.int32, pin_memory=True)
+            self._tab_host = host
+        host = host[: allc.numel()]
+        host.copy_(allc, non_blocking=True)
+        arrived = torch.cuda.Event()
+        arrived.record()
+        return host, arrived
+
+    def _exchange_peer(self, xb: Tensor, idx: Tensor, w: Tensor, vmask: Tensor | None, bounds: list, caches,
+                       mark) -> tuple[list, list[Tensor]]:
+        """Dispatch, rows out and partial sums back through peer memory (copy
+        engines), the exchange of one chunk overlapping the experts step of another.
+
+        The chunks' row / slot counts are counted first and exchanged; the host
+        reads them (it needs the copy sizes) while the rows are packed."""
+        G, me, n = self.world, self.rank, len(bounds)
+        T, d = xb.shape
+        k, E_loc = idx.shape[1], self.experts_per_rank
+        dev = xb.device
         if self._peer is None:
             self._peer = PeerExchange(self.group, dev)
         px = self._peer
-        # every rank's per-chunk, per-destination row and slot counts and chunk sizes: one gather
-        mine = torch.cat([torch.cat([cnt, torch.tensor([hi - lo], dtype=torch.int32, device=dev)])
-                          for (_, cnt, _), (lo, hi) in zip(disp, bounds)])
-        allc = torch.empty((G, n * (2 * G + 1)), dtype=torch.int32, device=dev)
-        dist.all_gather_into_tensor(allc, mine, group=self.group)
-        tab = allc.cpu().view(G, n, 2 * G + 1).tolist()
+        vm = (lambda lo, hi: None) if vmask is None else (lambda lo, hi: vmask[lo:hi])
+        cnts = torch.empty((n, 2 * G + 1), dtype=torch.int32, device=dev)
+        if hasattr(self.ops, "dispatch_count"):
+            for c, (lo, hi) in enumerate(bounds):
+                self.ops.dispatch_count(idx[lo:hi], vm(lo, hi), G, E_loc, c, out=cnts[c, :2 * G])
+            host, arrived = self._counts_tab(cnts, bounds)
+            disp = [self.ops.dispatch_pack(xb[lo:hi], idx[lo:hi], w[lo:hi], vm(lo, hi), G, E_loc, cnts[c, :2 * G], c)
+                    for c, (lo, hi) in enumerate(bounds)]
+        else:
+            disp = [self.ops.dispatch(xb[lo:hi], idx[lo:hi], w[lo:hi], vm(lo, hi), G, E_loc, c)
+                    for c, (lo, hi) in enumerate(bounds)]
+            for c in range(n):
+                cnts[c, :2 * G].copy_(disp[c][1])
+            host, arrived = self._counts_tab(cnts, bounds)
+        mark(2)
+        arrived.synchronize()
+        tab = host.view(G, n, 2 * G + 1).tolist()
         mark(3)
         rb = disp[0][0].shape[1]
         sizes = {}
@@ -438,26 +535,26 @@ class ExpertParallelMoE(nn.Module):
         self.last_exchange = ex
 
         def rows_pieces(c):  # my rows for g go after the rows of lower ranks in g's region
-            send, pieces, start = disp[c][0], [], 0
+            base, pieces, start = disp[c][0].data_ptr(), [], 0
             for g in range(G):
                 cnt = tab[me][c][g]
                 at = sum(tab[s][c][g] for s in range(me))
-                pieces.append((g, send[start:start + cnt].reshape(-1), at * rb))
+                pieces.append((g, base + start * rb, cnt * rb, at * rb))
                 start += cnt
             return pieces
 
         def back_pieces(c, partial):  # partials of the rows from s go where s keeps its segment for me
-            pieces, at_here = [], 0
+            base, pieces, at_here = partial.data_ptr(), [], 0
             for s in range(G):
                 cnt = tab[s][c][me]
                 at = sum(tab[s][c][g] for g in range(me))
-                pieces.append((s, partial[at_here:at_here + cnt].reshape(-1), at * d * 2))
+                pieces.append((s, base + at_here * d * 2, cnt * d * 2, at * d * 2))
                 at_here += cnt
             return pieces
 
         px.complete(px.issue("rows0", rows_pieces(0)))
         mark(4)
-        back_events = []
+        back_events, partials = [], []  # the partial tensors stay referenced until their copies are complete
         for c in range(n):
             nxt = px.issue(f"rows{c + 1}", rows_pieces(c + 1)) if c + 1 < n else None
             R = sum(tab[s][c][me] for s in range(G))
@@ -469,16 +566,18 @@ class ExpertParallelMoE(nn.Module):
                 for s in range(G):
                     seg.append(seg[-1] + tab[s][c][me])
                 dst = [px.address(s, f"back{c}", sum(tab[s][c][g] for g in range(me)) * d * 2) for s in range(G)]
-                self.ops.experts_to_peers(recv, R, slots_here, d, k, self.experts, seg, dst)
+                self.ops.experts_to_peers(recv, R, slots_here, d, k, self.experts, seg, dst, caches)
             else:
-                partial = self.ops.experts(recv, R, slots_here, d, k, self.experts)
-                back_events += px.issue(f"back{c}", back_pieces(c, partial))
+                partial = self._experts(recv, R, slots_here, d, k, caches)
+                partials.append(partial)
+                back_events += px.issue(f"back{c}", back_pieces(c, partial), lane=1)
             if nxt is not None:
                 px.complete(nxt)
         mark(5)
         px.complete(back_events)
+        del partials
         backs = []
         for c in range(n):
             sent = sum(tab[me][c][g] for g in range(G))
             backs.append(px.local(f"back{c}", sent * d * 2).view(torch.bfloat16).view(sent, d))
-        return backs
+        return disp, backs

@@ -112,3 +112,26 @@ def test_masked_tokens_and_a_rank_without_rows(moe_pkg):
     a, b = out.float(), ref["out"].float()
     assert (torch.linalg.norm(a - b) / torch.linalg.norm(b)).item() < 5e-3
     assert torch.all(a[valid == 0] == 0)
+
+
+def test_split_dispatch_matches_one_call(moe_pkg):
+    """dispatch_count + dispatch_pack (counts exchanged in between) write the same
+    counts, positions and row bytes as the one-call dispatch."""
+    c = moe_case(34, 1000, 512, 16, 4, 512, valid_frac=0.8)
+    moe = build_module(moe_pkg, c, DEV)
+    x = x_tensor(c, DEV)
+    valid = torch.from_numpy(c["valid"]).to(DEV)
+    ops = moe_pkg.CudaEPOps()
+    wr = moe.router.weight.detach().float().contiguous()
+    idx, w, _ = ops.route(x, wr, None, valid, 4, moe.norm_topk_prob)
+    for G in (1, 2, 4, 8):
+        send, counts, pos = ops.dispatch(x, idx, w, valid, G, 16 // G, slot=0)
+        send, counts, pos = send.clone(), counts.clone(), pos.clone()
+        out = torch.full((2 * G,), -7, dtype=torch.int32, device=DEV)
+        cnt = ops.dispatch_count(idx, valid, G, 16 // G, slot=1, out=out)
+        send2, counts2, pos2 = ops.dispatch_pack(x, idx, w, valid, G, 16 // G, cnt, slot=1)
+        torch.cuda.synchronize()
+        assert torch.equal(counts, counts2) and torch.equal(out, counts)
+        assert torch.equal(pos, pos2)
+        n = int(counts[:G].sum())
+        assert torch.equal(send[:n], send2[:n])

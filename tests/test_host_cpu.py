@@ -63,3 +63,25 @@ def test_unsupported_routing_variants_raise(moe_pkg):
     assert moe._unsupported_routing(None, None, None) == "mitotic twin routing"
     moe.mitotic_pairs = []
     assert moe._unsupported_routing(None, [0, 1], None) == "dense expert subsets"
+
+
+def test_expert_parallel_chunk_bounds(moe_pkg):
+    """Token chunks of the expert-parallel exchange: weighted cuts, equal chunks,
+    one chunk for short batches, and every token in exactly one chunk."""
+    from types import SimpleNamespace
+
+    cut = moe_pkg.ExpertParallelMoE._chunk_bounds
+
+    def bounds(T, chunks=1, weights=None, min_tokens=1024):
+        return cut(SimpleNamespace(chunks=chunks, chunk_weights=weights, min_chunk_tokens=min_tokens), T)
+
+    assert bounds(32768, 2, [0.6, 0.4]) == [(0, 19661), (19661, 32768)]
+    assert bounds(32768, 4) == [(0, 8192), (8192, 16384), (16384, 24576), (24576, 32768)]
+    assert bounds(1500, 2, [0.6, 0.4]) == [(0, 1500)]
+    assert bounds(0, 2) == [(0, 0)]
+    assert bounds(3000, 4) == [(0, 1500), (1500, 3000)]
+    for T in (1, 2047, 2048, 9999, 65536):
+        for ch, wts in ((1, None), (3, None), (2, [0.6, 0.4]), (3, [0.5, 0.3, 0.2])):
+            b = bounds(T, ch, wts)
+            assert b[0][0] == 0 and b[-1][1] == T
+            assert all(lo < hi for lo, hi in b) and all(b[i][1] == b[i + 1][0] for i in range(len(b) - 1))
