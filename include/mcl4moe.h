@@ -181,6 +181,19 @@ typedef struct mcl4moe_moe_args {
 size_t mcl4moe_moe_workspace_size(int T, int d, int E, int k, int F);
 int mcl4moe_moe_forward(const mcl4moe_moe_args* args, mcl4moe_stream_t stream);
 
+/* The layer forward from a routing the caller computed (replaces the grouped
+ * dispatch after routing, src/mcl4_coe/backbone.py:893-911, for the routing
+ * variants that feed it precomputed selections: mitotic twins :791-832,
+ * lineage families :274-305, coverage penalty :843-851, dense subsets
+ * :307-398).  Inputs topk_idx (int32 [T, k], expert ids; ids outside [0, E)
+ * mark slots that are not routed) and topk_w (fp32 [T, k]); the stable
+ * expert-major permutation, NVFP4 quantisation, grouped GEMMs and combine are
+ * those of mcl4moe_moe_forward.  router_w, logit_bias and sel_mask are not
+ * read; stats, when non-NULL, receives [0, 0, routed tokens, slot share per
+ * expert] (the caller computes the variant's losses); offs / perm as in
+ * mcl4moe_moe_forward.  Same workspace size. */
+int mcl4moe_moe_forward_routed(const mcl4moe_moe_args* args, mcl4moe_stream_t stream);
+
 /* Capacity in rows of the padded, expert-major activation buffers
  * (sum over experts of count rounded up to 256, bounded by T*k + 255*E). */
 int64_t mcl4moe_padded_rows(int T, int E, int k);

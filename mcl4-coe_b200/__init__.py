@@ -8,7 +8,7 @@ the thin PyTorch host side.  The directory name contains a dash, so import it
 through ``__graft_entry__.load_package()`` (registered as ``mcl4coe_b200``).
 """
 
-from . import _lib
+from . import _lib, routing_variants
 from .expert_parallel import CudaEPOps, ExpertParallelMoE
 from .moe import MoEConfig, SparseMoE, SwiGLUExpert
 from .nvfp4 import (

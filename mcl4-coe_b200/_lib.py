@@ -30,6 +30,7 @@ EXPORTS = (
     "mcl4moe_route_noalloc",
     "mcl4moe_moe_workspace_size",
     "mcl4moe_moe_forward",
+    "mcl4moe_moe_forward_routed",
     "mcl4moe_padded_rows",
     "mcl4moe_workspace_region",
     "mcl4moe_grouped_linear_workspace_size",
@@ -132,6 +133,8 @@ def load() -> ctypes.CDLL:
     lib.mcl4moe_moe_workspace_size.argtypes = [c_int, c_int, c_int, c_int, c_int]
     lib.mcl4moe_moe_forward.restype = c_int
     lib.mcl4moe_moe_forward.argtypes = [POINTER(MoeArgs), c_void_p]
+    lib.mcl4moe_moe_forward_routed.restype = c_int
+    lib.mcl4moe_moe_forward_routed.argtypes = [POINTER(MoeArgs), c_void_p]
     lib.mcl4moe_padded_rows.restype = c_int64
     lib.mcl4moe_padded_rows.argtypes = [c_int, c_int, c_int]
     lib.mcl4moe_workspace_region.restype = c_void_p

@@ -170,47 +170,36 @@ void* mcl4moe_workspace_region(void* workspace, int region, int T, int d, int E,
   }
 }
 
-int mcl4moe_moe_forward(const mcl4moe_moe_args* a, mcl4moe_stream_t stream) {
+}  // extern "C"
+
+namespace {
+
+// Checks shared by both forward entry points; `routed`: the caller supplies topk_idx / topk_w.
+int check_forward_args(const mcl4moe_moe_args* a, bool routed) {
   if (!a) return MCL4MOE_ERR_INVALID;
   int st = check_moe_shape(a->T, a->d, a->E, a->k, a->F);
   if (st != MCL4MOE_OK) return st;
-  if (!a->stats || !a->workspace || (a->T > 0 && (!a->x || !a->router_w || !a->out))) return MCL4MOE_ERR_INVALID;
+  if (!a->workspace || (a->T > 0 && (!a->x || !a->out))) return MCL4MOE_ERR_INVALID;
+  if (routed ? (a->T > 0 && (!a->topk_idx || !a->topk_w)) : (!a->stats || (a->T > 0 && !a->router_w)))
+    return MCL4MOE_ERR_INVALID;
   if (!a->w_up || !a->w_up_scales || !a->w_up_g || !a->w_dn || !a->w_dn_scales || !a->w_dn_g)
     return MCL4MOE_ERR_INVALID;
   if (!aligned16(a->x) || !aligned16(a->out) || !aligned16(a->w_up) || !aligned16(a->w_dn) ||
-      !aligned16(a->w_up_scales) || !aligned16(a->w_dn_scales) || !aligned16(a->router_w) ||
+      !aligned16(a->w_up_scales) || !aligned16(a->w_dn_scales) || (!routed && !aligned16(a->router_w)) ||
       (a->h_debug && !aligned16(a->h_debug)))
     return MCL4MOE_ERR_INVALID;
-  const MoeWorkspace w = moe_workspace(a->workspace, a->T, a->d, a->E, a->k, a->F);
-  if (a->workspace_bytes < w.bytes) return MCL4MOE_ERR_WORKSPACE;
-  cudaStream_t s = stream;
-  const int T = a->T, d = a->d, E = a->E, k = a->k, F = a->F;
-  // A caller-owned error word is sticky (kernels skip work while it is
-  // nonzero); the workspace's own word is cleared for every call.
-  int32_t* err = a->error_word ? a->error_word : w.err;
-  if (!a->error_word && cudaMemsetAsync(w.err, 0, sizeof(int32_t), s) != cudaSuccess) return MCL4MOE_ERR_CUDA;
-  int32_t* topk_idx = a->topk_idx ? a->topk_idx : w.topk_idx;
-  float* topk_w = a->topk_w ? a->topk_w : w.topk_w;
+  return MCL4MOE_OK;
+}
 
-  auto mark = [&](int i) -> int {
-    if (a->stage_events == nullptr || a->stage_events[i] == nullptr) return MCL4MOE_OK;
-    return cudaEventRecord(static_cast<cudaEvent_t>(a->stage_events[i]), s) == cudaSuccess ? MCL4MOE_OK
-                                                                                            : MCL4MOE_ERR_CUDA;
-  };
-  if ((st = mark(0)) != MCL4MOE_OK) return st;
-  st = launch_route(a->x, a->router_w, a->logit_bias, nullptr, a->valid, T, d, E, k, a->norm_topk_prob, topk_idx,
-                    topk_w, nullptr, a->sel_mask, w.counts, a->stats, a->offs, err, w.route, s);
+// Permutation + NVFP4 activation quantisation, gate/up GEMM with SwiGLU, down
+// GEMM with the routing weight, combine: everything after the expert layout.
+int forward_experts(const mcl4moe_moe_args* a, const MoeWorkspace& w, const int32_t* topk_idx, const float* topk_w,
+                    int32_t* err, cudaStream_t s, int (*mark)(const mcl4moe_moe_args*, int, cudaStream_t)) {
+  const int T = a->T, d = a->d, E = a->E, k = a->k, F = a->F;
+  int st = launch_permute_quantize(a->x, a->valid, topk_idx, topk_w, T, d, E, k, w.route, w.slot_pos, w.sorted_w,
+                                   a->perm, w.xq, w.xs, s);
   if (st != MCL4MOE_OK) return st;
-  if ((st = mark(1)) != MCL4MOE_OK) return st;
-  if (T == 0) {
-    for (int i = 2; i < 6; ++i)
-      if ((st = mark(i)) != MCL4MOE_OK) return st;
-    return MCL4MOE_OK;
-  }
-  st = launch_permute_quantize(a->x, a->valid, topk_idx, topk_w, T, d, E, k, w.route, w.slot_pos, w.sorted_w, a->perm,
-                               w.xq, w.xs, s);
-  if (st != MCL4MOE_OK) return st;
-  if ((st = mark(2)) != MCL4MOE_OK) return st;
+  if ((st = mark(a, 2, s)) != MCL4MOE_OK) return st;
   const int64_t mcap = padded_rows_cap(T, E, k);
 
   GemmArgs g1{};
@@ -231,7 +220,7 @@ int mcl4moe_moe_forward(const mcl4moe_moe_args* a, mcl4moe_stream_t stream) {
   g1.err = err;
   st = launch_grouped_gemm(w.xq, mcap, a->w_up, g1, s);
   if (st != MCL4MOE_OK) return st;
-  if ((st = mark(3)) != MCL4MOE_OK) return st;
+  if ((st = mark(a, 3, s)) != MCL4MOE_OK) return st;
 
   GemmArgs g2{};
   g2.pad_start = w.route.pad_start;
@@ -250,10 +239,74 @@ int mcl4moe_moe_forward(const mcl4moe_moe_args* a, mcl4moe_stream_t stream) {
   g2.err = err;
   st = launch_grouped_gemm(w.hq, mcap, a->w_dn, g2, s);
   if (st != MCL4MOE_OK) return st;
-  if ((st = mark(4)) != MCL4MOE_OK) return st;
+  if ((st = mark(a, 4, s)) != MCL4MOE_OK) return st;
   st = launch_combine(w.y, w.slot_pos, a->valid, T, k, d, a->out, s);
   if (st != MCL4MOE_OK) return st;
-  return mark(5);
+  return mark(a, 5, s);
+}
+
+int mark_stage(const mcl4moe_moe_args* a, int i, cudaStream_t s) {
+  if (a->stage_events == nullptr || a->stage_events[i] == nullptr) return MCL4MOE_OK;
+  return cudaEventRecord(static_cast<cudaEvent_t>(a->stage_events[i]), s) == cudaSuccess ? MCL4MOE_OK
+                                                                                          : MCL4MOE_ERR_CUDA;
+}
+
+// A caller-owned error word is sticky (kernels skip work while it is nonzero);
+// the workspace's own word is cleared for every call.
+int32_t* error_word(const mcl4moe_moe_args* a, const MoeWorkspace& w, cudaStream_t s, int* st) {
+  *st = MCL4MOE_OK;
+  if (a->error_word) return a->error_word;
+  if (cudaMemsetAsync(w.err, 0, sizeof(int32_t), s) != cudaSuccess) *st = MCL4MOE_ERR_CUDA;
+  return w.err;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mcl4moe_moe_forward(const mcl4moe_moe_args* a, mcl4moe_stream_t stream) {
+  int st = check_forward_args(a, false);
+  if (st != MCL4MOE_OK) return st;
+  const MoeWorkspace w = moe_workspace(a->workspace, a->T, a->d, a->E, a->k, a->F);
+  if (a->workspace_bytes < w.bytes) return MCL4MOE_ERR_WORKSPACE;
+  cudaStream_t s = stream;
+  const int T = a->T, d = a->d, E = a->E, k = a->k;
+  int32_t* err = error_word(a, w, s, &st);
+  if (st != MCL4MOE_OK) return st;
+  int32_t* topk_idx = a->topk_idx ? a->topk_idx : w.topk_idx;
+  float* topk_w = a->topk_w ? a->topk_w : w.topk_w;
+  if ((st = mark_stage(a, 0, s)) != MCL4MOE_OK) return st;
+  st = launch_route(a->x, a->router_w, a->logit_bias, nullptr, a->valid, T, d, E, k, a->norm_topk_prob, topk_idx,
+                    topk_w, nullptr, a->sel_mask, w.counts, a->stats, a->offs, err, w.route, s);
+  if (st != MCL4MOE_OK) return st;
+  if ((st = mark_stage(a, 1, s)) != MCL4MOE_OK) return st;
+  if (T == 0) {
+    for (int i = 2; i < 6; ++i)
+      if ((st = mark_stage(a, i, s)) != MCL4MOE_OK) return st;
+    return MCL4MOE_OK;
+  }
+  return forward_experts(a, w, topk_idx, topk_w, err, s, mark_stage);
+}
+
+int mcl4moe_moe_forward_routed(const mcl4moe_moe_args* a, mcl4moe_stream_t stream) {
+  int st = check_forward_args(a, true);
+  if (st != MCL4MOE_OK) return st;
+  const MoeWorkspace w = moe_workspace(a->workspace, a->T, a->d, a->E, a->k, a->F);
+  if (a->workspace_bytes < w.bytes) return MCL4MOE_ERR_WORKSPACE;
+  cudaStream_t s = stream;
+  const int T = a->T, E = a->E, k = a->k;
+  int32_t* err = error_word(a, w, s, &st);
+  if (st != MCL4MOE_OK) return st;
+  if ((st = mark_stage(a, 0, s)) != MCL4MOE_OK) return st;
+  st = launch_route_from_indices(a->topk_idx, a->valid, T, E, k, w.counts, a->stats, a->offs, w.route, s);
+  if (st != MCL4MOE_OK) return st;
+  if ((st = mark_stage(a, 1, s)) != MCL4MOE_OK) return st;
+  if (T == 0) {
+    for (int i = 2; i < 6; ++i)
+      if ((st = mark_stage(a, i, s)) != MCL4MOE_OK) return st;
+    return MCL4MOE_OK;
+  }
+  return forward_experts(a, w, a->topk_idx, a->topk_w, err, s, mark_stage);
 }
 
 size_t mcl4moe_grouped_linear_workspace_size(int64_t M, int K, int E) {

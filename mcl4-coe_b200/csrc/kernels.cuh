@@ -159,6 +159,11 @@ int launch_route(const uint16_t* x, const float* wr, const float* bias, const fl
                  float* sel_mask, int32_t* counts_out, float* stats, int32_t* offs_out, int32_t* err,
                  const RouteWorkspace& ws, cudaStream_t stream);
 
+// Expert layout (ranks, chunk counts, segment starts) from caller-supplied
+// expert ids [T, k] instead of the router; ids outside [0, E) are not routed.
+int launch_route_from_indices(const int32_t* topk_idx, const uint8_t* valid, int T, int E, int k, int32_t* counts_out,
+                              float* stats, int32_t* offs_out, const RouteWorkspace& ws, cudaStream_t stream);
+
 // Scatter each routed token's NVFP4 row into its k padded expert-major slots.
 int launch_permute_quantize(const uint16_t* x, const uint8_t* valid, const int32_t* topk_idx, const float* topk_w,
                             int T, int d, int E, int k, const RouteWorkspace& ws, int32_t* slot_pos, float* sorted_w,

@@ -49,15 +49,17 @@ __global__ void __launch_bounds__(256) permute_quant_kernel(
     return;
   }
   const int chunk = t / kRouteTokens;
-  int my_pos = 0;
+  int my_pos = -1;  // slots with an expert id outside [0, E) (caller-supplied routing) are not routed
   if (lane < k) {
     const int e = topk_idx[int64_t(t) * k + lane];
-    const int r = ws.local_rank[int64_t(t) * k + lane];
-    const int base = ws.chunk_excl[int64_t(chunk) * E + e] + r;
-    my_pos = ws.pad_start[e] + base;
+    if (e >= 0 && e < E) {
+      const int r = ws.local_rank[int64_t(t) * k + lane];
+      const int base = ws.chunk_excl[int64_t(chunk) * E + e] + r;
+      my_pos = ws.pad_start[e] + base;
+      sorted_w[my_pos] = topk_w[int64_t(t) * k + lane];
+      if (perm != nullptr) perm[ws.offs_start[e] + base] = t * k + lane;
+    }
     slot_pos[int64_t(t) * k + lane] = my_pos;
-    sorted_w[my_pos] = topk_w[int64_t(t) * k + lane];
-    if (perm != nullptr) perm[ws.offs_start[e] + base] = t * k + lane;
   }
   for (int b0 = 0; b0 < nblk; b0 += 32) {
     const int b = b0 + lane;
@@ -75,7 +77,7 @@ __global__ void __launch_bounds__(256) permute_quant_kernel(
     for (int q = 0; q < 4; ++q) word |= (__shfl_sync(0xffffffffu, s, base_lane + q) & 0xFFu) << (8 * q);
     for (int j = 0; j < k; ++j) {
       const int p = __shfl_sync(0xffffffffu, my_pos, j);
-      if (b < nblk) {
+      if (b < nblk && p >= 0) {
         *reinterpret_cast<uint2*>(xq + int64_t(p) * (d / 2) + b * 8) = pk;
         if ((lane & 3) == 0)
           *reinterpret_cast<uint32_t*>(xs + swizzled_scale_offset(uint64_t(p), uint32_t(b), uint32_t(nblk))) = word;
@@ -199,6 +201,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const uint16_t* __restrict
     if (routed) {
       for (int j = 0; j < k; ++j) {
         const int p = __shfl_sync(0xffffffffu, my_pos, j);
+        if (p < 0) continue;  // slot not routed (caller-supplied routing)
         const uint4 u = __ldg(reinterpret_cast<const uint4*>(y + int64_t(p) * d + c));
         const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll

@@ -556,6 +556,76 @@ __global__ void __launch_bounds__(256) route_scan_kernel(int C, int E, int k, Ro
   }
 }
 
+// ---------------------------------------------------------------- precomputed routing
+
+// Chunk ranks of caller-supplied expert ids (one CTA per 128-token chunk, the
+// router's chunking): slot (t, j) gets its rank among the chunk's slots of the
+// same expert in flattened order t*k + j, the order of the reference's stable
+// argsort of the selected experts (src/mcl4_coe/backbone.py:895-897).  Slots
+// of masked tokens and ids outside [0, E) get rank -1 and are not routed.
+// Each warp ranks 16 tokens (match_any per 32 slots), then the warps' counts
+// are scanned per expert.  Writes the chunk's per-expert counts (the router's
+// chunk counts) and zero probability sums; part_misc holds the chunk's routed
+// token count for the scan's statistics.
+__global__ void __launch_bounds__(256) route_ranks_kernel(const int32_t* __restrict__ topk_idx,
+                                                          const uint8_t* __restrict__ valid, int T, int E, int k,
+                                                          RouteWorkspace ws) {
+  __shared__ int32_t cnt[8 * kMaxExperts];
+  __shared__ int32_t n_tok;
+  pdl_wait();
+  pdl_trigger();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = blockIdx.x;
+  for (int i = threadIdx.x; i < 8 * E; i += blockDim.x) cnt[i] = 0;
+  if (threadIdx.x == 0) n_tok = 0;
+  if (c == 0 && threadIdx.x == 0) *ws.done = 0u;  // finished-expert counter of the scan
+  __syncthreads();
+  const int t0 = c * kRouteTokens + warp * 16;
+  const int t1 = min(T, t0 + 16);
+  const int64_t s0 = int64_t(t0) * k, s1 = t1 > t0 ? int64_t(t1) * k : s0;
+  int32_t* my = cnt + warp * E;
+  for (int64_t base = s0; base < s1; base += 32) {
+    const int64_t sl = base + lane;
+    int e = -1;
+    if (sl < s1) {
+      const int t = int(sl / k);
+      const int v = topk_idx[sl];
+      if ((valid == nullptr || valid[t] != 0) && v >= 0 && v < E) e = v;
+    }
+    const uint32_t peers = __match_any_sync(0xffffffffu, e);
+    const int before = __popc(peers & ((1u << lane) - 1u));
+    const int r = e >= 0 ? my[e] + before : -1;
+    __syncwarp();
+    if (e >= 0 && before == 0) my[e] += __popc(peers);
+    __syncwarp();
+    if (sl < s1) ws.local_rank[sl] = r;
+  }
+  if (lane < 16 && t0 + lane < t1 && (valid == nullptr || valid[t0 + lane] != 0)) atomicAdd(&n_tok, 1);
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int run = 0;
+    for (int w = 0; w < 8; ++w) {
+      const int v = cnt[w * E + e];
+      cnt[w * E + e] = run;
+      run += v;
+    }
+    ws.chunk_excl[int64_t(c) * E + e] = run;
+    ws.part_probs[int64_t(c) * E + e] = 0.f;
+  }
+  if (threadIdx.x == 0) {
+    ws.part_misc[2 * c] = 0.f;
+    ws.part_misc[2 * c + 1] = float(n_tok);
+  }
+  __syncthreads();
+  for (int64_t base = s0; base < s1; base += 32) {
+    const int64_t sl = base + lane;
+    if (sl >= s1) continue;
+    const int t = int(sl / k);
+    const int v = topk_idx[sl];
+    if ((valid == nullptr || valid[t] != 0) && v >= 0 && v < E) ws.local_rank[sl] += my[v];
+  }
+}
+
 // ---------------------------------------------------------------- host side
 
 namespace {
@@ -673,6 +743,21 @@ int launch_route(const uint16_t* x, const float* wr, const float* bias, const fl
       cudaSuccess)
     return MCL4MOE_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? MCL4MOE_OK : MCL4MOE_ERR_CUDA;
+}
+
+int launch_route_from_indices(const int32_t* topk_idx, const uint8_t* valid, int T, int E, int k, int32_t* counts_out,
+                              float* stats, int32_t* offs_out, const RouteWorkspace& ws, cudaStream_t stream) {
+  const int C = (T + kRouteTokens - 1) / kRouteTokens;
+  if (C > 0) {
+    if (launch_pdl(route_ranks_kernel, dim3(C), dim3(256), 0, stream, topk_idx, valid, T, E, k, ws) != cudaSuccess)
+      return MCL4MOE_ERR_CUDA;
+  } else if (cudaMemsetAsync(ws.done, 0, sizeof(uint32_t), stream) != cudaSuccess) {
+    return MCL4MOE_ERR_CUDA;
+  }
+  return launch_pdl(route_scan_kernel, dim3(E), dim3(256), 0, stream, C, E, k, ws, counts_out, stats, offs_out) ==
+                 cudaSuccess
+             ? MCL4MOE_OK
+             : MCL4MOE_ERR_CUDA;
 }
 
 }  // namespace mcl4

@@ -26,9 +26,12 @@ routing weight, and the k-way combine.  ``valid`` follows the reference's loop
 branch (src/mcl4_coe/backbone.py:913-1047): masked tokens are not routed and
 get zero output and a zero ``last_selected_mask`` row.
 
-Not yet served (raise ``NotImplementedError``): backward, mitotic twin
-routing, lineage families, coverage penalty, dense subsets, 2:4 sparse
-weights.
+Routing variants (mitotic twins, lineage families, recurrent coverage
+penalty, dense subsets with an optional sparse remainder, the sequence-diversity
+and mitotic-orthogonality losses) compute the reference's selection on the
+library's router logits (``routing_variants.py``) and run the experts through
+``mcl4moe_moe_forward_routed``.  Not served (raise ``NotImplementedError``):
+backward and 2:4 sparse weights.
 """
 
 from __future__ import annotations
@@ -121,6 +124,36 @@ class SparseMoE(nn.Module):
         self._ws_key: tuple | None = None
         self._graphs: dict | None = None  # CUDA-graph replay (enable_cuda_graph)
 
+    @torch.no_grad()
+    def configure_lineage_family_routing(self, num_roots: int = 64, *, top_families: int = 8,
+                                         child_share: float = 0.25) -> None:
+        """Root-anchored expert families for lineage routing (src/mcl4_coe/backbone.py:231-271):
+        each expert after the first ``num_roots`` joins the root whose up_proj weight is
+        most cosine-similar; a root keeps ``1 - child_share`` of its family's prior mass
+        and its descendants share the rest.  Out-of-range arguments switch it off."""
+        E = len(self.experts)
+        if num_roots <= 0 or top_families <= 0 or num_roots >= E:
+            self.lineage_num_roots = self.lineage_top_families = 0
+            self.lineage_root_ids = self.lineage_logit_prior = None
+            return
+        dev = self.router.weight.device
+        ups = torch.nn.functional.normalize(
+            torch.stack([e.up_proj.weight.detach().float().reshape(-1) for e in self.experts]), p=2.0, dim=-1,
+            eps=1e-8)
+        parent = (ups[num_roots:] @ ups[:num_roots].T).argmax(dim=-1)
+        root_ids = torch.cat([torch.arange(num_roots, dtype=torch.long, device=dev), parent.to(dev)])
+        family_size = torch.bincount(root_ids, minlength=num_roots).tolist()
+        share = float(max(0.0, min(0.95, child_share)))
+        prior = torch.ones(E, dtype=torch.float32, device=dev)
+        for e, r in enumerate(root_ids.tolist()):
+            if family_size[r] > 1:
+                prior[e] = max(1e-6, 1.0 - share) if e < num_roots else max(1e-6, share / float(family_size[r] - 1))
+        self.lineage_num_roots = int(num_roots)
+        self.lineage_top_families = int(min(top_families, num_roots))
+        self.lineage_child_share = share
+        self.lineage_root_ids = root_ids
+        self.lineage_logit_prior = torch.log(prior)
+
     def enable_cuda_graph(self, enabled: bool = True) -> None:
         """Serve repeated calls of one shape from a captured CUDA graph.
 
@@ -177,19 +210,16 @@ class SparseMoE(nn.Module):
         return mod
 
     # ------------------------------------------------------------------ helpers
-    def _unsupported_routing(self, prior_expert_mask, dense_expert_indices, dense_subset_k) -> str | None:
+    def _routing_variant(self, prior_expert_mask, dense_expert_indices, dense_subset_k) -> str | None:
+        """Which routing variant this call needs (None: plain top-k, served by one library call)."""
         if dense_expert_indices is not None and len(dense_expert_indices) > 0:
-            return "dense expert subsets"
+            return "dense"
         if self.dense_expert_indices or int(self.dense_subset_k if dense_subset_k is None else dense_subset_k) > 0:
-            return "dense expert subsets"
-        if self.mitotic_pairs:
-            return "mitotic twin routing"
-        if self.lineage_top_families > 0 and self.lineage_root_ids is not None:
-            return "lineage family routing"
-        if prior_expert_mask is not None and self.recurrent_coverage_penalty > 0.0:
-            return "recurrent coverage penalty"
-        if self.sequence_diversity_coef > 0.0 or self.mitotic_ortho_coef > 0.0:
-            return "sequence-diversity / mitotic-orthogonality losses"
+            return "dense"
+        if (self.mitotic_pairs or (self.lineage_top_families > 0 and self.lineage_root_ids is not None)
+                or (prior_expert_mask is not None and self.recurrent_coverage_penalty > 0.0)
+                or self.sequence_diversity_coef > 0.0 or self.mitotic_ortho_coef > 0.0):
+            return "sparse"
         return None
 
     def _workspace(self, T: int, d: int, E: int, k: int, F: int, device: torch.device) -> Tensor:
@@ -212,8 +242,8 @@ class SparseMoE(nn.Module):
     def forward(self, x: Tensor, valid: Tensor | None = None, *, prior_expert_mask: Tensor | None = None,
                 dense_expert_indices: Sequence[int] | Tensor | None = None,
                 dense_subset_k: int | None = None) -> tuple[Tensor, Tensor, Tensor, Tensor]:
-        if (self._graphs is not None and prior_expert_mask is None and dense_expert_indices is None
-                and dense_subset_k is None and x.is_cuda and not torch.is_grad_enabled()):
+        if (self._graphs is not None and x.is_cuda and not torch.is_grad_enabled()
+                and self._routing_variant(prior_expert_mask, dense_expert_indices, dense_subset_k) is None):
             return self._graph_forward(x.reshape(-1, x.shape[-1]).to(torch.bfloat16), valid, x.shape, x.dtype)
         r = self._forward_impl(x, valid, prior_expert_mask, dense_expert_indices, dense_subset_k, details=False)
         return r["out"], r["aux_loss"], r["router_z_loss"], r["counts"]
@@ -231,12 +261,15 @@ class SparseMoE(nn.Module):
         flat = x.reshape(-1, x.shape[-1])
         if flat.device.type != "cuda":
             raise ValueError("SparseMoE on B200 requires CUDA tensors (there is no CPU fallback)")
-        reason = self._unsupported_routing(prior_expert_mask, dense_expert_indices, dense_subset_k)
-        if reason is not None:
-            raise NotImplementedError(f"{reason} is not served by the B200 MoE path yet")
         if torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in self.parameters())):
             raise NotImplementedError("the B200 MoE path is forward-only: run it under torch.no_grad() "
                                       "or torch.inference_mode()")
+        variant = self._routing_variant(prior_expert_mask, dense_expert_indices, dense_subset_k)
+        if variant is not None:
+            if details or static is not None:
+                raise NotImplementedError("routing variants run through forward() only")
+            return self._forward_variant(x, valid, prior_expert_mask, dense_expert_indices, dense_subset_k,
+                                         variant)
         E = len(self.experts)
         if self.router.weight.shape[0] != E:
             raise ValueError("router rows must match the number of experts")
@@ -319,6 +352,161 @@ class SparseMoE(nn.Module):
                 res["hq"] = region(2, mcap * F // 2).view(mcap, F // 2).clone()
                 res["hs"] = region(3, mcap * F // 16).clone()
         return res
+
+    # ------------------------------------------------------------------ routing variants
+    def _router_logits(self, xb: Tensor, wr: Tensor, bias: Tensor | None) -> Tensor:
+        """fp32 router logits [T, E] from the library's router (the same logits its
+        top-k uses; the plain top-k it also computes is discarded)."""
+        lib = _lib.load()
+        T, d = xb.shape
+        E, k = wr.shape[0], self.top_k
+        dev = xb.device
+        logits = torch.empty((T, E), dtype=torch.float32, device=dev)
+        idx = torch.empty((max(T, 1), k), dtype=torch.int32, device=dev)
+        w = torch.empty((max(T, 1), k), dtype=torch.float32, device=dev)
+        counts = torch.empty((E,), dtype=torch.int32, device=dev)
+        stats = torch.empty((3 + E,), dtype=torch.float32, device=dev)
+        ws = torch.empty((max(lib.mcl4moe_route_workspace_size(T, E, k, d), 256),), dtype=torch.uint8, device=dev)
+        _lib.check(lib.mcl4moe_route(xb.data_ptr(), wr.data_ptr(), _opt_ptr(bias), None, None, T, d, E, k,
+                                     int(self.norm_topk_prob), idx.data_ptr(), w.data_ptr(), logits.data_ptr(), None,
+                                     counts.data_ptr(), stats.data_ptr(), ws.data_ptr(), ws.numel(), _stream_handle()),
+                   "mcl4moe_route")
+        return logits
+
+    def _forward_routed(self, xb: Tensor, vmask: Tensor | None, idx: Tensor, w: Tensor) -> Tensor:
+        """Layer output [T, d] (bf16) for a routing given as expert ids / weights [T, k_eff]
+        (``mcl4moe_moe_forward_routed``); rows of masked tokens are zero."""
+        T, d = xb.shape
+        k_eff = idx.shape[1]
+        if not 0 < k_eff <= 32:
+            raise NotImplementedError(f"routing with {k_eff} experts per token (the kernels take 1 to 32)")
+        E = len(self.experts)
+        F = self.experts[0].down_proj.weight.shape[1]
+        dev = xb.device
+        up = get_or_build_grouped_cache(self.experts, "up_proj")
+        dn = get_or_build_grouped_cache(self.experts, "down_proj")
+        idx = idx.to(device=dev, dtype=torch.int32).contiguous()
+        w = w.to(device=dev, dtype=torch.float32).contiguous()
+        out = torch.empty((T, d), dtype=torch.bfloat16, device=dev)
+        ws = self._workspace(T, d, E, k_eff, F, dev)
+        args = _lib.MoeArgs(
+            x=xb.data_ptr(), router_w=None, logit_bias=None, valid=_opt_ptr(vmask),
+            w_up=up.packed.data_ptr(), w_up_scales=up.scales.data_ptr(), w_up_g=up.g.data_ptr(),
+            w_dn=dn.packed.data_ptr(), w_dn_scales=dn.scales.data_ptr(), w_dn_g=dn.g.data_ptr(),
+            T=T, d=d, E=E, k=k_eff, F=F, norm_topk_prob=int(self.norm_topk_prob),
+            out=out.data_ptr(), stats=None, sel_mask=None, topk_idx=idx.data_ptr(), topk_w=w.data_ptr(),
+            offs=None, perm=None, h_debug=None, error_word=None, workspace=ws.data_ptr(), workspace_bytes=ws.numel())
+        _lib.check(_lib.load().mcl4moe_moe_forward_routed(args, _stream_handle()), "mcl4moe_moe_forward_routed")
+        return out
+
+    def _forward_variant(self, x, valid, prior_expert_mask, dense_expert_indices, dense_subset_k, variant):
+        """Routing variants (mitotic twins, lineage families, coverage penalty, dense
+        subsets, extra auxiliary losses): the reference's selection on the library's
+        router logits, then the native layer on that routing.  Masked tokens are
+        dropped before routing, as in the reference's loop branch and dense-subset
+        head (src/mcl4_coe/backbone.py:913-1047, :640-785)."""
+        from . import routing_variants as rv
+
+        flat = x.reshape(-1, x.shape[-1])
+        T, d = flat.shape
+        E = len(self.experts)
+        if self.router.weight.shape[0] != E:
+            raise ValueError("router rows must match the number of experts")
+        self.num_experts = E
+        dev = flat.device
+        flat_valid = (torch.ones(T, dtype=torch.bool, device=dev) if valid is None
+                      else valid.reshape(-1).to(device=dev).bool())
+        if flat_valid.numel() != T:
+            raise ValueError("valid must have one entry per token")
+        active = flat_valid.nonzero(as_tuple=False).squeeze(-1)
+        n_act = active.numel()
+        if n_act == 0:
+            zero = torch.zeros((), dtype=torch.float32, device=dev)
+            self.last_selected_mask = torch.zeros((*x.shape[:-1], E), dtype=torch.float32, device=dev)
+            return dict(out=torch.zeros_like(x), aux_loss=zero, router_z_loss=zero,
+                        counts=torch.zeros(E, dtype=torch.float32, device=dev))
+        xb = flat.to(torch.bfloat16).contiguous()
+        wr = self.router.weight.detach().to(device=dev, dtype=torch.float32).contiguous()
+        bias = None
+        if self.router_logit_bias is not None:
+            bias = self.router_logit_bias.detach().to(device=dev, dtype=torch.float32).contiguous()
+        logits = self._router_logits(xb, wr, bias).index_select(0, active)
+        prior = None
+        if prior_expert_mask is not None and self.recurrent_coverage_penalty > 0.0:
+            prior = prior_expert_mask.reshape(-1, E).to(dev).index_select(0, active)
+        vmask = None if valid is None else flat_valid.to(torch.uint8).contiguous()
+
+        def full_rows(t: Tensor, fill) -> Tensor:  # active-token rows -> all T rows
+            res = torch.full((T,) + tuple(t.shape[1:]), fill, dtype=t.dtype, device=dev)
+            res.index_copy_(0, active, t)
+            return res
+
+        with torch.autocast(device_type=dev.type, enabled=False):
+            if variant == "dense":
+                if dense_expert_indices is not None:
+                    dense_idx = ([int(i) for i in dense_expert_indices.detach().cpu().reshape(-1).tolist()]
+                                 if isinstance(dense_expert_indices, Tensor) else [int(i) for i in dense_expert_indices])
+                else:
+                    dense_idx = list(self.dense_expert_indices)
+                dense_k = int(self.dense_subset_k if dense_subset_k is None else dense_subset_k)
+                sel = rv.dense_selection(self, logits, prior, dense_idx, dense_k)
+                mask, aux, z, counts = rv.dense_statistics(self, logits, sel["probs"], sel["chosen"], sel["chosen_t"])
+                probs = sel["probs"]
+                # experts in ascending id order: the reference sums the subset's outputs in that order
+                order = sorted(range(len(sel["chosen"])), key=lambda i: sel["chosen"][i])
+                chosen_sorted = torch.tensor([sel["chosen"][i] for i in order], dtype=torch.int32, device=dev)
+                w_sorted = sel["weights"][:, order]
+                idx = full_rows(chosen_sorted.unsqueeze(0).expand(n_act, -1).contiguous(), -1)
+                out = self._forward_routed(xb, vmask, idx, full_rows(w_sorted.contiguous(), 0.0))
+                rem = rv.dense_remainder(self, sel, xb.dtype)
+                if rem is not None:
+                    sparse = self._forward_routed(xb, vmask, full_rows(rem["selected"].to(torch.int32), -1),
+                                                  full_rows(rem["weights"].contiguous(), 0.0))
+                    mixed = (rem["alpha_dense"] * out.index_select(0, active)
+                             + rem["alpha_rem"] * sparse.index_select(0, active))
+                    out = torch.zeros_like(out)
+                    out.index_copy_(0, active, mixed)
+            else:
+                probs, weights, selected = rv.sparse_selection(self, logits, prior)
+                aux, z, counts = rv.sparse_statistics(self, logits, probs, selected)
+                mask = torch.nn.functional.one_hot(selected, num_classes=E).sum(dim=1).to(torch.float32)
+                out = self._forward_routed(xb, vmask, full_rows(selected.to(torch.int32), -1),
+                                           full_rows(weights.contiguous(), 0.0))
+            aux = rv.add_extra_aux(self, aux, tuple(x.shape), probs, active, T, valid)
+        self.last_selected_mask = full_rows(mask, 0.0).view(*x.shape[:-1], E)
+        return dict(out=out.to(x.dtype).view_as(x), aux_loss=aux, router_z_loss=z, counts=counts.detach())
+
+    @torch.no_grad()
+    def forward_dense_subset(self, x: Tensor, expert_indices: Sequence[int] | Tensor, *,
+                             expert_weights: Tensor | None = None, valid: Tensor | None = None) -> Tensor:
+        """The listed experts on every token, summed with ``expert_weights`` ([M] shared
+        or [.., M] per token; none = weight 1), masked rows zero
+        (src/mcl4_coe/backbone.py:307-398, grouped path :352-379).  Runs as a routing
+        with the M experts (ascending id, the reference's summation order) in every
+        token's slots."""
+        if isinstance(expert_indices, Tensor):
+            ids = [int(i) for i in expert_indices.detach().cpu().reshape(-1).tolist()]
+        else:
+            ids = [int(i) for i in expert_indices]
+        flat = x.reshape(-1, x.shape[-1])
+        if not ids or flat.shape[0] == 0:
+            return torch.zeros_like(x)
+        if flat.device.type != "cuda":
+            raise ValueError("SparseMoE on B200 requires CUDA tensors (there is no CPU fallback)")
+        T, m = flat.shape[0], len(ids)
+        dev = flat.device
+        if expert_weights is None:
+            w = torch.ones((T, m), dtype=torch.float32, device=dev)
+        elif expert_weights.ndim == 1:
+            w = expert_weights.to(device=dev, dtype=torch.float32).view(1, m).expand(T, m)
+        else:
+            w = expert_weights.to(device=dev, dtype=torch.float32).reshape(-1, m)
+        order = sorted(range(m), key=lambda i: ids[i])
+        idx = torch.tensor([ids[i] for i in order], dtype=torch.int32, device=dev).view(1, m).expand(T, m)
+        w = w[:, order].contiguous()
+        vmask = None if valid is None else valid.reshape(-1).to(device=dev, dtype=torch.uint8).contiguous()
+        out = self._forward_routed(flat.to(torch.bfloat16).contiguous(), vmask, idx.contiguous(), w)
+        return out.to(x.dtype).view_as(x)
 
     def read_device_error(self) -> int:
         """Synchronise and return the error word of the last forward (0 = every

@@ -6,6 +6,8 @@ any machine; the golden files store SHA-256 digests of the large ones.
 
 from __future__ import annotations
 
+import zlib
+
 import numpy as np
 
 
@@ -121,6 +123,30 @@ def layer_case():
     return ("layer_c0", moe_case(400, 256, 256, 8, 2, 512))
 
 
+def variant_cases():
+    """Routing variants of SparseMoE (src/mcl4_coe/backbone.py:274-398, :640-1047):
+    (name, moe_case, options).  ``shape`` reshapes x to [B, S, d] (the
+    sequence-diversity loss needs a sequence axis); ``prior_frac`` draws a 0/1
+    prior_expert_mask; ``lineage`` = (num_roots, top_families, child_share)."""
+    def opt(**kw):
+        base = dict(pairs=(), lineage=None, coverage=0.0, prior_frac=None, dense_idx=None, dense_k=0,
+                    combine=False, seq_div=0.0, ortho=0.0, shape=None)
+        base.update(kw)
+        return base
+
+    return [
+        ("v_twins_norm", moe_case(500, 96, 256, 8, 2, 256, valid_frac=0.8), opt(pairs=((0, 4), (2, 6)))),
+        ("v_twins_nonorm", moe_case(501, 96, 256, 8, 2, 256, norm_topk_prob=False), opt(pairs=((1, 5), (3, 7)))),
+        ("v_lineage", moe_case(502, 96, 256, 12, 2, 256), opt(lineage=(4, 2, 0.25))),
+        ("v_coverage", moe_case(503, 96, 256, 8, 3, 256, valid_frac=0.9), opt(coverage=0.6, prior_frac=0.4)),
+        ("v_dense_idx", moe_case(504, 96, 256, 8, 2, 256, valid_frac=0.75), opt(dense_idx=(5, 1, 3))),
+        ("v_dense_k_mixed", moe_case(505, 96, 256, 8, 2, 256), opt(dense_k=2, combine=True, coverage=0.5,
+                                                                  prior_frac=0.3)),
+        ("v_aux_terms", moe_case(506, 96, 256, 8, 2, 256, valid_frac=0.85),
+         opt(pairs=((0, 1),), seq_div=0.1, ortho=0.05, shape=(4, 24))),
+    ]
+
+
 # The five benchmark configurations (seeds 0-4); shapes only — tensors are built
 # on the device by the tests / bench from these seeds.
 BENCH_CONFIGS = [
@@ -130,3 +156,11 @@ BENCH_CONFIGS = [
     dict(name="c3_granite_zipf", seed=3, t=65536, d=1536, e=32, k=8, f=512, e_grow=40, zipf_bias=True),
     dict(name="c4_decode", seed=4, t=64, d=2048, e=64, k=8, f=1024),
 ]
+
+
+def variant_prior(name: str, t: int, e: int, frac: float | None) -> np.ndarray | None:
+    """0/1 prior_expert_mask [t, e] of the variant case ``name`` (None when it has none)."""
+    if frac is None:
+        return None
+    return (rng(zlib.crc32(name.encode())).uniform(size=(t, e)) < frac).astype(np.float32)
+

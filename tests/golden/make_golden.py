@@ -17,6 +17,10 @@ outputs of the reference's own functions on seeded inputs:
 * ``layer.npz``       — the layer output of the unmodified ``SparseMoE.forward``
   whose expert projections were replaced by dequantised-FP4 linears built
   from the reference's ``_quantize_nvfp4_core`` / ``_dequantize_nvfp4``.
+* ``variants.npz``    — the same dequantised-FP4 layer with the routing
+  variants switched on (mitotic twins, lineage families, coverage penalty,
+  dense subsets, sequence-diversity / orthogonality losses): outputs, losses,
+  counts, ``last_selected_mask``, and the lineage configuration.
 
 Inputs come from numpy's PCG64 generator (platform independent); their
 SHA-256 digests are stored so the tests can regenerate and verify them
@@ -41,6 +45,8 @@ from inputs import (  # noqa: E402  (shared with the tests)
     act_quant_cases,
     layer_case,
     routing_cases,
+    variant_cases,
+    variant_prior,
     weight_quant_cases,
 )
 
@@ -151,6 +157,7 @@ def main() -> None:
             packed, scales, g = nv._quantize_nvfp4_core(wt, True, False, False)
             self.register_buffer("w_deq", nv._dequantize_nvfp4(
                 packed, nv._swizzle_scales(scales), g, wt.shape[0], wt.shape[1]))
+            self.register_buffer("weight", wt.clone())  # read by the orthogonality loss
 
         def forward(self, x):
             xf = x.float()
@@ -208,6 +215,48 @@ def main() -> None:
         out[f"{name}__topk_indices"] = rec["topk_indices"].numpy()
         out[f"{name}__perm"] = rec["perm"].numpy()
     np.savez_compressed(HERE / "layer.npz", **out)
+
+    # ---------------------------------------------------------------- routing variants
+    out = {}
+    for name, case, o in variant_cases():
+        cfg = bb.MCL4CEDConfig(d_model=case["d"], n_heads=4, expert_hidden_dim=case["f"], num_experts=case["e"],
+                               top_k=case["k"], norm_topk_prob=case["norm_topk_prob"],
+                               recurrent_coverage_penalty=o["coverage"], mitotic_ortho_coef=o["ortho"],
+                               sequence_diversity_coef=o["seq_div"], dense_subset_k=o["dense_k"],
+                               combine_dense_and_sparse=o["combine"])
+        moe = bb.SparseMoE(cfg).eval()
+        with torch.no_grad():
+            moe.router.weight.copy_(torch.from_numpy(case["wr"]))
+            for i, ex in enumerate(moe.experts):
+                ex.up_proj.weight.copy_(torch.from_numpy(case["w_up"][i]))
+                ex.down_proj.weight.copy_(torch.from_numpy(case["w_dn"][i]))
+        if o["pairs"]:
+            moe.mitotic_pairs = [tuple(p) for p in o["pairs"]]
+        if o["lineage"] is not None:
+            roots, fams, share = o["lineage"]
+            moe.configure_lineage_family_routing(roots, top_families=fams, child_share=share)
+            out[f"{name}__lineage_root_ids"] = moe.lineage_root_ids.numpy()
+            out[f"{name}__lineage_logit_prior"] = moe.lineage_logit_prior.numpy()
+        for i, ex in enumerate(moe.experts):
+            ex.up_proj = FakeQuantLinear(case["w_up"][i])
+            ex.down_proj = FakeQuantLinear(case["w_dn"][i])
+        x = torch.from_numpy(case["x_bf16_bits"].view(np.int16)).view(torch.bfloat16).reshape(case["t"], case["d"])
+        valid = None if case["valid"] is None else torch.from_numpy(case["valid"].astype(bool))
+        if o["shape"] is not None:
+            x = x.reshape(*o["shape"], case["d"])
+            valid = None if valid is None else valid.reshape(*o["shape"])
+        prior = variant_prior(name, case["t"], case["e"], o["prior_frac"])
+        prior_t = None if prior is None else torch.from_numpy(prior)
+        with torch.no_grad():
+            y, aux, z, counts = moe(x, valid=valid, prior_expert_mask=prior_t,
+                                    dense_expert_indices=None if o["dense_idx"] is None else list(o["dense_idx"]))
+        out[f"{name}__digest"] = np.array(digest(case["x_bf16_bits"], case["wr"], case["w_up"], case["w_dn"]))
+        out[f"{name}__out_bf16"] = y.reshape(case["t"], case["d"]).view(torch.int16).numpy().view(np.uint16)
+        out[f"{name}__aux"] = np.float32(aux.item())
+        out[f"{name}__z"] = np.float32(z.item())
+        out[f"{name}__counts"] = counts.numpy().astype(np.float32)
+        out[f"{name}__sel_mask"] = moe.last_selected_mask.reshape(case["t"], case["e"]).numpy().astype(np.float32)
+    np.savez_compressed(HERE / "variants.npz", **out)
     for p in sorted(HERE.glob("*.npz")):
         print(p.name, p.stat().st_size)
 

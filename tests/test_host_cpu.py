@@ -56,13 +56,22 @@ def test_mitotic_pairs_round_trip_through_state_dict(moe_pkg):
     assert b.mitotic_pairs == [(0, 3), (1, 2)]
 
 
-def test_unsupported_routing_variants_raise(moe_pkg):
+def test_routing_variant_detection(moe_pkg):
+    """Plain top-k takes the one-call path; every reference variant takes the routed path."""
     moe = moe_pkg.SparseMoE(_cfg(moe_pkg))
-    assert moe._unsupported_routing(None, None, None) is None
+    assert moe._routing_variant(None, None, None) is None
+    prior = torch.zeros(2, moe.num_experts)
+    assert moe._routing_variant(prior, None, None) is None  # no penalty configured
+    moe.recurrent_coverage_penalty = 0.5
+    assert moe._routing_variant(prior, None, None) == "sparse"
+    moe.recurrent_coverage_penalty = 0.0
     moe.mitotic_pairs = [(0, 1)]
-    assert moe._unsupported_routing(None, None, None) == "mitotic twin routing"
+    assert moe._routing_variant(None, None, None) == "sparse"
     moe.mitotic_pairs = []
-    assert moe._unsupported_routing(None, [0, 1], None) == "dense expert subsets"
+    assert moe._routing_variant(None, [0, 1], None) == "dense"
+    assert moe._routing_variant(None, None, 2) == "dense"
+    moe.sequence_diversity_coef = 0.1
+    assert moe._routing_variant(None, None, None) == "sparse"
 
 
 def test_expert_parallel_chunk_bounds(moe_pkg):
