@@ -61,6 +61,20 @@ int mcl4moe_device_supported(void);
 int mcl4moe_read_error(int32_t* device_error_word, int32_t* host_value, mcl4moe_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Replaces compute_2to4_mask (src/mcl4_coe/nvfp4.py:70-110), applied to a
+ * weight before its NVFP4 quantisation when a layer's sparsity_mode is not
+ * "none" (:1020-1023).  W fp32 [N, K] row-major; mode 1 = "2to4_row" (keep the
+ * two largest |w| of every 4 consecutive elements along K), mode 2 =
+ * "2to4_transposable" (per 4x4 tile the doubly 2:4 pattern of largest kept
+ * L1, first maximum in the reference's catalog order; falls back to mode 1
+ * when N % 4 != 0, as the reference does).  Writes w_masked = w * mask (fp32
+ * [N, K]; may alias w) and, when non-NULL, mask as 0/1 bytes [N, K].
+ * Requires K % 4 == 0 and 16-byte aligned w / w_masked.
+ * ------------------------------------------------------------------------ */
+int mcl4moe_mask_2to4(const float* w, int N, int K, int mode, float* w_masked, uint8_t* mask,
+                      mcl4moe_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Weight quantisation.
  * Replaces _quantize_grouped_weights_core (src/mcl4_coe/nvfp4.py:923-952)
  * and the dirty-expert refresh of _get_or_build_grouped_nvfp4_cache

@@ -12,7 +12,9 @@ from . import _lib, routing_variants
 from .expert_parallel import CudaEPOps, ExpertParallelMoE
 from .moe import MoEConfig, SparseMoE, SwiGLUExpert
 from .nvfp4 import (
+    SPARSITY_MODES,
     GroupedNVFP4Cache,
+    compute_2to4_mask,
     export_reference_cache,
     get_gemm_counts,
     get_or_build_grouped_cache,
@@ -34,6 +36,8 @@ __all__ = [
     "nvfp4_grouped_linear",
     "quantize_nvfp4",
     "reset_gemm_counts",
+    "compute_2to4_mask",
+    "SPARSITY_MODES",
 ]
 
 

@@ -23,6 +23,7 @@ EXPORTS = (
     "mcl4moe_device_supported",
     "mcl4moe_read_error",
     "mcl4moe_quantize_weights",
+    "mcl4moe_mask_2to4",
     "mcl4moe_quantize_activations",
     "mcl4moe_route_workspace_size",
     "mcl4moe_route",
@@ -110,6 +111,8 @@ def load() -> ctypes.CDLL:
     lib.mcl4moe_device_supported.restype = c_int
     lib.mcl4moe_read_error.restype = c_int
     lib.mcl4moe_read_error.argtypes = [c_void_p, POINTER(c_int32), c_void_p]
+    lib.mcl4moe_mask_2to4.restype = c_int
+    lib.mcl4moe_mask_2to4.argtypes = [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]
     lib.mcl4moe_quantize_weights.restype = c_int
     lib.mcl4moe_quantize_weights.argtypes = [POINTER(c_void_p), POINTER(c_int32), c_int, c_int, c_int,
                                              c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

@@ -119,6 +119,15 @@ int mcl4moe_quantize_weights(const float* const* w_ptrs, const int32_t* slots, i
                                  ref_b_bwd, ref_bs_bwd, amax_scratch, stream);
 }
 
+int mcl4moe_mask_2to4(const float* w, int N, int K, int mode, float* w_masked, uint8_t* mask,
+                      mcl4moe_stream_t stream) {
+  if (N < 0 || K < 0 || (mode != 1 && mode != 2) || (int64_t(N) * K > 0 && (!w || !w_masked))) return MCL4MOE_ERR_INVALID;
+  if (K % 4 != 0 || !aligned16(w) || !aligned16(w_masked) || (mask && reinterpret_cast<uintptr_t>(mask) % 4 != 0))
+    return MCL4MOE_ERR_INVALID;
+  if (mode == 2 && N % 4 != 0) mode = 1;  // src/mcl4_coe/nvfp4.py:90: tiles need both sides divisible by 4
+  return launch_mask_2to4(w, N, K, mode, w_masked, mask, stream);
+}
+
 int mcl4moe_quantize_activations(const uint16_t* x, int64_t rows, int cols, int64_t ld_x, uint8_t* packed,
                                  uint8_t* scales, int swizzled, mcl4moe_stream_t stream) {
   if (rows < 0 || cols <= 0 || ld_x < cols || !x || !packed || !scales) return MCL4MOE_ERR_INVALID;

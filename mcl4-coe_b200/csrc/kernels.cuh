@@ -150,6 +150,10 @@ int launch_quantize_weights(const float* const* w_ptrs, const int32_t* slots, in
                             uint8_t* scales, float* gscale, uint8_t* rb, uint8_t* rbs, uint8_t* rbb, uint8_t* rbbs,
                             float* amax, cudaStream_t stream);
 
+// 2:4 sparsity mask of W [N, K] (mode 1: 2 of every 4 along K; mode 2: doubly 2:4
+// per 4x4 tile) and the masked weights.
+int launch_mask_2to4(const float* w, int N, int K, int mode, float* w_masked, uint8_t* mask, cudaStream_t stream);
+
 int launch_quantize_activations(const uint16_t* x, int64_t rows, int cols, int64_t ld_x, uint8_t* packed,
                                 uint8_t* scales, int swizzled, cudaStream_t stream);
 

@@ -195,4 +195,122 @@ int launch_quantize_activations(const uint16_t* x, int64_t rows, int cols, int64
   return cudaGetLastError() == cudaSuccess ? MCL4MOE_OK : MCL4MOE_ERR_CUDA;
 }
 
+// ---------------------------------------------------------------- 2:4 sparsity masks
+
+namespace {
+
+// The 90 4x4 0/1 tiles with exactly two ones in every row and every column,
+// in the enumeration order of the reference's catalog
+// (src/mcl4_coe/nvfp4.py:50-67: rows r0..r3 each one of the six 2-of-4 row
+// patterns in the listed order, nested r0 outermost), bit 4*row + col.  The
+// order matters: the best pattern is the first maximum.
+struct Catalog2to4 {
+  uint16_t tile[90];
+};
+
+constexpr Catalog2to4 make_catalog_2to4() {
+  constexpr uint8_t rows[6] = {0x3, 0x5, 0x9, 0x6, 0xA, 0xC};  // bit c = column c: 1100 1010 1001 0110 0101 0011
+  Catalog2to4 c{};
+  int n = 0;
+  for (int a = 0; a < 6; ++a)
+    for (int b = 0; b < 6; ++b)
+      for (int e = 0; e < 6; ++e)
+        for (int f = 0; f < 6; ++f) {
+          bool ok = true;
+          for (int col = 0; col < 4; ++col) {
+            const int sum = ((rows[a] >> col) & 1) + ((rows[b] >> col) & 1) + ((rows[e] >> col) & 1) +
+                            ((rows[f] >> col) & 1);
+            ok = ok && sum == 2;
+          }
+          if (ok && n < 90)
+            c.tile[n++] = uint16_t(rows[a] | (rows[b] << 4) | (rows[e] << 8) | (rows[f] << 12));
+        }
+  return c;
+}
+
+constexpr Catalog2to4 kCatalogHost = make_catalog_2to4();
+static_assert(kCatalogHost.tile[89] != 0, "the doubly 2:4 catalog has 90 tiles");
+__constant__ Catalog2to4 kCatalog = kCatalogHost;
+
+// mode 2 (transposable): one thread per 4x4 tile of W [N, K]; the pattern with the
+// largest sum of kept |w| (summed in fp32 over the tile's 16 positions in row-major
+// order, dropped ones contributing +0), first maximum on ties
+// (src/mcl4_coe/nvfp4.py:98-110).  mode 1 (row): one thread per 4 consecutive
+// elements of a row, keeping the two largest |w| (lower index first on ties;
+// :90-96).  w_masked = w * mask (a dropped negative weight becomes -0, as the
+// reference's ``w * mask.float()``); mask (optional) 0/1 bytes [N, K].
+__global__ void __launch_bounds__(256) mask_2to4_kernel(const float* __restrict__ w, int N, int K, int mode,
+                                                        float* __restrict__ w_masked, uint8_t* __restrict__ mask) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (mode == 2) {
+    const int tiles_k = K / 4;
+    if (i >= int64_t(N / 4) * tiles_k) return;
+    const int64_t r0 = (i / tiles_k) * 4, c0 = (i % tiles_k) * 4;
+    float v[16], a[16];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const float4 q = *reinterpret_cast<const float4*>(w + (r0 + r) * K + c0);
+      v[4 * r] = q.x, v[4 * r + 1] = q.y, v[4 * r + 2] = q.z, v[4 * r + 3] = q.w;
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) a[j] = fabsf(v[j]);
+    int best = 0;
+    float best_s = -1.f;
+    for (int p = 0; p < 90; ++p) {
+      const uint32_t m = kCatalog.tile[p];
+      float sum = 0.f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) sum = __fadd_rn(sum, ((m >> j) & 1u) ? a[j] : 0.f);
+      if (sum > best_s) best_s = sum, best = p;  // strict: the first maximum wins
+    }
+    const uint32_t m = kCatalog.tile[best];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      float4 o;
+      o.x = __fmul_rn(v[4 * r], float((m >> (4 * r)) & 1u));
+      o.y = __fmul_rn(v[4 * r + 1], float((m >> (4 * r + 1)) & 1u));
+      o.z = __fmul_rn(v[4 * r + 2], float((m >> (4 * r + 2)) & 1u));
+      o.w = __fmul_rn(v[4 * r + 3], float((m >> (4 * r + 3)) & 1u));
+      *reinterpret_cast<float4*>(w_masked + (r0 + r) * K + c0) = o;
+      if (mask)
+        *reinterpret_cast<uint32_t*>(mask + (r0 + r) * K + c0) =
+            ((m >> (4 * r)) & 1u) | (((m >> (4 * r + 1)) & 1u) << 8) | (((m >> (4 * r + 2)) & 1u) << 16) |
+            (((m >> (4 * r + 3)) & 1u) << 24);
+    }
+  } else {
+    const int groups = K / 4;
+    if (i >= int64_t(N) * groups) return;
+    const int64_t base = (i / groups) * K + (i % groups) * 4;
+    const float4 q = *reinterpret_cast<const float4*>(w + base);
+    const float v[4] = {q.x, q.y, q.z, q.w};
+    int first = 0;
+    for (int j = 1; j < 4; ++j)
+      if (fabsf(v[j]) > fabsf(v[first])) first = j;
+    int second = first == 0 ? 1 : 0;
+    for (int j = 0; j < 4; ++j)
+      if (j != first && fabsf(v[j]) > fabsf(v[second])) second = j;
+    float o[4];
+    uint32_t mb = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const bool keep = j == first || j == second;
+      o[j] = __fmul_rn(v[j], keep ? 1.f : 0.f);
+      mb |= uint32_t(keep) << (8 * j);
+    }
+    *reinterpret_cast<float4*>(w_masked + base) = make_float4(o[0], o[1], o[2], o[3]);
+    if (mask) *reinterpret_cast<uint32_t*>(mask + base) = mb;
+  }
+}
+
+}  // namespace
+
+int launch_mask_2to4(const float* w, int N, int K, int mode, float* w_masked, uint8_t* mask, cudaStream_t stream) {
+  const int64_t items = mode == 2 ? int64_t(N / 4) * (K / 4) : int64_t(N) * (K / 4);
+  if (items == 0) return MCL4MOE_OK;
+  const int64_t blocks = (items + 255) / 256;
+  if (blocks > 0x7fffffff) return MCL4MOE_ERR_UNSUPPORTED;
+  mask_2to4_kernel<<<dim3(unsigned(blocks)), 256, 0, stream>>>(w, N, K, mode, w_masked, mask);
+  return cudaGetLastError() == cudaSuccess ? MCL4MOE_OK : MCL4MOE_ERR_CUDA;
+}
+
 }  // namespace mcl4

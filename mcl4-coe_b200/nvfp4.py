@@ -13,6 +13,10 @@ Mirrors the reference's operator seam (src/mcl4_coe/nvfp4.py):
   the causal-row mode, :197-225), returning packed codes, e4m3 scales, g = 1.
 * :func:`export_reference_cache` — the same weight bytes in the reference's
   cache layout (``B_fwd``, ``Bs_fwd``, ``Bg``, ``B_bwd``, ``Bs_bwd``).
+* :func:`compute_2to4_mask` — the 2:4 sparsity masks (:70-110); experts whose
+  projection carries ``sparsity_mode`` "2to4_row" / "2to4_transposable" (the
+  reference's ``NVFP4Linear``) are masked before quantisation, as the
+  reference's cache does (:1017-1024), and run on the same dense GEMMs.
 
 Everything runs on CUDA through ``libmcl4moe.so``; CPU tensors are rejected
 with ``ValueError`` like the reference's ``quantize_nvfp4`` (:245-246).
@@ -43,8 +47,44 @@ def _require_cuda(t: Tensor, what: str) -> None:
         raise ValueError(f"{what} requires a CUDA tensor (the B200 path has no CPU fallback)")
 
 
+SPARSITY_MODES = ("none", "2to4_row", "2to4_transposable")  # src/mcl4_coe/nvfp4.py:31
+_MASK_MODE = {"2to4_row": 1, "2to4_transposable": 2}
+
+
 def _sparsity_mode(layer: nn.Module) -> str:
-    return str(getattr(layer, "sparsity_mode", "none"))
+    mode = str(getattr(layer, "sparsity_mode", "none"))
+    if mode not in SPARSITY_MODES:
+        raise ValueError(f"sparsity mode must be one of {SPARSITY_MODES}, got {mode!r}")
+    return mode
+
+
+def _mask_2to4(weight: Tensor, mode: str) -> tuple[Tensor, Tensor]:
+    """(w * mask fp32 [N, K], mask uint8 [N, K]) on the device (``mcl4moe_mask_2to4``)."""
+    _require_cuda(weight, "the 2:4 sparsity mask")
+    w = weight.detach().to(torch.float32).contiguous()
+    n, k = w.shape
+    if k % 4:
+        raise ValueError("the B200 2:4 mask needs in_features divisible by 4")
+    masked = torch.empty_like(w)
+    mask = torch.empty((n, k), dtype=torch.uint8, device=w.device)
+    _lib.check(_lib.load().mcl4moe_mask_2to4(w.data_ptr(), n, k, _MASK_MODE[mode], masked.data_ptr(),
+                                             mask.data_ptr(), _stream_handle()), "mcl4moe_mask_2to4")
+    return masked, mask
+
+
+@torch.no_grad()
+def compute_2to4_mask(weight: Tensor, mode: str = "2to4_transposable") -> Tensor:
+    """Boolean 2:4 mask of a weight ``[out_features, in_features]``
+    (src/mcl4_coe/nvfp4.py:70-110): ``"2to4_row"`` keeps the two largest |w| of every
+    4 consecutive inputs; ``"2to4_transposable"`` keeps, per 4x4 tile, the doubly
+    2:4 pattern of largest kept L1, so W and W.T are both 2:4; ``"none"`` keeps all."""
+    if mode not in SPARSITY_MODES:
+        raise ValueError(f"sparsity mode must be one of {SPARSITY_MODES}, got {mode!r}")
+    if mode == "none":
+        return torch.ones_like(weight, dtype=torch.bool)
+    if weight.ndim != 2:
+        raise ValueError("compute_2to4_mask expects a 2D weight matrix")
+    return _mask_2to4(weight, mode)[1].bool()
 
 
 class GroupedNVFP4Cache:
@@ -63,6 +103,7 @@ class GroupedNVFP4Cache:
         self.scales = torch.zeros((e_count, n_pad * k // 16), dtype=torch.uint8, device=device)
         self.g = torch.empty((e_count,), dtype=torch.float32, device=device)
         self.amax = torch.empty((e_count,), dtype=torch.float32, device=device)
+        self.masks: list[Tensor | None] = [None] * e_count  # bool [N, K] of 2:4-sparse experts
         self.n, self.k = n, k
 
 
@@ -98,15 +139,14 @@ def get_or_build_grouped_cache(experts: nn.ModuleList, proj_name: str) -> Groupe
     if not weights:
         raise ValueError("experts must be non-empty")
     for layer in layers:
-        if _sparsity_mode(layer) != "none":
-            raise NotImplementedError("2:4 sparse NVFP4 weights are not supported by the B200 path yet")
         if getattr(layer, "bias", None) is not None:
             raise ValueError("grouped NVFP4 experts must be bias-free (src/mcl4_coe/backbone.py:543-544)")
     e_count = len(weights)
     n, k = weights[0].shape
     device = weights[0].device
     _require_cuda(weights[0], "the NVFP4 weight cache")
-    cur = [(w._version, w.data_ptr(), tuple(w.shape)) for w in weights]
+    modes = [_sparsity_mode(layer) for layer in layers]
+    cur = [(w._version, w.data_ptr(), tuple(w.shape), m) for w, m in zip(weights, modes)]
     store = getattr(experts, CACHE_ATTR, None)
     if store is None:
         store = {}
@@ -121,7 +161,16 @@ def get_or_build_grouped_cache(experts: nn.ModuleList, proj_name: str) -> Groupe
     if entry.versions == cur:
         return entry
     dirty = [i for i, (old, new) in enumerate(zip(entry.versions, cur)) if old != new]
-    quantize_weight_slots([weights[i] for i in dirty], dirty, entry)
+    staged = []
+    for i in dirty:  # 2:4-sparse experts are masked before quantisation (src/mcl4_coe/nvfp4.py:1017-1024)
+        if modes[i] == "none":
+            entry.masks[i] = None
+            staged.append(weights[i])
+        else:
+            masked, mask = _mask_2to4(weights[i], modes[i])
+            entry.masks[i] = mask.bool()
+            staged.append(masked)
+    quantize_weight_slots(staged, dirty, entry)
     entry.versions = cur
     return entry
 
@@ -137,7 +186,9 @@ def invalidate_cache(experts: nn.ModuleList) -> None:
 def export_reference_cache(experts: nn.ModuleList, proj_name: str) -> dict[str, Tensor]:
     """Quantise every expert of ``proj_name`` into the reference's cache layout
     (``_get_or_build_grouped_nvfp4_cache`` entries, src/mcl4_coe/nvfp4.py:994-998)."""
-    weights = [getattr(e, proj_name).weight for e in experts]
+    layers = [getattr(e, proj_name) for e in experts]
+    weights = [layer.weight if _sparsity_mode(layer) == "none" else _mask_2to4(layer.weight, _sparsity_mode(layer))[0]
+               for layer in layers]
     e_count = len(weights)
     n, k = weights[0].shape
     dev = weights[0].device

@@ -270,3 +270,60 @@ def weights_to_mma_layout(b_fwd: np.ndarray, bs_fwd: np.ndarray):
     packed = np.ascontiguousarray(b_fwd.transpose(0, 2, 1))
     sw = np.stack([swizzle_scales(bs_fwd[i]).reshape(-1) for i in range(e)])
     return packed, sw
+
+
+# --------------------------------------------------------------------------
+# 2:4 structured sparsity masks (applied before weight quantisation).
+# --------------------------------------------------------------------------
+
+def catalog_2to4() -> np.ndarray:
+    """The 90 4x4 0/1 tiles with two ones in every row and column, float32 [90, 16]
+    row-major, in the order of src/mcl4_coe/nvfp4.py:50-67 (four nested loops over
+    the six 2-of-4 row patterns, first row outermost)."""
+    rows = [(1, 1, 0, 0), (1, 0, 1, 0), (1, 0, 0, 1), (0, 1, 1, 0), (0, 1, 0, 1), (0, 0, 1, 1)]
+    tiles = [a + b + c + d for a in rows for b in rows for c in rows for d in rows
+             if all(a[j] + b[j] + c[j] + d[j] == 2 for j in range(4))]
+    return np.array(tiles, dtype=np.float32)
+
+
+def mask_2to4(w: np.ndarray, mode: str) -> np.ndarray:
+    """Boolean mask of ``compute_2to4_mask`` (src/mcl4_coe/nvfp4.py:70-110).
+
+    ``"2to4_row"`` (or a side not divisible by 4): the two largest |w| of every 4
+    consecutive elements of a row (zero-padded), ties to the lower index (the
+    reference's ``topk`` leaves tie order to the backend).  ``"2to4_transposable"``:
+    per 4x4 tile the catalog pattern with the largest float32 sum of kept |w|, first
+    maximum on ties (``argmax``)."""
+    rows, cols = w.shape
+    a = np.abs(w.astype(np.float32))
+    if mode == "2to4_row" or rows % 4 or cols % 4:
+        pad = round_up(cols, 4) - cols
+        g = np.pad(a, ((0, 0), (0, pad))).reshape(rows, -1, 4)
+        order = np.argsort(-g, axis=-1, kind="stable")[..., :2]
+        m = np.zeros(g.shape, dtype=bool)
+        np.put_along_axis(m, order, True, axis=-1)
+        return m.reshape(rows, -1)[:, :cols]
+    cat = catalog_2to4()
+    tiles = a.reshape(rows // 4, 4, cols // 4, 4).transpose(0, 2, 1, 3).reshape(-1, 16)
+    best = np.argmax(tiles @ cat.T, axis=-1)
+    chosen = cat[best].astype(bool)
+    return chosen.reshape(rows // 4, cols // 4, 4, 4).transpose(0, 2, 1, 3).reshape(rows, cols)
+
+
+def mask_tie_groups(w: np.ndarray, mode: str) -> np.ndarray:
+    """Boolean [N, K]: elements whose mask the reference leaves to tie order or to
+    float32 summation order — row mode: the 4-groups whose 2nd and 3rd largest |w|
+    are equal; transposable mode: the 4x4 tiles whose two best pattern scores are
+    within 2e-6 relative (the sums' rounding depends on the BLAS kernel's order)."""
+    rows, cols = w.shape
+    a = np.abs(w.astype(np.float32))
+    if mode == "2to4_row" or rows % 4 or cols % 4:
+        pad = round_up(cols, 4) - cols
+        g = np.sort(np.pad(a, ((0, 0), (0, pad))).reshape(rows, -1, 4), axis=-1)
+        tie = g[..., 1] == g[..., 2]
+        return np.repeat(tie, 4, axis=-1)[:, :cols]
+    tiles = a.reshape(rows // 4, 4, cols // 4, 4).transpose(0, 2, 1, 3).reshape(-1, 16).astype(np.float64)
+    s = np.sort(tiles @ catalog_2to4().astype(np.float64).T, axis=-1)
+    near = (s[:, -1] - s[:, -2]) <= 2e-6 * np.maximum(s[:, -1], 1e-30)
+    return np.repeat(near[:, None], 16, axis=1).reshape(rows // 4, cols // 4, 4, 4).transpose(0, 2, 1, 3).reshape(
+        rows, cols)

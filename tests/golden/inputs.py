@@ -164,3 +164,23 @@ def variant_prior(name: str, t: int, e: int, frac: float | None) -> np.ndarray |
         return None
     return (rng(zlib.crc32(name.encode())).uniform(size=(t, e)) < frac).astype(np.float32)
 
+
+def sparse_cases():
+    """(name, float32 [D, N, K]) stacks for the 2:4 masks (src/mcl4_coe/nvfp4.py:70-110):
+    the weight-quantiser stacks, a 256 x 256 random stack, and tiles with exact ties
+    (repeated magnitudes, zeros, sign-only differences)."""
+    r = rng(210)
+    big = (r.standard_normal((2, 256, 256), dtype=np.float32) * 0.02).astype(np.float32)
+    ties = np.tile(np.array([0.5, -0.5, 0.25, 0.0], np.float32), (1, 32, 16)).reshape(1, 32, 64)
+    ties = np.concatenate([ties, np.abs(ties), -ties], axis=0)
+    ties[1, 4:8, 8:12] = np.float32(0.75)
+    return weight_quant_cases() + [("w_big", big), ("w_ties", ties)]
+
+
+def sparse_layer_cases():
+    """(name, moe_case, sparsity mode of the experts' projections)."""
+    return [
+        ("s_transposable", moe_case(600, 128, 256, 8, 2, 256), "2to4_transposable"),
+        ("s_row", moe_case(601, 128, 256, 8, 2, 256, valid_frac=0.8), "2to4_row"),
+    ]
+

@@ -17,6 +17,9 @@ outputs of the reference's own functions on seeded inputs:
 * ``layer.npz``       — the layer output of the unmodified ``SparseMoE.forward``
   whose expert projections were replaced by dequantised-FP4 linears built
   from the reference's ``_quantize_nvfp4_core`` / ``_dequantize_nvfp4``.
+* ``sparse.npz``      — ``compute_2to4_mask`` (:70-110) in both modes, the grouped
+  quantiser's bytes of the masked weights (:1017-1024), and the dequantised-FP4
+  layer whose experts carry 2:4-masked weights.
 * ``variants.npz``    — the same dequantised-FP4 layer with the routing
   variants switched on (mitotic twins, lineage families, coverage penalty,
   dense subsets, sequence-diversity / orthogonality losses): outputs, losses,
@@ -45,6 +48,8 @@ from inputs import (  # noqa: E402  (shared with the tests)
     act_quant_cases,
     layer_case,
     routing_cases,
+    sparse_cases,
+    sparse_layer_cases,
     variant_cases,
     variant_prior,
     weight_quant_cases,
@@ -215,6 +220,34 @@ def main() -> None:
         out[f"{name}__topk_indices"] = rec["topk_indices"].numpy()
         out[f"{name}__perm"] = rec["perm"].numpy()
     np.savez_compressed(HERE / "layer.npz", **out)
+
+    # ---------------------------------------------------------------- 2:4 sparsity
+    out = {}
+    for name, w in sparse_cases():
+        out[f"{name}__digest"] = np.array(digest(w))
+        for mode in ("2to4_row", "2to4_transposable"):
+            masks = np.stack([nv.compute_2to4_mask(torch.from_numpy(w[i]), mode=mode).numpy() for i in range(len(w))])
+            out[f"{name}__{mode}__mask"] = masks.astype(np.uint8)
+            if w.shape[1] % 16 == 0 and w.shape[2] % 64 == 0:
+                masked = torch.from_numpy(w) * torch.from_numpy(masks).float()
+                b_fwd, bs_fwd, bg, _, _ = nv._quantize_grouped_weights_core(masked)
+                out[f"{name}__{mode}__b_fwd"] = b_fwd.numpy()
+                out[f"{name}__{mode}__bs_fwd"] = bs_fwd.view(torch.uint8).numpy()
+                out[f"{name}__{mode}__bg"] = bg.numpy()
+    for name, case, mode in sparse_layer_cases():
+        masked = {}
+        for proj, key in (("up_proj", "w_up"), ("down_proj", "w_dn")):
+            masked[key] = np.stack([(torch.from_numpy(case[key][i])
+                                     * nv.compute_2to4_mask(torch.from_numpy(case[key][i]), mode=mode).float()).numpy()
+                                    for i in range(case["e"])])
+        mcase = dict(case, w_up=masked["w_up"], w_dn=masked["w_dn"])
+        moe, y, aux, z, counts, rec = run(mcase, fake_experts=True)
+        out[f"{name}__digest"] = np.array(digest(case["x_bf16_bits"], case["wr"], case["w_up"], case["w_dn"]))
+        out[f"{name}__out_bf16"] = y.view(torch.int16).numpy().view(np.uint16)
+        out[f"{name}__aux"] = np.float32(aux.item())
+        out[f"{name}__z"] = np.float32(z.item())
+        out[f"{name}__counts"] = counts.numpy()
+    np.savez_compressed(HERE / "sparse.npz", **out)
 
     # ---------------------------------------------------------------- routing variants
     out = {}
