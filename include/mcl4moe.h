@@ -61,6 +61,36 @@ int mcl4moe_device_supported(void);
 int mcl4moe_read_error(int32_t* device_error_word, int32_t* host_value, mcl4moe_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Replaces quantize_nvfp4 / _quantize_nvfp4_core in the one-dimensional modes
+ * (src/mcl4_coe/nvfp4.py:197-259): 1x16 row blocks of a bf16 (dtype 0) or fp32
+ * (dtype 1) matrix x [rows, cols] (row stride ld elements) with global scale
+ * g = 1 (causal != 0, causal_row_scale=True) or g = max(amax/2688, FLT_MIN)
+ * (amax > 0, else 1).  packed: [rows, cols/2]; scales: the swizzled 128x4-atom
+ * layout of _swizzle_scales for rows_pad rows (multiple of 128, >= rows;
+ * padding rows get zero scales); global_scale: device fp32 [1];
+ * amax_scratch: device fp32 [1].  Requires cols % 64 == 0.
+ * ------------------------------------------------------------------------ */
+int mcl4moe_quantize_rows(const void* x, int dtype, int64_t rows, int cols, int64_t ld, int causal, uint8_t* packed,
+                          uint8_t* scales, int64_t rows_pad, float* global_scale, float* amax_scratch,
+                          mcl4moe_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Replaces nvfp4_mm (src/mcl4_coe/nvfp4.py:285-334) with a prequantised B,
+ * as _NVFP4Linear.forward calls it (:398-429): out (fp32 [M, N]) =
+ * deq(A) @ deq(B).T * g_a * g_b (+ bias [N], added after the scaling), where A
+ * is x (bf16 dtype 0 / fp32 dtype 1, [M, K] contiguous) quantised here in
+ * one-dimensional mode (causal: g_a = 1, else tensor-wise g_a) and B is
+ * packed [N, K/2] with swizzled scales for N rows and global scale b_g (device
+ * fp32 [1]) — the output of mcl4moe_quantize_rows or, for a weight,
+ * mcl4moe_quantize_weights with n = 1.  a_global_scale (device fp32 [1] or
+ * NULL) receives g_a.  Requires K % 256 == 0, N % 256 == 0 (pad otherwise).
+ * ------------------------------------------------------------------------ */
+size_t mcl4moe_nvfp4_mm_workspace_size(int64_t M, int K);
+int mcl4moe_nvfp4_mm(const void* x, int dtype, int64_t M, int K, int causal, const uint8_t* b, const uint8_t* b_scales,
+                     const float* b_g, int N, const float* bias, float* out, float* a_global_scale,
+                     int32_t* error_word, void* workspace, size_t workspace_bytes, mcl4moe_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Replaces compute_2to4_mask (src/mcl4_coe/nvfp4.py:70-110), applied to a
  * weight before its NVFP4 quantisation when a layer's sparsity_mode is not
  * "none" (:1020-1023).  W fp32 [N, K] row-major; mode 1 = "2to4_row" (keep the

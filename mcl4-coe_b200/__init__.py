@@ -18,7 +18,11 @@ from .nvfp4 import (
     export_reference_cache,
     get_gemm_counts,
     get_or_build_grouped_cache,
+    NVFP4Linear,
+    convert_linear_to_nvfp4,
     nvfp4_grouped_linear,
+    nvfp4_mm,
+    quantize_activations,
     quantize_nvfp4,
     reset_gemm_counts,
 )
@@ -38,6 +42,10 @@ __all__ = [
     "reset_gemm_counts",
     "compute_2to4_mask",
     "SPARSITY_MODES",
+    "NVFP4Linear",
+    "convert_linear_to_nvfp4",
+    "nvfp4_mm",
+    "quantize_activations",
 ]
 
 

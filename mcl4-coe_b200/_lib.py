@@ -24,6 +24,9 @@ EXPORTS = (
     "mcl4moe_read_error",
     "mcl4moe_quantize_weights",
     "mcl4moe_mask_2to4",
+    "mcl4moe_quantize_rows",
+    "mcl4moe_nvfp4_mm_workspace_size",
+    "mcl4moe_nvfp4_mm",
     "mcl4moe_quantize_activations",
     "mcl4moe_route_workspace_size",
     "mcl4moe_route",
@@ -111,6 +114,14 @@ def load() -> ctypes.CDLL:
     lib.mcl4moe_device_supported.restype = c_int
     lib.mcl4moe_read_error.restype = c_int
     lib.mcl4moe_read_error.argtypes = [c_void_p, POINTER(c_int32), c_void_p]
+    lib.mcl4moe_quantize_rows.restype = c_int
+    lib.mcl4moe_quantize_rows.argtypes = [c_void_p, c_int, c_int64, c_int, c_int64, c_int, c_void_p, c_void_p, c_int64,
+                                          c_void_p, c_void_p, c_void_p]
+    lib.mcl4moe_nvfp4_mm_workspace_size.restype = c_size_t
+    lib.mcl4moe_nvfp4_mm_workspace_size.argtypes = [c_int64, c_int]
+    lib.mcl4moe_nvfp4_mm.restype = c_int
+    lib.mcl4moe_nvfp4_mm.argtypes = [c_void_p, c_int, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int,
+                                     c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]
     lib.mcl4moe_mask_2to4.restype = c_int
     lib.mcl4moe_mask_2to4.argtypes = [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]
     lib.mcl4moe_quantize_weights.restype = c_int

@@ -128,6 +128,108 @@ int mcl4moe_mask_2to4(const float* w, int N, int K, int mode, float* w_masked, u
   return launch_mask_2to4(w, N, K, mode, w_masked, mask, stream);
 }
 
+int mcl4moe_quantize_rows(const void* x, int dtype, int64_t rows, int cols, int64_t ld, int causal, uint8_t* packed,
+                          uint8_t* scales, int64_t rows_pad, float* global_scale, float* amax_scratch,
+                          mcl4moe_stream_t stream) {
+  if (rows < 0 || cols <= 0 || (dtype != 0 && dtype != 1) || !packed || !scales || !global_scale || !amax_scratch)
+    return MCL4MOE_ERR_INVALID;
+  if (cols % 16 != 0) return MCL4MOE_ERR_INVALID;  // src/mcl4_coe/nvfp4.py:248-249
+  if (cols % 64 != 0) return MCL4MOE_ERR_UNSUPPORTED;
+  if (rows_pad < rows || rows_pad % 128 != 0 || ld < cols || (rows > 0 && !x)) return MCL4MOE_ERR_INVALID;
+  return launch_quantize_rows(x, dtype, rows, cols, ld, causal, packed, scales, rows_pad, global_scale, amax_scratch,
+                              nullptr, nullptr, stream);
+}
+
+}  // extern "C"
+
+namespace {
+
+struct MmWorkspace {
+  uint8_t* aq;
+  uint8_t* as;
+  int32_t* pad_start;
+  int32_t* counts;
+  int32_t* offs_start;
+  float* g_a;
+  float* g_ab;
+  float* amax;
+  int32_t* err;
+  size_t bytes;
+};
+
+MmWorkspace mm_workspace(void* base, int64_t M, int K) {
+  MmWorkspace w{};
+  const int64_t mp = (M + kSegRows - 1) / kSegRows * kSegRows;
+  uint8_t* p = static_cast<uint8_t*>(base);
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    uint8_t* r = p ? p + off : nullptr;
+    off += align256(bytes);
+    return r;
+  };
+  w.aq = take(size_t(mp) * K / 2);
+  w.as = take(size_t(mp) * K / 16);
+  w.pad_start = reinterpret_cast<int32_t*>(take(2 * sizeof(int32_t)));
+  w.counts = reinterpret_cast<int32_t*>(take(sizeof(int32_t)));
+  w.offs_start = reinterpret_cast<int32_t*>(take(sizeof(int32_t)));
+  w.g_a = reinterpret_cast<float*>(take(sizeof(float)));
+  w.g_ab = reinterpret_cast<float*>(take(sizeof(float)));
+  w.amax = reinterpret_cast<float*>(take(sizeof(float)));
+  w.err = reinterpret_cast<int32_t*>(take(sizeof(int32_t)));
+  w.bytes = off;
+  return w;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t mcl4moe_nvfp4_mm_workspace_size(int64_t M, int K) {
+  if (M < 0 || K <= 0) return 0;
+  return mm_workspace(nullptr, M, K).bytes;
+}
+
+int mcl4moe_nvfp4_mm(const void* x, int dtype, int64_t M, int K, int causal, const uint8_t* b, const uint8_t* b_scales,
+                     const float* b_g, int N, const float* bias, float* out, float* a_global_scale,
+                     int32_t* error_word, void* workspace, size_t workspace_bytes, mcl4moe_stream_t stream) {
+  if (M < 0 || K <= 0 || N <= 0 || (dtype != 0 && dtype != 1) || !b || !b_scales || !b_g || !out || !workspace)
+    return MCL4MOE_ERR_INVALID;
+  if (M > 0 && !x) return MCL4MOE_ERR_INVALID;
+  if (K % 16 != 0) return MCL4MOE_ERR_INVALID;
+  if (K % 256 != 0 || N % 256 != 0) return MCL4MOE_ERR_UNSUPPORTED;
+  if (!aligned16(out) || !aligned16(b) || !aligned16(b_scales) || (bias && !aligned16(bias))) return MCL4MOE_ERR_INVALID;
+  const MmWorkspace w = mm_workspace(workspace, M, K);
+  if (workspace_bytes < w.bytes) return MCL4MOE_ERR_WORKSPACE;
+  if (M == 0) return MCL4MOE_OK;
+  const int64_t mp = (M + kSegRows - 1) / kSegRows * kSegRows;
+  cudaStream_t s = stream;
+  int32_t* err = error_word ? error_word : w.err;
+  if (!error_word && cudaMemsetAsync(err, 0, sizeof(int32_t), s) != cudaSuccess) return MCL4MOE_ERR_CUDA;
+  int st = launch_quantize_rows(x, dtype, M, K, K, causal, w.aq, w.as, mp, w.g_a, w.amax, b_g, w.g_ab, s);
+  if (st != MCL4MOE_OK) return st;
+  if (a_global_scale && cudaMemcpyAsync(a_global_scale, w.g_a, sizeof(float), cudaMemcpyDeviceToDevice, s) !=
+                            cudaSuccess)
+    return MCL4MOE_ERR_CUDA;
+  if ((st = launch_single_segment(M, mp, w.pad_start, w.counts, w.offs_start, s)) != MCL4MOE_OK) return st;
+  GemmArgs g{};
+  g.pad_start = w.pad_start;
+  g.row_count = w.counts;
+  g.out_row_base = w.offs_start;
+  g.a_scales = w.as;
+  g.b_scales = b_scales;
+  g.b_g = w.g_ab;
+  g.E = 1;
+  g.K = K;
+  g.N_total = N;
+  g.n_tiles = N / 256;
+  g.mode = 1;
+  g.y32 = out;
+  g.bias = bias;
+  g.ldy = N;
+  g.err = err;
+  return launch_grouped_gemm(w.aq, mp, b, g, s);
+}
+
 int mcl4moe_quantize_activations(const uint16_t* x, int64_t rows, int cols, int64_t ld_x, uint8_t* packed,
                                  uint8_t* scales, int swizzled, mcl4moe_stream_t stream) {
   if (rows < 0 || cols <= 0 || ld_x < cols || !x || !packed || !scales) return MCL4MOE_ERR_INVALID;

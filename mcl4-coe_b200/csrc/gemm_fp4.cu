@@ -433,6 +433,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           tma_store_2d(&tmap_y, my_buf, c.nt * kBN + sub * 64, int(p));  // lane 0 holds the warp's first row
           bulk_commit_group();
         }
+      } else if (local < rows_e && args.y32 != nullptr) {
+        // fp32 rows acc * g [+ bias] into unpadded destination rows (single-matrix
+        // NVFP4 GEMM, src/mcl4_coe/nvfp4.py:318-334 and :425-427): product and sum
+        // rounded separately, as the reference's scaled_mm result + bias
+        const int64_t dst_row = args.out_row_base ? int64_t(args.out_row_base[c.e]) + local : p;
+        const int col0 = c.nt * kBN + sub * 64;
+        float4* dst = reinterpret_cast<float4*>(args.y32 + dst_row * args.ldy + col0);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const uint32_t* src = i < 8 ? va + 4 * i : vb + 4 * (i - 8);
+          float o[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            o[j] = __fmul_rn(__uint_as_float(src[j]), gb);
+            if (args.bias) o[j] = __fadd_rn(o[j], __ldg(args.bias + col0 + 4 * i + j));
+          }
+          dst[i] = make_float4(o[0], o[1], o[2], o[3]);
+        }
       } else if (local < rows_e) {
         // y rows into unpadded destination rows, valid rows only
         const int64_t dst_row = args.out_row_base ? int64_t(args.out_row_base[c.e]) + local : p;

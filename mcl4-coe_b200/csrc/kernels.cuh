@@ -150,6 +150,18 @@ int launch_quantize_weights(const float* const* w_ptrs, const int32_t* slots, in
                             uint8_t* scales, float* gscale, uint8_t* rb, uint8_t* rbs, uint8_t* rbb, uint8_t* rbbs,
                             float* amax, cudaStream_t stream);
 
+// One-dimensional NVFP4 rows (1x16 blocks) of a bf16 (dtype 0) or fp32 (dtype 1)
+// matrix with global scale g = 1 (causal) or amax/2688; packed [rows, cols/2],
+// swizzled scales for rows_pad rows (padding rows zero), g written to *g;
+// with g_b, *g_ab = g * *g_b.  amax: device scratch float.  cols % 64 == 0.
+int launch_quantize_rows(const void* x, int dtype, int64_t rows, int cols, int64_t ld, int causal, uint8_t* packed,
+                         uint8_t* scales, int64_t rows_pad, float* g, float* amax, const float* g_b, float* g_ab,
+                         cudaStream_t s);
+
+// pad_start = {0, rows_pad}, counts = {rows}, offs_start = {0}: one GEMM segment.
+int launch_single_segment(int64_t rows, int64_t rows_pad, int32_t* pad_start, int32_t* counts, int32_t* offs_start,
+                          cudaStream_t s);
+
 // 2:4 sparsity mask of W [N, K] (mode 1: 2 of every 4 along K; mode 2: doubly 2:4
 // per 4x4 tile) and the masked weights.
 int launch_mask_2to4(const float* w, int N, int K, int mode, float* w_masked, uint8_t* mask, cudaStream_t stream);
@@ -198,6 +210,8 @@ struct GemmArgs {
   uint16_t* h_dbg;              // mode 0: bf16 [M, F] or nullptr
   const float* row_w;           // mode 1: per padded row weight or nullptr
   uint16_t* y;                  // mode 1: bf16 output
+  float* y32;                   // mode 2: fp32 output instead of y (acc * g [+ bias]), or nullptr
+  const float* bias;            // mode 2 with y32: [N_total] added after the scale, or nullptr
   int64_t ldy;
   int32_t* err;
 };

@@ -7,6 +7,8 @@
 //   q   = e2m1(w * min(1/(s_t g), FLT_MAX))           packed along K
 // Activations restate _quantize_nvfp4_core(two_dimensional=False,
 // causal_row_scale=True) (src/mcl4_coe/nvfp4.py:197-225) with g = 1.
+#include <algorithm>
+
 #include "kernels.cuh"
 
 namespace mcl4 {
@@ -192,6 +194,123 @@ int launch_quantize_activations(const uint16_t* x, int64_t rows, int cols, int64
                                 uint8_t* scales, int swizzled, cudaStream_t stream) {
   if (rows == 0) return MCL4MOE_OK;
   act_quant_kernel<<<unsigned((rows + 7) / 8), 256, 0, stream>>>(x, rows, cols, ld_x, packed, scales, swizzled);
+  return cudaGetLastError() == cudaSuccess ? MCL4MOE_OK : MCL4MOE_ERR_CUDA;
+}
+
+// ---------------------------------------------------------------- 1-D rows with a global scale
+
+namespace {
+
+template <typename InT>
+__device__ __forceinline__ float load_f32(const InT* p);
+template <>
+__device__ __forceinline__ float load_f32<float>(const float* p) { return __ldg(p); }
+template <>
+__device__ __forceinline__ float load_f32<uint16_t>(const uint16_t* p) { return bf16_to_f32(__ldg(p)); }
+
+// max |x| over a [rows, cols] matrix (row stride ld) into *amax (zeroed before):
+// float bits of non-negative values order like unsigned ints.
+template <typename InT>
+__global__ void __launch_bounds__(256) rows_amax_kernel(const InT* __restrict__ x, int64_t rows, int cols, int64_t ld,
+                                                        float* amax) {
+  float m = 0.f;
+  const int64_t n = rows * cols;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
+    m = fmaxf(m, fabsf(load_f32(x + (i / cols) * ld + (i % cols))));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(reinterpret_cast<unsigned int*>(amax), __float_as_uint(m));
+}
+
+// g = 1 (causal row scales) or amax / 2688 clamped to the smallest normal
+// (src/mcl4_coe/nvfp4.py:203-208); optionally g_ab = g * g_b (the GEMM's scale).
+__global__ void rows_global_scale_kernel(const float* amax, int causal, float* g, const float* g_b, float* g_ab) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  float v = 1.f;
+  if (!causal) {
+    const float a = *amax;
+    v = fmaxf(a > 0.f ? __fdiv_rn(a, 2688.0f) : 1.0f, kFltMinNormal);
+  }
+  *g = v;
+  if (g_ab) *g_ab = __fmul_rn(v, *g_b);
+}
+
+// One warp per row, lane l takes 16-element blocks l, l+32, ...: scale
+// e4m3(min(amax16 / (6 g), 448)), inverse 1 / (scale * g), E2M1 codes of x * inverse
+// (src/mcl4_coe/nvfp4.py:209-225, one-dimensional mode); scales into the swizzled atoms.
+template <typename InT>
+__global__ void __launch_bounds__(256) rows_quant_kernel(const InT* __restrict__ x, int64_t rows, int cols, int64_t ld,
+                                                         const float* __restrict__ g_ptr, uint8_t* __restrict__ packed,
+                                                         uint8_t* __restrict__ scales) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float g = *g_ptr;
+  const float six_g = __fmul_rn(6.0f, g);
+  const int nblk = cols / 16;
+  for (int b = lane; b < nblk; b += 32) {
+    float v[16];
+    float m = 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      v[j] = load_f32(x + row * ld + b * 16 + j);
+      m = fmaxf(m, fabsf(v[j]));
+    }
+    const uint32_t sc = f32_to_e4m3(fminf(__fdiv_rn(m, six_g), 448.0f));
+    const float inv = inverse_decoding(__fmul_rn(e4m3_to_f32(sc), g));
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      lo |= e2m1_code(__fmul_rn(v[j], inv)) << (4 * j);
+      hi |= e2m1_code(__fmul_rn(v[8 + j], inv)) << (4 * j);
+    }
+    *reinterpret_cast<uint2*>(packed + row * (cols / 2) + b * 8) = make_uint2(lo, hi);
+    scales[swizzled_scale_offset(uint64_t(row), uint32_t(b), uint32_t(nblk))] = uint8_t(sc);
+  }
+}
+
+__global__ void single_segment_kernel(int64_t rows, int64_t rows_pad, int32_t* pad_start, int32_t* counts,
+                                      int32_t* offs_start) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  pad_start[0] = 0;
+  pad_start[1] = int32_t(rows_pad);
+  counts[0] = int32_t(rows);
+  offs_start[0] = 0;
+}
+
+}  // namespace
+
+int launch_quantize_rows(const void* x, int dtype, int64_t rows, int cols, int64_t ld, int causal, uint8_t* packed,
+                         uint8_t* scales, int64_t rows_pad, float* g, float* amax, const float* g_b, float* g_ab,
+                         cudaStream_t s) {
+  const size_t scale_bytes = size_t(rows_pad) * size_t(cols / 16);
+  if (cudaMemsetAsync(scales, 0, scale_bytes, s) != cudaSuccess) return MCL4MOE_ERR_CUDA;
+  if (!causal) {
+    if (cudaMemsetAsync(amax, 0, sizeof(float), s) != cudaSuccess) return MCL4MOE_ERR_CUDA;
+    const int64_t n = rows * cols;
+    const unsigned blocks = unsigned(std::min<int64_t>((n + 255) / 256, 4 * 148));
+    if (blocks > 0) {
+      if (dtype == 0)
+        rows_amax_kernel<uint16_t><<<blocks, 256, 0, s>>>(static_cast<const uint16_t*>(x), rows, cols, ld, amax);
+      else
+        rows_amax_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float*>(x), rows, cols, ld, amax);
+    }
+  }
+  rows_global_scale_kernel<<<1, 32, 0, s>>>(amax, causal, g, g_b, g_ab);
+  if (rows > 0) {
+    const unsigned blocks = unsigned((rows + 7) / 8);
+    if (dtype == 0)
+      rows_quant_kernel<uint16_t><<<blocks, 256, 0, s>>>(static_cast<const uint16_t*>(x), rows, cols, ld, g, packed,
+                                                        scales);
+    else
+      rows_quant_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float*>(x), rows, cols, ld, g, packed, scales);
+  }
+  return cudaGetLastError() == cudaSuccess ? MCL4MOE_OK : MCL4MOE_ERR_CUDA;
+}
+
+int launch_single_segment(int64_t rows, int64_t rows_pad, int32_t* pad_start, int32_t* counts, int32_t* offs_start,
+                          cudaStream_t s) {
+  single_segment_kernel<<<1, 32, 0, s>>>(rows, rows_pad, pad_start, counts, offs_start);
   return cudaGetLastError() == cudaSuccess ? MCL4MOE_OK : MCL4MOE_ERR_CUDA;
 }
 

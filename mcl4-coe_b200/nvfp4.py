@@ -9,8 +9,15 @@ Mirrors the reference's operator seam (src/mcl4_coe/nvfp4.py):
   (a new ModuleList, or a changed expert count) rebuilds it naturally.
 * :func:`nvfp4_grouped_linear` — same signature and result as the reference's
   ``nvfp4_grouped_linear(inputs, experts, proj_name, offs)`` (:1219-1227).
-* :func:`quantize_nvfp4` — activation quantisation (``_quantize_nvfp4_core`` in
-  the causal-row mode, :197-225), returning packed codes, e4m3 scales, g = 1.
+* :func:`quantize_activations` — the MoE path's activation quantisation
+  (``_quantize_nvfp4_core`` in the causal-row mode, :197-225): packed codes,
+  e4m3 scales (row-major or swizzled), g = 1.
+* :func:`quantize_nvfp4`, :func:`nvfp4_mm`, :class:`NVFP4Linear`,
+  :func:`convert_linear_to_nvfp4` — the single-matrix operators with the
+  reference's signatures (:235-259, :285-334, :398-542, :634-695): quantisation
+  in every mode but stochastic rounding, the NVFP4 GEMM with fp32 output on the
+  tcgen05 grouped kernel (one segment), the projection module with its cached
+  (optionally 2:4-masked) weight, forward only.
 * :func:`export_reference_cache` — the same weight bytes in the reference's
   cache layout (``B_fwd``, ``Bs_fwd``, ``Bg``, ``B_bwd``, ``Bs_bwd``).
 * :func:`compute_2to4_mask` — the 2:4 sparsity masks (:70-110); experts whose
@@ -207,8 +214,8 @@ def export_reference_cache(experts: nn.ModuleList, proj_name: str) -> dict[str, 
 
 
 @torch.no_grad()
-def quantize_nvfp4(matrix: Tensor, *, swizzled: bool = False) -> tuple[Tensor, Tensor, Tensor]:
-    """Activation quantisation with 1x16 row scales and global scale 1.
+def quantize_activations(matrix: Tensor, *, swizzled: bool = False) -> tuple[Tensor, Tensor, Tensor]:
+    """The MoE path's activation quantisation: 1x16 row scales and global scale 1.
 
     src/mcl4_coe/nvfp4.py:235-259 with ``causal_row_scale=True`` (no global
     amax, so later rows never influence earlier rows' bytes).  Returns
@@ -276,3 +283,246 @@ def nvfp4_grouped_linear(inputs: Tensor, experts: nn.ModuleList, proj_name: str,
     _lib.check(st, "mcl4moe_grouped_linear")
     _GEMM_COUNTS["forward"] += e_count
     return out
+
+
+# ---------------------------------------------------------------------------- single-matrix operators
+
+def _round_up(value: int, multiple: int) -> int:
+    return (value + multiple - 1) // multiple * multiple
+
+
+_FP4_DTYPE = getattr(torch, "float4_e2m1fn_x2", torch.uint8)
+
+
+@torch.no_grad()
+def quantize_nvfp4(matrix: Tensor, *, two_dimensional: bool = False, stochastic: bool = False,
+                   causal_row_scale: bool = False) -> tuple[Tensor, Tensor, Tensor]:
+    """Packed FP4 (``float4_e2m1fn_x2`` [R, C/2]), swizzled E4M3 scales ([R rounded to 128,
+    C/16 rounded to 4], the 128x4-atom layout) and fp32 global scale [1]
+    (src/mcl4_coe/nvfp4.py:235-259): one-dimensional 1x16 blocks with g = amax/2688, or
+    g = 1 when ``causal_row_scale``; ``two_dimensional``: 16x16 tiles with g = amax/2688.
+    Stochastic rounding (the backward's gradient quantisation) is not served."""
+    if matrix.ndim != 2 or not matrix.is_floating_point() or matrix.numel() == 0:
+        raise ValueError("NVFP4 quantization requires a nonempty floating-point matrix")
+    _require_cuda(matrix, "NVFP4 quantization")
+    rows, cols = matrix.shape
+    if cols % 16 or (two_dimensional and rows % 16):
+        raise ValueError("NVFP4 blocks require aligned dimensions divisible by 16")
+    if stochastic:
+        raise NotImplementedError("stochastic NVFP4 rounding (backward only) is not served by the B200 path")
+    dev = matrix.device
+    cp = _round_up(cols, 64)  # scale columns padded to whole 4-column atoms, as _swizzle_scales pads them
+    if two_dimensional:
+        w = matrix.detach().to(torch.float32)
+        if cp != cols:
+            w = torch.nn.functional.pad(w, (0, cp - cols))
+        cache = GroupedNVFP4Cache(1, rows, cp, dev)
+        quantize_weight_slots([w], [0], cache)
+        packed = cache.packed[0][:, : cols // 2].contiguous()
+        scales = cache.scales[0].view(_round_up(rows, 128), cp // 16)
+        return packed.view(_FP4_DTYPE), scales.view(torch.float8_e4m3fn), cache.g.clone()
+    x = matrix.detach()
+    dtype = 0 if x.dtype == torch.bfloat16 else 1
+    x = x.contiguous() if dtype == 0 else x.to(torch.float32).contiguous()
+    if cp != cols:
+        x = torch.nn.functional.pad(x, (0, cp - cols))
+    rp = _round_up(rows, 128)
+    packed = torch.empty((rows, cp // 2), dtype=torch.uint8, device=dev)
+    scales = torch.empty((rp, cp // 16), dtype=torch.uint8, device=dev)
+    g = torch.empty((1,), dtype=torch.float32, device=dev)
+    amax = torch.empty((1,), dtype=torch.float32, device=dev)
+    _lib.check(_lib.load().mcl4moe_quantize_rows(x.data_ptr(), dtype, rows, cp, cp, int(bool(causal_row_scale)),
+                                                 packed.data_ptr(), scales.data_ptr(), rp, g.data_ptr(),
+                                                 amax.data_ptr(), _stream_handle()), "mcl4moe_quantize_rows")
+    return packed[:, : cols // 2].contiguous().view(_FP4_DTYPE), scales.view(torch.float8_e4m3fn), g
+
+
+def _relayout_operand(packed: Tensor, scales: Tensor, rows: int, cols: int, rows_to: int, cols_to: int):
+    """A quantised operand (packed [>=rows, >=cols/2], swizzled scales for its padded shape)
+    zero-padded to [rows_to, cols_to] in the kernel layout (K a multiple of 256 so every
+    stage reads whole tiles; the swizzled order depends on the padded column count)."""
+    dev = packed.device
+    pk = torch.zeros((rows_to, cols_to // 2), dtype=torch.uint8, device=dev)
+    pk[:rows, : cols // 2] = packed.view(torch.uint8)[:rows, : cols // 2]
+    sc = scales.view(torch.uint8)
+    rp, cpb = sc.shape
+    plain = sc.view(rp // 128, cpb // 4, 32, 4, 4).permute(0, 3, 2, 1, 4).reshape(rp, cpb)[:rows, : cols // 16]
+    full = torch.zeros((_round_up(rows_to, 128), cols_to // 16), dtype=torch.uint8, device=dev)
+    full[:rows, : cols // 16] = plain
+    r2, c2 = full.shape
+    sw = full.view(r2 // 128, 4, 32, c2 // 4, 4).permute(0, 3, 2, 1, 4).contiguous().view(-1)
+    return pk, sw
+
+
+def _mm_prepared(a: Tensor, b_packed: Tensor, b_scales: Tensor, b_g: Tensor, n_pad: int, k_pad: int,
+                 causal_a: bool, bias: Tensor | None) -> Tensor:
+    """fp32 [M, n_pad] = deq(A) deq(B)^T g_a g_b (+ bias) on the kernels; B already in the
+    kernel layout for [n_pad, k_pad]."""
+    m, k = a.shape
+    dtype = 0 if a.dtype == torch.bfloat16 else 1
+    x = a.detach().contiguous() if dtype == 0 else a.detach().to(torch.float32).contiguous()
+    if k_pad != k:
+        x = torch.nn.functional.pad(x, (0, k_pad - k))
+    lib = _lib.load()
+    out = torch.empty((m, n_pad), dtype=torch.float32, device=a.device)
+    ws = torch.empty((max(lib.mcl4moe_nvfp4_mm_workspace_size(m, k_pad), 256),), dtype=torch.uint8, device=a.device)
+    _lib.check(lib.mcl4moe_nvfp4_mm(x.data_ptr(), dtype, m, k_pad, int(bool(causal_a)), b_packed.data_ptr(),
+                                    b_scales.data_ptr(), b_g.data_ptr(), n_pad, _ptr(bias), out.data_ptr(), None, None,
+                                    ws.data_ptr(), ws.numel(), _stream_handle()), "mcl4moe_nvfp4_mm")
+    return out
+
+
+@torch.no_grad()
+def nvfp4_mm(a: Tensor, b: Tensor, *, weight_b: bool = False, stochastic_a: bool = False, stochastic_b: bool = False,
+             causal_a: bool = False, prequantized_b: tuple[Tensor, Tensor, Tensor] | None = None,
+             _phase: str = "other") -> Tensor:
+    """``a @ b.T`` in NVFP4, fp32 result [M, N] (src/mcl4_coe/nvfp4.py:285-334): A quantised
+    one-dimensionally (g = 1 with ``causal_a``), B two-dimensionally with ``weight_b`` (else
+    one-dimensionally), or ``prequantized_b`` = (packed, swizzled scales, g) as
+    :func:`quantize_nvfp4` returns them for ``b`` padded to multiples of 32.  Runs on the
+    tcgen05 block-scaled GEMM with K and N padded to 256."""
+    if a.ndim != 2 or b.ndim != 2 or a.shape[1] != b.shape[1]:
+        raise ValueError("NVFP4 matmul expects a[M,K] and b[N,K]")
+    if a.device != b.device or a.device.type != "cuda":
+        raise ValueError("NVFP4 matmul requires both operands on the same CUDA device")
+    m, k = a.shape
+    n = b.shape[0]
+    if min(m, n, k) == 0:
+        raise ValueError("NVFP4 matmul requires nonempty operands")
+    if stochastic_a or stochastic_b:
+        raise NotImplementedError("stochastic NVFP4 rounding (backward only) is not served by the B200 path")
+    kp, np_ = _round_up(k, 256), _round_up(n, 256)
+    if prequantized_b is not None:
+        qb, sb, gb = prequantized_b
+        rows_b = sb.shape[0] if sb.ndim == 2 else _round_up(n, 32)
+        pk, sw = _relayout_operand(qb, sb.view(torch.uint8).view(rows_b, -1), _round_up(n, 32), _round_up(k, 32),
+                                   np_, kp)
+    else:
+        bp = b.detach()
+        if kp != k or np_ != n:
+            bp = torch.nn.functional.pad(bp.to(torch.float32 if weight_b else bp.dtype), (0, kp - k, 0, np_ - n))
+        qb, sb, gb = quantize_nvfp4(bp, two_dimensional=weight_b)
+        pk, sw = qb.view(torch.uint8), sb.view(torch.uint8).reshape(-1)
+    _GEMM_COUNTS[_phase] = _GEMM_COUNTS.get(_phase, 0) + 1
+    return _mm_prepared(a, pk, sw, gb.to(torch.float32).reshape(1), np_, kp, causal_a, None)[:, :n]
+
+
+class NVFP4Linear(nn.Linear):
+    """Projection on native NVFP4 GEMMs with optional 2:4 weight sparsity
+    (src/mcl4_coe/nvfp4.py:474-542).  Forward: 1x16 activation blocks (g = 1 with
+    ``causal_activation_scale``), the cached 16x16-tile weight (2:4-masked first when
+    ``sparsity_mode`` is not "none"), fp32 accumulation, ``+ bias`` in fp32, cast to the
+    input dtype.  CUDA only (no CPU fallback) and forward only."""
+
+    def __init__(self, in_features: int, out_features: int, bias: bool = True, device=None, dtype=None, *,
+                 sparsity_mode: str = "2to4_transposable", sr_ste_decay: float = 1e-4,
+                 causal_activation_scale: bool = True) -> None:
+        super().__init__(in_features, out_features, bias=bias, device=device, dtype=dtype)
+        if sparsity_mode not in SPARSITY_MODES:
+            raise ValueError(f"sparsity_mode must be one of {SPARSITY_MODES}")
+        self.sparsity_mode = sparsity_mode
+        self.sr_ste_decay = float(sr_ste_decay)
+        self.causal_activation_scale = bool(causal_activation_scale)
+        self._b200_weight_cache: tuple | None = None
+
+    @classmethod
+    def from_linear(cls, layer: nn.Linear, *, sparsity_mode: str = "2to4_transposable", sr_ste_decay: float = 1e-4,
+                    causal_activation_scale: bool = True) -> "NVFP4Linear":
+        converted = cls(layer.in_features, layer.out_features, bias=layer.bias is not None,
+                        device=layer.weight.device, dtype=layer.weight.dtype, sparsity_mode=sparsity_mode,
+                        sr_ste_decay=sr_ste_decay, causal_activation_scale=causal_activation_scale)
+        converted.load_state_dict(layer.state_dict())
+        converted.weight.requires_grad_(layer.weight.requires_grad)
+        if converted.bias is not None:
+            converted.bias.requires_grad_(layer.bias.requires_grad)
+        converted.train(layer.training)
+        return converted
+
+    @torch.no_grad()
+    def active_2to4_mask(self) -> Tensor:
+        """The current 2:4 boolean weight mask [out_features, in_features]."""
+        return compute_2to4_mask(self.weight, mode=self.sparsity_mode)
+
+    def _quantised_weight(self) -> tuple:
+        """(packed, swizzled scales, g, mask) of the weight padded to multiples of 256, cached
+        on (weight._version, data_ptr, shape, device, sparsity_mode) like
+        _get_or_build_weight_nvfp4_cache (src/mcl4_coe/nvfp4.py:358-389)."""
+        w = self.weight
+        key = (w._version, w.data_ptr(), tuple(w.shape), str(w.device), self.sparsity_mode)
+        c = self._b200_weight_cache
+        if c is not None and c[0] == key:
+            return c[1:]
+        n, k = w.shape
+        mask = None
+        w_eff = w.detach().to(torch.float32)
+        if self.sparsity_mode != "none":
+            w_eff, m8 = _mask_2to4(w_eff, self.sparsity_mode)
+            mask = m8.bool()
+        np_, kp = _round_up(n, 256), _round_up(k, 256)
+        if (np_, kp) != (n, k):
+            w_eff = torch.nn.functional.pad(w_eff, (0, kp - k, 0, np_ - n))
+        qb, sb, gb = quantize_nvfp4(w_eff, two_dimensional=True)
+        self._b200_weight_cache = (key, qb.view(torch.uint8), sb.view(torch.uint8).reshape(-1), gb, mask)
+        return self._b200_weight_cache[1:]
+
+    def forward(self, inputs: Tensor) -> Tensor:
+        if inputs.ndim < 1 or inputs.shape[-1] != self.in_features:
+            raise ValueError("NVFP4Linear input must end in in_features")
+        _require_cuda(inputs, "NVFP4Linear")
+        if torch.is_grad_enabled() and (inputs.requires_grad or self.weight.requires_grad):
+            raise NotImplementedError("NVFP4Linear on the B200 path is forward-only: run it under torch.no_grad()")
+        flat = inputs.reshape(-1, self.in_features)
+        if flat.shape[0] == 0:
+            return inputs.new_empty(*inputs.shape[:-1], self.out_features)
+        with torch.no_grad():
+            pk, sw, g, _ = self._quantised_weight()
+            n, k = self.weight.shape
+            np_, kp = _round_up(n, 256), _round_up(k, 256)
+            bias = None
+            if self.bias is not None:
+                bias = torch.zeros((np_,), dtype=torch.float32, device=flat.device)
+                bias[:n] = self.bias.detach().to(torch.float32)
+            _GEMM_COUNTS["forward"] = _GEMM_COUNTS.get("forward", 0) + 1
+            out = _mm_prepared(flat, pk, sw, g, np_, kp, self.causal_activation_scale, bias)[:, :n]
+        return out.to(inputs.dtype).reshape(*inputs.shape[:-1], self.out_features)
+
+
+def convert_linear_to_nvfp4(module: nn.Module, *, min_features: int = 32, experts_only: bool = True,
+                            sparsity_mode: str = "2to4_transposable", sr_ste_decay: float = 1e-4,
+                            causal_activation_scale: bool = True,
+                            exclude_names: tuple[str, ...] = ("router", "token_scorer", "ple", "route_",
+                                                              "start_query")) -> int:
+    """Replace eligible ``nn.Linear`` submodules by :class:`NVFP4Linear`
+    (src/mcl4_coe/nvfp4.py:598-695): with ``experts_only`` and any ``SwiGLUExpert`` present,
+    only the experts' ``up_proj`` / ``down_proj``; otherwise every Linear with both sides
+    >= ``min_features`` whose child name contains none of ``exclude_names``.  Returns the
+    number converted."""
+    kw = dict(sparsity_mode=sparsity_mode, sr_ste_decay=sr_ste_decay, causal_activation_scale=causal_activation_scale)
+
+    def eligible(layer) -> bool:
+        return (isinstance(layer, nn.Linear) and not isinstance(layer, NVFP4Linear)
+                and layer.in_features >= min_features and layer.out_features >= min_features)
+
+    if experts_only:
+        count = 0
+        for child in module.modules():
+            if child.__class__.__name__ == "SwiGLUExpert":
+                for attr in ("up_proj", "down_proj"):
+                    layer = getattr(child, attr, None)
+                    if eligible(layer):
+                        setattr(child, attr, NVFP4Linear.from_linear(layer, **kw))
+                        count += 1
+        if count > 0:
+            return count
+    count = 0
+    for name, child in list(module.named_children()):
+        if any(ex in name for ex in exclude_names):
+            continue
+        if eligible(child):
+            setattr(module, name, NVFP4Linear.from_linear(child, **kw))
+            count += 1
+        else:
+            count += convert_linear_to_nvfp4(child, min_features=min_features, experts_only=False,
+                                             exclude_names=exclude_names, **kw)
+    return count
+

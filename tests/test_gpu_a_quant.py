@@ -23,12 +23,12 @@ def test_activation_quantiser_matches_reference_golden(moe_pkg, golden, case):
     name, x, _ = case
     g = golden("quant_act")
     xt = torch.from_numpy(x).to(DEV).to(torch.bfloat16)
-    packed, scales, gs = moe_pkg.quantize_nvfp4(xt)
+    packed, scales, gs = moe_pkg.quantize_activations(xt)
     torch.cuda.synchronize()
     np.testing.assert_array_equal(packed.cpu().numpy(), g[f"{name}__packed"])
     np.testing.assert_array_equal(scales.view(torch.uint8).cpu().numpy(), g[f"{name}__scales"])
     assert float(gs) == 1.0
-    _, sw, _ = moe_pkg.quantize_nvfp4(xt, swizzled=True)
+    _, sw, _ = moe_pkg.quantize_activations(xt, swizzled=True)
     np.testing.assert_array_equal(sw.view(torch.uint8).cpu().numpy().reshape(g[f"{name}__swizzled"].shape),
                                   g[f"{name}__swizzled"])
 
@@ -39,8 +39,8 @@ def test_activation_quantiser_random_vs_oracle(moe_pkg, rows, cols):
     x = bf16_values((r.standard_normal((rows, cols), dtype=np.float32)
                      * np.power(10.0, r.uniform(-3, 3, size=(rows, 1))).astype(np.float32)))
     xt = torch.from_numpy(x).to(DEV).to(torch.bfloat16)
-    packed, scales, _ = moe_pkg.quantize_nvfp4(xt)
-    _, sw, _ = moe_pkg.quantize_nvfp4(xt, swizzled=True)
+    packed, scales, _ = moe_pkg.quantize_activations(xt)
+    _, sw, _ = moe_pkg.quantize_activations(xt, swizzled=True)
     op, os_ = nr.quantize_activations(x)
     np.testing.assert_array_equal(packed.cpu().numpy(), op)
     np.testing.assert_array_equal(scales.view(torch.uint8).cpu().numpy(), os_)

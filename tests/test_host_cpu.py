@@ -94,3 +94,27 @@ def test_expert_parallel_chunk_bounds(moe_pkg):
             b = bounds(T, ch, wts)
             assert b[0][0] == 0 and b[-1][1] == T
             assert all(lo < hi for lo, hi in b) and all(b[i][1] == b[i + 1][0] for i in range(len(b) - 1))
+
+
+def test_convert_linear_to_nvfp4(moe_pkg):
+    """src/mcl4_coe/nvfp4.py:598-695: expert projections only when SwiGLUExpert blocks
+    exist; otherwise eligible Linears outside the excluded names."""
+    from torch import nn
+
+    moe = moe_pkg.SparseMoE(_cfg(moe_pkg))
+    n = moe_pkg.convert_linear_to_nvfp4(moe, sparsity_mode="none")
+    assert n == 2 * moe.num_experts
+    assert all(isinstance(e.up_proj, moe_pkg.NVFP4Linear) and isinstance(e.down_proj, moe_pkg.NVFP4Linear)
+               for e in moe.experts)
+    assert type(moe.router) is nn.Linear
+    assert moe.experts[0].up_proj.sparsity_mode == "none" and moe.experts[0].up_proj.bias is None
+    assert moe_pkg.convert_linear_to_nvfp4(moe) == 0  # nothing left to convert
+
+    tree = nn.Sequential(nn.Linear(64, 64), nn.ReLU(), nn.Linear(64, 16))
+    tree.add_module("router_head", nn.Linear(64, 64))
+    assert moe_pkg.convert_linear_to_nvfp4(tree) == 1
+    assert isinstance(tree[0], moe_pkg.NVFP4Linear) and type(tree[2]) is nn.Linear
+    assert type(tree.router_head) is nn.Linear
+    assert tree[0].sparsity_mode == "2to4_transposable"
+    with pytest.raises(ValueError):
+        moe_pkg.NVFP4Linear(64, 64, sparsity_mode="dense")
