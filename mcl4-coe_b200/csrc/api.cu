@@ -137,7 +137,7 @@ int mcl4moe_quantize_rows(const void* x, int dtype, int64_t rows, int cols, int6
   if (cols % 64 != 0) return MCL4MOE_ERR_UNSUPPORTED;
   if (rows_pad < rows || rows_pad % 128 != 0 || ld < cols || (rows > 0 && !x)) return MCL4MOE_ERR_INVALID;
   return launch_quantize_rows(x, dtype, rows, cols, ld, causal, packed, scales, rows_pad, global_scale, amax_scratch,
-                              nullptr, nullptr, stream);
+                              nullptr, nullptr, 0, stream);
 }
 
 }  // extern "C"
@@ -205,7 +205,7 @@ int mcl4moe_nvfp4_mm(const void* x, int dtype, int64_t M, int K, int causal, con
   cudaStream_t s = stream;
   int32_t* err = error_word ? error_word : w.err;
   if (!error_word && cudaMemsetAsync(err, 0, sizeof(int32_t), s) != cudaSuccess) return MCL4MOE_ERR_CUDA;
-  int st = launch_quantize_rows(x, dtype, M, K, K, causal, w.aq, w.as, mp, w.g_a, w.amax, b_g, w.g_ab, s);
+  int st = launch_quantize_rows(x, dtype, M, K, K, causal, w.aq, w.as, mp, w.g_a, w.amax, b_g, w.g_ab, 1, s);
   if (st != MCL4MOE_OK) return st;
   if (a_global_scale && cudaMemcpyAsync(a_global_scale, w.g_a, sizeof(float), cudaMemcpyDeviceToDevice, s) !=
                             cudaSuccess)
@@ -216,6 +216,7 @@ int mcl4moe_nvfp4_mm(const void* x, int dtype, int64_t M, int K, int causal, con
   g.row_count = w.counts;
   g.out_row_base = w.offs_start;
   g.a_scales = w.as;
+  g.a_sf_rowmajor = 1;
   g.b_scales = b_scales;
   g.b_g = w.g_ab;
   g.E = 1;
@@ -317,6 +318,7 @@ int forward_experts(const mcl4moe_moe_args* a, const MoeWorkspace& w, const int3
   g1.pad_start = w.route.pad_start;
   g1.row_count = w.route.counts;
   g1.a_scales = w.xs;
+  g1.a_sf_rowmajor = 1;
   g1.b_scales = a->w_up_scales;
   g1.b_g = a->w_up_g;
   g1.E = E;
@@ -469,6 +471,7 @@ int mcl4moe_grouped_linear(const uint16_t* x, int64_t M, int K, const int32_t* o
   g.row_count = counts;
   g.out_row_base = offs_start;
   g.a_scales = xs;
+  g.a_sf_rowmajor = 1;
   g.b_scales = w_scales;
   g.b_g = w_g;
   g.E = E;

@@ -214,6 +214,14 @@ __device__ __host__ __forceinline__ uint64_t swizzled_scale_offset(uint64_t r, u
   return atom * 512 + (r & 31) * 16 + ((r >> 5) & 3) * 4 + (c & 3);
 }
 
+// Byte offset of scale (row r, 16-block c) in the row-major layout [rows, blocks_per_row]:
+// the A-operand scales of the grouped GEMMs' first projection (a row's scales are
+// contiguous, so a token's scatter writes them in whole sectors; the GEMM fetches a
+// stage's 128 rows x 16 scales with one 2-D TMA load).
+__device__ __host__ __forceinline__ uint64_t rowmajor_scale_offset(uint64_t r, uint32_t c, uint32_t blocks_per_row) {
+  return r * blocks_per_row + c;
+}
+
 // ---------------------------------------------------------------- PTX wrappers
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

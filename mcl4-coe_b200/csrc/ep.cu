@@ -245,7 +245,7 @@ __global__ void __launch_bounds__(256) ep_pad_kernel(const int32_t* __restrict__
 }
 
 // Receiver: copy each received row into the expert-major slots of its local
-// experts (codes as they are, scales into the swizzled atoms the GEMM reads),
+// experts (codes and scales as they are, into the row-major layout the GEMM reads),
 // in received-row order within an expert.  Extra CTAs zero padding-row scales.
 template <int EW>
 __global__ void __launch_bounds__(256) ep_scatter_kernel(const uint8_t* __restrict__ recv, int R, int d, int k,
@@ -269,7 +269,7 @@ __global__ void __launch_bounds__(256) ep_scatter_kernel(const uint8_t* __restri
     const int groups = nblk / 4;
     for (int i = threadIdx.x; i < (end - start) * groups; i += blockDim.x) {
       const int r = start + i / groups, g = i % groups;
-      *reinterpret_cast<uint32_t*>(xs + swizzled_scale_offset(uint64_t(r), uint32_t(4 * g), uint32_t(nblk))) = 0u;
+      *reinterpret_cast<uint32_t*>(xs + rowmajor_scale_offset(uint64_t(r), uint32_t(4 * g), uint32_t(nblk))) = 0u;
     }
     return;
   }
@@ -322,7 +322,7 @@ __global__ void __launch_bounds__(256) ep_scatter_kernel(const uint8_t* __restri
         *reinterpret_cast<uint4*>(xq + int64_t(p) * (d / 2) + c * 16) =
             *reinterpret_cast<const uint4*>(row + L.codes + c * 16);
       for (int q = lane; q < nblk / 4; q += 32)
-        *reinterpret_cast<uint32_t*>(xs + swizzled_scale_offset(uint64_t(p), uint32_t(4 * q), uint32_t(nblk))) =
+        *reinterpret_cast<uint32_t*>(xs + rowmajor_scale_offset(uint64_t(p), uint32_t(4 * q), uint32_t(nblk))) =
             *reinterpret_cast<const uint32_t*>(row + L.scales + 4 * q);
     }
   }
@@ -448,7 +448,7 @@ struct ExpertsWs {
   int32_t* slot_pos;   // [R, k]
   float* sorted_w;     // [mcap]
   uint8_t* xq;         // [mcap, d/2]
-  uint8_t* xs;         // swizzled [mcap * d/16]
+  uint8_t* xs;         // row-major [mcap, d/16]
   uint8_t* hq;         // [mcap, F/2]
   uint8_t* hs;         // swizzled [mcap * F/16]
   uint16_t* y;         // [mcap, d]
@@ -607,6 +607,7 @@ int ep_experts_impl(const uint8_t* recv_buf, int R, int slots, int d, int k, int
   g1.pad_start = w.pad_start;
   g1.row_count = w.counts;
   g1.a_scales = w.xs;
+  g1.a_sf_rowmajor = 1;
   g1.b_scales = w_up_scales;
   g1.b_g = w_up_g;
   g1.E = E_loc;

@@ -112,7 +112,8 @@ __device__ __forceinline__ int find_expert(const int32_t* pad_s, int E, int row)
 template <int MODE>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     grouped_gemm_fp4_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                            const __grid_constant__ CUtensorMap tmap_y, GemmArgs args) {
+                            const __grid_constant__ CUtensorMap tmap_y, const __grid_constant__ CUtensorMap tmap_sfa,
+                            GemmArgs args) {
   constexpr int S = Cfg<MODE>::kStages;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -152,6 +153,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tmap_a);
     prefetch_tmap(&tmap_b);
     if (MODE == 1) prefetch_tmap(&tmap_y);
+    if (args.a_sf_rowmajor) prefetch_tmap(&tmap_sfa);
   }
   if (warp == 1) {
     tmem_alloc_pair(smem_u32(tmem_slot), kTmemCols);
@@ -216,7 +218,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint32_t fb = map_shared_rank(full_bar(stage), 0);
           tma_load_2d_pair(st, &tmap_a, kb * (kBK / 2), row0, fb);
           tma_load_2d_pair(st + kOffB, &tmap_b, kb * (kBK / 2), brow, fb);
-          bulk_load(st + kOffSFA, asc + kb * 2048, kSFA, sfull_bar(stage));
+          if (args.a_sf_rowmajor)  // this CTA's 128 rows x 16 scales of the K block, row-major
+            tma_load_2d(st + kOffSFA, &tmap_sfa, kb * (kBK / 16), row0, sfull_bar(stage));
+          else
+            bulk_load(st + kOffSFA, asc + kb * 2048, kSFA, sfull_bar(stage));
           bulk_load(st + kOffSFB, bsc0 + kb * 2048, kSFBHalf, sfull_bar(stage));
           bulk_load(st + kOffSFB + kSFBHalf, bsc1 + kb * 2048, kSFBHalf, sfull_bar(stage));
           if (++stage == S) {
@@ -303,12 +308,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const uint32_t sf_col = tmem_base + lane_base + kSfCol0 + stage * kSfColsPerStage;
         // columns [0,16): SFA of K steps 0..3; [16,48): per K step, SFB half 0 then half 1
         uint32_t va[16], vb[32];
+        if (args.a_sf_rowmajor) {
+          // row-major [128][16] bytes: row l + 32 j holds the 4 scale words of K steps 0..3
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint4 a = *reinterpret_cast<const uint4*>(st + kOffSFA + (lane + 32 * j) * 16);
+            va[j] = a.x, va[4 + j] = a.y, va[8 + j] = a.z, va[12 + j] = a.w;
+          }
+        } else {
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint4 a = *reinterpret_cast<const uint4*>(st + kOffSFA + ks * 512 + lane * 16);
+            va[4 * ks] = a.x, va[4 * ks + 1] = a.y, va[4 * ks + 2] = a.z, va[4 * ks + 3] = a.w;
+          }
+        }
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks) {
-          const uint4 a = *reinterpret_cast<const uint4*>(st + kOffSFA + ks * 512 + lane * 16);
           const uint4 b0 = *reinterpret_cast<const uint4*>(st + kOffSFB + ks * 512 + lane * 16);
           const uint4 b1 = *reinterpret_cast<const uint4*>(st + kOffSFB + kSFBHalf + ks * 512 + lane * 16);
-          va[4 * ks] = a.x, va[4 * ks + 1] = a.y, va[4 * ks + 2] = a.z, va[4 * ks + 3] = a.w;
           vb[8 * ks] = b0.x, vb[8 * ks + 1] = b0.y, vb[8 * ks + 2] = b0.z, vb[8 * ks + 3] = b0.w;
           vb[8 * ks + 4] = b1.x, vb[8 * ks + 5] = b1.y, vb[8 * ks + 6] = b1.z, vb[8 * ks + 7] = b1.w;
         }
@@ -512,6 +529,20 @@ bool make_tmap(CUtensorMap* m, const void* base, uint64_t row_bytes, uint64_t ro
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 2-D map over row-major A scales [rows, K/16] (bytes), box 16 scales (one K block) x 128 rows,
+// no swizzle: the x coordinate is a multiple of 16 bytes and the row stride K/16 a multiple of 16.
+bool make_tmap_scales(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows) {
+  auto fn = encode_fn();
+  if (!fn || cols % 16 != 0) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols};
+  cuuint32_t box[2] = {16, 128};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // 2-D map over a bf16 [rows, ld] matrix, box 64 columns (128 bytes) x 32 rows, 128B swizzle (tile stores).
 bool make_tmap_store(CUtensorMap* m, const void* base, uint64_t ld, uint64_t rows) {
   auto fn = encode_fn();
@@ -546,13 +577,13 @@ int resident_pairs() {
 }
 
 template <int MODE>
-int launch_mode(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ty, const GemmArgs& args,
-                cudaStream_t stream) {
+int launch_mode(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ty, const CUtensorMap& tsa,
+                const GemmArgs& args, cudaStream_t stream) {
   static std::atomic<uint64_t> configured{0};
   if (!raise_smem_limit(grouped_gemm_fp4_kernel<MODE>, int(Cfg<MODE>::kSmem), configured)) return MCL4MOE_ERR_CUDA;
   const int pairs = resident_pairs<MODE>();
   return launch_pdl(grouped_gemm_fp4_kernel<MODE>, dim3(2 * pairs), dim3(kThreads), Cfg<MODE>::kSmem, stream, ta, tb,
-                    ty, args) == cudaSuccess
+                    ty, tsa, args) == cudaSuccess
              ? MCL4MOE_OK
              : MCL4MOE_ERR_CUDA;
 }
@@ -577,21 +608,24 @@ int launch_grouped_gemm(const uint8_t* a, int64_t a_rows, const uint8_t* b, cons
   if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) | reinterpret_cast<uintptr_t>(args.a_scales) |
        reinterpret_cast<uintptr_t>(args.b_scales)) & 15)
     return MCL4MOE_ERR_INVALID;
-  CUtensorMap ta, tb, ty;
+  CUtensorMap ta, tb, ty, tsa;
   if (!make_tmap(&ta, a, uint64_t(args.K) / 2, uint64_t(a_rows))) return MCL4MOE_ERR_CUDA;
   if (!make_tmap(&tb, b, uint64_t(args.K) / 2, uint64_t(args.E) * args.N_total)) return MCL4MOE_ERR_CUDA;
+  memset(&tsa, 0, sizeof(tsa));
+  if (args.a_sf_rowmajor && !make_tmap_scales(&tsa, args.a_scales, uint64_t(args.K) / 16, uint64_t(a_rows)))
+    return MCL4MOE_ERR_CUDA;
   if (args.mode == 0) {
     memset(&ty, 0, sizeof(ty));
-    return launch_mode<0>(ta, tb, ty, args, stream);
+    return launch_mode<0>(ta, tb, ty, tsa, args, stream);
   }
   if (args.out_row_base == nullptr) {
     // Tile stores write every padded row: y holds a_rows rows of ldy elements.
     if ((reinterpret_cast<uintptr_t>(args.y) & 15) || (args.ldy * 2) % 16 != 0) return MCL4MOE_ERR_INVALID;
     if (!make_tmap_store(&ty, args.y, uint64_t(args.ldy), uint64_t(a_rows))) return MCL4MOE_ERR_CUDA;
-    return launch_mode<1>(ta, tb, ty, args, stream);
+    return launch_mode<1>(ta, tb, ty, tsa, args, stream);
   }
   memset(&ty, 0, sizeof(ty));
-  return launch_mode<2>(ta, tb, ty, args, stream);
+  return launch_mode<2>(ta, tb, ty, tsa, args, stream);
 }
 
 }  // namespace mcl4

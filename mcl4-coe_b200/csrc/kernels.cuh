@@ -152,11 +152,12 @@ int launch_quantize_weights(const float* const* w_ptrs, const int32_t* slots, in
 
 // One-dimensional NVFP4 rows (1x16 blocks) of a bf16 (dtype 0) or fp32 (dtype 1)
 // matrix with global scale g = 1 (causal) or amax/2688; packed [rows, cols/2],
-// swizzled scales for rows_pad rows (padding rows zero), g written to *g;
-// with g_b, *g_ab = g * *g_b.  amax: device scratch float.  cols % 64 == 0.
+// scales for rows_pad rows (padding rows zero) in the 128x4 swizzled atoms or,
+// with rowmajor, [rows_pad, cols/16]; g written to *g; with g_b, *g_ab = g * *g_b.
+// amax: device scratch float.  cols % 64 == 0.
 int launch_quantize_rows(const void* x, int dtype, int64_t rows, int cols, int64_t ld, int causal, uint8_t* packed,
                          uint8_t* scales, int64_t rows_pad, float* g, float* amax, const float* g_b, float* g_ab,
-                         cudaStream_t s);
+                         int rowmajor, cudaStream_t s);
 
 // pad_start = {0, rows_pad}, counts = {rows}, offs_start = {0}: one GEMM segment.
 int launch_single_segment(int64_t rows, int64_t rows_pad, int32_t* pad_start, int32_t* counts, int32_t* offs_start,
@@ -200,7 +201,8 @@ struct GemmArgs {
   const int32_t* pad_start;     // [E + 1]
   const int32_t* row_count;     // [E] valid rows per expert (stores of rows beyond are skipped)
   const int32_t* out_row_base;  // [E] destination row of an expert's first row (nullptr: padded row index)
-  const uint8_t* a_scales;      // swizzled, padded rows
+  const uint8_t* a_scales;      // padded rows: row-major [rows, K/16] if a_sf_rowmajor, else 128x4 swizzled atoms
+  int a_sf_rowmajor;
   const uint8_t* b_scales;      // [E, N_total*K/16] swizzled
   const float* b_g;             // [E]
   int E, K, N_total, n_tiles, mode;

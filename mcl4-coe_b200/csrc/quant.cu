@@ -237,11 +237,12 @@ __global__ void rows_global_scale_kernel(const float* amax, int causal, float* g
 
 // One warp per row, lane l takes 16-element blocks l, l+32, ...: scale
 // e4m3(min(amax16 / (6 g), 448)), inverse 1 / (scale * g), E2M1 codes of x * inverse
-// (src/mcl4_coe/nvfp4.py:209-225, one-dimensional mode); scales into the swizzled atoms.
+// (src/mcl4_coe/nvfp4.py:209-225, one-dimensional mode); scales into the swizzled atoms
+// (the reference's output layout) or row-major (the GEMM's A operand).
 template <typename InT>
 __global__ void __launch_bounds__(256) rows_quant_kernel(const InT* __restrict__ x, int64_t rows, int cols, int64_t ld,
                                                          const float* __restrict__ g_ptr, uint8_t* __restrict__ packed,
-                                                         uint8_t* __restrict__ scales) {
+                                                         uint8_t* __restrict__ scales, int rowmajor) {
   const int lane = threadIdx.x & 31;
   const int64_t row = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -265,7 +266,8 @@ __global__ void __launch_bounds__(256) rows_quant_kernel(const InT* __restrict__
       hi |= e2m1_code(__fmul_rn(v[8 + j], inv)) << (4 * j);
     }
     *reinterpret_cast<uint2*>(packed + row * (cols / 2) + b * 8) = make_uint2(lo, hi);
-    scales[swizzled_scale_offset(uint64_t(row), uint32_t(b), uint32_t(nblk))] = uint8_t(sc);
+    scales[rowmajor ? rowmajor_scale_offset(uint64_t(row), uint32_t(b), uint32_t(nblk))
+                    : swizzled_scale_offset(uint64_t(row), uint32_t(b), uint32_t(nblk))] = uint8_t(sc);
   }
 }
 
@@ -282,7 +284,7 @@ __global__ void single_segment_kernel(int64_t rows, int64_t rows_pad, int32_t* p
 
 int launch_quantize_rows(const void* x, int dtype, int64_t rows, int cols, int64_t ld, int causal, uint8_t* packed,
                          uint8_t* scales, int64_t rows_pad, float* g, float* amax, const float* g_b, float* g_ab,
-                         cudaStream_t s) {
+                         int rowmajor, cudaStream_t s) {
   const size_t scale_bytes = size_t(rows_pad) * size_t(cols / 16);
   if (cudaMemsetAsync(scales, 0, scale_bytes, s) != cudaSuccess) return MCL4MOE_ERR_CUDA;
   if (!causal) {
@@ -301,9 +303,10 @@ int launch_quantize_rows(const void* x, int dtype, int64_t rows, int cols, int64
     const unsigned blocks = unsigned((rows + 7) / 8);
     if (dtype == 0)
       rows_quant_kernel<uint16_t><<<blocks, 256, 0, s>>>(static_cast<const uint16_t*>(x), rows, cols, ld, g, packed,
-                                                        scales);
+                                                        scales, rowmajor);
     else
-      rows_quant_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float*>(x), rows, cols, ld, g, packed, scales);
+      rows_quant_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float*>(x), rows, cols, ld, g, packed, scales,
+                                                     rowmajor);
   }
   return cudaGetLastError() == cudaSuccess ? MCL4MOE_OK : MCL4MOE_ERR_CUDA;
 }

@@ -16,8 +16,8 @@ namespace mcl4 {
 
 // ---------------------------------------------------------------- permute + quantise
 
-// Blocks [0, ceil(T/8)): one warp per token, quantise its row once and write
-// it to its k slots.  Blocks after: one per expert, zero the scales of the
+// Rows wider than 4096 elements.  Blocks [0, ceil(T/8)): one warp per token,
+// quantise its row once and write it to its k slots, 32 blocks at a time.  Blocks after: one per expert, zero the scales of the
 // padding rows of that expert's segment (zero scale => zero contribution).
 __global__ void __launch_bounds__(256) permute_quant_kernel(
     const uint16_t* __restrict__ x, const uint8_t* __restrict__ valid, const int32_t* __restrict__ topk_idx,
@@ -38,7 +38,7 @@ __global__ void __launch_bounds__(256) permute_quant_kernel(
     const int groups = nblk / 4;
     for (int i = threadIdx.x; i < (end - start) * groups; i += blockDim.x) {
       const int r = start + i / groups, g = i % groups;
-      *reinterpret_cast<uint32_t*>(xs + swizzled_scale_offset(uint64_t(r), uint32_t(4 * g), uint32_t(nblk))) = 0u;
+      *reinterpret_cast<uint32_t*>(xs + rowmajor_scale_offset(uint64_t(r), uint32_t(4 * g), uint32_t(nblk))) = 0u;
     }
     return;
   }
@@ -80,7 +80,98 @@ __global__ void __launch_bounds__(256) permute_quant_kernel(
       if (b < nblk && p >= 0) {
         *reinterpret_cast<uint2*>(xq + int64_t(p) * (d / 2) + b * 8) = pk;
         if ((lane & 3) == 0)
-          *reinterpret_cast<uint32_t*>(xs + swizzled_scale_offset(uint64_t(p), uint32_t(b), uint32_t(nblk))) = word;
+          *reinterpret_cast<uint32_t*>(xs + rowmajor_scale_offset(uint64_t(p), uint32_t(b), uint32_t(nblk))) = word;
+      }
+    }
+  }
+}
+
+// Rows of up to 32 * BPL 16-element blocks (d <= 512 * BPL): the same work as
+// permute_quant_kernel with the token's whole row loaded before the routing
+// lookups (which form a dependent chain of four loads) and every slot stored
+// after quantising, so each warp keeps its row's loads in flight together.
+template <int BPL>
+__global__ void __launch_bounds__(256) permute_quant_row_kernel(
+    const uint16_t* __restrict__ x, const uint8_t* __restrict__ valid, const int32_t* __restrict__ topk_idx,
+    const float* __restrict__ topk_w, int T, int d, int E, int k, RouteWorkspace ws, int32_t* __restrict__ slot_pos,
+    float* __restrict__ sorted_w, int32_t* __restrict__ perm, uint8_t* __restrict__ xq, uint8_t* __restrict__ xs) {
+  __shared__ float inv_tab[128];
+  fill_inverse_scale_table(inv_tab);
+  __syncthreads();
+  pdl_wait();     // routing and the expert layout are complete
+  pdl_trigger();  // the gate/up GEMM may launch (it waits for this grid's writes)
+  const int lane = threadIdx.x & 31;
+  const int nblk = d / 16;
+  const int token_blocks = (T + 7) / 8;
+  if (int(blockIdx.x) >= token_blocks) {  // zero the scales of the expert's padding rows
+    const int e = blockIdx.x - token_blocks;
+    const int start = ws.pad_start[e] + ws.counts[e];
+    const int end = ws.pad_start[e + 1];
+    const int groups = nblk / 4;
+    for (int i = threadIdx.x; i < (end - start) * groups; i += blockDim.x) {
+      const int r = start + i / groups, g = i % groups;
+      *reinterpret_cast<uint32_t*>(xs + rowmajor_scale_offset(uint64_t(r), uint32_t(4 * g), uint32_t(nblk))) = 0u;
+    }
+    return;
+  }
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (t >= T) return;
+  if (valid != nullptr && valid[t] == 0) {
+    if (lane < k) slot_pos[int64_t(t) * k + lane] = -1;
+    return;
+  }
+  uint4 u[BPL][2];
+#pragma unroll
+  for (int i = 0; i < BPL; ++i) {
+    const int b = lane + 32 * i;
+    if (b < nblk) {
+      const uint4* src = reinterpret_cast<const uint4*>(x + int64_t(t) * d + b * 16);
+      u[i][0] = __ldg(src);
+      u[i][1] = __ldg(src + 1);
+    }
+  }
+  const int chunk = t / kRouteTokens;
+  int my_pos = -1;  // slots with an expert id outside [0, E) (caller-supplied routing) are not routed
+  if (lane < k) {
+    const int e = topk_idx[int64_t(t) * k + lane];
+    if (e >= 0 && e < E) {
+      const int r = ws.local_rank[int64_t(t) * k + lane];
+      const int base = ws.chunk_excl[int64_t(chunk) * E + e] + r;
+      my_pos = ws.pad_start[e] + base;
+      sorted_w[my_pos] = topk_w[int64_t(t) * k + lane];
+      if (perm != nullptr) perm[ws.offs_start[e] + base] = t * k + lane;
+    }
+    slot_pos[int64_t(t) * k + lane] = my_pos;
+  }
+  uint2 pk[BPL];
+  uint32_t word[BPL];
+  const int base_lane = lane & ~3;
+#pragma unroll
+  for (int i = 0; i < BPL; ++i) {
+    const int b = lane + 32 * i;
+    uint32_t sc = 0;
+    pk[i] = make_uint2(0, 0);
+    if (b < nblk) {
+      const uint32_t wds[8] = {u[i][0].x, u[i][0].y, u[i][0].z, u[i][0].w, u[i][1].x, u[i][1].y, u[i][1].z, u[i][1].w};
+      sc = quantize_block16_bf16(wds, pk[i], inv_tab);
+    }
+    uint32_t wq = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) wq |= (__shfl_sync(0xffffffffu, sc, base_lane + q) & 0xFFu) << (8 * q);
+    word[i] = wq;
+  }
+  for (int j = 0; j < k; ++j) {
+    const int p = __shfl_sync(0xffffffffu, my_pos, j);
+    if (p < 0) continue;
+    uint8_t* row = xq + int64_t(p) * (d / 2);
+#pragma unroll
+    for (int i = 0; i < BPL; ++i) {
+      const int b = lane + 32 * i;
+      if (b < nblk) {
+        *reinterpret_cast<uint2*>(row + b * 8) = pk[i];
+        if ((lane & 3) == 0)
+          *reinterpret_cast<uint32_t*>(xs + rowmajor_scale_offset(uint64_t(p), uint32_t(b), uint32_t(nblk))) =
+              word[i];
       }
     }
   }
@@ -90,8 +181,24 @@ int launch_permute_quantize(const uint16_t* x, const uint8_t* valid, const int32
                             int T, int d, int E, int k, const RouteWorkspace& ws, int32_t* slot_pos, float* sorted_w,
                             int32_t* perm, uint8_t* xq, uint8_t* xs, cudaStream_t stream) {
   const int blocks = (T + 7) / 8 + E;
-  return launch_pdl(permute_quant_kernel, dim3(blocks), dim3(256), 0, stream, x, valid, topk_idx, topk_w, T, d, E, k,
-                    ws, slot_pos, sorted_w, perm, xq, xs) == cudaSuccess
+  const int bpl = (d / 16 + 31) / 32;
+  cudaError_t e;
+  if (bpl <= 1)
+    e = launch_pdl(permute_quant_row_kernel<1>, dim3(blocks), dim3(256), 0, stream, x, valid, topk_idx, topk_w, T, d,
+                   E, k, ws, slot_pos, sorted_w, perm, xq, xs);
+  else if (bpl <= 2)
+    e = launch_pdl(permute_quant_row_kernel<2>, dim3(blocks), dim3(256), 0, stream, x, valid, topk_idx, topk_w, T, d,
+                   E, k, ws, slot_pos, sorted_w, perm, xq, xs);
+  else if (bpl <= 4)
+    e = launch_pdl(permute_quant_row_kernel<4>, dim3(blocks), dim3(256), 0, stream, x, valid, topk_idx, topk_w, T, d,
+                   E, k, ws, slot_pos, sorted_w, perm, xq, xs);
+  else if (bpl <= 8)
+    e = launch_pdl(permute_quant_row_kernel<8>, dim3(blocks), dim3(256), 0, stream, x, valid, topk_idx, topk_w, T, d,
+                   E, k, ws, slot_pos, sorted_w, perm, xq, xs);
+  else
+    e = launch_pdl(permute_quant_kernel, dim3(blocks), dim3(256), 0, stream, x, valid, topk_idx, topk_w, T, d, E, k,
+                   ws, slot_pos, sorted_w, perm, xq, xs);
+  return e == cudaSuccess
              ? MCL4MOE_OK
              : MCL4MOE_ERR_CUDA;
 }
@@ -137,7 +244,7 @@ __global__ void __launch_bounds__(256) quant_grouped_rows_kernel(const uint16_t*
     const int groups = nblk / 4;
     for (int i = threadIdx.x; i < (end - start) * groups; i += blockDim.x) {
       const int r = start + i / groups, g = i % groups;
-      *reinterpret_cast<uint32_t*>(xs + swizzled_scale_offset(uint64_t(r), uint32_t(4 * g), uint32_t(nblk))) = 0u;
+      *reinterpret_cast<uint32_t*>(xs + rowmajor_scale_offset(uint64_t(r), uint32_t(4 * g), uint32_t(nblk))) = 0u;
     }
     return;
   }
@@ -169,7 +276,7 @@ __global__ void __launch_bounds__(256) quant_grouped_rows_kernel(const uint16_t*
 #pragma unroll
     for (int q = 0; q < 4; ++q) word |= (__shfl_sync(0xffffffffu, s, base_lane + q) & 0xFFu) << (8 * q);
     if ((lane & 3) == 0 && b < nblk)
-      *reinterpret_cast<uint32_t*>(xs + swizzled_scale_offset(uint64_t(p), uint32_t(b), uint32_t(nblk))) = word;
+      *reinterpret_cast<uint32_t*>(xs + rowmajor_scale_offset(uint64_t(p), uint32_t(b), uint32_t(nblk))) = word;
   }
 }
 
