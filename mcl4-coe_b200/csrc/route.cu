@@ -292,29 +292,47 @@ int launch_quantize_grouped_rows(const uint16_t* x, int64_t M, int K, const int3
 // One warp per token; lane handles 8 consecutive columns per step.  The k
 // slot rows are summed in slot order in float32 and rounded once to bf16
 // (src/mcl4_coe/backbone.py:1035-1041).
+// out[t] = bf16(sum_j y[slot(t, j)]) with the k terms added in slot order in fp32
+// (src/mcl4_coe/backbone.py:904-910; the routing weight is already in y).  One
+// warp per token and column range: grid.y splits the row into ranges of
+// cols_per_y columns, so a small batch still spreads over many warps.  BATCH
+// slot pieces are loaded before they are added: 8 for small batches (few warps,
+// latency-bound), 1 for large ones (bandwidth-bound; fewer registers, more warps).
+template <int BATCH>
 __global__ void __launch_bounds__(256) combine_kernel(const uint16_t* __restrict__ y,
                                                       const int32_t* __restrict__ slot_pos,
                                                       const uint8_t* __restrict__ valid, int T, int k, int d,
-                                                      uint16_t* __restrict__ out) {
+                                                      int cols_per_y, uint16_t* __restrict__ out) {
   pdl_wait();  // the down projection's rows are complete
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (t >= T) return;
   const bool routed = valid == nullptr || valid[t] != 0;
-  int my_pos = 0;
+  int my_pos = -1;
   if (routed && lane < k) my_pos = slot_pos[int64_t(t) * k + lane];
-  for (int c = lane * 8; c < d; c += 256) {
+  const int c_end = min(d, int(blockIdx.y + 1) * cols_per_y);
+  for (int c = int(blockIdx.y) * cols_per_y + lane * 8; c < c_end; c += 256) {
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     if (routed) {
-      for (int j = 0; j < k; ++j) {
-        const int p = __shfl_sync(0xffffffffu, my_pos, j);
-        if (p < 0) continue;  // slot not routed (caller-supplied routing)
-        const uint4 u = __ldg(reinterpret_cast<const uint4*>(y + int64_t(p) * d + c));
-        const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+      for (int j0 = 0; j0 < k; j0 += BATCH) {
+        uint4 u[BATCH];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          acc[2 * i] = __fadd_rn(acc[2 * i], bf16_to_f32(uint16_t(w4[i] & 0xFFFFu)));
-          acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], bf16_to_f32(uint16_t(w4[i] >> 16)));
+        for (int jj = 0; jj < BATCH; ++jj) {
+          const int p = __shfl_sync(0xffffffffu, my_pos, (j0 + jj) & 31);
+          u[jj] = (j0 + jj < k && p >= 0) ? __ldg(reinterpret_cast<const uint4*>(y + int64_t(p) * d + c))
+                                          : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int jj = 0; jj < BATCH; ++jj) {
+          if (j0 + jj >= k) break;
+          const int p = __shfl_sync(0xffffffffu, my_pos, (j0 + jj) & 31);
+          if (p < 0) continue;  // slot not routed (caller-supplied routing)
+          const uint32_t w4[4] = {u[jj].x, u[jj].y, u[jj].z, u[jj].w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            acc[2 * i] = __fadd_rn(acc[2 * i], bf16_to_f32(uint16_t(w4[i] & 0xFFFFu)));
+            acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], bf16_to_f32(uint16_t(w4[i] >> 16)));
+          }
         }
       }
     }
@@ -329,10 +347,18 @@ __global__ void __launch_bounds__(256) combine_kernel(const uint16_t* __restrict
 int launch_combine(const uint16_t* y, const int32_t* slot_pos, const uint8_t* valid, int T, int k, int d, uint16_t* out,
                    cudaStream_t stream) {
   if (T == 0) return MCL4MOE_OK;
-  return launch_pdl(combine_kernel, dim3((T + 7) / 8), dim3(256), 0, stream, y, slot_pos, valid, T, k, d, out) ==
-                 cudaSuccess
-             ? MCL4MOE_OK
-             : MCL4MOE_ERR_CUDA;
+  // enough warps to cover the SMs a few times: split each row into column ranges
+  // (multiples of 256 columns) while the token warps alone are fewer than ~16 per SM
+  const int chunks256 = d / 256;
+  int split = 1;
+  while (split < chunks256 && int64_t(T) * split < int64_t(16) * num_sms() && chunks256 % (2 * split) == 0) split *= 2;
+  const int cols_per_y = d / split;
+  const cudaError_t e =
+      split > 1 ? launch_pdl(combine_kernel<8>, dim3((T + 7) / 8, split), dim3(256), 0, stream, y, slot_pos, valid, T,
+                             k, d, cols_per_y, out)
+                : launch_pdl(combine_kernel<1>, dim3((T + 7) / 8, 1), dim3(256), 0, stream, y, slot_pos, valid, T, k,
+                             d, cols_per_y, out);
+  return e == cudaSuccess ? MCL4MOE_OK : MCL4MOE_ERR_CUDA;
 }
 
 }  // namespace mcl4
