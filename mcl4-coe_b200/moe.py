@@ -456,8 +456,11 @@ class SparseMoE(nn.Module):
                 order = sorted(range(len(sel["chosen"])), key=lambda i: sel["chosen"][i])
                 chosen_sorted = torch.tensor([sel["chosen"][i] for i in order], dtype=torch.int32, device=dev)
                 w_sorted = sel["weights"][:, order]
-                idx = full_rows(chosen_sorted.unsqueeze(0).expand(n_act, -1).contiguous(), -1)
-                out = self._forward_routed(xb, vmask, idx, full_rows(w_sorted.contiguous(), 0.0))
+                if sel["chosen"]:
+                    idx = full_rows(chosen_sorted.unsqueeze(0).expand(n_act, -1).contiguous(), -1)
+                    out = self._forward_routed(xb, vmask, idx, full_rows(w_sorted.contiguous(), 0.0))
+                else:  # no valid expert id: the subset contributes nothing (src/mcl4_coe/backbone.py:324-325)
+                    out = torch.zeros((T, d), dtype=torch.bfloat16, device=dev)
                 rem = rv.dense_remainder(self, sel, xb.dtype)
                 if rem is not None:
                     sparse = self._forward_routed(xb, vmask, full_rows(rem["selected"].to(torch.int32), -1),
