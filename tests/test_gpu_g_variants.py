@@ -155,3 +155,19 @@ def test_routed_forward_skips_out_of_range_ids(moe_pkg):
         b = moe._forward_routed(x, None, idx.to(DEV), w_keep.to(DEV))
     torch.cuda.synchronize()
     assert torch.equal(a, b)
+
+
+def test_dense_subset_without_valid_ids(moe_pkg):
+    """Only out-of-range dense ids: the subset contributes nothing (zeros), and with
+    combine_dense_and_sparse the sparse remainder alone is mixed in."""
+    case, opt = CASES["v_dense_idx"]
+    moe = _module(moe_pkg, case, opt)
+    T, d = case["t"], case["d"]
+    x = torch.from_numpy(case["x_bf16_bits"].view(np.int16).copy()).view(torch.bfloat16).reshape(T, d).to(DEV)
+    with torch.no_grad():
+        out, aux, z, counts = moe(x, dense_expert_indices=[99, -1])
+        assert torch.all(out == 0)
+        moe.combine_dense_and_sparse = True
+        mixed, _, _, _ = moe(x, dense_expert_indices=[99])
+    torch.cuda.synchronize()
+    assert torch.isfinite(mixed.float()).all() and mixed.abs().sum() > 0
