@@ -171,6 +171,34 @@ class CudaEPOps:
         return out
 
 
+def row_plan(tab: list, c: int, me: int) -> list[tuple[int, int, int, int]]:
+    """Row copies of rank ``me`` for chunk ``c``: ``(dest, first send row, rows, first row
+    in dest's receive region)``.  ``tab[s][c][g]`` = rows rank s sends to rank g; a sender's
+    rows are grouped by destination in rank order, and a receiver's region holds its
+    senders' rows in rank order, which is the row order its experts step reads."""
+    G = len(tab)
+    plan, start = [], 0
+    for g in range(G):
+        n = tab[me][c][g]
+        plan.append((g, start, n, sum(tab[s][c][g] for s in range(me))))
+        start += n
+    return plan
+
+
+def back_plan(tab: list, c: int, me: int) -> list[tuple[int, int, int, int]]:
+    """Partial-sum copies of rank ``me`` for chunk ``c``: ``(source rank, first partial row,
+    rows, first row in the source's return region)``.  Partial row i of a receiver belongs
+    to its i-th received row; the source keeps its returns in send order, so the combine
+    finds each token's partials at the rows it sent them from."""
+    G = len(tab)
+    plan, at_here = [], 0
+    for s in range(G):
+        n = tab[s][c][me]
+        plan.append((s, at_here, n, sum(tab[s][c][g] for g in range(me))))
+        at_here += n
+    return plan
+
+
 class PeerExchange:
     """Exchange between the ranks of one node through peer memory.
 
@@ -534,23 +562,13 @@ class ExpertParallelMoE(nn.Module):
             ex["slots"][0] += sum(tab[s][c][G + me] for s in range(G))
         self.last_exchange = ex
 
-        def rows_pieces(c):  # my rows for g go after the rows of lower ranks in g's region
-            base, pieces, start = disp[c][0].data_ptr(), [], 0
-            for g in range(G):
-                cnt = tab[me][c][g]
-                at = sum(tab[s][c][g] for s in range(me))
-                pieces.append((g, base + start * rb, cnt * rb, at * rb))
-                start += cnt
-            return pieces
+        def rows_pieces(c):
+            base = disp[c][0].data_ptr()
+            return [(g, base + src * rb, n * rb, dst * rb) for g, src, n, dst in row_plan(tab, c, me)]
 
-        def back_pieces(c, partial):  # partials of the rows from s go where s keeps its segment for me
-            base, pieces, at_here = partial.data_ptr(), [], 0
-            for s in range(G):
-                cnt = tab[s][c][me]
-                at = sum(tab[s][c][g] for g in range(me))
-                pieces.append((s, base + at_here * d * 2, cnt * d * 2, at * d * 2))
-                at_here += cnt
-            return pieces
+        def back_pieces(c, partial):
+            base = partial.data_ptr()
+            return [(s, base + src * d * 2, n * d * 2, dst * d * 2) for s, src, n, dst in back_plan(tab, c, me)]
 
         px.complete(px.issue("rows0", rows_pieces(0)))
         mark(4)

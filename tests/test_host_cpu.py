@@ -118,3 +118,33 @@ def test_convert_linear_to_nvfp4(moe_pkg):
     assert tree[0].sparsity_mode == "2to4_transposable"
     with pytest.raises(ValueError):
         moe_pkg.NVFP4Linear(64, 64, sparsity_mode="dense")
+
+
+def test_peer_exchange_plans_route_every_row(moe_pkg):
+    """Simulate every rank's row copies and partial-sum copies (row_plan / back_plan) on
+    random counts: each receiver's region holds its senders' rows in rank order, and each
+    sender gets every partial back at the row it sent it from."""
+    import random
+
+    ep = moe_pkg.expert_parallel
+    rnd = random.Random(3)
+    for G in (1, 2, 3, 8):
+        for n_chunks in (1, 2):
+            tab = [[[rnd.randint(0, 5) for _ in range(G)] + [0] * G + [0] for _ in range(n_chunks)]
+                   for _ in range(G)]
+            for c in range(n_chunks):
+                # sender s's send buffer: rows grouped by destination, labelled (s, g, i)
+                send = {s: [(s, g, i) for g in range(G) for i in range(tab[s][c][g])] for s in range(G)}
+                recv = {g: [None] * sum(tab[s][c][g] for s in range(G)) for g in range(G)}
+                for s in range(G):
+                    for g, src, n, dst in ep.row_plan(tab, c, s):
+                        recv[g][dst:dst + n] = send[s][src:src + n]
+                for g in range(G):
+                    assert recv[g] == [(s, g, i) for s in range(G) for i in range(tab[s][c][g])]
+                # the receiver's partial row j answers its received row j
+                back = {s: [None] * len(send[s]) for s in range(G)}
+                for g in range(G):
+                    for s, src, n, dst in ep.back_plan(tab, c, g):
+                        back[s][dst:dst + n] = recv[g][src:src + n]
+                for s in range(G):
+                    assert back[s] == send[s]
