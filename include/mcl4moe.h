@@ -68,7 +68,8 @@ int mcl4moe_read_error(int32_t* device_error_word, int32_t* host_value, mcl4moe_
  * (amax > 0, else 1).  packed: [rows, cols/2]; scales: the swizzled 128x4-atom
  * layout of _swizzle_scales for rows_pad rows (multiple of 128, >= rows;
  * padding rows get zero scales); global_scale: device fp32 [1];
- * amax_scratch: device fp32 [1].  Requires cols % 64 == 0.
+ * amax_scratch: device fp32 [1].  Requires cols % 64 == 0, x 16-byte aligned and
+ * a row stride of a multiple of 16 bytes.
  * ------------------------------------------------------------------------ */
 int mcl4moe_quantize_rows(const void* x, int dtype, int64_t rows, int cols, int64_t ld, int causal, uint8_t* packed,
                           uint8_t* scales, int64_t rows_pad, float* global_scale, float* amax_scratch,

@@ -136,6 +136,7 @@ int mcl4moe_quantize_rows(const void* x, int dtype, int64_t rows, int cols, int6
   if (cols % 16 != 0) return MCL4MOE_ERR_INVALID;  // src/mcl4_coe/nvfp4.py:248-249
   if (cols % 64 != 0) return MCL4MOE_ERR_UNSUPPORTED;
   if (rows_pad < rows || rows_pad % 128 != 0 || ld < cols || (rows > 0 && !x)) return MCL4MOE_ERR_INVALID;
+  if (!aligned16(x) || (ld * (dtype == 0 ? 2 : 4)) % 16 != 0) return MCL4MOE_ERR_INVALID;  // vector loads
   return launch_quantize_rows(x, dtype, rows, cols, ld, causal, packed, scales, rows_pad, global_scale, amax_scratch,
                               nullptr, nullptr, 0, stream);
 }

@@ -208,6 +208,29 @@ __device__ __forceinline__ float load_f32<float>(const float* p) { return __ldg(
 template <>
 __device__ __forceinline__ float load_f32<uint16_t>(const uint16_t* p) { return bf16_to_f32(__ldg(p)); }
 
+// The 16 values of a block starting at p (16-byte aligned) with vector loads.
+__device__ __forceinline__ void load_block16(const float* p, float (&v)[16]) {
+  const float4* q = reinterpret_cast<const float4*>(p);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float4 f = __ldg(q + i);
+    v[4 * i] = f.x, v[4 * i + 1] = f.y, v[4 * i + 2] = f.z, v[4 * i + 3] = f.w;
+  }
+}
+__device__ __forceinline__ void load_block16(const uint16_t* p, float (&v)[16]) {
+  const uint4* q = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const uint4 u = __ldg(q + i);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[8 * i + 2 * j] = bf16_to_f32(uint16_t(w[j] & 0xFFFFu));
+      v[8 * i + 2 * j + 1] = bf16_to_f32(uint16_t(w[j] >> 16));
+    }
+  }
+}
+
 // max |x| over a [rows, cols] matrix (row stride ld) into *amax (zeroed before):
 // float bits of non-negative values order like unsigned ints.
 template <typename InT>
@@ -252,11 +275,9 @@ __global__ void __launch_bounds__(256) rows_quant_kernel(const InT* __restrict__
   for (int b = lane; b < nblk; b += 32) {
     float v[16];
     float m = 0.f;
+    load_block16(x + row * ld + b * 16, v);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      v[j] = load_f32(x + row * ld + b * 16 + j);
-      m = fmaxf(m, fabsf(v[j]));
-    }
+    for (int j = 0; j < 16; ++j) m = fmaxf(m, fabsf(v[j]));
     const uint32_t sc = f32_to_e4m3(fminf(__fdiv_rn(m, six_g), 448.0f));
     const float inv = inverse_decoding(__fmul_rn(e4m3_to_f32(sc), g));
     uint32_t lo = 0, hi = 0;

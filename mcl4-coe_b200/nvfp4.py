@@ -479,9 +479,15 @@ class NVFP4Linear(nn.Linear):
             n, k = self.weight.shape
             np_, kp = _round_up(n, 256), _round_up(k, 256)
             bias = None
-            if self.bias is not None:
-                bias = torch.zeros((np_,), dtype=torch.float32, device=flat.device)
-                bias[:n] = self.bias.detach().to(torch.float32)
+            if self.bias is not None:  # fp32, zero-padded to the GEMM's N; rebuilt when the bias changes
+                b = self.bias
+                bkey = (b._version, b.data_ptr(), str(flat.device))
+                cached = getattr(self, "_b200_bias_cache", None)
+                if cached is None or cached[0] != bkey:
+                    padded = torch.zeros((np_,), dtype=torch.float32, device=flat.device)
+                    padded[:n] = b.detach().to(device=flat.device, dtype=torch.float32)
+                    self._b200_bias_cache = cached = (bkey, padded)
+                bias = cached[1]
             _GEMM_COUNTS["forward"] = _GEMM_COUNTS.get("forward", 0) + 1
             out = _mm_prepared(flat, pk, sw, g, np_, kp, self.causal_activation_scale, bias)[:, :n]
         return out.to(inputs.dtype).reshape(*inputs.shape[:-1], self.out_features)
