@@ -391,6 +391,17 @@ class ExpertParallelMoE(nn.Module):
                    transport: str = "auto", chunks: int = 0) -> "ExpertParallelMoE":
         """Shard a single-device layer (this package's or the reference's SparseMoE):
         the router is shared, this rank keeps its block of experts."""
+        variant = [name for name, on in (
+            ("mitotic twin routing", bool(getattr(moe, "mitotic_pairs", None))),
+            ("lineage family routing", getattr(moe, "lineage_top_families", 0) > 0
+             and getattr(moe, "lineage_root_ids", None) is not None),
+            ("dense expert subsets", bool(getattr(moe, "dense_expert_indices", ()))
+             or getattr(moe, "dense_subset_k", 0) > 0),
+            ("the recurrent coverage penalty", getattr(moe, "recurrent_coverage_penalty", 0.0) > 0.0),
+            ("sequence-diversity / mitotic-orthogonality losses", getattr(moe, "sequence_diversity_coef", 0.0) > 0.0
+             or getattr(moe, "mitotic_ortho_coef", 0.0) > 0.0)) if on]
+        if variant:
+            raise NotImplementedError(f"the expert-parallel layer routes plain top-k only; this layer uses {variant[0]}")
         E = len(moe.experts)
         cfg = type("Cfg", (), dict(d_model=moe.router.in_features, num_experts=E,
                                    expert_hidden_dim=moe.experts[0].down_proj.in_features, top_k=moe.top_k,

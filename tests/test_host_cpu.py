@@ -148,3 +148,29 @@ def test_peer_exchange_plans_route_every_row(moe_pkg):
                         back[s][dst:dst + n] = recv[g][src:src + n]
                 for s in range(G):
                     assert back[s] == send[s]
+
+
+def test_expert_parallel_refuses_routing_variants(moe_pkg):
+    """Sharding a layer whose routing is not plain top-k must not silently drop the variant."""
+    import os
+    import socket
+
+    import torch.distributed as dist
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=0, world_size=1)
+    try:
+        moe = moe_pkg.SparseMoE(_cfg(moe_pkg))
+        moe_pkg.ExpertParallelMoE.from_dense(moe)  # plain top-k: fine
+        moe.mitotic_pairs = [(0, 1)]
+        with pytest.raises(NotImplementedError, match="mitotic"):
+            moe_pkg.ExpertParallelMoE.from_dense(moe)
+        moe.mitotic_pairs = []
+        moe.dense_subset_k = 2
+        with pytest.raises(NotImplementedError, match="dense"):
+            moe_pkg.ExpertParallelMoE.from_dense(moe)
+    finally:
+        dist.destroy_process_group()
