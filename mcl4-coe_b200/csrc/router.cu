@@ -255,6 +255,7 @@ __global__ void __launch_bounds__(256) router_gemv_kernel(const uint16_t* __rest
                                                           const float* __restrict__ bias, int T, int d, int E,
                                                           float* __restrict__ logits) {
   extern __shared__ uint16_t xs[];  // [8][d] bf16
+  pdl_wait();  // x (and the router weight) are complete (PDL launch)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int t0 = blockIdx.x * 8, e = blockIdx.y * 8 + warp;
   const int nt = min(8, T - t0);
@@ -470,6 +471,8 @@ __global__ void __launch_bounds__(kTailThreads) router_logits_kernel(const float
   const TailSmem s = carve_tail(smem_raw, a.E, a.k);
   const int chunk = blockIdx.x;
   const int t0 = chunk * kRouteTokens;
+  pdl_wait();     // the logits are complete (PDL launch)
+  pdl_trigger();  // the scan may launch; it waits for this grid's writes
   if (chunk == 0 && threadIdx.x == 0) *ws.done = 0u;
   for (int i = threadIdx.x; i < kRouteTokens * a.E; i += blockDim.x) {
     const int tok = i / a.E, e = i - tok * a.E;
@@ -665,8 +668,10 @@ int launch_router_t(const uint16_t* x, const float* wr, const float* bias, const
     const size_t smem = tail_smem_bytes(a.E, a.k);
     static std::atomic<uint64_t> configured{0};
     if (!raise_smem_limit(router_logits_kernel<EW>, 200 * 1024, configured)) return MCL4MOE_ERR_CUDA;
-    router_logits_kernel<EW><<<C, kTailThreads, smem, stream>>>(logits_in, nullptr, a, ws);  // final logits
-    return cudaGetLastError() == cudaSuccess ? MCL4MOE_OK : MCL4MOE_ERR_CUDA;
+    return launch_pdl(router_logits_kernel<EW>, dim3(C), dim3(kTailThreads), smem, stream, logits_in,
+                      static_cast<const float*>(nullptr), a, ws) == cudaSuccess  // final logits
+               ? MCL4MOE_OK
+               : MCL4MOE_ERR_CUDA;
   }
   // split the router weight into three bf16 parts, then the tensor-core router
   const int64_t n = int64_t(a.E_pad) * a.d;
@@ -724,9 +729,9 @@ int launch_route(const uint16_t* x, const float* wr, const float* bias, const fl
         if (!raise_smem_limit(router_gemv_kernel, 200 * 1024, configured)) return MCL4MOE_ERR_CUDA;
       }
       if (smem > 200 * 1024) return MCL4MOE_ERR_UNSUPPORTED;
-      router_gemv_kernel<<<dim3((T + 7) / 8, (E + 7) / 8), 256, smem, stream>>>(x, wr, bias, T, d, E,
-                                                                              ws.small_logits);
-      if (cudaGetLastError() != cudaSuccess) return MCL4MOE_ERR_CUDA;
+      if (launch_pdl(router_gemv_kernel, dim3((T + 7) / 8, (E + 7) / 8), dim3(256), smem, stream, x, wr, bias, T, d,
+                     E, ws.small_logits) != cudaSuccess)
+        return MCL4MOE_ERR_CUDA;
       logits_in = ws.small_logits;  // final logits: the tail below adds no bias
     }
     int st;
