@@ -11,13 +11,30 @@ T=32768, d=2048, E=64, top-8, F=1024).  Synthetic data: x ~ N(0,1) bf16,
 router and expert weights ~ N(0, 0.02) fp32, quantised to NVFP4 once (the
 quantised-weight cache is reused across steps, as in the reference).
 
-Multi-GPU (torchrun, one process per GPU): weak scaling, every rank runs the
-full layer on its own T tokens with a replica of all experts (no collective on
-the data path); the expert-parallel layout is not used by this bench.
+Multi-GPU (torchrun, one process per GPU): weak scaling with expert
+parallelism.  Every rank routes its own T tokens; the experts are sharded in
+contiguous blocks of E/N (``ExpertParallelMoE``), each rank sends its tokens'
+NVFP4 rows to the ranks holding their experts and gets bf16 partial sums back
+(copy-engine copies into CUDA-IPC-mapped peer buffers, ordered by a
+one-element NCCL all-reduce).  ``value`` is the tokens of all ranks over the
+slowest rank's device time.
 
-``--impl reference`` times the reference path's CPU implementation (the numpy
-restatement in ``oracle/``) on this host's cores, rank 0 only, on a bounded
-token sample per step.
+CPU baselines (rank 0, 1 GPU): the reference's own ``SparseMoE.forward``
+(installed under ``baseline/_ref``) on the host cores with its expert
+projections replaced by dequantised-FP4 linears built from the reference's
+``_quantize_nvfp4_core`` / ``_dequantize_nvfp4`` (the "dequantised-FP4 CPU
+path"); the numpy restatement in ``oracle/`` stands in when ``baseline/_ref``
+is missing.  ``cpu_baseline`` runs the full batch once; ``--impl reference``
+runs a bounded token sample per step so that the whole run ends in minutes.
+
+``reference_gpu`` (1 GPU): the unmodified reference on the same B200 — its
+``SparseMoE.forward`` as dispatched (per-expert ``F.scaled_mm`` loop for the
+configurations with E*d >= 65536) and with its grouped branch (Triton
+``tl.dot_scaled`` kernels through ``nvfp4_grouped_linear``).
+
+``--fp4-peak`` measures the dense NVFP4 GEMM rate of cuBLAS (``F.scaled_mm``,
+16-element E4M3 block scales) at 8192^3, the FP4 counterpart of the bf16 GEMM
+peak in MEASURED_PEAKS.json.
 """
 
 from __future__ import annotations
@@ -134,35 +151,252 @@ def build_layer(pkg, cfg, device, rank):
     return moe, x
 
 
-def cpu_baseline_ours(moe, x, cfg, sample: int) -> dict:
-    """The oracle (numpy restatement of the reference path) on a token sample, on this host."""
+def _reference_modules():
+    """The reference package installed under baseline/_ref (``mcl4_coe.backbone``,
+    ``mcl4_coe.nvfp4``), or None when it is not installed."""
+    ref_dir = ROOT / "baseline" / "_ref"
+    if not (ref_dir / "mcl4_coe" / "backbone.py").exists():
+        return None
+    if str(ref_dir) not in sys.path:
+        sys.path.insert(0, str(ref_dir))
+    import mcl4_coe.backbone as bb
+    import mcl4_coe.nvfp4 as nv
+
+    return bb, nv
+
+
+def _host_threads() -> dict:
     import torch
 
-    sys.path.insert(0, str(ROOT))
-    from oracle import moe_ref, nvfp4_ref as nr
+    try:
+        from threadpoolctl import threadpool_info
 
-    pkg = sys.modules["mcl4coe_b200"]
-    experts = moe_ref.QuantizedExperts.__new__(moe_ref.QuantizedExperts)
-    deq = {}
-    for proj in ("up_proj", "down_proj"):
-        ref = pkg.export_reference_cache(moe.experts, proj)
-        b = ref["B_fwd"].cpu().numpy()
-        s = ref["Bs_fwd"].view(torch.uint8).cpu().numpy()
-        gsc = ref["Bg"].cpu().numpy()
-        deq[proj] = [nr.dequantize_grouped_weight(b, s, gsc, e) for e in range(cfg["e"])]
-    experts.up, experts.dn = deq["up_proj"], deq["down_proj"]
-    xs = x[:sample].float().cpu().numpy()
-    wr = moe.router.weight.detach().float().cpu().numpy()
-    bias = None if moe.router_logit_bias is None else moe.router_logit_bias.cpu().numpy()
-    moe_ref.moe_forward(xs[:8], wr, experts, cfg["k"], True, None, bias)  # warm-up
-    times = []
-    for _ in range(3):
+        blas = max((i.get("num_threads", 1) for i in threadpool_info()), default=1)
+    except Exception:
+        blas = None
+    return {"os_cpu_count": os.cpu_count(), "torch_threads": torch.get_num_threads(), "blas_threads": blas}
+
+
+def reference_cpu_layer(cfg, wr, w_up, w_dn, bias):
+    """The reference SparseMoE (loop branch on the CPU) with dequantised-FP4 expert
+    projections: every projection input is quantised to NVFP4 (1x16 blocks, g = 1)
+    and dequantised, the weights are the 16x16-tile NVFP4 weights dequantised, fp32
+    product rounded to bf16.  ``wr`` / ``w_up`` / ``w_dn`` are fp32 CPU tensors
+    ([E, d], [E, 2F, d], [E, d, F]); ``bias`` an optional [E] router logit bias,
+    added to the router output as the benchmark's skewed configuration defines it."""
+    import torch
+    from torch import nn
+    from torch.nn import functional as Fn
+
+    bb, nv = _reference_modules()
+
+    class DequantFP4Linear(nn.Module):
+        def __init__(self, weight):
+            super().__init__()
+            packed, scales, g = nv._quantize_nvfp4_core(weight, True, False, False)
+            self.register_buffer("w_deq", nv._dequantize_nvfp4(packed, nv._swizzle_scales(scales), g,
+                                                               weight.shape[0], weight.shape[1]))
+
+        def forward(self, x):
+            xf = x.float()
+            packed, scales, g = nv._quantize_nvfp4_core(xf, False, False, True)
+            xd = nv._dequantize_nvfp4(packed, nv._swizzle_scales(scales), g, xf.shape[0], xf.shape[1])
+            return Fn.linear(xd, self.w_deq).to(x.dtype)
+
+    E = wr.shape[0]
+    conf = bb.MCL4CEDConfig(d_model=cfg["d"], n_heads=4, expert_hidden_dim=cfg["f"], num_experts=E,
+                            top_k=cfg["k"], norm_topk_prob=True)
+    moe = bb.SparseMoE(conf).eval()
+    with torch.no_grad():
+        moe.router.weight.copy_(wr)
+        for i, ex in enumerate(moe.experts):
+            ex.up_proj = DequantFP4Linear(w_up[i])
+            ex.down_proj = DequantFP4Linear(w_dn[i])
+    if bias is not None:
+        _add_router_bias(bb, moe.router.weight, bias)
+    return moe
+
+
+def _add_router_bias(bb, router_weight, bias) -> None:
+    """The skewed configuration's additive router logit bias on the reference layer,
+    which computes its logits with ``F.linear(x.float(), router.weight.float())``
+    (src/mcl4_coe/backbone.py:929): wrap ``F.linear`` so that calls with this router
+    weight (``.float()`` of an fp32 tensor is the tensor itself) get the bias added."""
+    linear = bb.F.linear
+
+    def biased_linear(inp, weight, b=None):
+        out = linear(inp, weight, b)
+        return out + bias.to(out.device) if weight is router_weight else out
+
+    bb.F.linear = biased_linear
+
+
+def cpu_baseline_ours(moe, x, cfg) -> dict:
+    """The reference CPU path on this host's cores, over the full batch of the bench's
+    own inputs and weights (one forward after a short warm-up)."""
+    import torch
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    T = x.shape[0]
+    wr = moe.router.weight.detach().float().cpu()
+    bias = None if moe.router_logit_bias is None else moe.router_logit_bias.detach().float().cpu()
+    xs = x.cpu()
+    if _reference_modules() is not None:
+        w_up = torch.stack([e.up_proj.weight.detach().float().cpu() for e in moe.experts])
+        w_dn = torch.stack([e.down_proj.weight.detach().float().cpu() for e in moe.experts])
+        ref = reference_cpu_layer(cfg, wr, w_up, w_dn, bias)
+        del w_up, w_dn
+        with torch.no_grad():
+            ref(xs[: min(T, 256)].unsqueeze(0))  # warm-up
+            t0 = time.perf_counter()
+            ref(xs.unsqueeze(0))
+            t = time.perf_counter() - t0
+        kind, what = "reference", ("reference SparseMoE.forward (baseline/_ref, loop branch) with dequantised-FP4 "
+                                   "expert projections from the reference's own quantiser, torch on all host threads")
+    else:
+        sys.path.insert(0, str(ROOT))
+        from oracle import moe_ref, nvfp4_ref as nr
+
+        pkg = sys.modules["mcl4coe_b200"]
+        experts = moe_ref.QuantizedExperts.__new__(moe_ref.QuantizedExperts)
+        deq = {}
+        for proj in ("up_proj", "down_proj"):
+            r = pkg.export_reference_cache(moe.experts, proj)
+            b = r["B_fwd"].cpu().numpy()
+            sc = r["Bs_fwd"].view(torch.uint8).cpu().numpy()
+            gsc = r["Bg"].cpu().numpy()
+            deq[proj] = [nr.dequantize_grouped_weight(b, sc, gsc, e) for e in range(cfg["e"])]
+        experts.up, experts.dn = deq["up_proj"], deq["down_proj"]
+        xn = xs.float().numpy()
+        bn = None if bias is None else bias.numpy()
+        moe_ref.moe_forward(xn[:8], wr.numpy(), experts, cfg["k"], True, None, bn)
         t0 = time.perf_counter()
-        moe_ref.moe_forward(xs, wr, experts, cfg["k"], True, None, bias)
-        times.append(time.perf_counter() - t0)
-    t = statistics.median(times)
-    return {"value": sample / t, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
-            "sample": f"{sample} tokens of {cfg['name']} per run, median of 3 runs, numpy/BLAS on all host threads"}
+        moe_ref.moe_forward(xn, wr.numpy(), experts, cfg["k"], True, None, bn)
+        t = time.perf_counter() - t0
+        kind, what = "port", "numpy restatement of the reference path (oracle/), numpy/BLAS on all host threads"
+    thr = _host_threads()
+    return {"value": T / t, "unit": UNIT, "cores": thr["torch_threads"] if kind == "reference" else thr["blas_threads"],
+            "kind": kind, "seconds": t, **thr,
+            "sample": f"all {T} tokens of {cfg['name']} (one forward, unsampled): {what}"}
+
+
+def reference_gpu_leg(moe, x, cfg, steps: int) -> dict:
+    """The unmodified reference on this GPU: ``SparseMoE.forward`` as dispatched and with
+    its grouped branch, NVFP4Linear experts (sparsity "none", weights of our layer)."""
+    import torch
+
+    mods = _reference_modules()
+    if mods is None:
+        return {"unavailable": "reference not installed under baseline/_ref"}
+    bb, nv = mods
+    dev = x.device
+    T, d, E, k = x.shape[0], cfg["d"], cfg["e"], cfg["k"]
+    res = {}
+    try:
+        conf = bb.MCL4CEDConfig(d_model=d, n_heads=4, expert_hidden_dim=cfg["f"], num_experts=E, top_k=k,
+                                norm_topk_prob=True)
+        ref = bb.SparseMoE(conf).to(dev).eval()
+        with torch.no_grad():
+            ref.router.weight.copy_(moe.router.weight.detach().float())
+            for re_, ex in zip(ref.experts, moe.experts):
+                re_.up_proj.weight.copy_(ex.up_proj.weight.detach())
+                re_.down_proj.weight.copy_(ex.down_proj.weight.detach())
+        nv.convert_linear_to_nvfp4(ref, sparsity_mode="none")
+        ref.requires_grad_(False)
+        if moe.router_logit_bias is not None:
+            _add_router_bias(bb, ref.router.weight, moe.router_logit_bias.detach().float())
+        res["nvfp4_native"] = bool(nv.has_native_nvfp4(dev))
+        res["triton_grouped"] = bool(nv.has_triton_nvfp4_grouped(dev))
+        xin = x.unsqueeze(0)
+
+        def timed(fn, n):
+            for _ in range(2):
+                fn()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(n):
+                fn()
+            b.record()
+            torch.cuda.synchronize()
+            return a.elapsed_time(b) / n
+
+        with torch.no_grad():
+            branch = "grouped" if ref._can_use_grouped_dispatch(x) else "loop (per-expert F.scaled_mm)"
+            ms = timed(lambda: ref(xin), steps)
+            res["as_dispatched"] = {"branch": branch, "ms_per_step": ms, "value": T / (ms / 1e3), "unit": UNIT}
+            if res["triton_grouped"]:
+                ref._can_use_grouped_dispatch = lambda flat: bool(flat.is_cuda and flat.shape[0] > 0)
+                ms = timed(lambda: ref(xin), steps)
+                res["grouped_branch"] = {"ms_per_step": ms, "value": T / (ms / 1e3), "unit": UNIT,
+                                         "note": "SparseMoE.forward with _can_use_grouped_dispatch forced true: "
+                                                 "router, argsort permute, nvfp4_grouped_linear (Triton "
+                                                 "tl.dot_scaled) for up and down, bf16 SwiGLU, combine"}
+    except Exception as exc:  # the reference's GPU path failing is reported, not fatal
+        res["error"] = f"{type(exc).__name__}: {exc}"[:300]
+    finally:
+        torch.cuda.synchronize()
+    return res
+
+
+def fp4_peak(args) -> None:
+    """cuBLAS dense NVFP4 GEMM (F.scaled_mm with 1x16 E4M3 block scales + fp32 tensor
+    scales, the recipe of the reference's nvfp4_mm) at M = N = K = 8192: best of 10
+    (burst) and back to back for 4 s (sustained), with the clocks sampled meanwhile."""
+    import torch
+    from torch.nn import functional as Fn
+
+    sys.path.insert(0, str(ROOT))
+    from __graft_entry__ import load_package
+
+    pkg = load_package()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    n = 8192
+    g = torch.Generator(device=dev).manual_seed(0)
+    a = torch.randn((n, n), generator=g, device=dev).to(torch.bfloat16)
+    b = torch.randn((n, n), generator=g, device=dev).to(torch.bfloat16)
+    qa, sa, ga = pkg.quantize_nvfp4(a)
+    qb, sb, gb = pkg.quantize_nvfp4(b)
+    recipe = [Fn.ScalingType.BlockWise1x16, Fn.ScalingType.TensorWise]
+    swz = [Fn.SwizzleType.SWIZZLE_32_4_4, Fn.SwizzleType.NO_SWIZZLE]
+
+    def mm():
+        return Fn.scaled_mm(qa, qb.t(), scale_a=[sa, ga], scale_recipe_a=recipe, scale_b=[sb, gb],
+                            scale_recipe_b=recipe, swizzle_a=swz, swizzle_b=swz, output_dtype=torch.bfloat16)
+
+    for _ in range(3):
+        mm()
+    torch.cuda.synchronize()
+    flops = 2.0 * n ** 3
+    best = float("inf")
+    for _ in range(10):
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        mm()
+        s1.record()
+        torch.cuda.synchronize()
+        best = min(best, s0.elapsed_time(s1))
+    sampler = ClockSampler(str(torch.cuda.get_device_properties(dev).uuid)).start()
+    time.sleep(0.3)
+    iters, t_end = 0, time.time() + 4.0
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record()
+    while time.time() < t_end:
+        for _ in range(20):
+            mm()
+        iters += 20
+        torch.cuda.synchronize()
+    s1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    sust = s0.elapsed_time(s1) / iters
+    peaks = load_peaks()
+    print(json.dumps({"what": "dense NVFP4 GEMM, F.scaled_mm (cuBLASLt), 1x16 e4m3 block + fp32 tensor scales",
+                      "m_n_k": n, "burst_tflops": flops / (best / 1e3) / 1e12,
+                      "sustained_tflops": flops / (sust / 1e3) / 1e12, "burst_ms": best, "sustained_ms": sust,
+                      "bf16_tflops_measured": peaks["bf16"], "bf16_tflops_sustained_measured": peaks["bf16_sustained"],
+                      "clocks": clocks}), flush=True)
 
 
 def run_ours(args) -> None:
@@ -360,8 +594,15 @@ def run_ours(args) -> None:
         "gpu_launches": (KERNELS_PER_EP_FORWARD if ep else KERNELS_PER_FORWARD) * K,
         "clocks": clocks,
     }
+    if rank == 0 and world == 1 and not args.no_reference_gpu:
+        with torch.inference_mode():
+            result["reference_gpu"] = reference_gpu_leg(moe, x, cfg, max(3, min(K, 10)))
+        rg = result["reference_gpu"]
+        best = [v["value"] for key, v in rg.items() if isinstance(v, dict) and "value" in v]
+        if best:
+            rg["speedup_vs_best_reference_gpu"] = value / max(best)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        result["cpu_baseline"] = cpu_baseline_ours(moe, x, cfg, args.cpu_sample)
+        result["cpu_baseline"] = cpu_baseline_ours(moe, x, cfg)
     if rank == 0:
         print(json.dumps(result), flush=True)
     if world > 1:
@@ -371,43 +612,68 @@ def run_ours(args) -> None:
 
 # ---------------------------------------------------------------------------- reference arm
 def run_reference(args) -> None:
-    """The reference path's CPU implementation (oracle port), rank 0 only."""
+    """The reference path's CPU implementation on this host's cores, rank 0 only: the
+    reference's own SparseMoE.forward with dequantised-FP4 expert projections
+    (baseline/_ref), or the numpy restatement in oracle/ when it is not installed.
+    Each step is one forward over a bounded token sample of the configuration."""
     if int(os.environ.get("RANK", "0")) != 0:
         return
-    sys.path.insert(0, str(ROOT))
-    from oracle import moe_ref
+    import torch
 
+    sys.path.insert(0, str(ROOT))
+    torch.set_num_threads(os.cpu_count() or 1)
     cfg = CONFIGS[args.config]
     T, d, E, k, F = cfg["t"], cfg["d"], cfg["e"], cfg["k"], cfg["f"]
     r = np.random.Generator(np.random.PCG64(cfg["seed"]))
     wr = (r.standard_normal((E, d), dtype=np.float32) * 0.02).astype(np.float32)
     w_up = (r.standard_normal((E, 2 * F, d), dtype=np.float32) * 0.02).astype(np.float32)
     w_dn = (r.standard_normal((E, d, F), dtype=np.float32) * 0.02).astype(np.float32)
-    experts = moe_ref.QuantizedExperts(w_up, w_dn)  # weight quantisation: cached, not timed (as in the reference)
-    del w_up, w_dn
     bias = (2.0 * np.log(1.0 / np.arange(1, E + 1))).astype(np.float32) if cfg.get("zipf") else None
     sample = min(T, args.cpu_sample)
     x = r.standard_normal((T, d), dtype=np.float32)
+    if _reference_modules() is not None:
+        # weight quantisation happens here, once: cached, not timed (as in the reference)
+        layer = reference_cpu_layer(cfg, torch.from_numpy(wr), torch.from_numpy(w_up), torch.from_numpy(w_dn),
+                                    None if bias is None else torch.from_numpy(bias))
+        xt = torch.from_numpy(x).to(torch.bfloat16)
+
+        def fwd(lo):
+            with torch.no_grad():
+                layer(xt[lo:lo + sample].unsqueeze(0))
+
+        kind = "reference"
+        what = ("reference SparseMoE.forward (baseline/_ref, loop branch) with dequantised-FP4 expert projections "
+                "from the reference's own quantiser, torch on all host threads")
+    else:
+        from oracle import moe_ref
+
+        experts = moe_ref.QuantizedExperts(w_up, w_dn)
+
+        def fwd(lo):
+            moe_ref.moe_forward(x[lo:lo + sample], wr, experts, k, True, None, bias)
+
+        kind, what = "port", "numpy restatement of the reference SparseMoE forward on dequantised NVFP4 (oracle/)"
+    del w_up, w_dn
     times = []
     for i in range(args.warmup + args.steps):
         lo = (i * sample) % max(1, T - sample + 1)
-        xs = x[lo:lo + sample]
         t0 = time.perf_counter()
-        moe_ref.moe_forward(xs, wr, experts, k, True, None, bias)
+        fwd(lo)
         if i >= args.warmup:
             times.append(time.perf_counter() - t0)
     step = statistics.mean(times)
     value = sample / step
+    thr = _host_threads()
     res = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": step * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp32 math on NVFP4-dequantised operands",
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32 math on NVFP4-dequantised operands, bf16 I/O",
         "data": "synthetic (numpy PCG64, same shapes and distributions)",
         "config": {"workload": cfg["name"], "tokens_per_gpu": T, "d_model": d, "num_experts": E, "top_k": k,
                    "expert_ffn": F, "parallelism": "host cpu"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
-                         "sample": f"{sample} tokens of {cfg['name']} per step (numpy restatement of the "
-                                   "reference SparseMoE forward on dequantised NVFP4, all host threads)"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": thr["torch_threads"] if kind == "reference"
+                         else thr["blas_threads"], "kind": kind, **thr,
+                         "sample": f"{sample} tokens of {cfg['name']} per step: {what}"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(res), flush=True)
@@ -421,8 +687,12 @@ def main() -> None:
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
     ap.add_argument("--tokens", type=int, default=0, help="override the configuration's token count (profiling)")
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
-    ap.add_argument("--cpu-sample", type=int, default=256)
+    ap.add_argument("--cpu-sample", type=int, default=4096,
+                    help="--impl reference: tokens per step (a bounded sample of the configuration)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip timing the reference's own GPU path on this device")
+    ap.add_argument("--fp4-peak", action="store_true", help="measure the cuBLAS dense NVFP4 GEMM rate and exit")
     ap.add_argument("--cuda-graph", action="store_true",
                     help="1 GPU: serve the timed forwards from a captured CUDA graph (SparseMoE.enable_cuda_graph)")
     ap.add_argument("--ep-partials", default="copy", choices=("kernel", "copy"),
@@ -435,7 +705,9 @@ def main() -> None:
     if args.tokens > 0:
         CONFIGS[args.config] = dict(CONFIGS[args.config], t=args.tokens,
                                     name=f"{CONFIGS[args.config]['name']}_t{args.tokens}")
-    if args.impl == "reference":
+    if args.fp4_peak:
+        fp4_peak(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

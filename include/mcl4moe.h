@@ -150,9 +150,13 @@ int mcl4moe_quantize_activations(const uint16_t* x, int64_t rows, int cols, int6
  * logits_out fp32 [T, E] (nullable), sel_mask fp32 [T, E] (nullable),
  * counts int32 [E], stats fp32 [3 + E]: {aux_loss, z_loss, n_routed,
  * counts_fraction[E]} (the layer's aux, router_z_loss and counts outputs).
- * The router product runs on the tensor cores with the fp32 weight split into
+ * Batches of up to 1024 tokens with d <= 12800 compute the logits on the CUDA
+ * cores (fp32 FMA, fixed summation order); longer batches and wider rows run
+ * the router product on the tensor cores with the fp32 weight split into
  * three bf16 parts (fp32-accurate logits).  Requires E <= 256,
- * k <= min(E, 32), d % 64 == 0.
+ * k <= min(E, 32), d % 64 == 0, T * k <= 2^30 (counts, offsets and slot
+ * ranks are int32; larger batches return MCL4MOE_ERR_UNSUPPORTED and a
+ * workspace size of 0).
  * ------------------------------------------------------------------------ */
 size_t mcl4moe_route_workspace_size(int T, int E, int k, int d);
 int mcl4moe_route(const uint16_t* x, const float* wr, const float* logit_bias, const float* logits_in,
@@ -170,9 +174,11 @@ int mcl4moe_route(const uint16_t* x, const float* wr, const float* logit_bias, c
  * at E = 64, k = 8, d = 2048); a shape whose mcl4moe_route_workspace_size
  * exceeds it returns MCL4MOE_ERR_WORKSPACE.  The first call on a device (that
  * device current) does the set-up — it looks up the array's device address,
- * which may load the module — so make it before any stream capture; later
- * calls allocate nothing.  There is one array per device: calls on one
- * device must not overlap in time, or they race on the scratch.
+ * which may load the module — so make it before any stream capture; the
+ * address is kept per device and CUDA context, and the first call in a new
+ * context (after cudaDeviceReset) looks it up again.  Later calls allocate
+ * nothing.  There is one array per device: calls on one device must not
+ * overlap in time, or they race on the scratch.
  * ------------------------------------------------------------------------ */
 size_t mcl4moe_route_noalloc_scratch_bytes(void);
 int mcl4moe_route_noalloc(const uint16_t* x, const float* wr, const float* logit_bias, const float* logits_in,
@@ -268,7 +274,11 @@ int mcl4moe_grouped_linear(const uint16_t* x, int64_t M, int K, const int32_t* o
  * are the dispatch and combine steps around the grouped GEMMs when the experts
  * of SparseMoE (src/mcl4_coe/backbone.py:887-910) are sharded across GPUs.
  * The exchange between ranks (all-to-all of rows, then of partial sums) is
- * the caller's, e.g. NCCL through torch.distributed.
+ * the caller's.  The shipped Python layer (ExpertParallelMoE) copies the
+ * pieces with the copy engines straight into peer buffers mapped through CUDA
+ * IPC (mcl4moe_ipc_import + mcl4moe_copy_list_async below), ordered by a
+ * one-element NCCL all-reduce; over a non-NCCL process group (gloo) it uses
+ * torch.distributed's all_to_all_single.
  *
  * Dispatch row (mcl4moe_ep_row_bytes(d, k) bytes): NVFP4 codes [d/2], 1x16
  * E4M3 scales row-major [d/16], k int8 expert ids local to the destination

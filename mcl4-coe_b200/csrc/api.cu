@@ -61,7 +61,7 @@ int check_moe_shape(int T, int d, int E, int k, int F) {
   if (T < 0 || d <= 0 || E <= 0 || k <= 0 || F <= 0 || k > E) return MCL4MOE_ERR_INVALID;
   if (E > kMaxExperts || k > kMaxTopK) return MCL4MOE_ERR_UNSUPPORTED;
   if (d % 256 != 0 || F % 256 != 0) return MCL4MOE_ERR_UNSUPPORTED;
-  if (int64_t(T) * k > (int64_t(1) << 30)) return MCL4MOE_ERR_UNSUPPORTED;
+  if (int64_t(T) * k > kMaxRoutedSlots) return MCL4MOE_ERR_UNSUPPORTED;
   return MCL4MOE_OK;
 }
 
@@ -241,6 +241,7 @@ int mcl4moe_quantize_activations(const uint16_t* x, int64_t rows, int cols, int6
 }
 
 size_t mcl4moe_route_workspace_size(int T, int E, int k, int d) {
+  if (T < 0 || E <= 0 || k <= 0 || int64_t(T) * k > kMaxRoutedSlots) return 0;
   return route_workspace(nullptr, T, E, k, d > 0 ? d : 0).bytes;
 }
 
@@ -250,6 +251,7 @@ int mcl4moe_route(const uint16_t* x, const float* wr, const float* logit_bias, c
                   size_t workspace_bytes, mcl4moe_stream_t stream) {
   if (T < 0 || E <= 0 || k <= 0 || k > E || !topk_idx || !topk_w || !workspace) return MCL4MOE_ERR_INVALID;
   if (E > kMaxExperts || k > kMaxTopK) return MCL4MOE_ERR_UNSUPPORTED;
+  if (int64_t(T) * k > kMaxRoutedSlots) return MCL4MOE_ERR_UNSUPPORTED;  // int32 counts, offsets and ranks
   if (!logits_in) {
     if (!x || !wr || d <= 0) return MCL4MOE_ERR_INVALID;
     if (d % 64 != 0 || !aligned16(x) || !aligned16(wr)) return MCL4MOE_ERR_UNSUPPORTED;

@@ -12,6 +12,8 @@ constexpr int kMaxWeightBatch = 256;  // weight matrices per quantiser launch
 constexpr int kMaxExperts = 256;
 constexpr int kMaxTopK = 32;
 constexpr int kRouteTokens = 128;     // tokens per router CTA (= permutation chunk)
+// Routed slots per call (T * k): per-expert counts, offsets and slot ranks are int32.
+constexpr int64_t kMaxRoutedSlots = int64_t(1) << 30;
 
 // ---- workspace layout of the routing stage (all offsets 256-byte aligned)
 struct RouteWorkspace {
@@ -32,6 +34,8 @@ struct RouteWorkspace {
 // Batches up to this many tokens compute their fp32 router logits on the CUDA cores
 // (a few tokens leave the tensor-core router with one CTA walking d serially).
 constexpr int kRouteGemvMaxT = 1024;
+// ... and rows of at most kRouteGemvMaxSmem / 16 elements (8 staged bf16 rows per CTA).
+constexpr size_t kRouteGemvMaxSmem = 200 * 1024;
 
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 

@@ -722,13 +722,15 @@ int launch_route(const uint16_t* x, const float* wr, const float* bias, const fl
     a.logits_out = logits_out;
     a.sel_mask = sel_mask;
     a.err = err;
-    if (logits_in == nullptr && T <= kRouteGemvMaxT && ws.small_logits != nullptr) {
-      const size_t smem = sizeof(uint16_t) * 8 * size_t(d);
+    // The GEMV stages 8 bf16 token rows in shared memory (16 d bytes); wider rows take
+    // the tensor-core router, which streams d in 64-column boxes at any width.
+    const size_t gemv_smem = sizeof(uint16_t) * 8 * size_t(d);
+    if (logits_in == nullptr && T <= kRouteGemvMaxT && ws.small_logits != nullptr && gemv_smem <= kRouteGemvMaxSmem) {
+      const size_t smem = gemv_smem;
       if (smem > 48 * 1024) {
         static std::atomic<uint64_t> configured{0};
-        if (!raise_smem_limit(router_gemv_kernel, 200 * 1024, configured)) return MCL4MOE_ERR_CUDA;
+        if (!raise_smem_limit(router_gemv_kernel, int(kRouteGemvMaxSmem), configured)) return MCL4MOE_ERR_CUDA;
       }
-      if (smem > 200 * 1024) return MCL4MOE_ERR_UNSUPPORTED;
       if (launch_pdl(router_gemv_kernel, dim3((T + 7) / 8, (E + 7) / 8), dim3(256), smem, stream, x, wr, bias, T, d,
                      E, ws.small_logits) != cudaSuccess)
         return MCL4MOE_ERR_CUDA;

@@ -249,13 +249,18 @@ class SparseMoE(nn.Module):
         return r["out"], r["aux_loss"], r["router_z_loss"], r["counts"]
 
     @torch.no_grad()
-    def forward_details(self, x: Tensor, valid: Tensor | None = None) -> dict[str, Tensor]:
+    def forward_details(self, x: Tensor, valid: Tensor | None = None, *,
+                        quant_bytes: bool = False) -> dict[str, Tensor]:
         """Forward plus the routing internals: ``topk_idx``/``topk_w`` [T, k]
         (-1 / 0 for masked tokens), ``offs`` [E] (inclusive ends), ``perm``
         [n_routed*k] (flat slot ids t*k+j in stable expert-major order) and,
         when ``debug_capture_h`` is set, ``h`` (bf16 SwiGLU output in padded
-        expert-major rows) and ``pad_start`` [E+1]."""
-        return self._forward_impl(x, valid, None, None, None, details=True)
+        expert-major rows) and ``pad_start`` [E+1].  With ``quant_bytes`` also
+        the first GEMM's NVFP4 operand as the permute kernel wrote it:
+        ``xq`` [M, d/2] codes and ``xs`` [M, d/16] E4M3 scales (row-major) of
+        the M padded expert-major rows, ``slot_pos`` [T, k] (padded row of each
+        slot, -1 for masked tokens) and ``pad_start``."""
+        return self._forward_impl(x, valid, None, None, None, details="quant" if quant_bytes else True)
 
     def _forward_impl(self, x, valid, prior_expert_mask, dense_expert_indices, dense_subset_k, details, static=None):
         flat = x.reshape(-1, x.shape[-1])
@@ -339,18 +344,23 @@ class SparseMoE(nn.Module):
             n_routed = int(stats[2].item())
             res.update(extra)
             res["perm"] = extra["perm"][: n_routed * k]
-            if h_dbg is not None:
-                lib = _lib.load()
-                mcap = lib.mcl4moe_padded_rows(T, E, k)
+            lib = _lib.load()
+            mcap = lib.mcl4moe_padded_rows(T, E, k)
 
-                def region(idx: int, nbytes: int) -> Tensor:
-                    off = lib.mcl4moe_workspace_region(ws.data_ptr(), idx, T, d, E, k, F) - ws.data_ptr()
-                    return ws[off:off + nbytes]
+            def region(idx: int, nbytes: int) -> Tensor:
+                off = lib.mcl4moe_workspace_region(ws.data_ptr(), idx, T, d, E, k, F) - ws.data_ptr()
+                return ws[off:off + nbytes]
 
-                res["h"] = h_dbg
+            if h_dbg is not None or details == "quant":
                 res["pad_start"] = region(5, 4 * (E + 1)).view(torch.int32).clone()
+            if h_dbg is not None:
+                res["h"] = h_dbg
                 res["hq"] = region(2, mcap * F // 2).view(mcap, F // 2).clone()
                 res["hs"] = region(3, mcap * F // 16).clone()
+            if details == "quant" and T > 0:
+                res["xq"] = region(0, mcap * d // 2).view(mcap, d // 2).clone()
+                res["xs"] = region(1, mcap * d // 16).view(mcap, d // 16).clone()
+                res["slot_pos"] = region(6, 4 * T * k).view(torch.int32).view(T, k).clone()
         return res
 
     # ------------------------------------------------------------------ routing variants

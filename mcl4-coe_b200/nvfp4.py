@@ -5,8 +5,11 @@ Mirrors the reference's operator seam (src/mcl4_coe/nvfp4.py):
 * :func:`get_or_build_grouped_cache` — the quantised-weight cache of
   ``_get_or_build_grouped_nvfp4_cache`` (:962-1048): keyed by
   ``(E, N, K, device)``, only experts whose ``(weight._version,
-  weight.data_ptr())`` changed are re-quantised, so expert growth / pruning
-  (a new ModuleList, or a changed expert count) rebuilds it naturally.
+  weight.data_ptr())`` changed are re-quantised.  When expert growth or
+  pruning (a new ModuleList, or a changed expert count) makes a new cache, the
+  experts it keeps bring their NVFP4 bytes along by a device-to-device copy, so
+  only new or changed experts are quantised (the reference re-quantises every
+  expert of a rebuilt cache); ``CACHE_STATS`` counts both.
 * :func:`nvfp4_grouped_linear` — same signature and result as the reference's
   ``nvfp4_grouped_linear(inputs, experts, proj_name, offs)`` (:1219-1227).
 * :func:`quantize_activations` — the MoE path's activation quantisation
@@ -39,6 +42,11 @@ from torch import Tensor, nn
 from . import _lib
 
 CACHE_ATTR = "_mcl4_b200_nvfp4_cache"
+# Each projection module remembers the cache entry and slot that hold its NVFP4 bytes,
+# so a cache built for a new expert set copies them instead of re-quantising.
+SLOT_ATTR = "_mcl4_b200_nvfp4_slot"
+# Expert matrices quantised and carried over (copied from a previous cache) so far.
+CACHE_STATS = {"quantized": 0, "carried": 0}
 
 
 def _stream_handle() -> int:
@@ -165,6 +173,7 @@ def get_or_build_grouped_cache(experts: nn.ModuleList, proj_name: str) -> Groupe
     if entry is None or entry.shape_key != (e_count, n, k, str(device)):
         entry = GroupedNVFP4Cache(e_count, n, k, device)
         store[proj_name] = entry
+        _carry_over(layers, cur, entry)
     if entry.versions == cur:
         return entry
     dirty = [i for i, (old, new) in enumerate(zip(entry.versions, cur)) if old != new]
@@ -178,8 +187,41 @@ def get_or_build_grouped_cache(experts: nn.ModuleList, proj_name: str) -> Groupe
             entry.masks[i] = mask.bool()
             staged.append(masked)
     quantize_weight_slots(staged, dirty, entry)
+    CACHE_STATS["quantized"] += len(dirty)
     entry.versions = cur
+    for i in dirty:
+        setattr(layers[i], SLOT_ATTR, (entry, i))
     return entry
+
+
+def _carry_over(layers: list, cur: list, entry: GroupedNVFP4Cache) -> None:
+    """Copy into the new ``entry`` the NVFP4 bytes of every expert whose weight is
+    unchanged since a previous cache quantised it (expert growth / pruning keeps the
+    surviving experts' modules): same version, storage, shape and sparsity mode."""
+    src_slots: dict[int, list[tuple[int, int]]] = {}
+    owners: dict[int, GroupedNVFP4Cache] = {}
+    for i, layer in enumerate(layers):
+        prev = getattr(layer, SLOT_ATTR, None)
+        if prev is None:
+            continue
+        old, j = prev
+        if (old is entry or old.n != entry.n or old.k != entry.k or old.packed.device != entry.packed.device
+                or j >= len(old.versions) or old.versions[j] != cur[i]):
+            continue
+        owners[id(old)] = old
+        src_slots.setdefault(id(old), []).append((j, i))
+    for key, pairs in src_slots.items():
+        old = owners[key]
+        src = torch.tensor([j for j, _ in pairs], dtype=torch.long, device=entry.packed.device)
+        dst = torch.tensor([i for _, i in pairs], dtype=torch.long, device=entry.packed.device)
+        entry.packed.index_copy_(0, dst, old.packed.index_select(0, src))
+        entry.scales.index_copy_(0, dst, old.scales.index_select(0, src))
+        entry.g.index_copy_(0, dst, old.g.index_select(0, src))
+        for j, i in pairs:
+            entry.masks[i] = old.masks[j]
+            entry.versions[i] = cur[i]
+            setattr(layers[i], SLOT_ATTR, (entry, i))
+        CACHE_STATS["carried"] += len(pairs)
 
 
 def invalidate_cache(experts: nn.ModuleList) -> None:

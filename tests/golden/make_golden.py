@@ -2,7 +2,7 @@
 
 Run from the repository root, in a container that has the reference checkout:
 
-    python tests/golden/make_golden.py [--reference-src PATH]
+    python tests/golden/make_golden.py --reference-src PATH   (or MCL4_REFERENCE_SRC=PATH)
 
 It imports ``mcl4_coe`` from the reference's ``src/`` folder and records the
 outputs of the reference's own functions on seeded inputs:
@@ -68,8 +68,11 @@ def digest(*arrays: np.ndarray) -> str:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference-src", default=os.environ.get("MCL4_REFERENCE_SRC", "/root/reference/src"))
+    ap.add_argument("--reference-src", default=os.environ.get("MCL4_REFERENCE_SRC"),
+                    help="the reference checkout's src/ folder (or set MCL4_REFERENCE_SRC)")
     args = ap.parse_args()
+    if not args.reference_src:
+        ap.error("pass --reference-src PATH (the reference's src/ folder) or set MCL4_REFERENCE_SRC")
     sys.path.insert(0, args.reference_src)
     import torch
     from torch import nn

@@ -81,3 +81,24 @@ def near_tie_tokens(logits: np.ndarray, k: int, eps: float = 1e-5) -> np.ndarray
         return np.zeros(logits.shape[0], bool)
     s = -np.sort(-logits, axis=1)
     return (s[:, k - 1] - s[:, k]) <= eps
+
+
+def order_tie_tokens(logits: np.ndarray, k: int, eps: float = 1e-5) -> np.ndarray:
+    """Tokens whose top-k ORDER (not only membership) can flip under logit
+    rounding: two adjacent values among the k+1 largest lie within ``eps``."""
+    s = -np.sort(-logits, axis=1)
+    m = min(k + 1, logits.shape[1])
+    if m < 2:
+        return np.zeros(logits.shape[0], bool)
+    gaps = s[:, : m - 1] - s[:, 1:m]
+    return np.any(gaps <= eps, axis=1)
+
+
+def compare_routing_in_order(got_idx: np.ndarray, ref_idx: np.ndarray, logits: np.ndarray, k: int,
+                             eps: float = 1e-5) -> dict:
+    """Slot-by-slot comparison of two top-k selections [T, k] (same slot order
+    required) with the tokens excused as order ties counted separately."""
+    same = np.all(got_idx == ref_idx, axis=1)
+    ties = order_tie_tokens(logits, k, eps)
+    return dict(tokens=int(got_idx.shape[0]), mismatched=int((~same).sum()), order_ties=int(ties.sum()),
+                mismatched_outside_ties=int((~same & ~ties).sum()), mismatched_in_ties=int((~same & ties).sum()))

@@ -4,8 +4,9 @@ import numpy as np
 import pytest
 import torch
 
-from gpu_ref import near_tie_tokens, x_tensor
-from inputs import routing_cases
+from gpu_ref import order_tie_tokens, x_tensor
+from inputs import routing_cases, to_bf16_bits
+from oracle import moe_ref, nvfp4_ref as nr
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -72,8 +73,8 @@ def test_router_product_and_selection_vs_reference(moe_pkg, golden, case):
     r = _route(moe_pkg, c)
     ref_logits = g[f"{name}__logits"]
     np.testing.assert_allclose(r["logits"][act], ref_logits, rtol=1e-5, atol=2e-6)
-    tie = near_tie_tokens(ref_logits, c["k"])
-    same = np.all(np.sort(r["topk_idx"][act], 1) == np.sort(g[f"{name}__topk_indices"], 1), axis=1)
+    tie = order_tie_tokens(ref_logits, c["k"])
+    same = np.all(r["topk_idx"][act] == g[f"{name}__topk_indices"], axis=1)  # slot order included
     assert np.all(same | tie), f"{int((~same & ~tie).sum())} non-tie tokens routed differently"
     np.testing.assert_allclose(r["stats"][0], g[f"{name}__aux"], rtol=1e-4)
     np.testing.assert_allclose(r["stats"][1], g[f"{name}__z"], rtol=1e-4)
@@ -90,7 +91,23 @@ def test_tensor_core_router_on_tiled_batch(moe_pkg, golden, name):
     r = _route(moe_pkg, big)
     ref_logits = np.tile(g[f"{name}__logits"], (reps, 1))
     np.testing.assert_allclose(r["logits"], ref_logits, rtol=1e-5, atol=2e-6)
-    tie = near_tie_tokens(ref_logits, c["k"])
+    tie = order_tie_tokens(ref_logits, c["k"])
     ref_idx = np.tile(g[f"{name}__topk_indices"], (reps, 1))
-    same = np.all(np.sort(r["topk_idx"], 1) == np.sort(ref_idx, 1), axis=1)
+    same = np.all(r["topk_idx"] == ref_idx, axis=1)  # slot order included
     assert np.all(same | tie)
+
+
+def test_small_batch_wide_rows_take_tensor_core_router(moe_pkg):
+    """T <= 1024 with d above the CUDA-core GEMV's shared-memory limit (16 d bytes
+    <= 200 KiB): the call must still route, through the tensor-core router."""
+    T, d, E, k = 8, 12864, 16, 4
+    rng = np.random.default_rng(77)
+    xb = rng.standard_normal((T, d), dtype=np.float32)
+    wr = (rng.standard_normal((E, d), dtype=np.float32) * 0.02).astype(np.float32)
+    case = dict(t=T, d=d, e=E, k=k, norm_topk_prob=True, x_bf16_bits=to_bf16_bits(xb), wr=wr, valid=None,
+                logit_bias=None)
+    r = _route(moe_pkg, case)
+    ref = moe_ref.route(nr.bf16_bits_to_f32(case["x_bf16_bits"]).reshape(T, d), wr, k)
+    np.testing.assert_allclose(r["logits"], ref.logits, rtol=1e-5, atol=5e-6)
+    tie = order_tie_tokens(ref.logits, k)
+    assert np.all(np.all(r["topk_idx"] == ref.selected, axis=1) | tie)

@@ -8,7 +8,8 @@ import numpy as np
 import pytest
 import torch
 
-from gpu_ref import build_module, dequant_reference_layout, near_tie_tokens, rel_l2, token_reference, x_tensor
+from gpu_ref import (build_module, dequant_reference_layout, near_tie_tokens, order_tie_tokens, rel_l2,
+                     token_reference, x_tensor)
 from inputs import layer_case, moe_case
 from oracle import moe_ref, nvfp4_ref as nr
 
@@ -58,8 +59,8 @@ def test_layer_matches_oracle(moe_pkg, name):
     r = moe_ref.route(_x_np(c), c["wr"], c["k"], c["norm_topk_prob"], c["valid"], c["logit_bias"])
     act = r.active
     got_idx = det["topk_idx"].cpu().numpy()
-    tie = near_tie_tokens(r.logits, c["k"])
-    same = np.all(np.sort(got_idx[act], 1) == np.sort(r.selected, 1), axis=1)
+    tie = order_tie_tokens(r.logits, c["k"])
+    same = np.all(got_idx[act] == r.selected, axis=1)  # slot order included
     assert np.all(same | tie)
     # use the kernel's routing for the oracle layer so a near-tie flip cannot mask a GEMM error
     r.selected = got_idx[act].astype(np.int64)
@@ -139,14 +140,75 @@ def test_expert_growth_between_calls(moe_pkg):
         moe.router = router
         moe.num_experts = 40
         moe.router_logit_bias = torch.from_numpy(c["logit_bias"]).to(DEV)
+        before = dict(moe_pkg.nvfp4.CACHE_STATS)
         det = moe.forward_details(x)
     torch.cuda.synchronize()
     assert det["counts"].shape == (40,)
+    # only the 8 new experts are quantised (up and down); the 32 kept ones bring their bytes
+    assert moe_pkg.nvfp4.CACHE_STATS["quantized"] - before["quantized"] == 2 * 8
+    assert moe_pkg.nvfp4.CACHE_STATS["carried"] - before["carried"] == 2 * 32
     for cc, got in ((c32, out32), (c, det["out"].float().cpu().numpy())):
         experts = moe_ref.QuantizedExperts(cc["w_up"], cc["w_dn"])
         ref, _, _, counts, _ = moe_ref.moe_forward(_x_np(cc), cc["wr"], experts, cc["k"], True, None,
                                                    cc["logit_bias"])
         assert rel_l2(got, ref) < REL_L2 and np.abs(got - ref).max() < MAX_ABS
+
+
+def test_expert_prune_between_calls(moe_pkg):
+    """ExpertLifecycle's prune_experts (src/mcl4_coe/ornith_rl.py:536-593; the reference's
+    tests/test_mcl4_coe.py:353-365 grows 4 -> 5 and prunes back): E 40 -> 39 by removing
+    expert 17 from the middle (router rows and experts of the others kept in order), then
+    40 again by appending a copy of expert 3 (grow_experts' mitosis: same weights, router row
+    duplicated).  Outputs and statistics follow the oracle at every step, and the surviving
+    experts' NVFP4 bytes are carried over instead of re-quantised."""
+    c = moe_case(31, 512, 1024, 40, 8, 512)
+    moe = build_module(moe_pkg, c, DEV)
+    x = x_tensor(c, DEV)
+
+    def check(case, det):
+        experts = moe_ref.QuantizedExperts(case["w_up"], case["w_dn"])
+        ref, aux, z, counts, r = moe_ref.moe_forward(_x_np(case), case["wr"], experts, case["k"], True, None, None)
+        got = det["out"].float().cpu().numpy()
+        assert rel_l2(got, ref) < 5e-3 and np.abs(got - ref).max() < MAX_ABS
+        tie = order_tie_tokens(r.logits, case["k"])
+        same = np.all(det["topk_idx"].cpu().numpy() == r.selected, axis=1)
+        assert np.all(same | tie)
+        np.testing.assert_allclose(float(det["aux_loss"]), aux, rtol=1e-4)
+        np.testing.assert_allclose(det["counts"].cpu().numpy(), counts, rtol=0, atol=2.0 / (case["t"] * case["k"]))
+
+    with torch.no_grad():
+        check(c, moe.forward_details(x))
+        keep = [i for i in range(40) if i != 17]
+        moe.experts = torch.nn.ModuleList([moe.experts[i] for i in keep])
+        router = torch.nn.Linear(c["d"], 39, bias=False).to(DEV)
+        router.weight.copy_(moe.router.weight.detach()[keep])
+        moe.router = router
+        moe.num_experts = 39
+        before = dict(moe_pkg.nvfp4.CACHE_STATS)
+        det = moe.forward_details(x)
+        torch.cuda.synchronize()
+        assert det["counts"].shape == (39,)
+        assert moe_pkg.nvfp4.CACHE_STATS["quantized"] == before["quantized"]
+        assert moe_pkg.nvfp4.CACHE_STATS["carried"] - before["carried"] == 2 * 39
+        c39 = dict(c, e=39, wr=c["wr"][keep], w_up=c["w_up"][keep], w_dn=c["w_dn"][keep])
+        check(c39, det)
+        # grow back by mitosis of expert 3: a deep copy (new parameters, same values)
+        twin = moe_pkg.SwiGLUExpert(c["d"], c["f"]).to(DEV)
+        twin.load_state_dict(moe.experts[3].state_dict())
+        moe.experts = torch.nn.ModuleList(list(moe.experts) + [twin])
+        router = torch.nn.Linear(c["d"], 40, bias=False).to(DEV)
+        router.weight.copy_(torch.cat([moe.router.weight.detach(), moe.router.weight.detach()[3:4]]))
+        moe.router = router
+        moe.num_experts = 40
+        before = dict(moe_pkg.nvfp4.CACHE_STATS)
+        det = moe.forward_details(x)
+        torch.cuda.synchronize()
+        assert moe_pkg.nvfp4.CACHE_STATS["quantized"] - before["quantized"] == 2
+        assert moe_pkg.nvfp4.CACHE_STATS["carried"] - before["carried"] == 2 * 39
+        grown = [*keep, keep[3]]
+        c40 = dict(c, wr=c["wr"][grown], w_up=c["w_up"][grown], w_dn=c["w_dn"][grown])
+        check(c40, det)
+    assert moe.read_device_error() == 0
 
 
 def test_full_size_headline_config(moe_pkg):
@@ -181,8 +243,8 @@ def test_full_size_headline_config(moe_pkg):
     assert rel_l2(got, ref) < 5e-3 and np.abs(got - ref).max() < MAX_ABS
     # the routing of the sampled tokens agrees with the oracle's fp32 router (except near ties)
     r = moe_ref.route(_x_np(c)[sample], c["wr"], 8)
-    tie = near_tie_tokens(r.logits, 8)
-    same = np.all(np.sort(idx[sample], 1) == np.sort(r.selected, 1), axis=1)
+    tie = order_tie_tokens(r.logits, 8)
+    same = np.all(idx[sample] == r.selected, axis=1)  # slot order included
     assert np.all(same | tie)
 
 
