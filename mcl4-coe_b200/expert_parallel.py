@@ -32,7 +32,7 @@ from torch import Tensor, nn
 
 from . import _lib
 from .moe import SwiGLUExpert
-from .nvfp4 import get_or_build_grouped_cache
+from .nvfp4 import get_or_build_grouped_cache, seed_grouped_cache
 
 
 def _stream_handle() -> int:
@@ -412,6 +412,138 @@ class ExpertParallelMoE(nn.Module):
         mod.experts = nn.ModuleList(list(moe.experts)[lo:lo + mod.experts_per_rank])
         mod.router_logit_bias = getattr(moe, "router_logit_bias", None)
         return mod
+
+    @torch.no_grad()
+    def reshard(self, router: nn.Linear, old_to_new, *, parents: dict | None = None,
+                new_experts: dict | None = None) -> dict:
+        """Follow a change of the expert set between calls (ExpertLifecycle's
+        ``grow_experts`` / ``prune_experts``, src/mcl4_coe/ornith_rl.py:468-595, and the
+        trainer's in-place mitosis, src/mcl4_coe/trainer.py:1624-1712) while the experts
+        stay sharded: rank g owns ``[g*E'/G, (g+1)*E'/G)`` of the new count E'.
+
+        Every rank calls it with the same arguments (it is a collective):
+        ``router``: the new replicated router (E' rows);
+        ``old_to_new[i]``: the new index of old expert i, or None if it was pruned (the
+        ``ExpertMorphResult.old_to_new`` of the reference);
+        ``parents[j] = p``: new expert j is a copy of old expert p (mitosis);
+        ``new_experts[j]``: a module (``up_proj`` / ``down_proj``) for a new expert that
+        is neither kept nor copied, given on every rank.
+        Experts whose owner changes travel to their new rank with their weights and, on
+        CUDA, their NVFP4 bytes (one all-to-all); a copy takes its parent's bytes; only
+        the ``new_experts`` are quantised (by the next forward).  Experts that keep their
+        rank keep their modules, and their bytes are carried into the new cache.
+        Returns counts of the experts moved, copied and new, and the bytes sent.
+        Dense (non-2:4) experts only."""
+        G, me = self.world, self.rank
+        E_old, loc_old = self.num_experts, self.experts_per_rank
+        E_new = int(router.weight.shape[0])
+        parents, fresh = dict(parents or {}), dict(new_experts or {})
+        if len(old_to_new) != E_old:
+            raise ValueError(f"old_to_new must have one entry per current expert ({E_old})")
+        if E_new % G != 0 or E_new < self.top_k:
+            raise ValueError(f"the new expert count {E_new} must be a multiple of the group size {G} and >= top_k")
+        src: list = [None] * E_new  # old index of the expert (or its parent) that new slot j holds; -1: new
+        for i, j in enumerate(old_to_new):
+            if j is None:
+                continue
+            if not 0 <= int(j) < E_new or src[int(j)] is not None:
+                raise ValueError(f"old_to_new[{i}] = {j} is out of range or taken twice")
+            src[int(j)] = i
+        for j, par in parents.items():
+            if not 0 <= j < E_new or src[j] is not None or not 0 <= par < E_old:
+                raise ValueError(f"parents[{j}] = {par} is out of range or collides")
+            src[j] = int(par)
+        for j in fresh:
+            if not 0 <= j < E_new or src[j] is not None:
+                raise ValueError(f"new_experts[{j}] is out of range or collides")
+            src[j] = -1
+        if any(v is None for v in src):
+            raise ValueError("every new expert index needs a kept expert, a parent or a new module")
+        for ex in self.experts:
+            for proj in (ex.up_proj, ex.down_proj):
+                if str(getattr(proj, "sparsity_mode", "none")) != "none":
+                    raise NotImplementedError("resharding 2:4-sparse experts")
+        loc_new = E_new // G
+        owner_old = lambda i: i // loc_old  # noqa: E731
+        owner_new = lambda j: j // loc_new  # noqa: E731
+        ex0 = self.experts[0]
+        dev, wdtype = ex0.up_proj.weight.device, ex0.up_proj.weight.dtype
+        d, F = ex0.down_proj.weight.shape
+        move_bytes = hasattr(self.ops, "prepare")  # the CUDA steps keep NVFP4 caches; bring them along
+        caches = self.ops.prepare(self.experts) if move_bytes else None  # refreshed: bytes of current weights
+
+        def payload(li: int) -> list[Tensor]:
+            ex = self.experts[li]
+            parts = [ex.up_proj.weight.detach(), ex.down_proj.weight.detach()]
+            if move_bytes:
+                for c in caches:
+                    parts += [c.packed[li], c.scales[li], c.g[li:li + 1]]
+            return [t.contiguous().view(torch.uint8).reshape(-1) for t in parts]
+
+        sizes = [t.numel() for t in payload(0)]  # the same on every rank (same shapes)
+        per = sum(sizes)
+        moving = [j for j in range(E_new) if src[j] >= 0 and owner_old(src[j]) != owner_new(j)]
+        send_js = [[j for j in moving if owner_old(src[j]) == me and owner_new(j) == r] for r in range(G)]
+        recv_js = [[j for j in moving if owner_new(j) == me and owner_old(src[j]) == s_] for s_ in range(G)]
+        received: dict[int, list[Tensor]] = {}
+        sent = sum(len(js) for js in send_js) * per
+        if moving:  # the same decision on every rank: all of them enter the all-to-all
+            pieces = [torch.cat(payload(src[j] - me * loc_old)) for r in range(G) for j in send_js[r]]
+            send = torch.cat(pieces) if pieces else torch.empty((0,), dtype=torch.uint8, device=dev)
+            recv = torch.empty((sum(len(js) for js in recv_js) * per,), dtype=torch.uint8, device=dev)
+            dist.all_to_all_single(recv, send, [len(js) * per for js in recv_js], [len(js) * per for js in send_js],
+                                   group=self.group)
+            off = 0
+            for s_ in range(G):
+                for j in recv_js[s_]:
+                    chunk, parts = recv[off:off + per], []
+                    o = 0
+                    for n in sizes:
+                        parts.append(chunk[o:o + n])
+                        o += n
+                    received[j] = parts
+                    off += per
+
+        def module_from(up_bytes: Tensor, dn_bytes: Tensor) -> nn.Module:
+            ex = SwiGLUExpert(d, F).to(device=dev, dtype=wdtype)
+            ex.up_proj.weight.copy_(up_bytes.view(wdtype).view(2 * F, d))
+            ex.down_proj.weight.copy_(dn_bytes.view(wdtype).view(d, F))
+            return ex
+
+        new_list, filled_up, filled_dn = [], {}, {}
+        stats = dict(moved_in=0, copied=0, kept=0, new=0, bytes_sent=sent)
+        for li in range(loc_new):
+            j = me * loc_new + li
+            i = src[j]
+            if i < 0:
+                new_list.append(fresh[j].to(dev))
+                stats["new"] += 1
+                continue
+            if owner_old(i) == me:
+                lo = i - me * loc_old
+                if old_to_new[i] is not None and int(old_to_new[i]) == j:
+                    new_list.append(self.experts[lo])  # same module: its bytes are carried over
+                    stats["kept"] += 1
+                    continue
+                parts = payload(lo)  # a copy of a local parent
+                stats["copied"] += 1
+            else:
+                parts = received[j]
+                stats["moved_in"] += 1
+            new_list.append(module_from(parts[0], parts[1]))
+            if move_bytes:  # (packed, scales, g) as bytes; g back to its fp32 value
+                filled_up[li] = (parts[2], parts[3], parts[4].view(torch.float32))
+                filled_dn[li] = (parts[5], parts[6], parts[7].view(torch.float32))
+        experts = nn.ModuleList(new_list)
+        if move_bytes:
+            seed_grouped_cache(experts, "up_proj", filled_up)
+            seed_grouped_cache(experts, "down_proj", filled_dn)
+        self.router = router
+        self.experts = experts
+        self.num_experts = E_new
+        self.experts_per_rank = loc_new
+        self.expert_offset = me * loc_new
+        return stats
 
     def _all_to_all(self, out: Tensor, inp: Tensor, out_splits: list[int], in_splits: list[int]) -> None:
         dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)

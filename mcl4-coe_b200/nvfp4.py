@@ -161,7 +161,7 @@ def get_or_build_grouped_cache(experts: nn.ModuleList, proj_name: str) -> Groupe
     device = weights[0].device
     _require_cuda(weights[0], "the NVFP4 weight cache")
     modes = [_sparsity_mode(layer) for layer in layers]
-    cur = [(w._version, w.data_ptr(), tuple(w.shape), m) for w, m in zip(weights, modes)]
+    cur = _current_versions(layers)
     store = getattr(experts, CACHE_ATTR, None)
     if store is None:
         store = {}
@@ -222,6 +222,41 @@ def _carry_over(layers: list, cur: list, entry: GroupedNVFP4Cache) -> None:
             entry.versions[i] = cur[i]
             setattr(layers[i], SLOT_ATTR, (entry, i))
         CACHE_STATS["carried"] += len(pairs)
+
+
+def _current_versions(layers: list) -> list:
+    return [(layer.weight._version, layer.weight.data_ptr(), tuple(layer.weight.shape), _sparsity_mode(layer))
+            for layer in layers]
+
+
+@torch.no_grad()
+def seed_grouped_cache(experts: nn.ModuleList, proj_name: str, filled: dict) -> GroupedNVFP4Cache:
+    """Make the cache of ``experts`` (carrying over the bytes of experts a previous
+    cache holds) and install NVFP4 bytes quantised elsewhere: ``filled[i] = (packed
+    [N, K/2], scales [N_pad*K/16], g [1])`` for slot i, taken as the quantisation of
+    expert i's current weight (expert parallelism moves experts with their bytes)."""
+    layers = [getattr(e, proj_name) for e in experts]
+    n, k = layers[0].weight.shape
+    device = layers[0].weight.device
+    cur = _current_versions(layers)
+    store = getattr(experts, CACHE_ATTR, None)
+    if store is None:
+        store = {}
+        setattr(experts, CACHE_ATTR, store)
+    entry = store.get(proj_name)
+    if entry is None or entry.shape_key != (len(layers), n, k, str(device)):
+        entry = GroupedNVFP4Cache(len(layers), n, k, device)
+        store[proj_name] = entry
+        _carry_over(layers, cur, entry)
+    for i, (packed, scales, g) in filled.items():
+        entry.packed[i].copy_(packed.view(entry.packed[i].shape))
+        entry.scales[i].copy_(scales.view(entry.scales[i].shape))
+        entry.g[i:i + 1].copy_(g.view(1))
+        entry.masks[i] = None
+        entry.versions[i] = cur[i]
+        setattr(layers[i], SLOT_ATTR, (entry, i))
+    CACHE_STATS["carried"] += len(filled)
+    return entry
 
 
 def invalidate_cache(experts: nn.ModuleList) -> None:

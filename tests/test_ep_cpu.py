@@ -103,3 +103,67 @@ CASES = [
 @pytest.mark.parametrize("case", CASES, ids=lambda c: c["name"])
 def test_expert_parallel_matches_single_device_oracle(case):
     mp.spawn(_worker, args=(2, _free_port(), case), nprocs=2, join=True)
+
+
+def _reshard_worker(rank, world, port):
+    """Grow 4 -> 6 experts (one mitosis copy of expert 1, one new expert) and prune back to
+    4 (experts 1 and 4 removed) under expert parallelism; after each step every rank's
+    output must equal the single-device oracle layer over the full expert set."""
+    sys.path[:0] = [str(ROOT), str(HERE)]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from __graft_entry__ import load_package
+        from ep_oracle_ops import OracleEPOps
+        from oracle import moe_ref
+
+        pkg = load_package()
+        d, E, k, F, T = 256, 4, 2, 256, 32
+        dense = _dense_layer(pkg, d, E, k, F, 9, True)
+        ep = pkg.ExpertParallelMoE.from_dense(dense, ops=OracleEPOps())
+        r = np.random.default_rng(300 + rank)
+        x = torch.from_numpy(r.standard_normal((T, d)).astype(np.float32)).to(torch.bfloat16)
+
+        def check(router_w, w_up, w_dn):
+            out, aux, z, counts = ep(x)
+            ref, raux, rz, rcounts, _ = moe_ref.moe_forward(x.float().numpy(), router_w, moe_ref.QuantizedExperts(
+                w_up, w_dn), k, True)
+            got = out.float().numpy()
+            err = np.linalg.norm(got - ref) / np.linalg.norm(ref)
+            assert err < 5e-3 and np.abs(got - ref).max() < 1e-1, (rank, err)
+            np.testing.assert_array_equal(counts.numpy(), rcounts)
+
+        w_up = np.stack([e.up_proj.weight.detach().numpy() for e in dense.experts])
+        w_dn = np.stack([e.down_proj.weight.detach().numpy() for e in dense.experts])
+        wr = dense.router.weight.detach().numpy()
+        check(wr, w_up, w_dn)
+        # grow: expert 4 is a copy of expert 1 (router row duplicated), expert 5 is new
+        g = np.random.default_rng(11)  # identical on both ranks
+        fresh = pkg.SwiGLUExpert(d, F).requires_grad_(False)
+        fresh.up_proj.weight.copy_(torch.from_numpy((g.standard_normal((2 * F, d)) * 0.02).astype(np.float32)))
+        fresh.down_proj.weight.copy_(torch.from_numpy((g.standard_normal((d, F)) * 0.02).astype(np.float32)))
+        wr6 = np.concatenate([wr, wr[1:2], (g.standard_normal((1, d)) * 0.02).astype(np.float32)])
+        router6 = torch.nn.Linear(d, 6, bias=False).requires_grad_(False)
+        router6.weight.copy_(torch.from_numpy(wr6))
+        stats = ep.reshard(router6, [0, 1, 2, 3], parents={4: 1}, new_experts={5: fresh})
+        # 2 ranks: old blocks {0,1} {2,3} -> new {0,1,2} {3,4,5}: expert 2 moves 1 -> 0, the copy of 1 moves 0 -> 1
+        assert ep.num_experts == 6 and ep.experts_per_rank == 3 and len(ep.experts) == 3
+        assert stats["moved_in"] == 1 and stats["new"] == (1 if rank == 1 else 0)
+        w_up6 = np.concatenate([w_up, w_up[1:2], fresh.up_proj.weight.detach().numpy()[None]])
+        w_dn6 = np.concatenate([w_dn, w_dn[1:2], fresh.down_proj.weight.detach().numpy()[None]])
+        check(wr6, w_up6, w_dn6)
+        # prune experts 1 and 4: the others keep their order
+        keep = [0, 2, 3, 5]
+        router4 = torch.nn.Linear(d, 4, bias=False).requires_grad_(False)
+        router4.weight.copy_(torch.from_numpy(wr6[keep]))
+        ep.reshard(router4, [0, None, 1, 2, None, 3])
+        assert ep.num_experts == 4 and len(ep.experts) == 2
+        check(wr6[keep], w_up6[keep], w_dn6[keep])
+        with pytest.raises(ValueError):
+            ep.reshard(router4, [0, 1, 2])  # wrong length: rejected before any exchange
+    finally:
+        dist.destroy_process_group()
+
+
+def test_expert_parallel_reshard_grow_and_prune():
+    mp.spawn(_reshard_worker, args=(2, _free_port()), nprocs=2, join=True)

@@ -2,7 +2,8 @@
 
 Each rank shards the same layer (experts split in two), runs its own tokens
 through ``ExpertParallelMoE`` and compares with the full single-device layer on
-the same tokens.
+the same tokens; then the expert set grows 16 -> 20 (``reshard``) and the
+comparison repeats against the grown single-device layer.
 """
 
 import datetime
@@ -60,6 +61,36 @@ def _worker(rank, world, port):
                 assert torch.equal(counts, rcounts) and float(aux) == float(raux) and float(z) == float(rz)
             if ep._peer is not None:
                 ep._peer.close()
+        # growth 16 -> 20 under expert parallelism (8 -> 10 experts per rank): experts 8 and 9
+        # move from rank 1 to rank 0 with their NVFP4 bytes, 16 is a copy of expert 3 (sent by
+        # rank 0), 17 a copy of expert 12 (local to rank 1), 18 and 19 are new (quantised)
+        ep = pkg.ExpertParallelMoE.from_dense(dense)
+        x = torch.from_numpy(r.standard_normal((1024, 1024)).astype(np.float32)).to(dev, torch.bfloat16)
+        with torch.no_grad():
+            ep(x)
+        g = np.random.default_rng(77)
+        new_up = (g.standard_normal((2, 1024, 1024)) * 0.02).astype(np.float32)
+        new_dn = (g.standard_normal((2, 1024, 512)) * 0.02).astype(np.float32)
+        new_wr = (g.standard_normal((2, 1024)) * 0.02).astype(np.float32)
+        c20 = dict(c, e=20, wr=np.concatenate([c["wr"], c["wr"][[3, 12]], new_wr]),
+                   w_up=np.concatenate([c["w_up"], c["w_up"][[3, 12]], new_up]),
+                   w_dn=np.concatenate([c["w_dn"], c["w_dn"][[3, 12]], new_dn]))
+        dense20 = build_module(pkg, c20, dev)
+        fresh = {18 + i: dense20.experts[18 + i] for i in range(2)}
+        before = dict(pkg.nvfp4.CACHE_STATS)
+        stats = ep.reshard(dense20.router, list(range(16)), parents={16: 3, 17: 12}, new_experts=fresh)
+        assert stats["moved_in"] == (2 if rank == 0 else 1), stats
+        with torch.no_grad():
+            out, aux, z, counts = ep(x)
+            # only the new experts were quantised (up and down), and only where they live
+            assert pkg.nvfp4.CACHE_STATS["quantized"] - before["quantized"] == (0 if rank == 0 else 4)
+            ref, raux, rz, rcounts = dense20(x)
+        torch.cuda.synchronize()
+        a, b = out.float(), ref.float()
+        assert (torch.linalg.norm(a - b) / torch.linalg.norm(b)).item() < 5e-3
+        assert torch.equal(counts, rcounts)
+        if ep._peer is not None:
+            ep._peer.close()
         dist.barrier()
     finally:
         dist.destroy_process_group()
