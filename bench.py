@@ -595,7 +595,8 @@ def run_ours(args) -> None:
         "clocks": clocks,
     }
     if rank == 0 and world == 1 and not args.no_reference_gpu:
-        with torch.inference_mode():
+        # not under inference_mode: the reference keys its weight cache on ``Tensor._version``
+        with torch.no_grad():
             result["reference_gpu"] = reference_gpu_leg(moe, x, cfg, max(3, min(K, 10)))
         rg = result["reference_gpu"]
         best = [v["value"] for key, v in rg.items() if isinstance(v, dict) and "value" in v]

@@ -153,7 +153,8 @@ int mcl4moe_quantize_activations(const uint16_t* x, int64_t rows, int cols, int6
  * Batches of up to 1024 tokens with d <= 12800 compute the logits on the CUDA
  * cores (fp32 FMA, fixed summation order); longer batches and wider rows run
  * the router product on the tensor cores with the fp32 weight split into
- * three bf16 parts (fp32-accurate logits).  Requires E <= 256,
+ * three bf16 parts (exact products, fp32 accumulation on the tensor pipe: the
+ * logits' error grows with d, about 6.5e-5 at d = 12864).  Requires E <= 256,
  * k <= min(E, 32), d % 64 == 0, T * k <= 2^30 (counts, offsets and slot
  * ranks are int32; larger batches return MCL4MOE_ERR_UNSUPPORTED and a
  * workspace size of 0).
