@@ -327,3 +327,87 @@ def mask_tie_groups(w: np.ndarray, mode: str) -> np.ndarray:
     near = (s[:, -1] - s[:, -2]) <= 2e-6 * np.maximum(s[:, -1], 1e-30)
     return np.repeat(near[:, None], 16, axis=1).reshape(rows // 4, cols // 4, 4, 4).transpose(0, 2, 1, 3).reshape(
         rows, cols)
+
+
+# --------------------------------------------------------------------------
+# Stochastic rounding of gradients (backward of the grouped NVFP4 projection).
+# --------------------------------------------------------------------------
+
+_PHILOX_ROUND_A = np.uint64(0xD2511F53)
+_PHILOX_ROUND_B = np.uint64(0xCD9E8D57)
+_PHILOX_KEY_A = np.uint64(0x9E3779B9)
+_PHILOX_KEY_B = np.uint64(0xBB67AE85)
+_MASK32 = np.uint64(0xFFFFFFFF)
+
+
+def philox_first_word(counter: np.ndarray, seed: int) -> np.ndarray:
+    """Word 0 of Philox4x32-10 (Salmon, Moraes, Dror and Shaw, SC'11) for the counter
+    ``(counter, 0, 0, 0)`` and key ``(seed mod 2^32, seed >> 32)``: the draw of Triton's
+    ``tl.rand(seed, offset)`` for a 32-bit offset, which the reference's gradient
+    quantiser uses as its rounding noise (src/mcl4_coe/nvfp4.py:771-773)."""
+    c0 = np.asarray(counter).astype(np.uint64) & _MASK32
+    c1 = np.zeros_like(c0)
+    c2 = np.zeros_like(c0)
+    c3 = np.zeros_like(c0)
+    k0 = np.uint64(seed & 0xFFFFFFFF)
+    k1 = np.uint64((seed >> 32) & 0xFFFFFFFF)
+    for _ in range(10):
+        p0, p2 = c0, c2
+        hi_b = (_PHILOX_ROUND_B * p2) >> np.uint64(32)
+        hi_a = (_PHILOX_ROUND_A * p0) >> np.uint64(32)
+        c0 = hi_b ^ c1 ^ k0
+        c2 = hi_a ^ c3 ^ k1
+        c1 = (_PHILOX_ROUND_B * p2) & _MASK32
+        c3 = (_PHILOX_ROUND_A * p0) & _MASK32
+        k0 = (k0 + _PHILOX_KEY_A) & _MASK32
+        k1 = (k1 + _PHILOX_KEY_B) & _MASK32
+    return c0.astype(np.uint32)
+
+
+def uniform_from_word(w: np.ndarray) -> np.ndarray:
+    """Triton's ``uint_to_uniform_float`` for 32-bit words: the word as int32 x,
+    ``x < 0 ? -x - 1 : x``, times 4.6566127342e-10 in float32 (in [0, 1))."""
+    x = np.asarray(w, dtype=np.uint32).view(np.int32).astype(np.int64)
+    x = np.where(x < 0, -x - 1, x)
+    return (x.astype(np.float32) * np.float32(4.6566127342e-10)).astype(np.float32)
+
+
+def sr_global_scale(x: np.ndarray) -> np.float32:
+    """Tensor-wise global scale of a gradient (src/mcl4_coe/nvfp4.py:1129-1134):
+    ``max(amax/2688 if amax > 0 else 1, FLT_MIN)``."""
+    amax = np.float32(np.abs(np.asarray(x, np.float32)).max()) if np.size(x) else np.float32(0.0)
+    g = np.float32(amax / np.float32(2688.0)) if amax > 0 else np.float32(1.0)
+    return np.float32(max(g, FLT_MIN_NORMAL))
+
+
+def quantize_sr(x: np.ndarray, g: float, seed: int, row_index: np.ndarray | None = None):
+    """The stochastic branch of the reference's ``_nvfp4_quantize_1d_kernel``
+    (src/mcl4_coe/nvfp4.py:735-790 with ``STOCHASTIC=True``, codes :716-732):
+    per 16-element row block ``s = e4m3(min(amax / (6 g), 448))``, ``inv = 1/(s g)``
+    (0 when ``s g`` is 0), ``u = 2m | m+2 | m/2+4`` of ``m = min(|x inv|, 6)``,
+    ``code = min(trunc(u + U), 7)`` with ``U`` the Philox draw of element offset
+    ``row * K + col`` (32-bit wrap), sign 8 when ``x inv < 0``.
+
+    ``x``: float32 values of bf16 [M, K]; ``row_index``: the row number each row
+    has in the reference's matrix (default 0..M-1).  Returns ``(packed uint8 [M, K/2],
+    scales e4m3 bits [M, K/16])``."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, cols = x.shape
+    g = np.float32(g)
+    blocks = x.reshape(rows, cols // 16, 16)
+    amax = np.abs(blocks).max(axis=-1)
+    scales = f32_to_e4m3(np.minimum(amax / (np.float32(6.0) * g), np.float32(448.0)))
+    dec = (e4m3_to_f32(scales) * g).astype(np.float32)
+    with np.errstate(divide="ignore"):
+        inv = np.where(dec > 0, np.float32(1.0) / dec, np.float32(0.0)).astype(np.float32)
+    v = (blocks * inv[..., None]).reshape(rows, cols).astype(np.float32)
+    m = np.minimum(np.abs(v), np.float32(6.0))
+    u = np.where(m <= np.float32(2.0), m * np.float32(2.0),
+                 np.where(m <= np.float32(4.0), m + np.float32(2.0), m * np.float32(0.5) + np.float32(4.0)))
+    r = np.arange(rows, dtype=np.uint64) if row_index is None else np.asarray(row_index, np.uint64)
+    offsets = (r[:, None] * np.uint64(cols) + np.arange(cols, dtype=np.uint64)[None, :]) & _MASK32
+    noise = uniform_from_word(philox_first_word(offsets, int(seed)))
+    with np.errstate(invalid="ignore"):
+        code = np.minimum(np.floor((u + noise).astype(np.float32)), 7).astype(np.uint8)
+    code = code | ((v < 0).astype(np.uint8) << np.uint8(3))
+    return _pack_codes(code), scales

@@ -184,3 +184,24 @@ def sparse_layer_cases():
         ("s_row", moe_case(601, 128, 256, 8, 2, 256, valid_frac=0.8), "2to4_row"),
     ]
 
+
+
+def sr_quant_cases():
+    """(name, bf16 bits [M, K], seed) for the stochastic-rounding gradient quantiser
+    (the reference's _nvfp4_quantize_1d_kernel with STOCHASTIC=True): gradient-like
+    magnitudes, an all-zero row block, signed zeros and the E2M1 edge rows scaled down."""
+    cases = []
+    r = rng(700)
+    g = (r.standard_normal((40, 256), dtype=np.float32) * 0.01).astype(np.float32)
+    cases.append(("sr_grad_40x256", to_bf16_bits(g), 12345))
+    r = rng(701)
+    g = (r.standard_normal((64, 1024), dtype=np.float32) * 1e-4).astype(np.float32)
+    g[5] = 0.0
+    g[9, :512] = -0.0
+    g[17:21] = _edge_rows(1024) * np.float32(1e-3)
+    g[30] = np.float32(3e-2) * np.sign(g[30])
+    cases.append(("sr_mixed_64x1024", to_bf16_bits(g), 7))
+    r = rng(702)
+    g = (r.standard_normal((33, 512), dtype=np.float32) * np.float32(2.0)).astype(np.float32)
+    cases.append(("sr_ragged_33x512", to_bf16_bits(g), 2 ** 31 - 1))
+    return cases

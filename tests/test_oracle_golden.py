@@ -108,3 +108,34 @@ def test_swizzle_is_the_tcgen05_scale_atom():
         for c in range(cols):
             off = ((r // 128) * (cols // 4) + c // 4) * 512 + (r % 32) * 16 + ((r % 128) // 32) * 4 + c % 4
             assert sw[off] == s[r, c]
+
+
+def test_sr_quantiser_matches_reference_kernel(golden):
+    """The stochastic-rounding gradient quantiser (Philox noise, codes, scales) against the
+    reference's own Triton kernel run on the CPU interpreter (tests/golden/make_golden_sr.py).
+    Blocks whose scale the interpreter's numpy fp8 emulation rounds differently from the
+    hardware's round-to-nearest (``rn_scales``) are the only ones allowed to differ."""
+    from inputs import sr_quant_cases
+
+    g = golden("sr_quant")
+    total_blocks = compared = 0
+    for name, bits, seed in sr_quant_cases():
+        np.testing.assert_array_equal(g[f"{name}__x_bits"], bits)
+        x = nr.bf16_bits_to_f32(bits)
+        gs = nr.sr_global_scale(x)
+        assert gs == g[f"{name}__g"][0]
+        packed, scales = nr.quantize_sr(x, gs, int(g[f"{name}__seed"]))
+        np.testing.assert_array_equal(scales, g[f"{name}__rn_scales"])
+        same = g[f"{name}__scales"] == g[f"{name}__rn_scales"]
+        np.testing.assert_array_equal(scales[same], g[f"{name}__scales"][same])
+        keep = np.repeat(same, 8, axis=1)
+        np.testing.assert_array_equal(packed[keep], g[f"{name}__packed"][keep])
+        total_blocks += same.size
+        compared += int(same.sum())
+    assert compared > 0.98 * total_blocks  # the emulation differences are rare edge blocks
+
+
+def test_philox_matches_published_known_answer():
+    """Philox4x32-10 known-answer vector of Salmon et al. (Random123 kat_vectors):
+    counter 0, key 0 -> first word 0x6627e8d5."""
+    assert int(nr.philox_first_word(np.array([0], np.uint64), 0)[0]) == 0x6627E8D5
