@@ -124,6 +124,15 @@ int mcl4moe_quantize_weights(const float* const* w_ptrs, const int32_t* slots, i
                              uint8_t* ref_bs_fwd, uint8_t* ref_b_bwd, uint8_t* ref_bs_bwd, float* amax_scratch,
                              mcl4moe_stream_t stream);
 
+/* The same quantisation plus the transposed copy the backward's input-gradient
+ * GEMM reads (the reference's B_bwd / Bs_bwd, src/mcl4_coe/nvfp4.py:947-951,
+ * in the kernel layout): packed_t [E, K, N/2] (row k of W^T packs the (n, n+1)
+ * pairs) and scales_t [E, K*N/16], the 16x16 tile scales swizzled for the K rows
+ * of W^T.  Requires K % 128 == 0 in addition. */
+int mcl4moe_quantize_weights_t(const float* const* w_ptrs, const int32_t* slots, int n, int N, int K,
+                               uint8_t* packed, uint8_t* scales, float* global_scale, uint8_t* packed_t,
+                               uint8_t* scales_t, float* amax_scratch, mcl4moe_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Activation quantisation, 1x16 row blocks with global scale 1.
  * Replaces _quantize_nvfp4_core(x, two_dimensional=False,
@@ -228,6 +237,13 @@ typedef struct mcl4moe_moe_args {
   /* Optional cudaEvent_t[6] (NULL to skip): recorded on the stream before
    * routing and after routing, permutation, gate/up GEMM, down GEMM and combine. */
   void* const* stage_events;
+  /* Training forward (all NULL for inference): what mcl4moe_moe_backward_experts
+   * reads, in the padded expert-major rows (M_cap = mcl4moe_padded_rows(T, E, k)). */
+  uint16_t* up_save;          /* bf16 [M_cap, 2F]: gate | value, bf16(acc * g) of the gate/up GEMM, or NULL */
+  uint16_t* x_rows_save;      /* bf16 [M_cap, d]: the permuted input rows (padding rows zero), or NULL */
+  uint16_t* y_save;           /* bf16 [M_cap, d]: unweighted down-projection rows bf16(acc * g); the combine then
+                                 weights each slot as bf16(y * bf16(w)).  NULL: weighted rows stay internal */
+  float* logits_out;          /* fp32 [T, E] router logits (mcl4moe_moe_forward only), or NULL */
 } mcl4moe_moe_args;
 
 size_t mcl4moe_moe_workspace_size(int T, int d, int E, int k, int F);
@@ -246,13 +262,83 @@ int mcl4moe_moe_forward(const mcl4moe_moe_args* args, mcl4moe_stream_t stream);
  * mcl4moe_moe_forward.  Same workspace size. */
 int mcl4moe_moe_forward_routed(const mcl4moe_moe_args* args, mcl4moe_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * Backward (training).  Replaces the autograd path of SparseMoE.forward's
+ * grouped branch (src/mcl4_coe/backbone.py:853-911) through
+ * _NVFP4GroupedLinear.backward (src/mcl4_coe/nvfp4.py:1112-1216).
+ *
+ * mcl4moe_quantize_rows_sr: the reference's stochastic-rounding gradient
+ * quantiser (_nvfp4_quantize_1d_kernel with STOCHASTIC=True, :735-790, as the
+ * backward launches it at :1128-1151): tensor-wise global scale
+ * max(amax/2688 if amax > 0 else 1, FLT_MIN) written to global_scale, per 1x16
+ * block s = e4m3(min(amax16 / (6 g), 448)), codes floor(u + U) clamped to 7 with
+ * U the Philox4x32-10 draw of Triton's tl.rand(seed, row * cols + col).  x bf16
+ * [rows, cols] contiguous; packed [rows, cols/2]; scales row-major
+ * [rows, cols/16]; amax_scratch device fp32 [1].  cols % 128 == 0.
+ *
+ * mcl4moe_moe_backward_experts: from the gradient d_out of the layer output
+ * and what the training forward saved (mcl4moe_moe_args' up_save / y_save and
+ * the routing: slot_pos, topk_w and the expert layout pad_start / counts /
+ * offs_start), computes in the padded expert-major rows:
+ *   d_y    = bf16(d_out[t] * bf16(w))         (the down projection's output grad)
+ *   d_w    = bf16(sum_c bf16(d_out[t,c] * y))  (routing-weight grad, [T, k])
+ *   d_h    = SR(d_y) x W_down   (grouped NVFP4 GEMM on the transposed weights)
+ *   d_up   = [d_gate | d_val] from the SwiGLU derivative
+ *   d_rows = SR(d_up) x W_up
+ * The weight gradients (d_y^T h, d_up^T x_rows per expert) and the router's
+ * matrix products are the caller's.  seed_down / seed_up: the noise seeds of
+ * the two quantisations.
+ * mcl4moe_router_backward: d_logits [T, E] from d_w, the saved logits and
+ * routing, the forward's stats and the upstream gradients of aux_loss / z_loss
+ * (device fp32 scalars or NULL for 0).
+ * mcl4moe_moe_backward_dx: d_x[t] = bf16(sum_j d_rows[slot(t, j)] +
+ * d_x_router[t]) (fp32 d_x_router [T, d] or NULL).
+ * ------------------------------------------------------------------------ */
+typedef struct mcl4moe_moe_bwd_args {
+  int T, d, E, k, F;
+  const uint16_t* d_out;          /* bf16 [T, d] */
+  const int32_t* slot_pos;        /* int32 [T, k]: padded row of slot (t, j), -1 when not routed */
+  const float* topk_w;            /* fp32 [T, k] routing weights of the forward */
+  const int32_t* pad_start;       /* int32 [E + 1] padded row start of each expert segment */
+  const int32_t* counts;          /* int32 [E] routed rows per expert */
+  const int32_t* offs_start;      /* int32 [E] first row of each expert in the unpadded order */
+  const uint16_t* y_save;         /* bf16 [M_cap, d] unweighted down-projection rows */
+  const uint16_t* up_save;        /* bf16 [M_cap, 2F] gate | value rows */
+  const uint8_t* w_up_t;          /* up_proj^T in the kernel layout [E, d, F] bytes (2F codes per row) */
+  const uint8_t* w_up_t_scales;   /* [E, d*2F/16] swizzled */
+  const float* w_up_g;            /* [E] */
+  const uint8_t* w_dn_t;          /* down_proj^T [E, F, d/2] */
+  const uint8_t* w_dn_t_scales;   /* [E, F*d/16] swizzled */
+  const float* w_dn_g;            /* [E] */
+  uint64_t seed_down, seed_up;
+  uint16_t* d_y;                  /* out bf16 [M_cap, d] (padding rows zero) */
+  uint16_t* d_up;                 /* out bf16 [M_cap, 2F] */
+  uint16_t* d_rows;               /* out bf16 [M_cap, d] gradient of the permuted input rows */
+  float* d_w;                     /* out fp32 [T, k] */
+  int32_t* error_word;            /* as in mcl4moe_moe_args */
+  void* workspace;
+  size_t workspace_bytes;
+} mcl4moe_moe_bwd_args;
+
+int mcl4moe_quantize_rows_sr(const uint16_t* x, int64_t rows, int cols, uint64_t seed, uint8_t* packed,
+                             uint8_t* scales, float* global_scale, float* amax_scratch, mcl4moe_stream_t stream);
+size_t mcl4moe_moe_backward_workspace_size(int T, int d, int E, int k, int F);
+int mcl4moe_moe_backward_experts(const mcl4moe_moe_bwd_args* args, mcl4moe_stream_t stream);
+int mcl4moe_router_backward(const float* logits, const int32_t* topk_idx, const float* topk_w, const float* d_w,
+                            const uint8_t* valid, const float* stats, const float* d_aux, const float* d_z, int T,
+                            int E, int k, int norm_topk_prob, float* d_logits, mcl4moe_stream_t stream);
+int mcl4moe_moe_backward_dx(const uint16_t* d_rows, const int32_t* slot_pos, const float* d_x_router, int T, int k,
+                            int d, uint16_t* d_x, mcl4moe_stream_t stream);
+
 /* Capacity in rows of the padded, expert-major activation buffers
  * (sum over experts of count rounded up to 256, bounded by T*k + 255*E). */
 int64_t mcl4moe_padded_rows(int T, int E, int k);
 
-/* Device pointer of a named region inside a forward workspace (for tests and
- * debugging): 0 xq, 1 xs, 2 hq, 3 hs, 4 y, 5 pad_start, 6 slot_pos, 7 sorted_w,
- * 8 the int32 device error word used when args.error_word is NULL. */
+/* Device pointer of a named region inside a forward workspace (for tests,
+ * debugging and the backward's inputs): 0 xq, 1 xs, 2 hq, 3 hs, 4 y,
+ * 5 pad_start [E+1], 6 slot_pos [T, k], 7 sorted_w, 8 the int32 device error
+ * word used when args.error_word is NULL, 9 counts [E] (routed rows per
+ * expert), 10 offs_start [E] (first unpadded row of each expert). */
 void* mcl4moe_workspace_region(void* workspace, int region, int T, int d, int E, int k, int F);
 
 /* ------------------------------------------------------------------------

@@ -53,6 +53,12 @@ EXPORTS = (
     "mcl4moe_ipc_close",
     "mcl4moe_copy_async",
     "mcl4moe_copy_list_async",
+    "mcl4moe_quantize_weights_t",
+    "mcl4moe_quantize_rows_sr",
+    "mcl4moe_moe_backward_workspace_size",
+    "mcl4moe_moe_backward_experts",
+    "mcl4moe_router_backward",
+    "mcl4moe_moe_backward_dx",
 )
 
 
@@ -88,6 +94,25 @@ class MoeArgs(ctypes.Structure):
         ("workspace", c_void_p),
         ("workspace_bytes", c_size_t),
         ("stage_events", POINTER(c_void_p)),
+        ("up_save", c_void_p),
+        ("x_rows_save", c_void_p),
+        ("y_save", c_void_p),
+        ("logits_out", c_void_p),
+    ]
+
+
+class MoeBwdArgs(ctypes.Structure):
+    """Mirror of ``mcl4moe_moe_bwd_args``."""
+
+    _fields_ = [
+        ("T", c_int), ("d", c_int), ("E", c_int), ("k", c_int), ("F", c_int),
+        ("d_out", c_void_p), ("slot_pos", c_void_p), ("topk_w", c_void_p), ("pad_start", c_void_p),
+        ("counts", c_void_p), ("offs_start", c_void_p), ("y_save", c_void_p), ("up_save", c_void_p),
+        ("w_up_t", c_void_p), ("w_up_t_scales", c_void_p), ("w_up_g", c_void_p),
+        ("w_dn_t", c_void_p), ("w_dn_t_scales", c_void_p), ("w_dn_g", c_void_p),
+        ("seed_down", ctypes.c_uint64), ("seed_up", ctypes.c_uint64),
+        ("d_y", c_void_p), ("d_up", c_void_p), ("d_rows", c_void_p), ("d_w", c_void_p),
+        ("error_word", c_void_p), ("workspace", c_void_p), ("workspace_bytes", c_size_t),
     ]
 
 
@@ -193,6 +218,21 @@ def load() -> ctypes.CDLL:
     lib.mcl4moe_copy_async.argtypes = [c_void_p, c_void_p, c_size_t, c_void_p]
     lib.mcl4moe_copy_list_async.restype = c_int
     lib.mcl4moe_copy_list_async.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int]
+    lib.mcl4moe_quantize_weights_t.restype = c_int
+    lib.mcl4moe_quantize_weights_t.argtypes = [POINTER(c_void_p), POINTER(c_int32), c_int, c_int, c_int, c_void_p,
+                                               c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]
+    lib.mcl4moe_quantize_rows_sr.restype = c_int
+    lib.mcl4moe_quantize_rows_sr.argtypes = [c_void_p, c_int64, c_int, ctypes.c_uint64, c_void_p, c_void_p, c_void_p,
+                                             c_void_p, c_void_p]
+    lib.mcl4moe_moe_backward_workspace_size.restype = c_size_t
+    lib.mcl4moe_moe_backward_workspace_size.argtypes = [c_int, c_int, c_int, c_int, c_int]
+    lib.mcl4moe_moe_backward_experts.restype = c_int
+    lib.mcl4moe_moe_backward_experts.argtypes = [POINTER(MoeBwdArgs), c_void_p]
+    lib.mcl4moe_router_backward.restype = c_int
+    lib.mcl4moe_router_backward.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                            c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p]
+    lib.mcl4moe_moe_backward_dx.restype = c_int
+    lib.mcl4moe_moe_backward_dx.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]
     _lib = lib
     return lib
 
@@ -210,5 +250,5 @@ def check(status: int, what: str) -> None:
     raise RuntimeError(msg)
 
 
-__all__ = ["load", "check", "MoeArgs", "EXPORTS", "LIB_PATH", "ExtensionMissing",
+__all__ = ["load", "check", "MoeArgs", "MoeBwdArgs", "EXPORTS", "LIB_PATH", "ExtensionMissing",
            "c_float", "c_uint8", "c_uint16"]

@@ -16,7 +16,8 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
 LIB = HERE / "libmcl4moe.so"
-SOURCES = ["quant.cu", "router.cu", "route.cu", "gemm_fp4.cu", "api.cu", "noalloc.cu", "ep.cu", "peer.cu"]
+SOURCES = ["quant.cu", "router.cu", "route.cu", "gemm_fp4.cu", "api.cu", "noalloc.cu", "ep.cu", "peer.cu",
+           "backward.cu"]
 HEADERS = ["common.cuh", "kernels.cuh"]
 
 NVCC_FLAGS = [

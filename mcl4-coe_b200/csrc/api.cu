@@ -119,6 +119,21 @@ int mcl4moe_quantize_weights(const float* const* w_ptrs, const int32_t* slots, i
                                  ref_b_bwd, ref_bs_bwd, amax_scratch, stream);
 }
 
+int mcl4moe_quantize_weights_t(const float* const* w_ptrs, const int32_t* slots, int n, int N, int K,
+                               uint8_t* packed, uint8_t* scales, float* global_scale, uint8_t* packed_t,
+                               uint8_t* scales_t, float* amax_scratch, mcl4moe_stream_t stream) {
+  if (n < 0 || N <= 0 || K <= 0 || !w_ptrs || !slots || !packed || !scales || !global_scale || !amax_scratch ||
+      !packed_t || !scales_t)
+    return MCL4MOE_ERR_INVALID;
+  if (N % 16 != 0 || K % 16 != 0) return MCL4MOE_ERR_INVALID;
+  if (K % 128 != 0) return MCL4MOE_ERR_UNSUPPORTED;
+  for (int i = 0; i < n; ++i)
+    if (!w_ptrs[i] || !aligned16(w_ptrs[i]) || slots[i] < 0) return MCL4MOE_ERR_INVALID;
+  if (n == 0) return MCL4MOE_OK;
+  return launch_quantize_weights(w_ptrs, slots, n, N, K, packed, scales, global_scale, nullptr, nullptr, nullptr,
+                                 nullptr, amax_scratch, stream, packed_t, scales_t);
+}
+
 int mcl4moe_mask_2to4(const float* w, int N, int K, int mode, float* w_masked, uint8_t* mask,
                       mcl4moe_stream_t stream) {
   if (N < 0 || K < 0 || (mode != 1 && mode != 2) || (int64_t(N) * K > 0 && (!w || !w_masked))) return MCL4MOE_ERR_INVALID;
@@ -281,6 +296,8 @@ void* mcl4moe_workspace_region(void* workspace, int region, int T, int d, int E,
     case 6: return w.slot_pos;
     case 7: return w.sorted_w;
     case 8: return w.err;
+    case 9: return w.route.counts;
+    case 10: return w.route.offs_start;
     default: return nullptr;
   }
 }
@@ -301,8 +318,10 @@ int check_forward_args(const mcl4moe_moe_args* a, bool routed) {
     return MCL4MOE_ERR_INVALID;
   if (!aligned16(a->x) || !aligned16(a->out) || !aligned16(a->w_up) || !aligned16(a->w_dn) ||
       !aligned16(a->w_up_scales) || !aligned16(a->w_dn_scales) || (!routed && !aligned16(a->router_w)) ||
-      (a->h_debug && !aligned16(a->h_debug)))
+      (a->h_debug && !aligned16(a->h_debug)) || !aligned16(a->up_save) || !aligned16(a->x_rows_save) ||
+      !aligned16(a->y_save))
     return MCL4MOE_ERR_INVALID;
+  if (a->x_rows_save && a->d > 4096) return MCL4MOE_ERR_UNSUPPORTED;  // training rows of up to 4096
   return MCL4MOE_OK;
 }
 
@@ -312,7 +331,7 @@ int forward_experts(const mcl4moe_moe_args* a, const MoeWorkspace& w, const int3
                     int32_t* err, cudaStream_t s, int (*mark)(const mcl4moe_moe_args*, int, cudaStream_t)) {
   const int T = a->T, d = a->d, E = a->E, k = a->k, F = a->F;
   int st = launch_permute_quantize(a->x, a->valid, topk_idx, topk_w, T, d, E, k, w.route, w.slot_pos, w.sorted_w,
-                                   a->perm, w.xq, w.xs, s);
+                                   a->perm, w.xq, w.xs, s, a->x_rows_save);
   if (st != MCL4MOE_OK) return st;
   if ((st = mark(a, 2, s)) != MCL4MOE_OK) return st;
   const int64_t mcap = padded_rows_cap(T, E, k);
@@ -333,6 +352,7 @@ int forward_experts(const mcl4moe_moe_args* a, const MoeWorkspace& w, const int3
   g1.hq = w.hq;
   g1.hs = w.hs;
   g1.h_dbg = a->h_debug;
+  g1.up_save = a->up_save;
   g1.err = err;
   st = launch_grouped_gemm(w.xq, mcap, a->w_up, g1, s);
   if (st != MCL4MOE_OK) return st;
@@ -349,14 +369,15 @@ int forward_experts(const mcl4moe_moe_args* a, const MoeWorkspace& w, const int3
   g2.N_total = d;
   g2.n_tiles = d / 256;
   g2.mode = 1;
-  g2.row_w = w.sorted_w;
-  g2.y = w.y;
+  // training keeps the unweighted rows (the routing-weight gradient needs them) and weights in the combine
+  g2.row_w = a->y_save ? nullptr : w.sorted_w;
+  g2.y = a->y_save ? a->y_save : w.y;
   g2.ldy = d;
   g2.err = err;
   st = launch_grouped_gemm(w.hq, mcap, a->w_dn, g2, s);
   if (st != MCL4MOE_OK) return st;
   if ((st = mark(a, 4, s)) != MCL4MOE_OK) return st;
-  st = launch_combine(w.y, w.slot_pos, a->valid, T, k, d, a->out, s);
+  st = launch_combine(g2.y, w.slot_pos, a->valid, T, k, d, a->out, s, a->y_save ? w.sorted_w : nullptr);
   if (st != MCL4MOE_OK) return st;
   return mark(a, 5, s);
 }
@@ -393,7 +414,7 @@ int mcl4moe_moe_forward(const mcl4moe_moe_args* a, mcl4moe_stream_t stream) {
   float* topk_w = a->topk_w ? a->topk_w : w.topk_w;
   if ((st = mark_stage(a, 0, s)) != MCL4MOE_OK) return st;
   st = launch_route(a->x, a->router_w, a->logit_bias, nullptr, a->valid, T, d, E, k, a->norm_topk_prob, topk_idx,
-                    topk_w, nullptr, a->sel_mask, w.counts, a->stats, a->offs, err, w.route, s);
+                    topk_w, a->logits_out, a->sel_mask, w.counts, a->stats, a->offs, err, w.route, s);
   if (st != MCL4MOE_OK) return st;
   if ((st = mark_stage(a, 1, s)) != MCL4MOE_OK) return st;
   if (T == 0) {

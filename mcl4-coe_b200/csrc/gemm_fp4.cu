@@ -37,6 +37,8 @@
 //                                  staged in 128B-swizzled shared memory and
 //                                  written with TMA tile stores (full lines)
 //                                  (src/mcl4_coe/backbone.py:903)
+//                MODE 3 (gate/up, training): MODE 0 that also stores the bf16 gate and
+//                                  value columns for the backward
 //                MODE 2 (grouped linear): as MODE 1 into unpadded destination
 //                                  rows with per-row stores of valid rows only
 // Pipelines: smem stages with full (A/B bytes and TMEM scales of both CTAs,
@@ -81,14 +83,15 @@ constexpr uint32_t kWarpStoreBytes = 32 * 64 * 2;  // one epilogue warp's 32 row
 
 template <int MODE>
 struct Cfg {
-  static constexpr int kStages = MODE == 0 ? 5 : 4;
+  static constexpr int kStages = (MODE == 0 || MODE == 3) ? 5 : 4;
   static constexpr uint32_t kStoreBytes = MODE == 1 ? kEpiWarps * kWarpStoreBytes : 0;
   static constexpr size_t kSmem = 1024 /*align*/ + size_t(kStages) * kStageBytes + kStoreBytes + kBarBytes +
                                   sizeof(int32_t) * (kMaxExperts + 1) + sizeof(float) * 128;
 };
 
 static_assert(kStageBytes % 1024 == 0, "stage must keep 1024-byte alignment for 128B swizzle");
-static_assert(Cfg<0>::kSmem <= 232448 && Cfg<1>::kSmem <= 232448 && Cfg<2>::kSmem <= 232448, "shared memory");
+static_assert(Cfg<0>::kSmem <= 232448 && Cfg<1>::kSmem <= 232448 && Cfg<2>::kSmem <= 232448 && Cfg<3>::kSmem <= 232448,
+              "shared memory");
 static_assert(kSfCol0 + Cfg<0>::kStages * kSfColsPerStage <= kTmemCols, "TMEM budget");
 static_assert(8 * (3 * Cfg<0>::kStages + 2) + 4 <= kBarBytes, "barrier area");
 static_assert(kSegRows == 2 * kBM, "a CTA pair covers one 256-row segment block");
@@ -138,7 +141,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const bool leader = rank == 0;
   const int pair = int(cluster_id_x()), npairs = int(cluster_count_x());
 
-  if (MODE == 0 && tid < 128) s_inv[tid] = inverse_decoding(e4m3_to_f32(uint32_t(tid)));
+  if ((MODE == 0 || MODE == 3) && tid < 128) s_inv[tid] = inverse_decoding(e4m3_to_f32(uint32_t(tid)));
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(full_bar(s), 1 + 2 * kSfWarps);
@@ -182,7 +185,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     return c;
   };
   auto b_rows = [&](const TileCoord& c, int& lr0, int& lr1) {  // local B rows of the tile's two 128-row halves
-    if (MODE == 0) {
+    if (MODE == 0 || MODE == 3) {
       lr0 = c.nt * 128;           // gate rows
       lr1 = args.F + c.nt * 128;  // value rows
     } else {
@@ -357,14 +360,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       // per-tile scalars first: their load latency overlaps the MMAs of this tile
       const int64_t p = int64_t(c.pm) * kSegRows + int64_t(rank) * kBM + row_in_tile;  // padded row
       const int local = int(p - pad_s[c.e]);
-      const float gb = __ldg(args.b_g + c.e);
+      // acc * (g_a * g_b), the reference's order (src/mcl4_coe/nvfp4.py:869); g_a = 1 unless given
+      const float gb = args.a_g != nullptr ? __fmul_rn(__ldg(args.a_g), __ldg(args.b_g + c.e)) : __ldg(args.b_g + c.e);
       const int rows_e = args.row_count ? __ldg(args.row_count + c.e) : (1 << 30);
-      const float wrow = (MODE != 0 && args.row_w && local < rows_e) ? __ldg(args.row_w + p) : 0.f;
+      const float wrow = (MODE != 0 && MODE != 3 && args.row_w && local < rows_e) ? __ldg(args.row_w + p) : 0.f;
       if (!mbar_wait(tfull_bar, acc_phase, args.err, 301)) break;
       acc_phase ^= 1u;
       tc_fence_after();
       uint32_t va[32], vb[32];
-      if (MODE == 0) {
+      if (MODE == 0 || MODE == 3) {
         tmem_ld32(lane_addr + sub * 32, va);        // gate columns
         tmem_ld32(lane_addr + 128 + sub * 32, vb);  // value columns
       } else {
@@ -376,7 +380,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader);  // accumulator may be overwritten now
 
-      if (MODE == 0) {
+      if (MODE == 0 || MODE == 3) {
         // up = bf16(acc * g); h = bf16(bf16(silu(gate)) * value) (src/mcl4_coe/backbone.py:572-574),
         // then NVFP4 with 1x16 row scales (src/mcl4_coe/nvfp4.py:197-225).
         const int F = args.F;
@@ -396,6 +400,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             f2unpack(fmul2(f2pack(__uint_as_float(vb[j]), __uint_as_float(vb[j + 1])), gb2), b0, b1);
             const uint32_t gg = pack_bf16x2(a0, a1);
             const uint32_t uu = pack_bf16x2(b0, b1);
+            if (MODE == 3) {  // training: the backward's SwiGLU derivative needs gate and value
+              uint16_t* row = args.up_save + p * (2 * F) + (hb0 + blk) * 16 + 2 * pr;
+              *reinterpret_cast<uint32_t*>(row) = gg;
+              *reinterpret_cast<uint32_t*>(row + F) = uu;
+            }
             silu_f32x2(bf16x2_lo(gg), bf16x2_hi(gg), s0, s1);
             hh[pr] = bf16x2_mul(pack_bf16x2(s0, s1), uu);
             mx = bf16x2_max(mx, hh[pr] & 0x7FFF7FFFu);
@@ -616,7 +625,9 @@ int launch_grouped_gemm(const uint8_t* a, int64_t a_rows, const uint8_t* b, cons
     return MCL4MOE_ERR_CUDA;
   if (args.mode == 0) {
     memset(&ty, 0, sizeof(ty));
-    return launch_mode<0>(ta, tb, ty, tsa, args, stream);
+    // MODE 3: the same gate/up kernel that also stores gate | value for the backward
+    return args.up_save != nullptr ? launch_mode<3>(ta, tb, ty, tsa, args, stream)
+                                   : launch_mode<0>(ta, tb, ty, tsa, args, stream);
   }
   if (args.out_row_base == nullptr) {
     // Tile stores write every padded row: y holds a_rows rows of ldy elements.

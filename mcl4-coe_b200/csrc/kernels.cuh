@@ -150,9 +150,12 @@ inline int64_t padded_rows_cap(int64_t T, int E, int k) {
 }
 
 // ---- launchers (return MCL4MOE_* status)
+// t_packed / t_scales (nullable): W^T [K, N] in the kernel layout (packed [E, K, N/2], the 16x16 tile scales
+// swizzled for K rows padded to 128), the B operand of the backward's input-gradient GEMM.
 int launch_quantize_weights(const float* const* w_ptrs, const int32_t* slots, int n, int N, int K, uint8_t* packed,
                             uint8_t* scales, float* gscale, uint8_t* rb, uint8_t* rbs, uint8_t* rbb, uint8_t* rbbs,
-                            float* amax, cudaStream_t stream);
+                            float* amax, cudaStream_t stream, uint8_t* t_packed = nullptr,
+                            uint8_t* t_scales = nullptr);
 
 // One-dimensional NVFP4 rows (1x16 blocks) of a bf16 (dtype 0) or fp32 (dtype 1)
 // matrix with global scale g = 1 (causal) or amax/2688; packed [rows, cols/2],
@@ -188,7 +191,7 @@ int launch_route_from_indices(const int32_t* topk_idx, const uint8_t* valid, int
 // Scatter each routed token's NVFP4 row into its k padded expert-major slots.
 int launch_permute_quantize(const uint16_t* x, const uint8_t* valid, const int32_t* topk_idx, const float* topk_w,
                             int T, int d, int E, int k, const RouteWorkspace& ws, int32_t* slot_pos, float* sorted_w,
-                            int32_t* perm, uint8_t* xq, uint8_t* xs, cudaStream_t stream);
+                            int32_t* perm, uint8_t* xq, uint8_t* xs, cudaStream_t stream, uint16_t* xg = nullptr);
 
 // Grouped-linear helpers: padded layout from inclusive ends, and row scatter.
 int launch_pad_from_offs(const int32_t* offs, int E, int32_t* pad_start, int32_t* offs_start, int32_t* counts,
@@ -197,8 +200,9 @@ int launch_quantize_grouped_rows(const uint16_t* x, int64_t M, int K, const int3
                                  const int32_t* counts, int E, uint8_t* xq, uint8_t* xs, cudaStream_t stream);
 
 // out[t] = bf16(sum_j y[slot_pos[t, j]]) for valid tokens, 0 otherwise.
+// row_w (nullable): per padded row routing weight; y then holds unweighted rows, each weighted as bf16(y * bf16(w)).
 int launch_combine(const uint16_t* y, const int32_t* slot_pos, const uint8_t* valid, int T, int k, int d, uint16_t* out,
-                   cudaStream_t stream);
+                   cudaStream_t stream, const float* row_w = nullptr);
 
 // ---- grouped block-scaled FP4 GEMM (tcgen05)
 struct GemmArgs {
@@ -214,6 +218,9 @@ struct GemmArgs {
   uint8_t* hq;                  // mode 0: [M, F/2]
   uint8_t* hs;                  // mode 0: swizzled [M/128 * F/64 * 512]
   uint16_t* h_dbg;              // mode 0: bf16 [M, F] or nullptr
+  uint16_t* up_save;            // mode 0: bf16 [M, 2F] gate | value rows bf16(acc * g) (training), or nullptr
+  const float* a_g;             // modes 1/2: device scalar global scale of A (the output is acc * (a_g * b_g[e])),
+                                // or nullptr for g_a = 1
   const float* row_w;           // mode 1: per padded row weight or nullptr
   uint16_t* y;                  // mode 1: bf16 output
   float* y32;                   // mode 2: fp32 output instead of y (acc * g [+ bias]), or nullptr
@@ -223,6 +230,22 @@ struct GemmArgs {
 };
 
 int launch_grouped_gemm(const uint8_t* a, int64_t a_rows, const uint8_t* b, const GemmArgs& args, cudaStream_t stream);
+
+// ---- backward (backward.cu)
+int launch_sr_quant(const uint16_t* x, int64_t rows, int cols, const float* amax, uint64_t seed,
+                    const int32_t* pad_start, const int32_t* counts, const int32_t* offs_start, int E,
+                    uint8_t* packed, uint8_t* scales, float* g_out, cudaStream_t stream);
+int launch_bf16_amax(const uint16_t* x, int64_t n, float* amax, cudaStream_t stream);
+int launch_slot_grad(const uint16_t* d_out, const uint16_t* y, const int32_t* slot_pos, const float* topk_w, int T,
+                     int k, int d, const int32_t* pad_start, const int32_t* counts, int E, uint16_t* d_y, float* d_w,
+                     float* amax, cudaStream_t stream);
+int launch_swiglu_bwd(const uint16_t* d_h, const uint16_t* up, int64_t rows_cap, const int32_t* pad_end, int F,
+                      uint16_t* d_up, float* amax, cudaStream_t stream);
+int launch_router_bwd(const float* logits, const int32_t* topk_idx, const float* topk_w, const float* d_w,
+                      const uint8_t* valid, const float* stats, const float* d_aux, const float* d_z, int T, int E,
+                      int k, int norm, float* d_logits, cudaStream_t stream);
+int launch_dx_combine(const uint16_t* d_rows, const int32_t* slot_pos, const float* dxr, int T, int k, int d,
+                      uint16_t* d_x, cudaStream_t stream);
 
 int num_sms();
 

@@ -39,7 +39,8 @@ __global__ void __launch_bounds__(256) weight_amax_kernel(WeightBatch batch, int
 __global__ void __launch_bounds__(128) weight_quant_kernel(WeightBatch batch, int N, int K, const float* amax,
                                                            uint8_t* packed, uint8_t* scales, float* gscale,
                                                            uint8_t* ref_b_fwd, uint8_t* ref_bs_fwd,
-                                                           uint8_t* ref_b_bwd, uint8_t* ref_bs_bwd) {
+                                                           uint8_t* ref_b_bwd, uint8_t* ref_bs_bwd, uint8_t* t_packed,
+                                                           uint8_t* t_scales) {
   const int i = blockIdx.z;
   const float* w = batch.w[i];
   const int slot = batch.slot[i];
@@ -128,11 +129,30 @@ __global__ void __launch_bounds__(128) weight_quant_kernel(WeightBatch batch, in
 #pragma unroll
     for (int c = 0; c < 8; ++c) b[size_t(c0 + c) * (N / 16) + (n0 >> 4)] = uint8_t(s);
   }
+  if (t_packed) {  // W^T in the kernel layout [E, K, N/2]: row k packs (n, n+1) pairs, the bytes of B_bwd
+    uint8_t* b = t_packed + size_t(slot) * K * (N / 2);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      uint32_t lo = 0, hi = 0;
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        lo |= (((codes[2 * np] >> (4 * c)) & 0xFu) | (((codes[2 * np + 1] >> (4 * c)) & 0xFu) << 4)) << (8 * np);
+        hi |= (((codes[2 * np + 8] >> (4 * c)) & 0xFu) | (((codes[2 * np + 9] >> (4 * c)) & 0xFu) << 4)) << (8 * np);
+      }
+      *reinterpret_cast<uint2*>(b + size_t(c0 + c) * (N / 2) + (n0 >> 1)) = make_uint2(lo, hi);
+    }
+  }
+  if (t_scales) {  // the same 16x16 tile scale, swizzled for the K rows of W^T (N/16 blocks per row)
+    uint8_t* b = t_scales + size_t(slot) * ((K + 127) / 128 * 128) * (N / 16);
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      b[swizzled_scale_offset(uint64_t(c0 + c), uint32_t(n0 >> 4), uint32_t(N / 16))] = uint8_t(s);
+  }
 }
 
 int launch_quantize_weights(const float* const* w_ptrs, const int32_t* slots, int n, int N, int K, uint8_t* packed,
                             uint8_t* scales, float* gscale, uint8_t* rb, uint8_t* rbs, uint8_t* rbb, uint8_t* rbbs,
-                            float* amax, cudaStream_t stream) {
+                            float* amax, cudaStream_t stream, uint8_t* t_packed, uint8_t* t_scales) {
   for (int base = 0; base < n; base += kMaxWeightBatch) {
     const int cnt = n - base < kMaxWeightBatch ? n - base : kMaxWeightBatch;
     WeightBatch batch{};
@@ -146,7 +166,8 @@ int launch_quantize_weights(const float* const* w_ptrs, const int32_t* slots, in
     if (gx > 512) gx = 512;
     weight_amax_kernel<<<dim3(gx, cnt), 256, 0, stream>>>(batch, numel, amax + base);
     weight_quant_kernel<<<dim3(N / 16, (K + 1023) / 1024, cnt), 128, 0, stream>>>(batch, N, K, amax + base, packed,
-                                                                                   scales, gscale, rb, rbs, rbb, rbbs);
+                                                                                   scales, gscale, rb, rbs, rbb, rbbs,
+                                                                                   t_packed, t_scales);
     if (cudaGetLastError() != cudaSuccess) return MCL4MOE_ERR_CUDA;
   }
   return MCL4MOE_OK;

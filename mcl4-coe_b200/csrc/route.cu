@@ -94,7 +94,8 @@ template <int BPL>
 __global__ void __launch_bounds__(256) permute_quant_row_kernel(
     const uint16_t* __restrict__ x, const uint8_t* __restrict__ valid, const int32_t* __restrict__ topk_idx,
     const float* __restrict__ topk_w, int T, int d, int E, int k, RouteWorkspace ws, int32_t* __restrict__ slot_pos,
-    float* __restrict__ sorted_w, int32_t* __restrict__ perm, uint8_t* __restrict__ xq, uint8_t* __restrict__ xs) {
+    float* __restrict__ sorted_w, int32_t* __restrict__ perm, uint8_t* __restrict__ xq, uint8_t* __restrict__ xs,
+    uint16_t* __restrict__ xg) {
   __shared__ float inv_tab[128];
   fill_inverse_scale_table(inv_tab);
   __syncthreads();
@@ -103,7 +104,7 @@ __global__ void __launch_bounds__(256) permute_quant_row_kernel(
   const int lane = threadIdx.x & 31;
   const int nblk = d / 16;
   const int token_blocks = (T + 7) / 8;
-  if (int(blockIdx.x) >= token_blocks) {  // zero the scales of the expert's padding rows
+  if (int(blockIdx.x) >= token_blocks) {  // zero the scales (and bf16 copies) of the expert's padding rows
     const int e = blockIdx.x - token_blocks;
     const int start = ws.pad_start[e] + ws.counts[e];
     const int end = ws.pad_start[e + 1];
@@ -111,6 +112,11 @@ __global__ void __launch_bounds__(256) permute_quant_row_kernel(
     for (int i = threadIdx.x; i < (end - start) * groups; i += blockDim.x) {
       const int r = start + i / groups, g = i % groups;
       *reinterpret_cast<uint32_t*>(xs + rowmajor_scale_offset(uint64_t(r), uint32_t(4 * g), uint32_t(nblk))) = 0u;
+    }
+    if (xg != nullptr) {
+      const int64_t n16 = int64_t(end - start) * (d / 8);
+      uint4* dst = reinterpret_cast<uint4*>(xg + int64_t(start) * d);
+      for (int64_t i = threadIdx.x; i < n16; i += blockDim.x) dst[i] = make_uint4(0u, 0u, 0u, 0u);
     }
     return;
   }
@@ -172,6 +178,11 @@ __global__ void __launch_bounds__(256) permute_quant_row_kernel(
         if ((lane & 3) == 0)
           *reinterpret_cast<uint32_t*>(xs + rowmajor_scale_offset(uint64_t(p), uint32_t(b), uint32_t(nblk))) =
               word[i];
+        if (xg != nullptr) {  // training: the bf16 row for the weight gradient of the gate/up projection
+          uint4* dst = reinterpret_cast<uint4*>(xg + int64_t(p) * d + b * 16);
+          dst[0] = u[i][0];
+          dst[1] = u[i][1];
+        }
       }
     }
   }
@@ -179,22 +190,23 @@ __global__ void __launch_bounds__(256) permute_quant_row_kernel(
 
 int launch_permute_quantize(const uint16_t* x, const uint8_t* valid, const int32_t* topk_idx, const float* topk_w,
                             int T, int d, int E, int k, const RouteWorkspace& ws, int32_t* slot_pos, float* sorted_w,
-                            int32_t* perm, uint8_t* xq, uint8_t* xs, cudaStream_t stream) {
+                            int32_t* perm, uint8_t* xq, uint8_t* xs, cudaStream_t stream, uint16_t* xg) {
   const int blocks = (T + 7) / 8 + E;
   const int bpl = (d / 16 + 31) / 32;
+  if (xg != nullptr && bpl > 8) return MCL4MOE_ERR_UNSUPPORTED;  // bf16 row copies: rows of up to 4096
   cudaError_t e;
   if (bpl <= 1)
     e = launch_pdl(permute_quant_row_kernel<1>, dim3(blocks), dim3(256), 0, stream, x, valid, topk_idx, topk_w, T, d,
-                   E, k, ws, slot_pos, sorted_w, perm, xq, xs);
+                   E, k, ws, slot_pos, sorted_w, perm, xq, xs, xg);
   else if (bpl <= 2)
     e = launch_pdl(permute_quant_row_kernel<2>, dim3(blocks), dim3(256), 0, stream, x, valid, topk_idx, topk_w, T, d,
-                   E, k, ws, slot_pos, sorted_w, perm, xq, xs);
+                   E, k, ws, slot_pos, sorted_w, perm, xq, xs, xg);
   else if (bpl <= 4)
     e = launch_pdl(permute_quant_row_kernel<4>, dim3(blocks), dim3(256), 0, stream, x, valid, topk_idx, topk_w, T, d,
-                   E, k, ws, slot_pos, sorted_w, perm, xq, xs);
+                   E, k, ws, slot_pos, sorted_w, perm, xq, xs, xg);
   else if (bpl <= 8)
     e = launch_pdl(permute_quant_row_kernel<8>, dim3(blocks), dim3(256), 0, stream, x, valid, topk_idx, topk_w, T, d,
-                   E, k, ws, slot_pos, sorted_w, perm, xq, xs);
+                   E, k, ws, slot_pos, sorted_w, perm, xq, xs, xg);
   else
     e = launch_pdl(permute_quant_kernel, dim3(blocks), dim3(256), 0, stream, x, valid, topk_idx, topk_w, T, d, E, k,
                    ws, slot_pos, sorted_w, perm, xq, xs);
@@ -298,11 +310,14 @@ int launch_quantize_grouped_rows(const uint16_t* x, int64_t M, int K, const int3
 // cols_per_y columns, so a small batch still spreads over many warps.  BATCH
 // slot pieces are loaded before they are added: 8 for small batches (few warps,
 // latency-bound), 1 for large ones (bandwidth-bound; fewer registers, more warps).
-template <int BATCH>
+// WEIGHTED: y holds unweighted rows and each slot's term is bf16(y * bf16(row_w[slot row]))
+// (the training forward keeps the unweighted rows for the routing-weight gradient).
+template <int BATCH, bool WEIGHTED>
 __global__ void __launch_bounds__(256) combine_kernel(const uint16_t* __restrict__ y,
                                                       const int32_t* __restrict__ slot_pos,
                                                       const uint8_t* __restrict__ valid, int T, int k, int d,
-                                                      int cols_per_y, uint16_t* __restrict__ out) {
+                                                      int cols_per_y, uint16_t* __restrict__ out,
+                                                      const float* __restrict__ row_w) {
   pdl_wait();  // the down projection's rows are complete
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -327,7 +342,13 @@ __global__ void __launch_bounds__(256) combine_kernel(const uint16_t* __restrict
           if (j0 + jj >= k) break;
           const int p = __shfl_sync(0xffffffffu, my_pos, (j0 + jj) & 31);
           if (p < 0) continue;  // slot not routed (caller-supplied routing)
-          const uint32_t w4[4] = {u[jj].x, u[jj].y, u[jj].z, u[jj].w};
+          uint32_t w4[4] = {u[jj].x, u[jj].y, u[jj].z, u[jj].w};
+          if (WEIGHTED) {
+            const float wb = round_bf16(__ldg(row_w + p));
+            const uint32_t ww = pack_bf16x2(wb, wb);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) w4[i] = bf16x2_mul(w4[i], ww);
+          }
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             acc[2 * i] = __fadd_rn(acc[2 * i], bf16_to_f32(uint16_t(w4[i] & 0xFFFFu)));
@@ -345,7 +366,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const uint16_t* __restrict
 }
 
 int launch_combine(const uint16_t* y, const int32_t* slot_pos, const uint8_t* valid, int T, int k, int d, uint16_t* out,
-                   cudaStream_t stream) {
+                   cudaStream_t stream, const float* row_w) {
   if (T == 0) return MCL4MOE_OK;
   // enough warps to cover the SMs a few times: split each row into column ranges
   // (multiples of 256 columns) while the token warps alone are fewer than ~16 per SM
@@ -353,11 +374,18 @@ int launch_combine(const uint16_t* y, const int32_t* slot_pos, const uint8_t* va
   int split = 1;
   while (split < chunks256 && int64_t(T) * split < int64_t(16) * num_sms() && chunks256 % (2 * split) == 0) split *= 2;
   const int cols_per_y = d / split;
-  const cudaError_t e =
-      split > 1 ? launch_pdl(combine_kernel<8>, dim3((T + 7) / 8, split), dim3(256), 0, stream, y, slot_pos, valid, T,
-                             k, d, cols_per_y, out)
-                : launch_pdl(combine_kernel<1>, dim3((T + 7) / 8, 1), dim3(256), 0, stream, y, slot_pos, valid, T, k,
-                             d, cols_per_y, out);
+  const dim3 grid((T + 7) / 8, split);
+  cudaError_t e;
+  if (row_w != nullptr)
+    e = split > 1 ? launch_pdl(combine_kernel<8, true>, grid, dim3(256), 0, stream, y, slot_pos, valid, T, k, d,
+                               cols_per_y, out, row_w)
+                  : launch_pdl(combine_kernel<1, true>, grid, dim3(256), 0, stream, y, slot_pos, valid, T, k, d,
+                               cols_per_y, out, row_w);
+  else
+    e = split > 1 ? launch_pdl(combine_kernel<8, false>, grid, dim3(256), 0, stream, y, slot_pos, valid, T, k, d,
+                               cols_per_y, out, row_w)
+                  : launch_pdl(combine_kernel<1, false>, grid, dim3(256), 0, stream, y, slot_pos, valid, T, k, d,
+                               cols_per_y, out, row_w);
   return e == cudaSuccess ? MCL4MOE_OK : MCL4MOE_ERR_CUDA;
 }
 

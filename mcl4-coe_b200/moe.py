@@ -30,13 +30,21 @@ Routing variants (mitotic twins, lineage families, recurrent coverage
 penalty, dense subsets with an optional sparse remainder, the sequence-diversity
 and mitotic-orthogonality losses) compute the reference's selection on the
 library's router logits (``routing_variants.py``) and run the experts through
-``mcl4moe_moe_forward_routed``.  Not served (raise ``NotImplementedError``):
-backward and 2:4 sparse weights.
+``mcl4moe_moe_forward_routed``.
+
+Training: under autograd (plain top-k routing) the forward keeps the gate / value
+rows, the permuted bf16 inputs, h and the unweighted down-projection rows, and the
+backward runs the reference's _NVFP4GroupedLinear.backward path
+(src/mcl4_coe/nvfp4.py:1112-1216) on the library: stochastic-rounded NVFP4
+gradients into grouped NVFP4 input-gradient GEMMs on the transposed weights, the
+SwiGLU and routing derivatives, and bf16-operand weight gradients.  Routing
+variants run forward only (``NotImplementedError`` under autograd).
 """
 
 from __future__ import annotations
 
 import ctypes
+import random
 from dataclasses import dataclass
 from typing import Any, Sequence
 
@@ -266,10 +274,11 @@ class SparseMoE(nn.Module):
         flat = x.reshape(-1, x.shape[-1])
         if flat.device.type != "cuda":
             raise ValueError("SparseMoE on B200 requires CUDA tensors (there is no CPU fallback)")
-        if torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in self.parameters())):
-            raise NotImplementedError("the B200 MoE path is forward-only: run it under torch.no_grad() "
-                                      "or torch.inference_mode()")
         variant = self._routing_variant(prior_expert_mask, dense_expert_indices, dense_subset_k)
+        if torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in self.parameters())):
+            if variant is not None or details or static is not None:
+                raise NotImplementedError("training (autograd) runs plain top-k routing through forward() only")
+            return self._forward_train(x, valid)
         if variant is not None:
             if details or static is not None:
                 raise NotImplementedError("routing variants run through forward() only")
@@ -362,6 +371,19 @@ class SparseMoE(nn.Module):
                 res["xs"] = region(1, mcap * d // 16).view(mcap, d // 16).clone()
                 res["slot_pos"] = region(6, 4 * T * k).view(torch.int32).view(T, k).clone()
         return res
+
+    # ------------------------------------------------------------------ training
+    def _forward_train(self, x: Tensor, valid: Tensor | None) -> dict:
+        """Forward under autograd: the same library forward, which also keeps what the
+        backward reads (``_MoETrainFunction``)."""
+        E = len(self.experts)
+        if self.router.weight.shape[0] != E:
+            raise ValueError("router rows must match the number of experts")
+        self.num_experts = E
+        ups = [e.up_proj.weight for e in self.experts]
+        dns = [e.down_proj.weight for e in self.experts]
+        out, aux, z, counts = _MoETrainFunction.apply(self, x, valid, self.router.weight, *ups, *dns)
+        return dict(out=out, aux_loss=aux, router_z_loss=z, counts=counts)
 
     # ------------------------------------------------------------------ routing variants
     def _router_logits(self, xb: Tensor, wr: Tensor, bias: Tensor | None) -> Tensor:
@@ -550,3 +572,161 @@ class SparseMoE(nn.Module):
                 self.mitotic_pairs = []
         super()._load_from_state_dict(state_dict, prefix, local_metadata, strict, missing_keys, unexpected_keys,
                                       error_msgs)
+
+
+def _region(ws: Tensor, idx: int, nbytes: int, T: int, d: int, E: int, k: int, F: int) -> Tensor:
+    lib = _lib.load()
+    off = lib.mcl4moe_workspace_region(ws.data_ptr(), idx, T, d, E, k, F) - ws.data_ptr()
+    return ws[off:off + nbytes]
+
+
+def _weight_grads(d_rows: Tensor, rows: Tensor, offs: Tensor) -> Tensor:
+    """Per-expert ``d_rows[seg]^T @ rows[seg]`` in float32 ([E, N, K]) over the padded
+    expert segments ending at ``offs``: the reference's ``_grouped_wgrad_kernel``
+    (src/mcl4_coe/nvfp4.py:877-920, bf16 operands, fp32 accumulation).  A plain grouped
+    bf16 GEMM: cuBLAS / CUTLASS through ``torch._grouped_mm``, or per expert where
+    that is not available."""
+    try:
+        return torch._grouped_mm(d_rows.t(), rows, offs=offs, out_dtype=torch.float32)
+    except (RuntimeError, TypeError, AttributeError):
+        ends = offs.tolist()
+        res, start = [], 0
+        for end in ends:
+            res.append(d_rows[start:end].t().float() @ rows[start:end].float())
+            start = end
+        return torch.stack(res)
+
+
+class _MoETrainFunction(torch.autograd.Function):
+    """The layer under autograd (src/mcl4_coe/backbone.py:787-911 with
+    _NVFP4GroupedLinear, src/mcl4_coe/nvfp4.py:1051-1216).
+
+    Forward: ``mcl4moe_moe_forward`` with the training saves (gate | value rows, the
+    permuted bf16 input rows, h, the unweighted down-projection rows, the router
+    logits).  Backward: ``mcl4moe_moe_backward_experts`` (routing-weight and
+    down-projection output gradients, stochastic-rounded NVFP4 input-gradient GEMMs on
+    the transposed weights, SwiGLU derivative), ``mcl4moe_router_backward`` (softmax /
+    top-k / renormalisation / aux / z derivative), the router's fp32 matrix products,
+    ``mcl4moe_moe_backward_dx`` and the per-expert weight gradients."""
+
+    @staticmethod
+    def forward(ctx, mod, x, valid, wr_param, *expert_weights):
+        lib = _lib.load()
+        flat = x.reshape(-1, x.shape[-1])
+        T, d = flat.shape
+        E = len(mod.experts)
+        k = mod.top_k
+        F = mod.experts[0].down_proj.weight.shape[1]
+        dev = flat.device
+        up = get_or_build_grouped_cache(mod.experts, "up_proj", with_bwd=True)
+        dn = get_or_build_grouped_cache(mod.experts, "down_proj", with_bwd=True)
+        xb = flat.detach().to(torch.bfloat16).contiguous()
+        wr = wr_param.detach().to(torch.float32).contiguous()
+        bias = None
+        if mod.router_logit_bias is not None:
+            bias = mod.router_logit_bias.detach().to(device=dev, dtype=torch.float32).contiguous()
+        vmask = None if valid is None else valid.reshape(-1).to(device=dev, dtype=torch.uint8).contiguous()
+        mcap = lib.mcl4moe_padded_rows(T, E, k)
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        out = torch.empty((T, d), **bf)
+        stats = torch.empty((3 + E,), dtype=torch.float32, device=dev)
+        sel = torch.empty((T, E), dtype=torch.float32, device=dev)
+        topk_idx = torch.empty((T, k), dtype=torch.int32, device=dev)
+        topk_w = torch.empty((T, k), dtype=torch.float32, device=dev)
+        logits = torch.empty((T, E), dtype=torch.float32, device=dev)
+        up_save = torch.empty((mcap, 2 * F), **bf)
+        x_rows = torch.empty((mcap, d), **bf)
+        y_save = torch.empty((mcap, d), **bf)
+        h_save = torch.empty((mcap, F), **bf)
+        ws = mod._workspace(T, d, E, k, F, dev)
+        args = _lib.MoeArgs(
+            x=xb.data_ptr(), router_w=wr.data_ptr(), logit_bias=_opt_ptr(bias), valid=_opt_ptr(vmask),
+            w_up=up.packed.data_ptr(), w_up_scales=up.scales.data_ptr(), w_up_g=up.g.data_ptr(),
+            w_dn=dn.packed.data_ptr(), w_dn_scales=dn.scales.data_ptr(), w_dn_g=dn.g.data_ptr(),
+            T=T, d=d, E=E, k=k, F=F, norm_topk_prob=int(mod.norm_topk_prob),
+            out=out.data_ptr(), stats=stats.data_ptr(), sel_mask=sel.data_ptr(),
+            topk_idx=topk_idx.data_ptr(), topk_w=topk_w.data_ptr(), offs=None, perm=None,
+            h_debug=h_save.data_ptr() if T > 0 else None, error_word=None, workspace=ws.data_ptr(),
+            workspace_bytes=ws.numel(), up_save=up_save.data_ptr() if T > 0 else None,
+            x_rows_save=x_rows.data_ptr() if T > 0 else None, y_save=y_save.data_ptr() if T > 0 else None,
+            logits_out=logits.data_ptr() if T > 0 else None)
+        _lib.check(lib.mcl4moe_moe_forward(args, _stream_handle()), "mcl4moe_moe_forward")
+        # the expert layout of this call (the workspace is reused by the next call)
+        slot_pos = _region(ws, 6, 4 * T * k, T, d, E, k, F).view(torch.int32).view(T, k).clone()
+        pad_start = _region(ws, 5, 4 * (E + 1), T, d, E, k, F).view(torch.int32).clone()
+        counts_i = _region(ws, 9, 4 * E, T, d, E, k, F).view(torch.int32).clone()
+        offs_start = _region(ws, 10, 4 * E, T, d, E, k, F).view(torch.int32).clone()
+        mod.last_selected_mask = sel.view(*x.shape[:-1], E)
+        ctx.mod = mod
+        ctx.shape = (T, d, E, k, F)
+        ctx.x_shape, ctx.x_dtype = x.shape, x.dtype
+        ctx.caches = (up, dn)
+        ctx.save_for_backward(xb, wr, vmask, topk_idx, topk_w, logits, stats, slot_pos, pad_start, counts_i,
+                              offs_start, up_save, x_rows, y_save, h_save)
+        aux, z, counts = stats[0].clone(), stats[1].clone(), stats[3:3 + E].clone()
+        ctx.mark_non_differentiable(counts)
+        return out.to(x.dtype).view(x.shape), aux, z, counts
+
+    @staticmethod
+    def backward(ctx, d_out, d_aux, d_z, _d_counts):
+        lib = _lib.load()
+        (xb, wr, vmask, topk_idx, topk_w, logits, stats, slot_pos, pad_start, counts_i, offs_start, up_save, x_rows,
+         y_save, h_save) = ctx.saved_tensors
+        mod = ctx.mod
+        up, dn = ctx.caches
+        T, d, E, k, F = ctx.shape
+        dev = xb.device
+        mcap = up_save.shape[0]
+        n_exp = len(mod.experts)
+        if d_out is None:
+            d_out = torch.zeros((T, d), dtype=torch.bfloat16, device=dev)
+        d_out = d_out.reshape(T, d).to(torch.bfloat16).contiguous()
+        f32 = dict(dtype=torch.float32, device=dev)
+        d_aux = torch.zeros((), **f32) if d_aux is None else d_aux.detach().to(torch.float32).reshape(()).contiguous()
+        d_z = torch.zeros((), **f32) if d_z is None else d_z.detach().to(torch.float32).reshape(()).contiguous()
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        d_y = torch.empty((mcap, d), **bf)
+        d_up = torch.empty((mcap, 2 * F), **bf)
+        d_rows = torch.empty((mcap, d), **bf)
+        d_w = torch.zeros((T, k), **f32)
+        ws = torch.empty((max(lib.mcl4moe_moe_backward_workspace_size(T, d, E, k, F), 256),), dtype=torch.uint8,
+                         device=dev)
+        args = _lib.MoeBwdArgs(
+            T=T, d=d, E=E, k=k, F=F, d_out=d_out.data_ptr(), slot_pos=slot_pos.data_ptr(),
+            topk_w=topk_w.data_ptr(), pad_start=pad_start.data_ptr(), counts=counts_i.data_ptr(),
+            offs_start=offs_start.data_ptr(), y_save=y_save.data_ptr(), up_save=up_save.data_ptr(),
+            w_up_t=up.packed_t.data_ptr(), w_up_t_scales=up.scales_t.data_ptr(), w_up_g=up.g.data_ptr(),
+            w_dn_t=dn.packed_t.data_ptr(), w_dn_t_scales=dn.scales_t.data_ptr(), w_dn_g=dn.g.data_ptr(),
+            seed_down=random.getrandbits(31), seed_up=random.getrandbits(31),  # src/mcl4_coe/nvfp4.py:1140
+            d_y=d_y.data_ptr(), d_up=d_up.data_ptr(), d_rows=d_rows.data_ptr(), d_w=d_w.data_ptr(),
+            error_word=None, workspace=ws.data_ptr(), workspace_bytes=ws.numel())
+        stream = _stream_handle()
+        if T > 0:
+            _lib.check(lib.mcl4moe_moe_backward_experts(args, stream), "mcl4moe_moe_backward_experts")
+        d_logits = torch.empty((T, E), **f32)
+        _lib.check(lib.mcl4moe_router_backward(logits.data_ptr(), topk_idx.data_ptr(), topk_w.data_ptr(),
+                                               d_w.data_ptr(), _opt_ptr(vmask), stats.data_ptr(), d_aux.data_ptr(),
+                                               d_z.data_ptr(), T, E, k, int(mod.norm_topk_prob),
+                                               d_logits.data_ptr(), stream), "mcl4moe_router_backward")
+        # the router's fp32 products (F.linear(x.float(), W) at src/mcl4_coe/backbone.py:790)
+        d_x_router = (d_logits @ wr).contiguous()
+        d_wr = d_logits.t() @ xb.float()
+        d_x = torch.empty((T, d), **bf)
+        _lib.check(lib.mcl4moe_moe_backward_dx(d_rows.data_ptr(), slot_pos.data_ptr(), d_x_router.data_ptr(), T, k, d,
+                                               d_x.data_ptr(), stream), "mcl4moe_moe_backward_dx")
+        # expert weight gradients over the padded segments (padding rows are zero in d_y / d_up)
+        rows = int(pad_start[E].item()) if T > 0 else 0
+        ends = pad_start[1:].contiguous()
+        if rows > 0:
+            dw_dn = _weight_grads(d_y[:rows], h_save[:rows], ends)
+            dw_up = _weight_grads(d_up[:rows], x_rows[:rows], ends)
+        else:
+            dw_dn = torch.zeros((E, d, F), **f32)
+            dw_up = torch.zeros((E, 2 * F, d), **f32)
+        ups = [e.up_proj.weight for e in mod.experts]
+        dns = [e.down_proj.weight for e in mod.experts]
+        g_up = [dw_up[i].to(ups[i].dtype) if ctx.needs_input_grad[4 + i] else None for i in range(n_exp)]
+        g_dn = [dw_dn[i].to(dns[i].dtype) if ctx.needs_input_grad[4 + n_exp + i] else None for i in range(n_exp)]
+        g_x = d_x.to(ctx.x_dtype).view(ctx.x_shape) if ctx.needs_input_grad[1] else None
+        g_wr = d_wr.to(mod.router.weight.dtype) if ctx.needs_input_grad[3] else None
+        return (None, g_x, None, g_wr, *g_up, *g_dn)

@@ -120,6 +120,20 @@ class GroupedNVFP4Cache:
         self.amax = torch.empty((e_count,), dtype=torch.float32, device=device)
         self.masks: list[Tensor | None] = [None] * e_count  # bool [N, K] of 2:4-sparse experts
         self.n, self.k = n, k
+        # W^T in the kernel layout (the backward's input-gradient operand), made on demand
+        self.packed_t: Tensor | None = None
+        self.scales_t: Tensor | None = None
+
+    def enable_transposed(self) -> None:
+        """Allocate the transposed copy (packed [E, K, N/2], swizzled scales [E, K*N/16]);
+        every slot must then be quantised again."""
+        if self.packed_t is not None:
+            return
+        e_count, dev = self.packed.shape[0], self.packed.device
+        self.packed_t = torch.empty((e_count, self.k, self.n // 2), dtype=torch.uint8, device=dev)
+        self.scales_t = torch.zeros((e_count, (self.k + 127) // 128 * 128 * (self.n // 16)), dtype=torch.uint8,
+                                    device=dev)
+        self.versions = [None] * e_count
 
 
 def quantize_weight_slots(weights: list[Tensor], slots: list[int], cache: GroupedNVFP4Cache,
@@ -137,6 +151,12 @@ def quantize_weight_slots(weights: list[Tensor], slots: list[int], cache: Groupe
     ptrs = (ctypes.c_void_p * n_w)(*[w.data_ptr() for w in staged])
     slot_arr = (ctypes.c_int32 * n_w)(*slots)
     ref = ref_out or {}
+    if cache.packed_t is not None and ref_out is None:
+        st = lib.mcl4moe_quantize_weights_t(ptrs, slot_arr, n_w, cache.n, cache.k, cache.packed.data_ptr(),
+                                            cache.scales.data_ptr(), cache.g.data_ptr(), cache.packed_t.data_ptr(),
+                                            cache.scales_t.data_ptr(), cache.amax.data_ptr(), _stream_handle())
+        _lib.check(st, "mcl4moe_quantize_weights_t")
+        return
     st = lib.mcl4moe_quantize_weights(ptrs, slot_arr, n_w, cache.n, cache.k, cache.packed.data_ptr(),
                                       cache.scales.data_ptr(), cache.g.data_ptr(), _ptr(ref.get("B_fwd")),
                                       _ptr(ref.get("Bs_fwd")), _ptr(ref.get("B_bwd")), _ptr(ref.get("Bs_bwd")),
@@ -147,7 +167,7 @@ def quantize_weight_slots(weights: list[Tensor], slots: list[int], cache: Groupe
 
 
 @torch.no_grad()
-def get_or_build_grouped_cache(experts: nn.ModuleList, proj_name: str) -> GroupedNVFP4Cache:
+def get_or_build_grouped_cache(experts: nn.ModuleList, proj_name: str, with_bwd: bool = False) -> GroupedNVFP4Cache:
     """src/mcl4_coe/nvfp4.py:962-1048 on the B200 kernels (see module docstring)."""
     layers = [getattr(e, proj_name) for e in experts]
     weights = [layer.weight for layer in layers]
@@ -172,8 +192,12 @@ def get_or_build_grouped_cache(experts: nn.ModuleList, proj_name: str) -> Groupe
     entry = store.get(proj_name)
     if entry is None or entry.shape_key != (e_count, n, k, str(device)):
         entry = GroupedNVFP4Cache(e_count, n, k, device)
+        if with_bwd:
+            entry.enable_transposed()
         store[proj_name] = entry
         _carry_over(layers, cur, entry)
+    elif with_bwd and entry.packed_t is None:
+        entry.enable_transposed()  # training starts: every expert also needs its transposed copy
     if entry.versions == cur:
         return entry
     dirty = [i for i, (old, new) in enumerate(zip(entry.versions, cur)) if old != new]
@@ -206,7 +230,8 @@ def _carry_over(layers: list, cur: list, entry: GroupedNVFP4Cache) -> None:
             continue
         old, j = prev
         if (old is entry or old.n != entry.n or old.k != entry.k or old.packed.device != entry.packed.device
-                or j >= len(old.versions) or old.versions[j] != cur[i]):
+                or j >= len(old.versions) or old.versions[j] != cur[i]
+                or (entry.packed_t is not None and old.packed_t is None)):
             continue
         owners[id(old)] = old
         src_slots.setdefault(id(old), []).append((j, i))
@@ -217,6 +242,9 @@ def _carry_over(layers: list, cur: list, entry: GroupedNVFP4Cache) -> None:
         entry.packed.index_copy_(0, dst, old.packed.index_select(0, src))
         entry.scales.index_copy_(0, dst, old.scales.index_select(0, src))
         entry.g.index_copy_(0, dst, old.g.index_select(0, src))
+        if entry.packed_t is not None:
+            entry.packed_t.index_copy_(0, dst, old.packed_t.index_select(0, src))
+            entry.scales_t.index_copy_(0, dst, old.scales_t.index_select(0, src))
         for j, i in pairs:
             entry.masks[i] = old.masks[j]
             entry.versions[i] = cur[i]

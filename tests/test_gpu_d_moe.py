@@ -279,9 +279,12 @@ def test_empty_and_fully_masked_batches(moe_pkg):
     assert torch.all(moe.last_selected_mask == 0)
 
 
-def test_forward_requires_no_grad(moe_pkg):
+def test_routing_variants_are_forward_only(moe_pkg):
+    """Plain top-k routing trains (tests/test_gpu_k_backward.py); a routing variant under
+    autograd is refused rather than run without its gradient."""
     c = moe_case(24, 16, 256, 8, 2, 512)
     moe = build_module(moe_pkg, c, DEV)
+    moe.dense_subset_k = 2
     with pytest.raises(NotImplementedError):
         moe(x_tensor(c, DEV))
 
