@@ -339,6 +339,40 @@ def reference_gpu_leg(moe, x, cfg, steps: int) -> dict:
     return res
 
 
+def train_step_timing(moe, x, steps: int) -> dict:
+    """One training step of the layer: forward with the backward's saves, then the
+    backward (stochastic-rounded NVFP4 input-gradient GEMMs, the SwiGLU / routing /
+    router derivatives, bf16-operand weight gradients) for an upstream gradient of the
+    output plus the auxiliary and z losses; CUDA events around the steps."""
+    import torch
+
+    moe.requires_grad_(True)
+    xg = x.detach().clone().requires_grad_(True)
+    g = torch.Generator(device=x.device).manual_seed(123)
+    gout = torch.randn(x.shape, generator=g, device=x.device).to(torch.bfloat16)
+    one = torch.ones((), device=x.device)
+
+    def step():
+        out, aux, z, _ = moe(xg)
+        torch.autograd.backward([out, aux, z], [gout, one * 0.01, one * 0.001])
+        moe.zero_grad(set_to_none=True)
+        xg.grad = None
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    moe.requires_grad_(False)
+    ms = a.elapsed_time(b) / steps
+    return {"ms_per_step": ms, "value": x.shape[0] / (ms / 1e3), "unit": UNIT, "steps": steps,
+            "what": "forward + backward (input, router and expert weight gradients) of the layer"}
+
+
 def fp4_peak(args) -> None:
     """cuBLAS dense NVFP4 GEMM (F.scaled_mm with 1x16 E4M3 block scales + fp32 tensor
     scales, the recipe of the reference's nvfp4_mm) at M = N = K = 8192: best of 10
@@ -594,6 +628,8 @@ def run_ours(args) -> None:
         "gpu_launches": (KERNELS_PER_EP_FORWARD if ep else KERNELS_PER_FORWARD) * K,
         "clocks": clocks,
     }
+    if world == 1 and not ep and not args.no_train:
+        result["train"] = train_step_timing(moe, x, max(3, min(K, 10)))
     if rank == 0 and world == 1 and not args.no_reference_gpu:
         # not under inference_mode: the reference keys its weight cache on ``Tensor._version``
         with torch.no_grad():
@@ -694,6 +730,7 @@ def main() -> None:
     ap.add_argument("--no-reference-gpu", action="store_true",
                     help="skip timing the reference's own GPU path on this device")
     ap.add_argument("--fp4-peak", action="store_true", help="measure the cuBLAS dense NVFP4 GEMM rate and exit")
+    ap.add_argument("--no-train", action="store_true", help="skip timing a training step (forward + backward)")
     ap.add_argument("--cuda-graph", action="store_true",
                     help="1 GPU: serve the timed forwards from a captured CUDA graph (SparseMoE.enable_cuda_graph)")
     ap.add_argument("--ep-partials", default="copy", choices=("kernel", "copy"),

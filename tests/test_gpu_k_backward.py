@@ -264,7 +264,7 @@ def test_training_end_to_end(moe_pkg):
         ref_out, ref_aux, ref_z, ref_counts = moe(x.detach())
     out, aux, z, counts = moe(x)
     assert torch.equal(out.detach(), ref_out) and torch.equal(counts, ref_counts)
-    assert float(aux) == float(ref_aux) and float(z) == float(ref_z)
+    assert float(aux.detach()) == float(ref_aux) and float(z.detach()) == float(ref_z)
     g = torch.Generator(device=DEV).manual_seed(4)
     gout = torch.randn((T, d), generator=g, device=DEV)
     loss = (out.float() * gout).sum() + 0.01 * aux + 0.001 * z
@@ -285,9 +285,21 @@ def test_training_end_to_end(moe_pkg):
     wr = moe.router.weight.detach().clone().requires_grad_(True)
     xr = x.detach().float().clone().requires_grad_(True)
 
-    def fq(a):  # NVFP4 fake quantisation with a straight-through gradient
-        q = torch.from_numpy(nr.fake_quantize_activations(a.detach().float().cpu().numpy())).to(DEV)
-        return a + (q - a).detach()
+    class QLinear(torch.autograd.Function):
+        """fq(a) @ w^T in the forward; the backward of the reference's NVFP4 projection
+        without its stochastic rounding: input gradient g @ w, weight gradient g^T @ a
+        with the UNQUANTISED input (src/mcl4_coe/nvfp4.py:1172-1216)."""
+
+        @staticmethod
+        def forward(ctx, a, w):
+            ctx.save_for_backward(a, w)
+            q = torch.from_numpy(nr.fake_quantize_activations(a.detach().float().cpu().numpy())).to(DEV)
+            return q @ w.t()
+
+        @staticmethod
+        def backward(ctx, gr):
+            a, w = ctx.saved_tensors
+            return gr @ w, gr.t() @ a
 
     logits = xr @ wr.t()
     probs = torch.softmax(logits, dim=-1)
@@ -298,9 +310,9 @@ def test_training_end_to_end(moe_pkg):
         tt, jj = (idx == e).nonzero(as_tuple=True)
         if tt.numel() == 0:
             continue
-        upv = fq(xr[tt]) @ w_up[e].t()
+        upv = QLinear.apply(xr[tt], w_up[e])
         hv = torch.nn.functional.silu(upv[:, :F]) * upv[:, F:]
-        y = fq(hv) @ w_dn[e].t()
+        y = QLinear.apply(hv, w_dn[e])
         out_ref = out_ref.index_add(0, tt, y * wts[tt, jj][:, None])
     n = T
     cnt = torch.zeros(E, device=DEV).scatter_add_(0, idx.reshape(-1), torch.ones(T * k, device=DEV)) / (T * k)
@@ -316,11 +328,31 @@ def test_training_end_to_end(moe_pkg):
 
     g_dn = torch.stack([ex.down_proj.weight.grad for ex in moe.experts])
     g_up = torch.stack([ex.up_proj.weight.grad for ex in moe.experts])
+    print(f"\n[train] rel err: dW_down {rel(g_dn, w_dn.grad):.2e} dW_router {rel(moe.router.weight.grad, wr.grad):.2e} "
+          f"dW_up {rel(g_up, w_up.grad):.2e} dx {rel(x.grad, xr.grad):.2e}")
     # the down projection's weight gradient sees exact bf16 operands: close to fp32
-    assert rel(g_dn, w_dn.grad) < 3e-2, rel(g_dn, w_dn.grad)
+    assert rel(g_dn, w_dn.grad) < 1.5e-2, rel(g_dn, w_dn.grad)
     assert rel(moe.router.weight.grad, wr.grad) < 5e-2, rel(moe.router.weight.grad, wr.grad)
     # behind one (up) or two (x) stochastic-rounded NVFP4 gradients: agreement within their noise
     assert cos(g_up, w_up.grad) > 0.95 and rel(g_up, w_up.grad) < 0.35, (cos(g_up, w_up.grad), rel(g_up, w_up.grad))
     assert cos(x.grad, xr.grad) > 0.95 and rel(x.grad, xr.grad) < 0.35, (cos(x.grad, xr.grad), rel(x.grad, xr.grad))
-    print(f"\n[train] rel err: dW_down {rel(g_dn, w_dn.grad):.2e} dW_router {rel(moe.router.weight.grad, wr.grad):.2e} "
-          f"dW_up {rel(g_up, w_up.grad):.2e} dx {rel(x.grad, xr.grad):.2e}")
+
+
+def test_stochastic_rounding_is_unbiased_end_to_end(moe_pkg):
+    """Averaging the input gradient over independent backward passes (fresh noise seeds,
+    as the reference draws per call) shrinks its distance to the mean: the stochastic
+    rounding adds zero-mean noise, not a bias."""
+    c, moe = _train_case(moe_pkg, seed=63, t=256, d=512, e=8, k=2, f=512)
+    x = x_tensor(c, DEV).requires_grad_(True)
+    out = moe(x)[0]
+    g = torch.Generator(device=DEV).manual_seed(9)
+    gout = torch.randn(out.shape, generator=g, device=DEV)
+    loss = (out.float() * gout).sum()
+    grads = [torch.autograd.grad(loss, x, retain_graph=True)[0].float() for _ in range(16)]
+    mean = torch.stack(grads).mean(0)
+    single = torch.stack([torch.linalg.norm(gr - mean) for gr in grads]).mean().item()
+    avg4 = torch.stack([torch.linalg.norm(torch.stack(grads[i:i + 4]).mean(0) - mean)
+                        for i in range(0, 16, 4)]).mean().item()
+    # independent zero-mean noise: averaging 4 passes halves the spread (1/sqrt(4))
+    assert avg4 < 0.65 * single, (avg4, single)
+    assert not torch.equal(grads[0], grads[1])  # a new seed per backward call
