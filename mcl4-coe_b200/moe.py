@@ -580,6 +580,10 @@ def _region(ws: Tensor, idx: int, nbytes: int, T: int, d: int, E: int, k: int, F
     return ws[off:off + nbytes]
 
 
+# How the expert weight gradients were computed so far (grouped call or per-expert products).
+WGRAD_CALLS = {"grouped_mm": 0, "per_expert": 0}
+
+
 def _weight_grads(d_rows: Tensor, rows: Tensor, offs: Tensor) -> Tensor:
     """Per-expert ``d_rows[seg]^T @ rows[seg]`` in float32 ([E, N, K]) over the padded
     expert segments ending at ``offs``: the reference's ``_grouped_wgrad_kernel``
@@ -587,8 +591,11 @@ def _weight_grads(d_rows: Tensor, rows: Tensor, offs: Tensor) -> Tensor:
     bf16 GEMM: cuBLAS / CUTLASS through ``torch._grouped_mm``, or per expert where
     that is not available."""
     try:
-        return torch._grouped_mm(d_rows.t(), rows, offs=offs, out_dtype=torch.float32)
+        res = torch._grouped_mm(d_rows.t(), rows, offs=offs, out_dtype=torch.float32)
+        WGRAD_CALLS["grouped_mm"] += 1
+        return res
     except (RuntimeError, TypeError, AttributeError):
+        WGRAD_CALLS["per_expert"] += 1
         ends = offs.tolist()
         res, start = [], 0
         for end in ends:

@@ -328,6 +328,9 @@ def test_training_end_to_end(moe_pkg):
 
     g_dn = torch.stack([ex.down_proj.weight.grad for ex in moe.experts])
     g_up = torch.stack([ex.up_proj.weight.grad for ex in moe.experts])
+    from importlib import import_module
+
+    print(f"\n[train] weight-gradient calls: {import_module(type(moe).__module__).WGRAD_CALLS}")
     print(f"\n[train] rel err: dW_down {rel(g_dn, w_dn.grad):.2e} dW_router {rel(moe.router.weight.grad, wr.grad):.2e} "
           f"dW_up {rel(g_up, w_up.grad):.2e} dx {rel(x.grad, xr.grad):.2e}")
     # the down projection's weight gradient sees exact bf16 operands: close to fp32
