@@ -373,6 +373,36 @@ def train_step_timing(moe, x, steps: int) -> dict:
             "what": "forward + backward (input, router and expert weight gradients) of the layer"}
 
 
+def cublas_fp4_tflops(pkg, device, n: int = 8192, reps: int = 10) -> float:
+    """Best-of-``reps`` dense NVFP4 GEMM rate of cuBLAS (``F.scaled_mm`` with the reference's
+    recipe: 1x16 E4M3 block scales + fp32 tensor scale) at n^3, in TFLOP/s."""
+    import torch
+    from torch.nn import functional as Fn
+
+    g = torch.Generator(device=device).manual_seed(0)
+    qa, sa, ga = pkg.quantize_nvfp4(torch.randn((n, n), generator=g, device=device).to(torch.bfloat16))
+    qb, sb, gb = pkg.quantize_nvfp4(torch.randn((n, n), generator=g, device=device).to(torch.bfloat16))
+    recipe = [Fn.ScalingType.BlockWise1x16, Fn.ScalingType.TensorWise]
+    swz = [Fn.SwizzleType.SWIZZLE_32_4_4, Fn.SwizzleType.NO_SWIZZLE]
+
+    def mm():
+        return Fn.scaled_mm(qa, qb.t(), scale_a=[sa, ga], scale_recipe_a=recipe, scale_b=[sb, gb],
+                            scale_recipe_b=recipe, swizzle_a=swz, swizzle_b=swz, output_dtype=torch.bfloat16)
+
+    for _ in range(3):
+        mm()
+    torch.cuda.synchronize()
+    best = float("inf")
+    for _ in range(reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        mm()
+        b.record()
+        torch.cuda.synchronize()
+        best = min(best, a.elapsed_time(b))
+    return 2.0 * n ** 3 / (best / 1e3) / 1e12
+
+
 def fp4_peak(args) -> None:
     """cuBLAS dense NVFP4 GEMM (F.scaled_mm with 1x16 E4M3 block scales + fp32 tensor
     scales, the recipe of the reference's nvfp4_mm) at M = N = K = 8192: best of 10
@@ -628,6 +658,15 @@ def run_ours(args) -> None:
         "gpu_launches": (KERNELS_PER_EP_FORWARD if ep else KERNELS_PER_FORWARD) * K,
         "clocks": clocks,
     }
+    if world == 1 and not ep and not decode:
+        # the FP4 counterpart of MEASURED_PEAKS.json's cuBLAS bf16 figure, measured here on this GPU
+        try:
+            with torch.no_grad():
+                cub = cublas_fp4_tflops(pkg, dev)
+            result["roofline"]["cublas_nvfp4_tflops"] = cub
+            result["roofline"]["frac_of_cublas_nvfp4"] = result["roofline"]["achieved"] / cub
+        except Exception as exc:  # a library without the NVFP4 recipe: report, do not fail the bench
+            result["roofline"]["cublas_nvfp4_tflops"] = f"unavailable: {type(exc).__name__}: {exc}"[:200]
     if world == 1 and not ep and not args.no_train:
         result["train"] = train_step_timing(moe, x, max(3, min(K, 10)))
     if rank == 0 and world == 1 and not args.no_reference_gpu:
