@@ -324,6 +324,15 @@ int mcl4moe_quantize_rows_sr(const uint16_t* x, int64_t rows, int cols, uint64_t
                              uint8_t* scales, float* global_scale, float* amax_scratch, mcl4moe_stream_t stream);
 size_t mcl4moe_moe_backward_workspace_size(int T, int d, int E, int k, int F);
 int mcl4moe_moe_backward_experts(const mcl4moe_moe_bwd_args* args, mcl4moe_stream_t stream);
+/* Expert weight gradients: dW[e] = G[rows of e]^T X[rows of e] in fp32 ([E, N, K]) for
+ * bf16 row-major G [rows, N] (d_y or d_up) and X [rows, K] (h or the permuted input
+ * rows), the rows of expert e being [pad_start[e], pad_start[e+1]) (padding rows of G
+ * zero); an expert without rows gets zeros.  Replaces _grouped_wgrad_kernel
+ * (src/mcl4_coe/nvfp4.py:877-920).  Requires N % 128 == 0, K % 256 == 0,
+ * rows % 256 == 0 (the padded row capacity). */
+int mcl4moe_moe_backward_wgrad(const uint16_t* g, const uint16_t* x, int64_t rows, int N, int K,
+                               const int32_t* pad_start, int E, float* dw, int32_t* error_word,
+                               mcl4moe_stream_t stream);
 int mcl4moe_router_backward(const float* logits, const int32_t* topk_idx, const float* topk_w, const float* d_w,
                             const uint8_t* valid, const float* stats, const float* d_aux, const float* d_z, int T,
                             int E, int k, int norm_topk_prob, float* d_logits, mcl4moe_stream_t stream);

@@ -59,6 +59,7 @@ EXPORTS = (
     "mcl4moe_moe_backward_experts",
     "mcl4moe_router_backward",
     "mcl4moe_moe_backward_dx",
+    "mcl4moe_moe_backward_wgrad",
 )
 
 
@@ -231,6 +232,9 @@ def load() -> ctypes.CDLL:
     lib.mcl4moe_router_backward.restype = c_int
     lib.mcl4moe_router_backward.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                             c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p]
+    lib.mcl4moe_moe_backward_wgrad.restype = c_int
+    lib.mcl4moe_moe_backward_wgrad.argtypes = [c_void_p, c_void_p, c_int64, c_int, c_int, c_void_p, c_int, c_void_p,
+                                               c_void_p, c_void_p]
     lib.mcl4moe_moe_backward_dx.restype = c_int
     lib.mcl4moe_moe_backward_dx.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]
     _lib = lib

@@ -17,7 +17,7 @@ HERE = Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
 LIB = HERE / "libmcl4moe.so"
 SOURCES = ["quant.cu", "router.cu", "route.cu", "gemm_fp4.cu", "api.cu", "noalloc.cu", "ep.cu", "peer.cu",
-           "backward.cu"]
+           "backward.cu", "wgrad.cu"]
 HEADERS = ["common.cuh", "kernels.cuh"]
 
 NVCC_FLAGS = [

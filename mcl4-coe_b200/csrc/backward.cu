@@ -590,6 +590,19 @@ int mcl4moe_moe_backward_experts(const mcl4moe_moe_bwd_args* a, mcl4moe_stream_t
                     a->counts, E, a->d_rows, err, s);
 }
 
+int mcl4moe_moe_backward_wgrad(const uint16_t* g, const uint16_t* x, int64_t rows, int N, int K,
+                               const int32_t* pad_start, int E, float* dw, int32_t* error_word,
+                               mcl4moe_stream_t stream) {
+  if (rows < 0 || N <= 0 || K <= 0 || E <= 0 || !pad_start || !dw || (rows > 0 && (!g || !x)))
+    return MCL4MOE_ERR_INVALID;
+  if (N % 128 != 0 || K % 256 != 0 || rows % 256 != 0 || E > kMaxExperts) return MCL4MOE_ERR_UNSUPPORTED;
+  if (!aligned16(g) || !aligned16(x) || !aligned16(dw)) return MCL4MOE_ERR_INVALID;
+  if (rows == 0) return cudaMemsetAsync(dw, 0, sizeof(float) * size_t(E) * N * K, stream) == cudaSuccess
+                            ? MCL4MOE_OK
+                            : MCL4MOE_ERR_CUDA;
+  return launch_wgrad(g, x, rows, N, K, pad_start, E, dw, error_word, stream);
+}
+
 int mcl4moe_router_backward(const float* logits, const int32_t* topk_idx, const float* topk_w, const float* d_w,
                             const uint8_t* valid, const float* stats, const float* d_aux, const float* d_z, int T,
                             int E, int k, int norm_topk_prob, float* d_logits, mcl4moe_stream_t stream) {

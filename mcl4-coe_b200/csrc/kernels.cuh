@@ -246,6 +246,9 @@ int launch_router_bwd(const float* logits, const int32_t* topk_idx, const float*
                       int k, int norm, float* d_logits, cudaStream_t stream);
 int launch_dx_combine(const uint16_t* d_rows, const int32_t* slot_pos, const float* dxr, int T, int k, int d,
                       uint16_t* d_x, cudaStream_t stream);
+// dW[e] = G[seg e]^T X[seg e] (fp32 [E, N, K]) over the padded segments of pad_start (wgrad.cu).
+int launch_wgrad(const uint16_t* g, const uint16_t* x, int64_t rows, int N, int K, const int32_t* pad_start, int E,
+                 float* dw, int32_t* err, cudaStream_t stream);
 
 int num_sms();
 

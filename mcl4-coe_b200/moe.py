@@ -580,28 +580,17 @@ def _region(ws: Tensor, idx: int, nbytes: int, T: int, d: int, E: int, k: int, F
     return ws[off:off + nbytes]
 
 
-# How the expert weight gradients were computed so far (grouped call or per-expert products).
-WGRAD_CALLS = {"grouped_mm": 0, "per_expert": 0}
-
-
-def _weight_grads(d_rows: Tensor, rows: Tensor, offs: Tensor) -> Tensor:
+def _weight_grads(d_rows: Tensor, rows: Tensor, pad_start: Tensor, E: int) -> Tensor:
     """Per-expert ``d_rows[seg]^T @ rows[seg]`` in float32 ([E, N, K]) over the padded
-    expert segments ending at ``offs``: the reference's ``_grouped_wgrad_kernel``
-    (src/mcl4_coe/nvfp4.py:877-920, bf16 operands, fp32 accumulation).  A plain grouped
-    bf16 GEMM: cuBLAS / CUTLASS through ``torch._grouped_mm``, or per expert where
-    that is not available."""
-    try:
-        res = torch._grouped_mm(d_rows.t(), rows, offs=offs, out_dtype=torch.float32)
-        WGRAD_CALLS["grouped_mm"] += 1
-        return res
-    except (RuntimeError, TypeError, AttributeError):
-        WGRAD_CALLS["per_expert"] += 1
-        ends = offs.tolist()
-        res, start = [], 0
-        for end in ends:
-            res.append(d_rows[start:end].t().float() @ rows[start:end].float())
-            start = end
-        return torch.stack(res)
+    expert segments of ``pad_start`` (``mcl4moe_moe_backward_wgrad``: the reference's
+    ``_grouped_wgrad_kernel``, src/mcl4_coe/nvfp4.py:877-920, on tcgen05)."""
+    mcap, n = d_rows.shape
+    k = rows.shape[1]
+    dw = torch.empty((E, n, k), dtype=torch.float32, device=d_rows.device)
+    _lib.check(_lib.load().mcl4moe_moe_backward_wgrad(d_rows.data_ptr(), rows.data_ptr(), mcap, n, k,
+                                                      pad_start.data_ptr(), E, dw.data_ptr(), None, _stream_handle()),
+               "mcl4moe_moe_backward_wgrad")
+    return dw
 
 
 class _MoETrainFunction(torch.autograd.Function):
@@ -614,7 +603,8 @@ class _MoETrainFunction(torch.autograd.Function):
     down-projection output gradients, stochastic-rounded NVFP4 input-gradient GEMMs on
     the transposed weights, SwiGLU derivative), ``mcl4moe_router_backward`` (softmax /
     top-k / renormalisation / aux / z derivative), the router's fp32 matrix products,
-    ``mcl4moe_moe_backward_dx`` and the per-expert weight gradients."""
+    ``mcl4moe_moe_backward_dx`` and the per-expert weight gradients
+    (``mcl4moe_moe_backward_wgrad``)."""
 
     @staticmethod
     def forward(ctx, mod, x, valid, wr_param, *expert_weights):
@@ -722,11 +712,9 @@ class _MoETrainFunction(torch.autograd.Function):
         _lib.check(lib.mcl4moe_moe_backward_dx(d_rows.data_ptr(), slot_pos.data_ptr(), d_x_router.data_ptr(), T, k, d,
                                                d_x.data_ptr(), stream), "mcl4moe_moe_backward_dx")
         # expert weight gradients over the padded segments (padding rows are zero in d_y / d_up)
-        rows = int(pad_start[E].item()) if T > 0 else 0
-        ends = pad_start[1:].contiguous()
-        if rows > 0:
-            dw_dn = _weight_grads(d_y[:rows], h_save[:rows], ends)
-            dw_up = _weight_grads(d_up[:rows], x_rows[:rows], ends)
+        if T > 0:
+            dw_dn = _weight_grads(d_y, h_save, pad_start, E)
+            dw_up = _weight_grads(d_up, x_rows, pad_start, E)
         else:
             dw_dn = torch.zeros((E, d, F), **f32)
             dw_up = torch.zeros((E, 2 * F, d), **f32)

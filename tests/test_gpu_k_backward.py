@@ -328,9 +328,6 @@ def test_training_end_to_end(moe_pkg):
 
     g_dn = torch.stack([ex.down_proj.weight.grad for ex in moe.experts])
     g_up = torch.stack([ex.up_proj.weight.grad for ex in moe.experts])
-    from importlib import import_module
-
-    print(f"\n[train] weight-gradient calls: {import_module(type(moe).__module__).WGRAD_CALLS}")
     print(f"\n[train] rel err: dW_down {rel(g_dn, w_dn.grad):.2e} dW_router {rel(moe.router.weight.grad, wr.grad):.2e} "
           f"dW_up {rel(g_up, w_up.grad):.2e} dx {rel(x.grad, xr.grad):.2e}")
     # the down projection's weight gradient sees exact bf16 operands: close to fp32
@@ -359,3 +356,26 @@ def test_stochastic_rounding_is_unbiased_end_to_end(moe_pkg):
     # independent zero-mean noise: averaging 4 passes halves the spread (1/sqrt(4))
     assert avg4 < 0.65 * single, (avg4, single)
     assert not torch.equal(grads[0], grads[1])  # a new seed per backward call
+
+
+@pytest.mark.parametrize("N,K", [(512, 256), (256, 1024)])
+def test_wgrad_gemm_per_expert_products(moe_pkg, N, K):
+    """mcl4moe_moe_backward_wgrad (tcgen05, MN-major operands) against fp32 products per
+    expert segment, with an empty expert (zeros) and segments of 256 to 1024 rows."""
+    lib = moe_pkg.library()
+    seg = [512, 0, 256, 1024, 256]
+    E = len(seg)
+    pad = torch.tensor([0] + list(np.cumsum(seg)), dtype=torch.int32, device=DEV)
+    rows = int(pad[-1]) + 256  # capacity beyond the last segment is not read
+    g = torch.Generator(device=DEV).manual_seed(21)
+    G = torch.randn((rows, N), generator=g, device=DEV).to(torch.bfloat16)
+    X = torch.randn((rows, K), generator=g, device=DEV).to(torch.bfloat16)
+    dw = torch.full((E, N, K), float("nan"), device=DEV)
+    moe_pkg._lib.check(lib.mcl4moe_moe_backward_wgrad(G.data_ptr(), X.data_ptr(), rows, N, K, pad.data_ptr(), E,
+                                                      dw.data_ptr(), None, torch.cuda.current_stream().cuda_stream),
+                       "wgrad")
+    torch.cuda.synchronize()
+    for e in range(E):
+        a, b = int(pad[e]), int(pad[e + 1])
+        ref = G[a:b].float().t() @ X[a:b].float() if b > a else torch.zeros((N, K), device=DEV)
+        torch.testing.assert_close(dw[e], ref, rtol=1e-4, atol=1e-3)
