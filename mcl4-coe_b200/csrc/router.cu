@@ -247,9 +247,10 @@ __global__ void __launch_bounds__(256) router_split_kernel(const float* __restri
 // ---------------------------------------------------------------- small-batch router
 
 // fp32 logits of a small batch on the CUDA cores: CTA (token block of 8, expert
-// block of 8); warp w owns expert e0 + w, lane l accumulates elements l, l+32, ...
-// of d for the 8 tokens with fp32 fma, then a fixed xor tree sums the lanes
-// (deterministic).  logits[t, e] = sum_k x[t, k] * Wr[e, k] (+ bias[e]).
+// block of 8); warp w owns expert e0 + w, lane l accumulates the 4-element groups
+// 4l, 4l + 128, ... of d for the 8 tokens with fp32 fma (16-byte weight loads, four
+// groups in flight), then a fixed xor tree sums the lanes (deterministic).
+// logits[t, e] = sum_k x[t, k] * Wr[e, k] (+ bias[e]).
 __global__ void __launch_bounds__(256) router_gemv_kernel(const uint16_t* __restrict__ x,
                                                           const float* __restrict__ wr,
                                                           const float* __restrict__ bias, int T, int d, int E,
@@ -269,11 +270,19 @@ __global__ void __launch_bounds__(256) router_gemv_kernel(const uint16_t* __rest
   pdl_trigger();
   if (e >= E) return;
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  const float* wrow = wr + int64_t(e) * d;
-  for (int kk = lane; kk < d; kk += 32) {
-    const float wv = __ldg(wrow + kk);
+  const float4* wrow = reinterpret_cast<const float4*>(wr + int64_t(e) * d);
+  const int groups = d / 4;  // d % 64 == 0
+#pragma unroll 4
+  for (int gq = lane; gq < groups; gq += 32) {
+    const float4 wv = __ldg(wrow + gq);
 #pragma unroll
-    for (int r = 0; r < 8; ++r) acc[r] = __fmaf_rn(bf16_to_f32(xs[r * d + kk]), wv, acc[r]);
+    for (int r = 0; r < 8; ++r) {
+      const uint2 xv = *reinterpret_cast<const uint2*>(xs + r * d + 4 * gq);
+      acc[r] = __fmaf_rn(bf16x2_lo(xv.x), wv.x, acc[r]);
+      acc[r] = __fmaf_rn(bf16x2_hi(xv.x), wv.y, acc[r]);
+      acc[r] = __fmaf_rn(bf16x2_lo(xv.y), wv.z, acc[r]);
+      acc[r] = __fmaf_rn(bf16x2_hi(xv.y), wv.w, acc[r]);
+    }
   }
 #pragma unroll
   for (int r = 0; r < 8; ++r) {
@@ -302,6 +311,12 @@ struct RouterTcArgs {
   float* logits_out;
   float* sel_mask;
   int32_t* err;
+  // one chunk (T <= 128) on the logits path: the tail kernel also lays out the expert
+  // segments and finalises the statistics (route_scan_kernel's work), so no scan launch
+  int fuse_scan;
+  int32_t* counts_out;
+  float* stats;
+  int32_t* offs_out;
 };
 
 template <int EW>
@@ -462,6 +477,49 @@ __global__ void __launch_bounds__(kTcThreads) router_tc_kernel(const __grid_cons
   }
 }
 
+// route_scan_kernel's result for a single chunk, by the chunk's own CTA after its
+// tail: the chunk counts are the expert totals (exclusive prefix 0), the chunk's
+// probability and statistic sums are the totals.  Same arithmetic as the scan.
+__device__ void finish_single_chunk(int E, int k, const RouteWorkspace& ws, int32_t* counts_out, float* stats,
+                                    int32_t* offs_out) {
+  __shared__ int32_t itmp[64];
+  __shared__ float ftmp[32];
+  const int tid = threadIdx.x;
+  int32_t cnt = 0;
+  float ps = 0.f;
+  if (tid < E) {
+    cnt = ws.chunk_excl[tid];
+    ps = ws.part_probs[tid];
+    ws.chunk_excl[tid] = 0;
+    ws.counts[tid] = cnt;
+    ws.probs_sum[tid] = ps;
+  }
+  const float lse2 = ws.part_misc[0], n = ws.part_misc[1];
+  int32_t ignore;
+  const int32_t ustart = block_exclusive_scan(cnt, itmp, ignore);
+  const int32_t padded = (cnt + kSegRows - 1) / kSegRows * kSegRows;
+  const int32_t pstart = block_exclusive_scan(padded, itmp, ignore);
+  float term = 0.f;
+  if (tid < E) {
+    ws.offs_start[tid] = ustart;
+    ws.pad_start[tid] = pstart;
+    if (tid == E - 1) ws.pad_start[E] = pstart + padded;
+    if (offs_out) offs_out[tid] = ustart + cnt;
+    if (counts_out) counts_out[tid] = cnt;
+    if (stats) {
+      const float cf = n > 0.f ? __fdiv_rn(float(cnt), n * float(k)) : 0.f;
+      stats[3 + tid] = cf;
+      term = n > 0.f ? __fmul_rn(cf, __fdiv_rn(ps, n)) : 0.f;
+    }
+  }
+  const float aux = block_sum(term, ftmp);
+  if (tid == 0 && stats) {
+    stats[0] = n > 0.f ? __fmul_rn(float(E), aux) : 0.f;
+    stats[1] = n > 0.f ? __fdiv_rn(lse2, n) : 0.f;
+    stats[2] = n;
+  }
+}
+
 // Router tail on given logits (parity checks against recorded reference logits).
 template <int EW>
 __global__ void __launch_bounds__(kTailThreads) router_logits_kernel(const float* __restrict__ logits_in,
@@ -482,6 +540,10 @@ __global__ void __launch_bounds__(kTailThreads) router_logits_kernel(const float
   __syncthreads();
   route_tail<EW>(s, threadIdx.x, chunk, a.T, a.E, a.k, a.norm_topk, a.valid, a.topk_idx, a.topk_w, a.logits_out,
                  a.sel_mask, ws, BlockSync());
+  if (a.fuse_scan) {
+    __syncthreads();  // the tail's chunk counts and sums (global memory of this block) are complete
+    finish_single_chunk(a.E, a.k, ws, a.counts_out, a.stats, a.offs_out);
+  }
 }
 
 // ---------------------------------------------------------------- scan
@@ -737,11 +799,18 @@ int launch_route(const uint16_t* x, const float* wr, const float* bias, const fl
       logits_in = ws.small_logits;  // final logits: the tail below adds no bias
     }
     int st;
+    if (logits_in != nullptr && T <= kRouteTokens) {  // one chunk: the tail kernel finishes the scan
+      a.fuse_scan = 1;
+      a.counts_out = counts_out;
+      a.stats = stats;
+      a.offs_out = offs_out;
+    }
     if (E <= 32) st = launch_router_t<1>(x, wr, bias, logits_in, a, ws, stream);
     else if (E <= 64) st = launch_router_t<2>(x, wr, bias, logits_in, a, ws, stream);
     else if (E <= 128) st = launch_router_t<4>(x, wr, bias, logits_in, a, ws, stream);
     else st = launch_router_t<8>(x, wr, bias, logits_in, a, ws, stream);
     if (st != MCL4MOE_OK) return st;
+    if (a.fuse_scan) return cudaGetLastError() == cudaSuccess ? MCL4MOE_OK : MCL4MOE_ERR_CUDA;
   } else if (cudaMemsetAsync(ws.done, 0, sizeof(uint32_t), stream) != cudaSuccess) {
     return MCL4MOE_ERR_CUDA;  // no router CTA ran: reset the finished-expert counter here
   }
