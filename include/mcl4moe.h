@@ -92,6 +92,51 @@ int mcl4moe_nvfp4_mm(const void* x, int dtype, int64_t M, int K, int causal, con
                      int32_t* error_word, void* workspace, size_t workspace_bytes, mcl4moe_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Stochastic rounding in the single-matrix operators (quantize_nvfp4 with
+ * stochastic=True, nvfp4_mm with stochastic_a=True, src/mcl4_coe/nvfp4.py:186-194,
+ * :285-334), as _NVFP4Linear.backward uses them (:431-472).  Codes are
+ * min(trunc(u + U), 7) with u the scaled magnitude of the deterministic rule and
+ * U in [0, 1) a Philox4x32-10 draw keyed by `seed` at offset row * cols + col
+ * (the reference draws U with torch.rand_like: same distribution, different
+ * stream).  Scales and global scales are those of the round-to-nearest mode.
+ *
+ * mcl4moe_quantize_rows_stochastic: mcl4moe_quantize_rows with stochastic codes.
+ * mcl4moe_nvfp4_mm_sr: mcl4moe_nvfp4_mm with A quantised stochastically (the
+ *   input gradient, grad_output x W: B = the weight's transposed 16x16-tile
+ *   quantisation, mcl4moe_quantize_weights_t with n = 1).
+ * mcl4moe_nvfp4_linear_wgrad: the weight gradient
+ *   dW = nvfp4_mm(H16(G^T), H16(X^T), stochastic_a=True)  (:454-459)
+ *   for grad_output G [M, N] and inputs X [M, K] (row-major, bf16 dtype 0 or
+ *   fp32 dtype 1), H16 the fixed-sign orthonormal Walsh-Hadamard transform over
+ *   groups of 16 tokens (_hadamard16, :337-355): H16(G^T) quantised
+ *   stochastically (noise offset n * round_up(M, 256) + token), H16(X^T) to
+ *   nearest, each with its tensor-wise global scale.  dw: fp32
+ *   [N, round_up(K, 256)] (columns >= K are zero); d_bias (fp32 [N] or NULL):
+ *   the column sums of G (:468-469).  M == 0 gives zeros.
+ * ------------------------------------------------------------------------ */
+int mcl4moe_quantize_rows_stochastic(const void* x, int dtype, int64_t rows, int cols, int64_t ld, int causal,
+                                     uint64_t seed, uint8_t* packed, uint8_t* scales, int64_t rows_pad,
+                                     float* global_scale, float* amax_scratch, mcl4moe_stream_t stream);
+int mcl4moe_nvfp4_mm_sr(const void* x, int dtype, int64_t M, int K, int causal, uint64_t seed, const uint8_t* b,
+                        const uint8_t* b_scales, const float* b_g, int N, const float* bias, float* out,
+                        float* a_global_scale, int32_t* error_word, void* workspace, size_t workspace_bytes,
+                        mcl4moe_stream_t stream);
+/* mcl4moe_quantize_hadamard_t: one operand of that product on its own,
+ * quantize_nvfp4(_hadamard16(y.t()), stochastic) for y [M, C] (row-major, bf16
+ * dtype 0 or fp32 dtype 1) with the token dimension zero-padded to kt
+ * (multiple of 128, >= M) and the rows to rows_out (multiple of 32, >= C; of 128
+ * when swizzled): packed [rows_out, kt/2], scales row-major [rows_out, kt/16] or
+ * the swizzled 128x4 atoms, global_scale = max(amax/2688 or 1, FLT_MIN) of the
+ * transformed matrix (device fp32 [1]); amax_scratch device fp32 [1]. */
+int mcl4moe_quantize_hadamard_t(const void* y, int dtype, int64_t M, int C, int64_t kt, int rows_out, int stochastic,
+                                uint64_t seed, uint8_t* packed, uint8_t* scales, int swizzled, float* global_scale,
+                                float* amax_scratch, mcl4moe_stream_t stream);
+size_t mcl4moe_nvfp4_linear_wgrad_workspace_size(int64_t M, int N, int K);
+int mcl4moe_nvfp4_linear_wgrad(const void* grad, int grad_dtype, const void* x, int x_dtype, int64_t M, int N, int K,
+                               uint64_t seed, float* dw, float* d_bias, int32_t* error_word, void* workspace,
+                               size_t workspace_bytes, mcl4moe_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Replaces compute_2to4_mask (src/mcl4_coe/nvfp4.py:70-110), applied to a
  * weight before its NVFP4 quantisation when a layer's sparsity_mode is not
  * "none" (:1020-1023).  W fp32 [N, K] row-major; mode 1 = "2to4_row" (keep the

@@ -60,6 +60,11 @@ EXPORTS = (
     "mcl4moe_router_backward",
     "mcl4moe_moe_backward_dx",
     "mcl4moe_moe_backward_wgrad",
+    "mcl4moe_quantize_rows_stochastic",
+    "mcl4moe_nvfp4_mm_sr",
+    "mcl4moe_quantize_hadamard_t",
+    "mcl4moe_nvfp4_linear_wgrad_workspace_size",
+    "mcl4moe_nvfp4_linear_wgrad",
 )
 
 
@@ -235,6 +240,22 @@ def load() -> ctypes.CDLL:
     lib.mcl4moe_moe_backward_wgrad.restype = c_int
     lib.mcl4moe_moe_backward_wgrad.argtypes = [c_void_p, c_void_p, c_int64, c_int, c_int, c_void_p, c_int, c_void_p,
                                                c_void_p, c_void_p]
+    lib.mcl4moe_quantize_rows_stochastic.restype = c_int
+    lib.mcl4moe_quantize_rows_stochastic.argtypes = [c_void_p, c_int, c_int64, c_int, c_int64, c_int, ctypes.c_uint64,
+                                                     c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p]
+    lib.mcl4moe_nvfp4_mm_sr.restype = c_int
+    lib.mcl4moe_nvfp4_mm_sr.argtypes = [c_void_p, c_int, c_int64, c_int, c_int, ctypes.c_uint64, c_void_p, c_void_p,
+                                        c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
+                                        c_void_p]
+    lib.mcl4moe_quantize_hadamard_t.restype = c_int
+    lib.mcl4moe_quantize_hadamard_t.argtypes = [c_void_p, c_int, c_int64, c_int, c_int64, c_int, c_int, ctypes.c_uint64,
+                                                c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p]
+    lib.mcl4moe_nvfp4_linear_wgrad_workspace_size.restype = c_size_t
+    lib.mcl4moe_nvfp4_linear_wgrad_workspace_size.argtypes = [c_int64, c_int, c_int]
+    lib.mcl4moe_nvfp4_linear_wgrad.restype = c_int
+    lib.mcl4moe_nvfp4_linear_wgrad.argtypes = [c_void_p, c_int, c_void_p, c_int, c_int64, c_int, c_int,
+                                               ctypes.c_uint64, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
+                                               c_void_p]
     lib.mcl4moe_moe_backward_dx.restype = c_int
     lib.mcl4moe_moe_backward_dx.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]
     _lib = lib

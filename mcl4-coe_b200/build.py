@@ -17,8 +17,8 @@ HERE = Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
 LIB = HERE / "libmcl4moe.so"
 SOURCES = ["quant.cu", "router.cu", "route.cu", "gemm_fp4.cu", "api.cu", "noalloc.cu", "ep.cu", "peer.cu",
-           "backward.cu", "wgrad.cu"]
-HEADERS = ["common.cuh", "kernels.cuh"]
+           "backward.cu", "wgrad.cu", "linear_bwd.cu"]
+HEADERS = ["common.cuh", "kernels.cuh", "sr.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -156,6 +156,19 @@ int mcl4moe_quantize_rows(const void* x, int dtype, int64_t rows, int cols, int6
                               nullptr, nullptr, 0, stream);
 }
 
+int mcl4moe_quantize_rows_stochastic(const void* x, int dtype, int64_t rows, int cols, int64_t ld, int causal,
+                                     uint64_t seed, uint8_t* packed, uint8_t* scales, int64_t rows_pad,
+                                     float* global_scale, float* amax_scratch, mcl4moe_stream_t stream) {
+  if (rows < 0 || cols <= 0 || (dtype != 0 && dtype != 1) || !packed || !scales || !global_scale || !amax_scratch)
+    return MCL4MOE_ERR_INVALID;
+  if (cols % 16 != 0) return MCL4MOE_ERR_INVALID;
+  if (cols % 64 != 0) return MCL4MOE_ERR_UNSUPPORTED;
+  if (rows_pad < rows || rows_pad % 128 != 0 || ld < cols || (rows > 0 && !x)) return MCL4MOE_ERR_INVALID;
+  if (!aligned16(x) || (ld * (dtype == 0 ? 2 : 4)) % 16 != 0) return MCL4MOE_ERR_INVALID;
+  return launch_quantize_rows(x, dtype, rows, cols, ld, causal, packed, scales, rows_pad, global_scale, amax_scratch,
+                              nullptr, nullptr, 0, stream, 1, seed);
+}
+
 }  // extern "C"
 
 namespace {
@@ -205,9 +218,15 @@ size_t mcl4moe_nvfp4_mm_workspace_size(int64_t M, int K) {
   return mm_workspace(nullptr, M, K).bytes;
 }
 
-int mcl4moe_nvfp4_mm(const void* x, int dtype, int64_t M, int K, int causal, const uint8_t* b, const uint8_t* b_scales,
-                     const float* b_g, int N, const float* bias, float* out, float* a_global_scale,
-                     int32_t* error_word, void* workspace, size_t workspace_bytes, mcl4moe_stream_t stream) {
+}  // extern "C"
+
+namespace {
+
+// nvfp4_mm with A quantised here (round to nearest, or stochastic with `seed`).
+int nvfp4_mm_impl(const void* x, int dtype, int64_t M, int K, int causal, int stochastic, uint64_t seed,
+                  const uint8_t* b, const uint8_t* b_scales, const float* b_g, int N, const float* bias, float* out,
+                  float* a_global_scale, int32_t* error_word, void* workspace, size_t workspace_bytes,
+                  cudaStream_t stream) {
   if (M < 0 || K <= 0 || N <= 0 || (dtype != 0 && dtype != 1) || !b || !b_scales || !b_g || !out || !workspace)
     return MCL4MOE_ERR_INVALID;
   if (M > 0 && !x) return MCL4MOE_ERR_INVALID;
@@ -221,7 +240,8 @@ int mcl4moe_nvfp4_mm(const void* x, int dtype, int64_t M, int K, int causal, con
   cudaStream_t s = stream;
   int32_t* err = error_word ? error_word : w.err;
   if (!error_word && cudaMemsetAsync(err, 0, sizeof(int32_t), s) != cudaSuccess) return MCL4MOE_ERR_CUDA;
-  int st = launch_quantize_rows(x, dtype, M, K, K, causal, w.aq, w.as, mp, w.g_a, w.amax, b_g, w.g_ab, 1, s);
+  int st = launch_quantize_rows(x, dtype, M, K, K, causal, w.aq, w.as, mp, w.g_a, w.amax, b_g, w.g_ab, 1, s,
+                                stochastic, seed);
   if (st != MCL4MOE_OK) return st;
   if (a_global_scale && cudaMemcpyAsync(a_global_scale, w.g_a, sizeof(float), cudaMemcpyDeviceToDevice, s) !=
                             cudaSuccess)
@@ -245,6 +265,25 @@ int mcl4moe_nvfp4_mm(const void* x, int dtype, int64_t M, int K, int causal, con
   g.ldy = N;
   g.err = err;
   return launch_grouped_gemm(w.aq, mp, b, g, s);
+}
+
+}  // namespace
+
+extern "C" {
+
+int mcl4moe_nvfp4_mm(const void* x, int dtype, int64_t M, int K, int causal, const uint8_t* b, const uint8_t* b_scales,
+                     const float* b_g, int N, const float* bias, float* out, float* a_global_scale,
+                     int32_t* error_word, void* workspace, size_t workspace_bytes, mcl4moe_stream_t stream) {
+  return nvfp4_mm_impl(x, dtype, M, K, causal, 0, 0, b, b_scales, b_g, N, bias, out, a_global_scale, error_word,
+                       workspace, workspace_bytes, stream);
+}
+
+int mcl4moe_nvfp4_mm_sr(const void* x, int dtype, int64_t M, int K, int causal, uint64_t seed, const uint8_t* b,
+                        const uint8_t* b_scales, const float* b_g, int N, const float* bias, float* out,
+                        float* a_global_scale, int32_t* error_word, void* workspace, size_t workspace_bytes,
+                        mcl4moe_stream_t stream) {
+  return nvfp4_mm_impl(x, dtype, M, K, causal, 1, seed, b, b_scales, b_g, N, bias, out, a_global_scale, error_word,
+                       workspace, workspace_bytes, stream);
 }
 
 int mcl4moe_quantize_activations(const uint16_t* x, int64_t rows, int cols, int64_t ld_x, uint8_t* packed,

@@ -16,35 +16,11 @@
 // the noise of a row uses its index in the reference's unpadded layout
 // (offs_start[e] + local), so the stochastic codes are the reference's.
 #include "kernels.cuh"
+#include "sr.cuh"
 
 namespace mcl4 {
 
 namespace {
-
-// Word 0 of Philox4x32-10 (Salmon, Moraes, Dror, Shaw, "Parallel random numbers:
-// as easy as 1, 2, 3", SC'11) for counter (c0, 0, 0, 0) and key (k0, k1): the
-// draw of Triton's tl.randint(seed, offset) for a 32-bit offset.
-__device__ __forceinline__ uint32_t philox_word0(uint32_t c0, uint32_t k0, uint32_t k1) {
-  uint32_t c1 = 0u, c2 = 0u, c3 = 0u;
-#pragma unroll
-  for (int r = 0; r < 10; ++r) {
-    const uint32_t p0 = c0, p2 = c2;
-    c0 = __umulhi(0xCD9E8D57u, p2) ^ c1 ^ k0;
-    c2 = __umulhi(0xD2511F53u, p0) ^ c3 ^ k1;
-    c1 = 0xCD9E8D57u * p2;
-    c3 = 0xD2511F53u * p0;
-    k0 += 0x9E3779B9u;
-    k1 += 0xBB67AE85u;
-  }
-  return c0;
-}
-
-// Triton's uint_to_uniform_float for 32-bit words: int32 x, x < 0 ? -x - 1 : x,
-// times 4.6566127342e-10 in float32.
-__device__ __forceinline__ float uniform_from_word(uint32_t w) {
-  const int32_t x = int32_t((w & 0x80000000u) ? ~w : w);
-  return __fmul_rn(__int2float_rn(x), 4.6566127342e-10f);
-}
 
 // One 16-element block of bf16 values (8 packed words) quantised with stochastic
 // rounding: scale byte returned, 8 packed bytes written.  off0: noise offset of

@@ -161,10 +161,11 @@ int launch_quantize_weights(const float* const* w_ptrs, const int32_t* slots, in
 // matrix with global scale g = 1 (causal) or amax/2688; packed [rows, cols/2],
 // scales for rows_pad rows (padding rows zero) in the 128x4 swizzled atoms or,
 // with rowmajor, [rows_pad, cols/16]; g written to *g; with g_b, *g_ab = g * *g_b.
-// amax: device scratch float.  cols % 64 == 0.
+// amax: device scratch float.  cols % 64 == 0.  stochastic: stochastic rounding with
+// noise seed `seed` (offsets row * cols + col).
 int launch_quantize_rows(const void* x, int dtype, int64_t rows, int cols, int64_t ld, int causal, uint8_t* packed,
                          uint8_t* scales, int64_t rows_pad, float* g, float* amax, const float* g_b, float* g_ab,
-                         int rowmajor, cudaStream_t s);
+                         int rowmajor, cudaStream_t s, int stochastic = 0, uint64_t seed = 0);
 
 // pad_start = {0, rows_pad}, counts = {rows}, offs_start = {0}: one GEMM segment.
 int launch_single_segment(int64_t rows, int64_t rows_pad, int32_t* pad_start, int32_t* counts, int32_t* offs_start,

@@ -10,6 +10,7 @@
 #include <algorithm>
 
 #include "kernels.cuh"
+#include "sr.cuh"
 
 namespace mcl4 {
 
@@ -282,11 +283,14 @@ __global__ void rows_global_scale_kernel(const float* amax, int causal, float* g
 // One warp per row, lane l takes 16-element blocks l, l+32, ...: scale
 // e4m3(min(amax16 / (6 g), 448)), inverse 1 / (scale * g), E2M1 codes of x * inverse
 // (src/mcl4_coe/nvfp4.py:209-225, one-dimensional mode); scales into the swizzled atoms
-// (the reference's output layout) or row-major (the GEMM's A operand).
-template <typename InT>
+// (the reference's output layout) or row-major (the GEMM's A operand).  SR: stochastic
+// rounding (the gradient quantisation of the backward), noise of element (row, col) the
+// Philox draw at offset row * cols + col (32-bit wrap) under key (k0, k1).
+template <typename InT, bool SR>
 __global__ void __launch_bounds__(256) rows_quant_kernel(const InT* __restrict__ x, int64_t rows, int cols, int64_t ld,
                                                          const float* __restrict__ g_ptr, uint8_t* __restrict__ packed,
-                                                         uint8_t* __restrict__ scales, int rowmajor) {
+                                                         uint8_t* __restrict__ scales, int rowmajor, uint32_t k0,
+                                                         uint32_t k1) {
   const int lane = threadIdx.x & 31;
   const int64_t row = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -302,10 +306,19 @@ __global__ void __launch_bounds__(256) rows_quant_kernel(const InT* __restrict__
     const uint32_t sc = f32_to_e4m3(fminf(__fdiv_rn(m, six_g), 448.0f));
     const float inv = inverse_decoding(__fmul_rn(e4m3_to_f32(sc), g));
     uint32_t lo = 0, hi = 0;
+    if constexpr (SR) {
+      const uint32_t off0 = uint32_t(uint64_t(row) * uint64_t(cols)) + uint32_t(b * 16);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      lo |= e2m1_code(__fmul_rn(v[j], inv)) << (4 * j);
-      hi |= e2m1_code(__fmul_rn(v[8 + j], inv)) << (4 * j);
+      for (int j = 0; j < 8; ++j) {
+        lo |= e2m1_code_sr(__fmul_rn(v[j], inv), sr_uniform(off0 + j, k0, k1)) << (4 * j);
+        hi |= e2m1_code_sr(__fmul_rn(v[8 + j], inv), sr_uniform(off0 + 8 + j, k0, k1)) << (4 * j);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        lo |= e2m1_code(__fmul_rn(v[j], inv)) << (4 * j);
+        hi |= e2m1_code(__fmul_rn(v[8 + j], inv)) << (4 * j);
+      }
     }
     *reinterpret_cast<uint2*>(packed + row * (cols / 2) + b * 8) = make_uint2(lo, hi);
     scales[rowmajor ? rowmajor_scale_offset(uint64_t(row), uint32_t(b), uint32_t(nblk))
@@ -326,7 +339,7 @@ __global__ void single_segment_kernel(int64_t rows, int64_t rows_pad, int32_t* p
 
 int launch_quantize_rows(const void* x, int dtype, int64_t rows, int cols, int64_t ld, int causal, uint8_t* packed,
                          uint8_t* scales, int64_t rows_pad, float* g, float* amax, const float* g_b, float* g_ab,
-                         int rowmajor, cudaStream_t s) {
+                         int rowmajor, cudaStream_t s, int stochastic, uint64_t seed) {
   const size_t scale_bytes = size_t(rows_pad) * size_t(cols / 16);
   if (cudaMemsetAsync(scales, 0, scale_bytes, s) != cudaSuccess) return MCL4MOE_ERR_CUDA;
   if (!causal) {
@@ -343,12 +356,17 @@ int launch_quantize_rows(const void* x, int dtype, int64_t rows, int cols, int64
   rows_global_scale_kernel<<<1, 32, 0, s>>>(amax, causal, g, g_b, g_ab);
   if (rows > 0) {
     const unsigned blocks = unsigned((rows + 7) / 8);
-    if (dtype == 0)
-      rows_quant_kernel<uint16_t><<<blocks, 256, 0, s>>>(static_cast<const uint16_t*>(x), rows, cols, ld, g, packed,
-                                                        scales, rowmajor);
+    const uint32_t k0 = uint32_t(seed), k1 = uint32_t(seed >> 32);
+    const uint16_t* xh = static_cast<const uint16_t*>(x);
+    const float* xf = static_cast<const float*>(x);
+    if (dtype == 0 && stochastic)
+      rows_quant_kernel<uint16_t, true><<<blocks, 256, 0, s>>>(xh, rows, cols, ld, g, packed, scales, rowmajor, k0, k1);
+    else if (dtype == 0)
+      rows_quant_kernel<uint16_t, false><<<blocks, 256, 0, s>>>(xh, rows, cols, ld, g, packed, scales, rowmajor, k0, k1);
+    else if (stochastic)
+      rows_quant_kernel<float, true><<<blocks, 256, 0, s>>>(xf, rows, cols, ld, g, packed, scales, rowmajor, k0, k1);
     else
-      rows_quant_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float*>(x), rows, cols, ld, g, packed, scales,
-                                                     rowmajor);
+      rows_quant_kernel<float, false><<<blocks, 256, 0, s>>>(xf, rows, cols, ld, g, packed, scales, rowmajor, k0, k1);
   }
   return cudaGetLastError() == cudaSuccess ? MCL4MOE_OK : MCL4MOE_ERR_CUDA;
 }

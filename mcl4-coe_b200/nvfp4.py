@@ -399,6 +399,13 @@ def _round_up(value: int, multiple: int) -> int:
 _FP4_DTYPE = getattr(torch, "float4_e2m1fn_x2", torch.uint8)
 
 
+def _noise_seed() -> int:
+    """31-bit stochastic-rounding seed from torch's default CPU generator, so
+    ``torch.manual_seed`` makes the rounding noise reproducible as it does for the
+    reference's ``torch.rand_like`` draws."""
+    return int(torch.randint(0, 2 ** 31 - 1, (1,)).item())
+
+
 @torch.no_grad()
 def quantize_nvfp4(matrix: Tensor, *, two_dimensional: bool = False, stochastic: bool = False,
                    causal_row_scale: bool = False) -> tuple[Tensor, Tensor, Tensor]:
@@ -406,15 +413,18 @@ def quantize_nvfp4(matrix: Tensor, *, two_dimensional: bool = False, stochastic:
     C/16 rounded to 4], the 128x4-atom layout) and fp32 global scale [1]
     (src/mcl4_coe/nvfp4.py:235-259): one-dimensional 1x16 blocks with g = amax/2688, or
     g = 1 when ``causal_row_scale``; ``two_dimensional``: 16x16 tiles with g = amax/2688.
-    Stochastic rounding (the backward's gradient quantisation) is not served."""
+    ``stochastic`` (one-dimensional): codes min(trunc(u + U), 7) with U uniform in [0, 1)
+    from Philox4x32-10 under a seed drawn from torch's default generator (the reference
+    draws U with ``torch.rand_like``); two-dimensional stochastic rounding, which no
+    reference caller uses, raises NotImplementedError."""
     if matrix.ndim != 2 or not matrix.is_floating_point() or matrix.numel() == 0:
         raise ValueError("NVFP4 quantization requires a nonempty floating-point matrix")
     _require_cuda(matrix, "NVFP4 quantization")
     rows, cols = matrix.shape
     if cols % 16 or (two_dimensional and rows % 16):
         raise ValueError("NVFP4 blocks require aligned dimensions divisible by 16")
-    if stochastic:
-        raise NotImplementedError("stochastic NVFP4 rounding (backward only) is not served by the B200 path")
+    if stochastic and two_dimensional:
+        raise NotImplementedError("two-dimensional stochastic NVFP4 rounding is not served by the B200 path")
     dev = matrix.device
     cp = _round_up(cols, 64)  # scale columns padded to whole 4-column atoms, as _swizzle_scales pads them
     if two_dimensional:
@@ -436,9 +446,16 @@ def quantize_nvfp4(matrix: Tensor, *, two_dimensional: bool = False, stochastic:
     scales = torch.empty((rp, cp // 16), dtype=torch.uint8, device=dev)
     g = torch.empty((1,), dtype=torch.float32, device=dev)
     amax = torch.empty((1,), dtype=torch.float32, device=dev)
-    _lib.check(_lib.load().mcl4moe_quantize_rows(x.data_ptr(), dtype, rows, cp, cp, int(bool(causal_row_scale)),
-                                                 packed.data_ptr(), scales.data_ptr(), rp, g.data_ptr(),
-                                                 amax.data_ptr(), _stream_handle()), "mcl4moe_quantize_rows")
+    lib = _lib.load()
+    if stochastic:
+        _lib.check(lib.mcl4moe_quantize_rows_stochastic(x.data_ptr(), dtype, rows, cp, cp, int(bool(causal_row_scale)),
+                                                        _noise_seed(), packed.data_ptr(), scales.data_ptr(), rp,
+                                                        g.data_ptr(), amax.data_ptr(), _stream_handle()),
+                   "mcl4moe_quantize_rows_stochastic")
+    else:
+        _lib.check(lib.mcl4moe_quantize_rows(x.data_ptr(), dtype, rows, cp, cp, int(bool(causal_row_scale)),
+                                             packed.data_ptr(), scales.data_ptr(), rp, g.data_ptr(), amax.data_ptr(),
+                                             _stream_handle()), "mcl4moe_quantize_rows")
     return packed[:, : cols // 2].contiguous().view(_FP4_DTYPE), scales.view(torch.float8_e4m3fn), g
 
 
@@ -460,9 +477,9 @@ def _relayout_operand(packed: Tensor, scales: Tensor, rows: int, cols: int, rows
 
 
 def _mm_prepared(a: Tensor, b_packed: Tensor, b_scales: Tensor, b_g: Tensor, n_pad: int, k_pad: int,
-                 causal_a: bool, bias: Tensor | None) -> Tensor:
+                 causal_a: bool, bias: Tensor | None, stochastic_a: bool = False) -> Tensor:
     """fp32 [M, n_pad] = deq(A) deq(B)^T g_a g_b (+ bias) on the kernels; B already in the
-    kernel layout for [n_pad, k_pad]."""
+    kernel layout for [n_pad, k_pad]; A rounded stochastically with ``stochastic_a``."""
     m, k = a.shape
     dtype = 0 if a.dtype == torch.bfloat16 else 1
     x = a.detach().contiguous() if dtype == 0 else a.detach().to(torch.float32).contiguous()
@@ -471,9 +488,15 @@ def _mm_prepared(a: Tensor, b_packed: Tensor, b_scales: Tensor, b_g: Tensor, n_p
     lib = _lib.load()
     out = torch.empty((m, n_pad), dtype=torch.float32, device=a.device)
     ws = torch.empty((max(lib.mcl4moe_nvfp4_mm_workspace_size(m, k_pad), 256),), dtype=torch.uint8, device=a.device)
-    _lib.check(lib.mcl4moe_nvfp4_mm(x.data_ptr(), dtype, m, k_pad, int(bool(causal_a)), b_packed.data_ptr(),
-                                    b_scales.data_ptr(), b_g.data_ptr(), n_pad, _ptr(bias), out.data_ptr(), None, None,
-                                    ws.data_ptr(), ws.numel(), _stream_handle()), "mcl4moe_nvfp4_mm")
+    if stochastic_a:
+        _lib.check(lib.mcl4moe_nvfp4_mm_sr(x.data_ptr(), dtype, m, k_pad, int(bool(causal_a)), _noise_seed(),
+                                           b_packed.data_ptr(), b_scales.data_ptr(), b_g.data_ptr(), n_pad, _ptr(bias),
+                                           out.data_ptr(), None, None, ws.data_ptr(), ws.numel(), _stream_handle()),
+                   "mcl4moe_nvfp4_mm_sr")
+    else:
+        _lib.check(lib.mcl4moe_nvfp4_mm(x.data_ptr(), dtype, m, k_pad, int(bool(causal_a)), b_packed.data_ptr(),
+                                        b_scales.data_ptr(), b_g.data_ptr(), n_pad, _ptr(bias), out.data_ptr(), None,
+                                        None, ws.data_ptr(), ws.numel(), _stream_handle()), "mcl4moe_nvfp4_mm")
     return out
 
 
@@ -484,8 +507,9 @@ def nvfp4_mm(a: Tensor, b: Tensor, *, weight_b: bool = False, stochastic_a: bool
     """``a @ b.T`` in NVFP4, fp32 result [M, N] (src/mcl4_coe/nvfp4.py:285-334): A quantised
     one-dimensionally (g = 1 with ``causal_a``), B two-dimensionally with ``weight_b`` (else
     one-dimensionally), or ``prequantized_b`` = (packed, swizzled scales, g) as
-    :func:`quantize_nvfp4` returns them for ``b`` padded to multiples of 32.  Runs on the
-    tcgen05 block-scaled GEMM with K and N padded to 256."""
+    :func:`quantize_nvfp4` returns them for ``b`` padded to multiples of 32.
+    ``stochastic_a`` / ``stochastic_b``: stochastic rounding of that operand (one-dimensional
+    only for B).  Runs on the tcgen05 block-scaled GEMM with K and N padded to 256."""
     if a.ndim != 2 or b.ndim != 2 or a.shape[1] != b.shape[1]:
         raise ValueError("NVFP4 matmul expects a[M,K] and b[N,K]")
     if a.device != b.device or a.device.type != "cuda":
@@ -494,8 +518,8 @@ def nvfp4_mm(a: Tensor, b: Tensor, *, weight_b: bool = False, stochastic_a: bool
     n = b.shape[0]
     if min(m, n, k) == 0:
         raise ValueError("NVFP4 matmul requires nonempty operands")
-    if stochastic_a or stochastic_b:
-        raise NotImplementedError("stochastic NVFP4 rounding (backward only) is not served by the B200 path")
+    if stochastic_b and weight_b and prequantized_b is None:
+        raise NotImplementedError("two-dimensional stochastic NVFP4 rounding is not served by the B200 path")
     kp, np_ = _round_up(k, 256), _round_up(n, 256)
     if prequantized_b is not None:
         qb, sb, gb = prequantized_b
@@ -506,10 +530,84 @@ def nvfp4_mm(a: Tensor, b: Tensor, *, weight_b: bool = False, stochastic_a: bool
         bp = b.detach()
         if kp != k or np_ != n:
             bp = torch.nn.functional.pad(bp.to(torch.float32 if weight_b else bp.dtype), (0, kp - k, 0, np_ - n))
-        qb, sb, gb = quantize_nvfp4(bp, two_dimensional=weight_b)
+        qb, sb, gb = quantize_nvfp4(bp, two_dimensional=weight_b, stochastic=stochastic_b)
         pk, sw = qb.view(torch.uint8), sb.view(torch.uint8).reshape(-1)
     _GEMM_COUNTS[_phase] = _GEMM_COUNTS.get(_phase, 0) + 1
-    return _mm_prepared(a, pk, sw, gb.to(torch.float32).reshape(1), np_, kp, causal_a, None)[:, :n]
+    return _mm_prepared(a, pk, sw, gb.to(torch.float32).reshape(1), np_, kp, causal_a, None,
+                        stochastic_a=stochastic_a)[:, :n]
+
+
+def _linear_weight_grad(gradient: Tensor, inputs: Tensor, with_bias: bool) -> tuple[Tensor, Tensor | None]:
+    """fp32 [N, K] ``nvfp4_mm(_hadamard16(gradient.t()), _hadamard16(inputs.t()),
+    stochastic_a=True)`` and, with ``with_bias``, the fp32 column sums of ``gradient``
+    (src/mcl4_coe/nvfp4.py:454-459, :468-469), on mcl4moe_nvfp4_linear_wgrad."""
+    m, n = gradient.shape
+    k = inputs.shape[1]
+    dev = gradient.device
+
+    def operand(t: Tensor) -> tuple[Tensor, int]:
+        if t.dtype == torch.bfloat16:
+            return t.contiguous(), 0
+        return t.to(torch.float32).contiguous(), 1
+
+    g, gdt = operand(gradient.detach())
+    x, xdt = operand(inputs.detach())
+    kp = _round_up(k, 256)
+    lib = _lib.load()
+    dw = torch.empty((n, kp), dtype=torch.float32, device=dev)
+    db = torch.empty((n,), dtype=torch.float32, device=dev) if with_bias else None
+    ws = torch.empty((max(lib.mcl4moe_nvfp4_linear_wgrad_workspace_size(m, n, k), 256),), dtype=torch.uint8,
+                     device=dev)
+    _lib.check(lib.mcl4moe_nvfp4_linear_wgrad(g.data_ptr(), gdt, x.data_ptr(), xdt, m, n, k, _noise_seed(),
+                                              dw.data_ptr(), _ptr(db), None, ws.data_ptr(), ws.numel(),
+                                              _stream_handle()), "mcl4moe_nvfp4_linear_wgrad")
+    _GEMM_COUNTS["wgrad"] = _GEMM_COUNTS.get("wgrad", 0) + 1
+    return dw[:, :k], db
+
+
+class _NVFP4LinearFunction(torch.autograd.Function):
+    """_NVFP4Linear (src/mcl4_coe/nvfp4.py:391-472) on the kernels.  Forward: the
+    layer's NVFP4 GEMM.  Backward: input gradient = stochastic-rounded gradient x the
+    weight's transposed 16x16-tile quantisation (mcl4moe_nvfp4_mm_sr); weight gradient =
+    the Hadamard16-transformed NVFP4 product (mcl4moe_nvfp4_linear_wgrad) plus the SR-STE
+    decay of masked-out weights; bias gradient = fp32 column sums of the gradient."""
+
+    @staticmethod
+    def forward(ctx, flat, weight, bias, layer):
+        ctx.layer = layer
+        ctx.bias_dtype = None if bias is None else bias.dtype
+        ctx.save_for_backward(flat, weight)
+        with torch.no_grad():
+            return layer._forward_flat(flat)
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        flat, weight = ctx.saved_tensors
+        layer = ctx.layer
+        n, k = weight.shape
+        gradient = grad_output.reshape(-1, n)
+        grad_inputs = grad_weight = grad_bias = None
+        need_bias = ctx.bias_dtype is not None and ctx.needs_input_grad[2]
+        with torch.no_grad():
+            if ctx.needs_input_grad[0]:
+                pk_t, sw_t, g, _ = layer._quantised_weight(transposed=True)
+                np_, kp = _round_up(n, 256), _round_up(k, 256)
+                _GEMM_COUNTS["dgrad"] = _GEMM_COUNTS.get("dgrad", 0) + 1
+                grad_inputs = _mm_prepared(gradient, pk_t, sw_t, g, kp, np_, False, None,
+                                           stochastic_a=True)[:, :k].to(flat.dtype)
+            db = None
+            if ctx.needs_input_grad[1]:
+                dw, db = _linear_weight_grad(gradient, flat, need_bias)
+                grad_weight = dw.to(weight.dtype)
+                mask = layer._quantised_weight()[3]
+                if mask is not None and layer.sr_ste_decay > 0.0:
+                    # SR-STE (src/mcl4_coe/nvfp4.py:460-466): decay of the masked-out weights
+                    grad_weight = grad_weight + layer.sr_ste_decay * (~mask).to(weight.dtype) * weight
+            if need_bias:
+                if db is None:
+                    db = gradient.float().sum(dim=0)
+                grad_bias = db.to(ctx.bias_dtype)
+        return grad_inputs, grad_weight, grad_bias, None
 
 
 class NVFP4Linear(nn.Linear):
@@ -517,7 +615,9 @@ class NVFP4Linear(nn.Linear):
     (src/mcl4_coe/nvfp4.py:474-542).  Forward: 1x16 activation blocks (g = 1 with
     ``causal_activation_scale``), the cached 16x16-tile weight (2:4-masked first when
     ``sparsity_mode`` is not "none"), fp32 accumulation, ``+ bias`` in fp32, cast to the
-    input dtype.  CUDA only (no CPU fallback) and forward only."""
+    input dtype.  Under autograd it trains like the reference (_NVFP4Linear.backward,
+    :431-472): stochastic-rounded NVFP4 input and weight gradients, the weight gradient
+    through the Hadamard16 transform.  CUDA only (no CPU fallback)."""
 
     def __init__(self, in_features: int, out_features: int, bias: bool = True, device=None, dtype=None, *,
                  sparsity_mode: str = "2to4_transposable", sr_ste_decay: float = 1e-4,
@@ -528,7 +628,7 @@ class NVFP4Linear(nn.Linear):
         self.sparsity_mode = sparsity_mode
         self.sr_ste_decay = float(sr_ste_decay)
         self.causal_activation_scale = bool(causal_activation_scale)
-        self._b200_weight_cache: tuple | None = None
+        self._b200_weight_cache: list | None = None
 
     @classmethod
     def from_linear(cls, layer: nn.Linear, *, sparsity_mode: str = "2to4_transposable", sr_ste_decay: float = 1e-4,
@@ -548,54 +648,74 @@ class NVFP4Linear(nn.Linear):
         """The current 2:4 boolean weight mask [out_features, in_features]."""
         return compute_2to4_mask(self.weight, mode=self.sparsity_mode)
 
-    def _quantised_weight(self) -> tuple:
+    def _quantised_weight(self, transposed: bool = False) -> tuple:
         """(packed, swizzled scales, g, mask) of the weight padded to multiples of 256, cached
         on (weight._version, data_ptr, shape, device, sparsity_mode) like
-        _get_or_build_weight_nvfp4_cache (src/mcl4_coe/nvfp4.py:358-389)."""
+        _get_or_build_weight_nvfp4_cache (src/mcl4_coe/nvfp4.py:358-389); ``transposed``:
+        the 16x16-tile quantisation of the masked weight's transpose [K, N] (the
+        backward's ``bwd_q``, built on first use and cached with the same key)."""
         w = self.weight
         key = (w._version, w.data_ptr(), tuple(w.shape), str(w.device), self.sparsity_mode)
         c = self._b200_weight_cache
-        if c is not None and c[0] == key:
-            return c[1:]
-        n, k = w.shape
-        mask = None
-        w_eff = w.detach().to(torch.float32)
-        if self.sparsity_mode != "none":
-            w_eff, m8 = _mask_2to4(w_eff, self.sparsity_mode)
-            mask = m8.bool()
+        if c is None or c[0] != key:
+            n, k = w.shape
+            mask = None
+            w_eff = w.detach().to(torch.float32)
+            if self.sparsity_mode != "none":
+                w_eff, m8 = _mask_2to4(w_eff, self.sparsity_mode)
+                mask = m8.bool()
+            np_, kp = _round_up(n, 256), _round_up(k, 256)
+            if (np_, kp) != (n, k):
+                w_eff = torch.nn.functional.pad(w_eff, (0, kp - k, 0, np_ - n))
+            qb, sb, gb = quantize_nvfp4(w_eff, two_dimensional=True)
+            c = self._b200_weight_cache = [key, qb.view(torch.uint8), sb.view(torch.uint8).reshape(-1), gb, mask,
+                                           None]
+        if not transposed:
+            return tuple(c[1:5])
+        if c[5] is None:
+            n, k = w.shape
+            w_eff = w.detach().to(torch.float32)
+            if c[4] is not None:
+                w_eff = w_eff * c[4].to(torch.float32)
+            np_, kp = _round_up(n, 256), _round_up(k, 256)
+            wt = torch.zeros((kp, np_), dtype=torch.float32, device=w_eff.device)
+            wt[:k, :n] = w_eff.t()
+            qt, st, gt = quantize_nvfp4(wt, two_dimensional=True)
+            c[5] = (qt.view(torch.uint8), st.view(torch.uint8).reshape(-1), gt)
+        return (*c[5], c[4])
+
+    def _forward_flat(self, flat: Tensor) -> Tensor:
+        """[M, in_features] -> [M, out_features] in flat.dtype (no autograd)."""
+        pk, sw, g, _ = self._quantised_weight()
+        n, k = self.weight.shape
         np_, kp = _round_up(n, 256), _round_up(k, 256)
-        if (np_, kp) != (n, k):
-            w_eff = torch.nn.functional.pad(w_eff, (0, kp - k, 0, np_ - n))
-        qb, sb, gb = quantize_nvfp4(w_eff, two_dimensional=True)
-        self._b200_weight_cache = (key, qb.view(torch.uint8), sb.view(torch.uint8).reshape(-1), gb, mask)
-        return self._b200_weight_cache[1:]
+        bias = None
+        if self.bias is not None:  # fp32, zero-padded to the GEMM's N; rebuilt when the bias changes
+            b = self.bias
+            bkey = (b._version, b.data_ptr(), str(flat.device))
+            cached = getattr(self, "_b200_bias_cache", None)
+            if cached is None or cached[0] != bkey:
+                padded = torch.zeros((np_,), dtype=torch.float32, device=flat.device)
+                padded[:n] = b.detach().to(device=flat.device, dtype=torch.float32)
+                self._b200_bias_cache = cached = (bkey, padded)
+            bias = cached[1]
+        _GEMM_COUNTS["forward"] = _GEMM_COUNTS.get("forward", 0) + 1
+        return _mm_prepared(flat, pk, sw, g, np_, kp, self.causal_activation_scale, bias)[:, :n].to(flat.dtype)
 
     def forward(self, inputs: Tensor) -> Tensor:
         if inputs.ndim < 1 or inputs.shape[-1] != self.in_features:
             raise ValueError("NVFP4Linear input must end in in_features")
         _require_cuda(inputs, "NVFP4Linear")
-        if torch.is_grad_enabled() and (inputs.requires_grad or self.weight.requires_grad):
-            raise NotImplementedError("NVFP4Linear on the B200 path is forward-only: run it under torch.no_grad()")
         flat = inputs.reshape(-1, self.in_features)
         if flat.shape[0] == 0:
             return inputs.new_empty(*inputs.shape[:-1], self.out_features)
-        with torch.no_grad():
-            pk, sw, g, _ = self._quantised_weight()
-            n, k = self.weight.shape
-            np_, kp = _round_up(n, 256), _round_up(k, 256)
-            bias = None
-            if self.bias is not None:  # fp32, zero-padded to the GEMM's N; rebuilt when the bias changes
-                b = self.bias
-                bkey = (b._version, b.data_ptr(), str(flat.device))
-                cached = getattr(self, "_b200_bias_cache", None)
-                if cached is None or cached[0] != bkey:
-                    padded = torch.zeros((np_,), dtype=torch.float32, device=flat.device)
-                    padded[:n] = b.detach().to(device=flat.device, dtype=torch.float32)
-                    self._b200_bias_cache = cached = (bkey, padded)
-                bias = cached[1]
-            _GEMM_COUNTS["forward"] = _GEMM_COUNTS.get("forward", 0) + 1
-            out = _mm_prepared(flat, pk, sw, g, np_, kp, self.causal_activation_scale, bias)[:, :n]
-        return out.to(inputs.dtype).reshape(*inputs.shape[:-1], self.out_features)
+        if torch.is_grad_enabled() and (inputs.requires_grad or self.weight.requires_grad
+                                        or (self.bias is not None and self.bias.requires_grad)):
+            out = _NVFP4LinearFunction.apply(flat, self.weight, self.bias, self)
+        else:
+            with torch.no_grad():
+                out = self._forward_flat(flat)
+        return out.reshape(*inputs.shape[:-1], self.out_features)
 
 
 def convert_linear_to_nvfp4(module: nn.Module, *, min_features: int = 32, experts_only: bool = True,

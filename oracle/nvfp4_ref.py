@@ -411,3 +411,87 @@ def quantize_sr(x: np.ndarray, g: float, seed: int, row_index: np.ndarray | None
         code = np.minimum(np.floor((u + noise).astype(np.float32)), 7).astype(np.uint8)
     code = code | ((v < 0).astype(np.uint8) << np.uint8(3))
     return _pack_codes(code), scales
+
+
+# --------------------------------------------------------------------------
+# Backward of the single-matrix projection (_NVFP4Linear.backward).
+# --------------------------------------------------------------------------
+
+# src/mcl4_coe/nvfp4.py:172-178 — signs of the 16 Hadamard rows.
+HADAMARD16_SIGNS = np.array([1, 1, 1, -1, 1, -1, -1, -1, -1, -1, -1, 1, -1, 1, -1, -1], dtype=np.float32)
+
+
+def hadamard16_matrix() -> np.ndarray:
+    """src/mcl4_coe/nvfp4.py:337-346: ``eye(16) * signs`` (row i scaled by sign i), four
+    butterfly stages over each row's entries (pairs ``(i, i + w)`` inside blocks of ``2w``
+    become ``(a + b, a - b)``, w = 1, 2, 4, 8), times 0.25: ``h16[i, j] = signs[i] *
+    (-1)^popcount(i & j) / 4``, orthonormal."""
+    v = np.eye(16, dtype=np.float32) * HADAMARD16_SIGNS[:, None]
+    for w in (1, 2, 4, 8):
+        p = v.reshape(16, 16 // (2 * w), 2, w)
+        left, right = p[:, :, 0, :].copy(), p[:, :, 1, :].copy()
+        v = np.stack((left + right, left - right), axis=2).reshape(16, 16)
+    return (v * np.float32(0.25)).astype(np.float32)
+
+
+def hadamard16(matrix: np.ndarray) -> np.ndarray:
+    """src/mcl4_coe/nvfp4.py:349-355: columns zero-padded to a multiple of 16, every
+    16-column group times ``h16`` — evaluated in float32 as sign flips, the four
+    butterfly stages (pairs ``(i, i + w)`` inside blocks of ``2w``, w = 1, 2, 4, 8) and the
+    exact scale 1/4, the operation order of the CUDA kernel.  The reference's fp32
+    matmul sums the same 16 signed terms in its own order, so the two agree to float32
+    rounding (pinned against the reference's function by a golden fixture)."""
+    x = np.asarray(matrix, dtype=np.float32)
+    rows, cols = x.shape
+    cp = round_up(cols, 16)
+    if cp != cols:
+        x = np.pad(x, ((0, 0), (0, cp - cols)))
+    v = (x.reshape(-1, 16) * HADAMARD16_SIGNS[None, :]).astype(np.float32)
+    for w in (1, 2, 4, 8):
+        p = v.reshape(-1, 16 // (2 * w), 2, w)
+        a, b = p[:, :, 0, :].copy(), p[:, :, 1, :].copy()
+        v = np.stack((a + b, a - b), axis=2).reshape(-1, 16).astype(np.float32)
+    return (v * np.float32(0.25)).reshape(rows, cp).astype(np.float32)
+
+
+def quantize_nvfp4_sr(values: np.ndarray, seed: int, causal_row_scale: bool = False):
+    """``quantize_nvfp4(stochastic=True)`` in the one-dimensional mode
+    (src/mcl4_coe/nvfp4.py:197-225 with the stochastic branch of ``_e2m1_codes``,
+    :186-194): scales and global scale as :func:`quantize_nvfp4_core`, codes
+    ``min(trunc(u + U), 7) | signbit << 3``.  The reference draws ``U`` with
+    ``torch.rand_like``; this build draws it from Philox4x32-10 (:func:`philox_first_word`)
+    at offset ``row * cols + col`` (32-bit wrap) under ``seed`` — the same uniform
+    distribution, so the codes are the reference's in law, and bit-exact against the
+    CUDA kernels for the same seed.  Returns ``(packed [R, C/2], scales [R, C/16], g [1])``."""
+    values = np.ascontiguousarray(values, dtype=np.float32)
+    rows, cols = values.shape
+    _, scales, g = quantize_nvfp4_core(values, False, causal_row_scale)
+    dec = (e4m3_to_f32(scales) * g[0]).astype(np.float32)
+    inv = _inverse_decoding(dec)
+    v = (values.reshape(rows, cols // 16, 16) * inv[..., None]).reshape(rows, cols).astype(np.float32)
+    m = np.minimum(np.abs(v), np.float32(6.0))
+    u = np.where(m <= np.float32(2.0), m * np.float32(2.0),
+                 np.where(m <= np.float32(4.0), m + np.float32(2.0), m * np.float32(0.5) + np.float32(4.0)))
+    offsets = (np.arange(rows, dtype=np.uint64)[:, None] * np.uint64(cols)
+               + np.arange(cols, dtype=np.uint64)[None, :]) & _MASK32
+    noise = uniform_from_word(philox_first_word(offsets, int(seed)))
+    code = np.minimum(np.floor((u + noise).astype(np.float32)), 7).astype(np.uint8)
+    code = code | (np.signbit(v).astype(np.uint8) << np.uint8(3))
+    return _pack_codes(code), scales, g
+
+
+def linear_wgrad_operand(y: np.ndarray, kt: int, rows_out: int, stochastic: bool, seed: int = 0):
+    """One operand of the weight gradient of ``_NVFP4Linear.backward``
+    (src/mcl4_coe/nvfp4.py:454-459): ``quantize_nvfp4(_hadamard16(y.T))`` for ``y``
+    [M, C] (the gradient, stochastic, or the input, to nearest), the token dimension
+    zero-padded to ``kt`` and the rows to ``rows_out`` (as nvfp4_mm pads before its
+    GEMM; zero rows and columns quantise to zero codes and scales and leave the global
+    scale alone).  Returns ``(packed [rows_out, kt/2], scales [rows_out, kt/16], g [1])``."""
+    y = np.asarray(y, dtype=np.float32)
+    m, c = y.shape
+    t = np.zeros((rows_out, kt), dtype=np.float32)
+    t[:c, :m] = y.T
+    h = hadamard16(t)
+    if stochastic:
+        return quantize_nvfp4_sr(h, seed)
+    return quantize_nvfp4_core(h, False, False)

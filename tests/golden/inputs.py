@@ -205,3 +205,24 @@ def sr_quant_cases():
     g = (r.standard_normal((33, 512), dtype=np.float32) * np.float32(2.0)).astype(np.float32)
     cases.append(("sr_ragged_33x512", to_bf16_bits(g), 2 ** 31 - 1))
     return cases
+
+
+def hadamard_cases():
+    """(name, float32 [M, C]) matrices for the single-matrix weight gradient's
+    Hadamard16 transform and quantisation (src/mcl4_coe/nvfp4.py:337-355, :454-459):
+    inputs-like and gradient-like values, token counts that are not multiples of 16,
+    an outlier column, an all-zero column and bf16-representable values."""
+    cases = []
+    r = rng(800)
+    x = bf16_values(r.standard_normal((40, 48), dtype=np.float32))
+    x[:, 7] *= np.float32(50.0)
+    x[:, 11] = 0.0
+    cases.append(("ht_inputs_40x48", x))
+    r = rng(801)
+    g = bf16_values((r.standard_normal((37, 32), dtype=np.float32) * np.float32(1e-3)).astype(np.float32))
+    g[3] = -0.0
+    cases.append(("ht_grad_37x32", g))
+    r = rng(802)
+    y = r.standard_normal((150, 64), dtype=np.float32)
+    cases.append(("ht_f32_150x64", y))
+    return cases

@@ -91,8 +91,8 @@ def test_nvfp4_mm_rejects_bad_operands(moe_pkg):
         moe_pkg.nvfp4_mm(a, torch.zeros((4, 16), device=DEV))
     with pytest.raises(ValueError):
         moe_pkg.nvfp4_mm(a, torch.zeros((4, 32)))
-    with pytest.raises(NotImplementedError):
-        moe_pkg.nvfp4_mm(a, torch.zeros((4, 32), device=DEV), stochastic_a=True)
+    with pytest.raises(NotImplementedError):  # two-dimensional stochastic rounding: no reference caller
+        moe_pkg.nvfp4_mm(a, torch.zeros((4, 32), device=DEV), weight_b=True, stochastic_b=True)
 
 
 @pytest.mark.parametrize("sparsity", ["none", "2to4_transposable", "2to4_row"])

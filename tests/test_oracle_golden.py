@@ -139,3 +139,54 @@ def test_philox_matches_published_known_answer():
     """Philox4x32-10 known-answer vector of Salmon et al. (Random123 kat_vectors):
     counter 0, key 0 -> first word 0x6627e8d5."""
     assert int(nr.philox_first_word(np.array([0], np.uint64), 0)[0]) == 0x6627E8D5
+
+
+def test_hadamard16_matches_reference(golden):
+    """The Hadamard16 matrix, the transform of ``y.T`` and the round-to-nearest
+    quantisation of the transformed, 32-padded matrix (the weight-gradient operand of
+    ``_NVFP4Linear.backward``) against the reference's own functions
+    (tests/golden/make_golden_hadamard.py).  The transform sums 16 signed terms: the
+    oracle's butterfly order and the reference's matmul agree exactly on bf16-valued
+    inputs and to float32 rounding on fp32 inputs; the bytes agree exactly."""
+    from inputs import hadamard_cases
+
+    g = golden("hadamard")
+    np.testing.assert_array_equal(nr.hadamard16_matrix().view(np.uint32), g["h16"].view(np.uint32))
+    h = nr.hadamard16_matrix().astype(np.float64)
+    np.testing.assert_allclose(h @ h.T, np.eye(16), atol=1e-7)
+    for name, y in hadamard_cases():
+        np.testing.assert_array_equal(g[f"{name}/y"], y)
+        ht = nr.hadamard16(y.T)
+        ref = g[f"{name}/ht"]
+        assert ht.shape == ref.shape
+        np.testing.assert_allclose(ht, ref, rtol=0, atol=4e-7 * float(np.abs(ref).max()))
+        if name != "ht_f32_150x64":  # bf16-valued inputs: every partial sum is exact
+            np.testing.assert_array_equal(ht.view(np.uint32), ref.view(np.uint32))
+        m, c = y.shape
+        packed, scales, gs = nr.linear_wgrad_operand(y, nr.round_up(m, 32), nr.round_up(c, 32), stochastic=False)
+        np.testing.assert_array_equal(packed, g[f"{name}/packed"])
+        np.testing.assert_array_equal(scales, g[f"{name}/scales"])
+        np.testing.assert_array_equal(gs.view(np.uint32), g[f"{name}/g"].view(np.uint32))
+
+
+def test_single_matrix_sr_codes_bracket_the_value():
+    """quantize_nvfp4(stochastic=True) oracle: scales and global scale are the
+    round-to-nearest ones, every code is the floor or the ceiling of the scaled
+    magnitude's E2M1 position, and the mean over seeds converges to the value."""
+    r = np.random.default_rng(5)
+    x = nr.round_bf16((r.standard_normal((8, 64)) * 0.01).astype(np.float32))
+    p_rn, s_rn, g_rn = nr.quantize_nvfp4_core(x, False, False)
+    acc = np.zeros_like(x, dtype=np.float64)
+    n = 400
+    for seed in range(n):
+        p, s, gs = nr.quantize_nvfp4_sr(x, seed)
+        np.testing.assert_array_equal(s, s_rn)
+        assert gs[0] == g_rn[0]
+        deq = nr.dequantize(p, s, gs[0], 8, 64)
+        acc += deq
+        lo = nr.dequantize(p_rn, s_rn, g_rn[0], 8, 64)
+        step = np.repeat(nr.e4m3_to_f32(s).astype(np.float64) * gs[0], 16, axis=1) * 2.0
+        assert np.all(np.abs(deq.astype(np.float64) - lo) <= step * (1 + 1e-6))
+    mean = acc / n
+    scale = np.repeat(nr.e4m3_to_f32(s_rn).astype(np.float64) * g_rn[0], 16, axis=1)
+    assert np.abs(mean - x).max() <= 0.25 * scale.max()
