@@ -79,12 +79,12 @@ constexpr uint32_t kSfCol0 = 256;         // accumulator uses columns [0, 256)
 constexpr uint32_t kSfColsPerStage = 48;  // SFA 4 x 4 + SFB 4 x 8
 constexpr uint32_t kIdesc = idesc_nvf4(256, 256);
 constexpr uint32_t kBarBytes = 256;
-constexpr uint32_t kWarpStoreBytes = 32 * 64 * 2;  // one epilogue warp's 32 rows x 64 bf16 (MODE 1)
+constexpr uint32_t kWarpStoreBytes = 32 * 64 * 2;  // one epilogue warp's 32 rows x 64 bf16 (MODES 1, 3)
 
 template <int MODE>
 struct Cfg {
-  static constexpr int kStages = (MODE == 0 || MODE == 3) ? 5 : 4;
-  static constexpr uint32_t kStoreBytes = MODE == 1 ? kEpiWarps * kWarpStoreBytes : 0;
+  static constexpr int kStages = MODE == 0 ? 5 : 4;
+  static constexpr uint32_t kStoreBytes = (MODE == 1 || MODE == 3) ? kEpiWarps * kWarpStoreBytes : 0;
   static constexpr size_t kSmem = 1024 /*align*/ + size_t(kStages) * kStageBytes + kStoreBytes + kBarBytes +
                                   sizeof(int32_t) * (kMaxExperts + 1) + sizeof(float) * 128;
 };
@@ -122,7 +122,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
   uint8_t* smem = smem_raw + (base - raw_addr);
-  const uint32_t store_base = base + S * kStageBytes;  // MODE 1 output staging (1024-aligned)
+  const uint32_t store_base = base + S * kStageBytes;  // MODE 1 / 3 output staging (1024-aligned)
   const uint32_t bar_base = store_base + Cfg<MODE>::kStoreBytes;
   // full: even CTA only; A/B bytes of both CTAs plus the scale writers of both
   // CTAs (their TMEM scales are in place), so the MMA issuer waits once per stage.
@@ -155,7 +155,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmap_a);
     prefetch_tmap(&tmap_b);
-    if (MODE == 1) prefetch_tmap(&tmap_y);
+    if (MODE == 1 || MODE == 3) prefetch_tmap(&tmap_y);
     if (args.a_sf_rowmajor) prefetch_tmap(&tmap_sfa);
   }
   if (warp == 1) {
@@ -387,9 +387,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int hb0 = c.nt * 8 + sub * 2;  // first 16-column block of h handled here
         uint32_t packed[4];
         uint32_t sword = 0;
+        // MODE 3: the warp's 32 x 32 gate and value bf16 blocks go through two 64B-swizzled
+        // smem tiles (row = lane, 16-byte chunk c at c ^ ((row >> 1) & 3)) and two TMA stores
+        const uint32_t gate_buf = my_buf, val_buf = my_buf + kWarpStoreBytes / 2;
+        if (MODE == 3) {
+          if (lane == 0) bulk_wait_read_all();  // the previous tile's stores have read these tiles
+          __syncwarp();
+        }
 #pragma unroll
         for (int blk = 0; blk < 2; ++blk) {
           uint32_t hh[8];
+          uint32_t gq[4], uq[4];
           uint32_t mx = 0;
           const uint64_t gb2 = f2pack(gb, gb);
 #pragma unroll
@@ -401,9 +409,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const uint32_t gg = pack_bf16x2(a0, a1);
             const uint32_t uu = pack_bf16x2(b0, b1);
             if (MODE == 3) {  // training: the backward's SwiGLU derivative needs gate and value
-              uint16_t* row = args.up_save + p * (2 * F) + (hb0 + blk) * 16 + 2 * pr;
-              *reinterpret_cast<uint32_t*>(row) = gg;
-              *reinterpret_cast<uint32_t*>(row + F) = uu;
+              gq[pr & 3] = gg;
+              uq[pr & 3] = uu;
+              if ((pr & 3) == 3) {
+                const uint32_t off = uint32_t(lane) * 64u + (uint32_t((blk * 2 + (pr >> 2)) ^ ((lane >> 1) & 3)) << 4);
+                st_shared_v4(gate_buf + off, make_uint4(gq[0], gq[1], gq[2], gq[3]));
+                st_shared_v4(val_buf + off, make_uint4(uq[0], uq[1], uq[2], uq[3]));
+              }
             }
             silu_f32x2(bf16x2_lo(gg), bf16x2_hi(gg), s0, s1);
             hh[pr] = bf16x2_mul(pack_bf16x2(s0, s1), uu);
@@ -428,6 +440,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             uint4* dst = reinterpret_cast<uint4*>(args.h_dbg + p * F + (hb0 + blk) * 16);
             dst[0] = make_uint4(hh[0], hh[1], hh[2], hh[3]);
             dst[1] = make_uint4(hh[4], hh[5], hh[6], hh[7]);
+          }
+        }
+        if (MODE == 3) {
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {  // lane 0 holds the warp's first row
+            tma_store_2d(&tmap_y, gate_buf, c.nt * 128 + sub * 32, int(p));
+            tma_store_2d(&tmap_y, val_buf, F + c.nt * 128 + sub * 32, int(p));
+            bulk_commit_group();
           }
         }
         *reinterpret_cast<uint4*>(args.hq + p * (F / 2) + hb0 * 8) =
@@ -495,7 +516,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
       }
     }
-    if (MODE == 1 && lane == 0) bulk_wait_all();
+    if ((MODE == 1 || MODE == 3) && lane == 0) bulk_wait_all();
   }
 
   pdl_trigger();  // the next kernel may launch; it waits for this grid's writes
@@ -565,6 +586,20 @@ bool make_tmap_store(CUtensorMap* m, const void* base, uint64_t ld, uint64_t row
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 2-D map over the training save gate | value (bf16 [rows, 2F]), box 32 columns x 32 rows,
+// 64B swizzle: one epilogue warp's gate or value block.
+bool make_tmap_up_save(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 2};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // Number of CTA pairs that can be resident at once (one CTA per SM).
 template <int MODE>
 int resident_pairs() {
@@ -625,9 +660,11 @@ int launch_grouped_gemm(const uint8_t* a, int64_t a_rows, const uint8_t* b, cons
     return MCL4MOE_ERR_CUDA;
   if (args.mode == 0) {
     memset(&ty, 0, sizeof(ty));
+    if (args.up_save == nullptr) return launch_mode<0>(ta, tb, ty, tsa, args, stream);
     // MODE 3: the same gate/up kernel that also stores gate | value for the backward
-    return args.up_save != nullptr ? launch_mode<3>(ta, tb, ty, tsa, args, stream)
-                                   : launch_mode<0>(ta, tb, ty, tsa, args, stream);
+    if ((reinterpret_cast<uintptr_t>(args.up_save) & 15) || args.F % 128 != 0) return MCL4MOE_ERR_INVALID;
+    if (!make_tmap_up_save(&ty, args.up_save, 2 * uint64_t(args.F), uint64_t(a_rows))) return MCL4MOE_ERR_CUDA;
+    return launch_mode<3>(ta, tb, ty, tsa, args, stream);
   }
   if (args.out_row_base == nullptr) {
     // Tile stores write every padded row: y holds a_rows rows of ldy elements.
