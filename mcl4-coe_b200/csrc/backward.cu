@@ -27,21 +27,16 @@ namespace {
 // the block's first element.
 __device__ __forceinline__ uint32_t sr_block16(const uint32_t (&w)[8], float g, uint32_t k0, uint32_t k1,
                                                uint32_t off0, uint2& packed) {
-  float v[16];
   float amax = 0.f;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    v[2 * i] = bf16x2_lo(w[i]);
-    v[2 * i + 1] = bf16x2_hi(w[i]);
-    amax = fmaxf(amax, fmaxf(fabsf(v[2 * i]), fabsf(v[2 * i + 1])));
-  }
+  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fmaxf(fabsf(bf16x2_lo(w[i])), fabsf(bf16x2_hi(w[i]))));
   const uint32_t s = f32_to_e4m3(fminf(__fdiv_rn(amax, __fmul_rn(6.0f, g)), 448.0f));
   const float dec = __fmul_rn(e4m3_to_f32(s), g);
   const float inv = dec > 0.f ? __fdiv_rn(1.0f, dec) : 0.f;
   uint32_t lo = 0u, hi = 0u;
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
-    const float x = __fmul_rn(v[i], inv);
+    const float x = __fmul_rn((i & 1) ? bf16x2_hi(w[i >> 1]) : bf16x2_lo(w[i >> 1]), inv);
     const float m = fminf(fabsf(x), 6.0f);
     const float u = m <= 2.0f ? __fmul_rn(m, 2.0f) : (m <= 4.0f ? __fadd_rn(m, 2.0f) : __fadd_rn(__fmul_rn(m, 0.5f), 4.0f));
     const float r = __fadd_rn(u, uniform_from_word(philox_word0(off0 + uint32_t(i), k0, k1)));
@@ -166,19 +161,32 @@ __global__ void __launch_bounds__(256) slot_grad_kernel(const uint16_t* __restri
   const float wb = round_bf16(topk_w[s]);
   const uint32_t ww = pack_bf16x2(wb, wb);
   float acc = 0.f, mx = 0.f;
-  for (int c = lane * 8; c < d; c += 256) {
-    const uint4 g = __ldg(reinterpret_cast<const uint4*>(d_out + t * d + c));
-    const uint4 yv = __ldg(reinterpret_cast<const uint4*>(y + int64_t(p) * d + c));
-    const uint32_t gw[4] = {g.x, g.y, g.z, g.w}, yw[4] = {yv.x, yv.y, yv.z, yv.w};
-    uint32_t o[4];
+  // four 256-column steps per pass: all eight 16-byte loads are in flight before the math
+  for (int c0 = lane * 8; c0 < d; c0 += 1024) {
+    uint4 g[4], yv[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      o[i] = bf16x2_mul(gw[i], ww);
-      const uint32_t pr = bf16x2_mul(gw[i], yw[i]);
-      acc = __fadd_rn(__fadd_rn(acc, bf16x2_lo(pr)), bf16x2_hi(pr));
-      mx = fmaxf(mx, fmaxf(fabsf(bf16x2_lo(o[i])), fabsf(bf16x2_hi(o[i]))));
+    for (int u = 0; u < 4; ++u) {
+      const int c = c0 + u * 256;
+      if (c < d) {
+        g[u] = __ldg(reinterpret_cast<const uint4*>(d_out + t * d + c));
+        yv[u] = __ldg(reinterpret_cast<const uint4*>(y + int64_t(p) * d + c));
+      }
     }
-    *reinterpret_cast<uint4*>(d_y + int64_t(p) * d + c) = make_uint4(o[0], o[1], o[2], o[3]);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int c = c0 + u * 256;
+      if (c >= d) break;
+      const uint32_t gw[4] = {g[u].x, g[u].y, g[u].z, g[u].w}, yw[4] = {yv[u].x, yv[u].y, yv[u].z, yv[u].w};
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        o[i] = bf16x2_mul(gw[i], ww);
+        const uint32_t pr = bf16x2_mul(gw[i], yw[i]);
+        acc = __fadd_rn(__fadd_rn(acc, bf16x2_lo(pr)), bf16x2_hi(pr));
+        mx = fmaxf(mx, fmaxf(fabsf(bf16x2_lo(o[i])), fabsf(bf16x2_hi(o[i]))));
+      }
+      *reinterpret_cast<uint4*>(d_y + int64_t(p) * d + c) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {

@@ -260,11 +260,20 @@ __global__ void __launch_bounds__(256) router_gemv_kernel(const uint16_t* __rest
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int t0 = blockIdx.x * 8, e = blockIdx.y * 8 + warp;
   const int nt = min(8, T - t0);
-  for (int i = threadIdx.x; i < 8 * d / 8; i += blockDim.x) {  // 16-byte chunks
-    const int r = i / (d / 8), c = i - r * (d / 8);
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (r < nt) v = __ldg(reinterpret_cast<const uint4*>(x + int64_t(t0 + r) * d) + c);
-    reinterpret_cast<uint4*>(xs)[i] = v;
+  // the 8 token rows into shared memory in 16-byte chunks, 8 loads in flight per thread
+  const int nchunk = 8 * d / 8;
+  for (int base = threadIdx.x; base < nchunk; base += 8 * 256) {
+    uint4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = base + u * 256;
+      const int r = i / (d / 8), c = i - r * (d / 8);
+      v[u] = make_uint4(0, 0, 0, 0);
+      if (i < nchunk && r < nt) v[u] = __ldg(reinterpret_cast<const uint4*>(x + int64_t(t0 + r) * d) + c);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (base + u * 256 < nchunk) reinterpret_cast<uint4*>(xs)[base + u * 256] = v[u];
   }
   __syncthreads();
   pdl_trigger();
@@ -532,10 +541,26 @@ __global__ void __launch_bounds__(kTailThreads) router_logits_kernel(const float
   pdl_wait();     // the logits are complete (PDL launch)
   pdl_trigger();  // the scan may launch; it waits for this grid's writes
   if (chunk == 0 && threadIdx.x == 0) *ws.done = 0u;
-  for (int i = threadIdx.x; i < kRouteTokens * a.E; i += blockDim.x) {
-    const int tok = i / a.E, e = i - tok * a.E;
-    const float lv = (t0 + tok < a.T) ? logits_in[int64_t(t0 + tok) * a.E + e] : 0.f;
-    s.logits[tok * s.lds + e] = bias ? __fadd_rn(lv, bias[e]) : lv;
+  // the chunk's logits into shared memory, 16 loads in flight per thread (a loop that
+  // waits on each load before the next would pay one memory latency per element)
+  constexpr int kBatch = 16;
+  const int n = kRouteTokens * a.E;
+  for (int base = threadIdx.x; base < n; base += kBatch * kTailThreads) {
+    float lv[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int i = base + u * kTailThreads;
+      const int tok = i / a.E;
+      lv[u] = (i < n && t0 + tok < a.T) ? __ldg(logits_in + int64_t(t0) * a.E + i) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int i = base + u * kTailThreads;
+      if (i < n) {
+        const int tok = i / a.E, e = i - tok * a.E;
+        s.logits[tok * s.lds + e] = bias ? __fadd_rn(lv[u], __ldg(bias + e)) : lv[u];
+      }
+    }
   }
   __syncthreads();
   route_tail<EW>(s, threadIdx.x, chunk, a.T, a.E, a.k, a.norm_topk, a.valid, a.topk_idx, a.topk_w, a.logits_out,
