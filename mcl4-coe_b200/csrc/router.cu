@@ -30,8 +30,9 @@ namespace mcl4 {
 
 namespace {
 
-constexpr int kTailThreads = 256;  // 8 warps run the tail
+constexpr int kTailThreads = 512;   // 16 warps run the tail of the tensor-core router
 constexpr int kTcThreads = 64 + kTailThreads;
+constexpr int kLogitsThreads = 1024;  // the tail-only kernel (given logits): 32 warps
 
 struct TailSmem {
   float* logits;   // [128][E + 1] logits (bias included), overwritten with the routed probabilities
@@ -40,12 +41,13 @@ struct TailSmem {
   float* lse2;     // [128] lse^2 of routed tokens (0 otherwise)
   float* nval;     // [128] 1 for routed tokens
   uint32_t* bal;   // [4][E] per 32-token group: ballot of the tokens that selected expert e
+  float* part;     // [4][E + 2] partial column sums (tails of more than 256 threads)
   int lds;
 };
 
 __host__ __device__ inline size_t tail_smem_bytes(int E, int k) {
   return sizeof(float) * kRouteTokens * (E + 1) + 2 * sizeof(int32_t) * kRouteTokens * k +
-         2 * sizeof(float) * kRouteTokens + sizeof(uint32_t) * 4 * E + 64;
+         2 * sizeof(float) * kRouteTokens + sizeof(uint32_t) * 4 * E + sizeof(float) * 4 * (E + 2) + 64;
 }
 
 __device__ inline TailSmem carve_tail(uint8_t* base, int E, int k) {
@@ -57,29 +59,32 @@ __device__ inline TailSmem carve_tail(uint8_t* base, int E, int k) {
   t.lse2 = t.selp + kRouteTokens * k;
   t.nval = t.lse2 + kRouteTokens;
   t.bal = reinterpret_cast<uint32_t*>(t.nval + kRouteTokens);
+  t.part = reinterpret_cast<float*>(t.bal + 4 * E);
   return t;
 }
 
 // Softmax / top-k / statistics / stable ranks of one 128-token chunk whose
-// logits (bias included) are in ``s.logits``.  Runs on 256 threads with ids
-// ``g`` 0..255; ``sync()`` is a barrier over exactly those threads.
+// logits (bias included) are in ``s.logits``.  Runs on NT threads (256, 512 or
+// 1024) with ids ``g`` 0..NT-1; ``sync()`` is a barrier over exactly those threads.
 //
-// Token-parallel: a group of TPT = max(2, EW) adjacent threads owns one token
-// and holds 32 of its logits each (experts h*32 .. h*32+31 for member h), so a
-// pass covers 256/TPT tokens and the chunk takes TPT/2 passes.  Softmax and
-// top-k (largest probability first, ties to the lower expert index, as
-// torch.topk on the reference's probabilities) combine across the group with
-// xor shuffles.  Per-expert probability sums are column sums over the chunk's
-// tokens in token order; stable ranks come from one ballot per expert and
-// 32-token group.  Semantics: src/mcl4_coe/backbone.py:787-883.
-template <int EW, class Sync>
+// Token-parallel: a group of TPT adjacent threads owns one token and holds VPT of
+// its logits each (experts h*VPT .. h*VPT+VPT-1 for member h); a pass covers
+// NT/TPT tokens.  Softmax and top-k (largest probability first, ties to the lower
+// expert index, as torch.topk on the reference's probabilities) combine across
+// the group with xor shuffles.  Per-expert probability sums are column sums over
+// the chunk's tokens in token order (in NT/256 consecutive token ranges added in
+// order when NT > 256); stable ranks come from one ballot per expert and 32-token
+// group.  Semantics: src/mcl4_coe/backbone.py:787-883.
+template <int EW, int NT, class Sync>
 __device__ void route_tail(const TailSmem& s, int g, int chunk, int T, int E, int k, int norm_topk,
                            const uint8_t* __restrict__ valid, int32_t* __restrict__ topk_idx,
                            float* __restrict__ topk_w, float* __restrict__ logits_out, float* __restrict__ sel_mask,
                            const RouteWorkspace& ws, Sync sync) {
-  constexpr int TPT = EW < 2 ? 2 : EW;  // threads per token
-  constexpr int VPT = 32;               // logits per thread (E <= 32 * TPT)
-  constexpr int kPass = kTailThreads / TPT;
+  constexpr int kMinTpt = NT / kRouteTokens > 2 ? NT / kRouteTokens : 2;
+  constexpr int TPT = EW > kMinTpt ? EW : kMinTpt;  // threads per token
+  constexpr int VPT = 32 * EW / TPT;                // logits per thread (E <= 32 * EW)
+  constexpr int kPass = NT / TPT;
+  static_assert(TPT <= 32 && VPT >= 1 && VPT <= 32 && kRouteTokens % kPass == 0, "tail shape");
   const int h = g % TPT;
   const int t0 = chunk * kRouteTokens;
   for (int pass = 0; pass < kRouteTokens / kPass; ++pass) {
@@ -165,23 +170,30 @@ __device__ void route_tail(const TailSmem& s, int g, int chunk, int T, int E, in
   }
   sync();
 
-  // per-chunk statistics: column sums in token order
-  for (int c = g; c < E + 2; c += kTailThreads) {
+  // per-chunk statistics: column sums in token order (P consecutive token ranges)
+  constexpr int P = NT / 256 > 0 ? NT / 256 : 1;
+  constexpr int kRange = kRouteTokens / P;
+  for (int idx = g; idx < (E + 2) * P; idx += NT) {
+    const int c = idx % (E + 2), part = idx / (E + 2);
+    const float* col = c < E ? s.logits + c : (c == E ? s.lse2 : s.nval);
+    const int stride = c < E ? s.lds : 1;
     float acc = 0.f;
-    if (c < E) {
-      for (int tok = 0; tok < kRouteTokens; ++tok) acc = __fadd_rn(acc, s.logits[tok * s.lds + c]);
-      ws.part_probs[int64_t(chunk) * E + c] = acc;
+    for (int tok = part * kRange; tok < (part + 1) * kRange; ++tok) acc = __fadd_rn(acc, col[tok * stride]);
+    if (P == 1) {
+      if (c < E) ws.part_probs[int64_t(chunk) * E + c] = acc;
+      else ws.part_misc[int64_t(chunk) * 2 + (c - E)] = acc;
     } else {
-      const float* col = c == E ? s.lse2 : s.nval;
-      for (int tok = 0; tok < kRouteTokens; ++tok) acc = __fadd_rn(acc, col[tok]);
-      ws.part_misc[int64_t(chunk) * 2 + (c - E)] = acc;
+      s.part[part * (E + 2) + c] = acc;
     }
   }
 
-  // stable ranks: warps 0..3 own 32 tokens each (lane = token); one ballot per expert
+  // stable ranks: warp w owns the 32 tokens of group w % 4 (lane = token) and the
+  // experts e with e % (NT / 128) == w / 4; one ballot per expert
   const int lane = g & 31, warp = g >> 5;
-  if (warp < 4) {
-    const int tok = warp * 32 + lane;
+  {
+    constexpr int kSlices = NT / 128;
+    const int grp = warp & 3, slice = warp >> 2;
+    const int tok = grp * 32 + lane;
     uint32_t mw[EW];
 #pragma unroll
     for (int i = 0; i < EW; ++i) mw[i] = 0;
@@ -191,18 +203,29 @@ __device__ void route_tail(const TailSmem& s, int g, int chunk, int T, int E, in
       for (int i = 0; i < EW; ++i)
         if (e >= 0 && (e >> 5) == i) mw[i] |= 1u << (e & 31);
     }
+    for (int e = slice; e < E; e += kSlices) {
+      uint32_t word = 0;
 #pragma unroll
-    for (int i = 0; i < EW; ++i)
-      for (int b = 0; b < 32; ++b) {
-        const uint32_t bal = __ballot_sync(0xffffffffu, (mw[i] >> b) & 1u);
-        if (lane == b && i * 32 + b < E) s.bal[warp * E + i * 32 + b] = bal;
-      }
+      for (int i = 0; i < EW; ++i)
+        if ((e >> 5) == i) word = mw[i];
+      const uint32_t bal = __ballot_sync(0xffffffffu, (word >> (e & 31)) & 1u);
+      if (lane == 0) s.bal[grp * E + e] = bal;
+    }
   }
   sync();
-  for (int e = g; e < E; e += kTailThreads)
+  if (P > 1) {
+    for (int c = g; c < E + 2; c += NT) {
+      float acc = s.part[c];
+#pragma unroll
+      for (int part = 1; part < P; ++part) acc = __fadd_rn(acc, s.part[part * (E + 2) + c]);
+      if (c < E) ws.part_probs[int64_t(chunk) * E + c] = acc;
+      else ws.part_misc[int64_t(chunk) * 2 + (c - E)] = acc;
+    }
+  }
+  for (int e = g; e < E; e += NT)
     ws.chunk_excl[int64_t(chunk) * E + e] =
         __popc(s.bal[e]) + __popc(s.bal[E + e]) + __popc(s.bal[2 * E + e]) + __popc(s.bal[3 * E + e]);
-  for (int i = g; i < kRouteTokens * k; i += kTailThreads) {
+  for (int i = g; i < kRouteTokens * k; i += NT) {
     const int tok = i / k;
     if (t0 + tok >= T) continue;
     const int e = s.sel[i];
@@ -219,8 +242,8 @@ __device__ void route_tail(const TailSmem& s, int g, int chunk, int T, int E, in
 struct BlockSync {
   __device__ void operator()() const { __syncthreads(); }
 };
-struct TailBarrier {  // named barrier 1 over the 256 tail threads of the tensor-core router
-  __device__ void operator()() const { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+struct TailBarrier {  // named barrier 1 over the tail threads of the tensor-core router
+  __device__ void operator()() const { asm volatile("bar.sync 1, %0;" ::"n"(kTailThreads) : "memory"); }
 };
 
 }  // namespace
@@ -438,11 +461,10 @@ __global__ void __launch_bounds__(kTcThreads) router_tc_kernel(const __grid_cons
   } else {
     // tail warps: TMEM logits -> shared memory (+ bias), then softmax / top-k / ranks
     const int g = tid - 64;
-    const int q = warp & 3, half = (warp - 2) >> 2;
+    const int q = warp & 3, grp = (warp - 2) >> 2;  // TMEM lane quarter; column group
     const TailSmem s = carve_tail(smem, a.E, a.k);
     const bool ok = mbar_wait(tfull_bar, 0, a.err, 311);
     tc_fence_after();
-    const int cols = a.E_pad / 2;  // a multiple of 8
     const int row = q * 32 + lane;
     const uint32_t lane_addr = tmem_base + (uint32_t(q * 32) << 16);
     auto ld8 = [&](uint32_t col, uint32_t (&v)[8]) {
@@ -451,7 +473,7 @@ __global__ void __launch_bounds__(kTcThreads) router_tc_kernel(const __grid_cons
                    : "r"(lane_addr + col)
                    : "memory");
     };
-    for (int c0 = half * cols; c0 < (half + 1) * cols; c0 += 8) {
+    for (int c0 = grp * 8; c0 < a.E_pad; c0 += (kTailThreads / 128) * 8) {  // E_pad: a multiple of 16
       uint32_t v[8], vm[8], vl[8];
       if (ok) {
         ld8(c0, v);
@@ -475,7 +497,8 @@ __global__ void __launch_bounds__(kTcThreads) router_tc_kernel(const __grid_cons
     tc_fence_before();
     TailBarrier()();
     pdl_trigger();  // the scan kernel may launch; it waits for this grid's writes
-    route_tail<EW>(s, g, chunk, a.T, a.E, a.k, a.norm_topk, a.valid, a.topk_idx, a.topk_w, a.logits_out, a.sel_mask,
+    route_tail<EW, kTailThreads>(s, g, chunk, a.T, a.E, a.k, a.norm_topk, a.valid, a.topk_idx, a.topk_w,
+                                 a.logits_out, a.sel_mask,
                    ws, TailBarrier());
   }
   tc_fence_before();
@@ -531,7 +554,7 @@ __device__ void finish_single_chunk(int E, int k, const RouteWorkspace& ws, int3
 
 // Router tail on given logits (parity checks against recorded reference logits).
 template <int EW>
-__global__ void __launch_bounds__(kTailThreads) router_logits_kernel(const float* __restrict__ logits_in,
+__global__ void __launch_bounds__(kLogitsThreads) router_logits_kernel(const float* __restrict__ logits_in,
                                                                      const float* __restrict__ bias, RouterTcArgs a,
                                                                      RouteWorkspace ws) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -545,17 +568,17 @@ __global__ void __launch_bounds__(kTailThreads) router_logits_kernel(const float
   // waits on each load before the next would pay one memory latency per element)
   constexpr int kBatch = 16;
   const int n = kRouteTokens * a.E;
-  for (int base = threadIdx.x; base < n; base += kBatch * kTailThreads) {
+  for (int base = threadIdx.x; base < n; base += kBatch * kLogitsThreads) {
     float lv[kBatch];
 #pragma unroll
     for (int u = 0; u < kBatch; ++u) {
-      const int i = base + u * kTailThreads;
+      const int i = base + u * kLogitsThreads;
       const int tok = i / a.E;
       lv[u] = (i < n && t0 + tok < a.T) ? __ldg(logits_in + int64_t(t0) * a.E + i) : 0.f;
     }
 #pragma unroll
     for (int u = 0; u < kBatch; ++u) {
-      const int i = base + u * kTailThreads;
+      const int i = base + u * kLogitsThreads;
       if (i < n) {
         const int tok = i / a.E, e = i - tok * a.E;
         s.logits[tok * s.lds + e] = bias ? __fadd_rn(lv[u], __ldg(bias + e)) : lv[u];
@@ -563,7 +586,8 @@ __global__ void __launch_bounds__(kTailThreads) router_logits_kernel(const float
     }
   }
   __syncthreads();
-  route_tail<EW>(s, threadIdx.x, chunk, a.T, a.E, a.k, a.norm_topk, a.valid, a.topk_idx, a.topk_w, a.logits_out,
+  route_tail<EW, kLogitsThreads>(s, threadIdx.x, chunk, a.T, a.E, a.k, a.norm_topk, a.valid, a.topk_idx, a.topk_w,
+                                 a.logits_out,
                  a.sel_mask, ws, BlockSync());
   if (a.fuse_scan) {
     __syncthreads();  // the tail's chunk counts and sums (global memory of this block) are complete
@@ -755,7 +779,7 @@ int launch_router_t(const uint16_t* x, const float* wr, const float* bias, const
     const size_t smem = tail_smem_bytes(a.E, a.k);
     static std::atomic<uint64_t> configured{0};
     if (!raise_smem_limit(router_logits_kernel<EW>, 200 * 1024, configured)) return MCL4MOE_ERR_CUDA;
-    return launch_pdl(router_logits_kernel<EW>, dim3(C), dim3(kTailThreads), smem, stream, logits_in,
+    return launch_pdl(router_logits_kernel<EW>, dim3(C), dim3(kLogitsThreads), smem, stream, logits_in,
                       static_cast<const float*>(nullptr), a, ws) == cudaSuccess  // final logits
                ? MCL4MOE_OK
                : MCL4MOE_ERR_CUDA;
