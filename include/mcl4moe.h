@@ -388,6 +388,15 @@ int mcl4moe_moe_backward_dx(const uint16_t* d_rows, const int32_t* slot_pos, con
  * (sum over experts of count rounded up to 256, bounded by T*k + 255*E). */
 int64_t mcl4moe_padded_rows(int T, int E, int k);
 
+/* Expert GEMM tiling of mcl4moe_moe_forward / mcl4moe_moe_forward_routed (a tuning
+ * knob with no counterpart in the reference; process-wide): 0 = chosen by shape (the
+ * default: single-CTA 128-row tiles when an inference call averages at most 64 routed
+ * rows per expert, CTA-pair 256-row tiles otherwise), 1 = always pair tiles, 2 =
+ * single-CTA tiles for every inference call (training calls, which pass up_save /
+ * y_save, always use pair tiles).  Both tilings give the same bytes.  Returns the
+ * previous mode, or -1 for a mode outside [0, 2]. */
+int mcl4moe_set_expert_tiling(int mode);
+
 /* Device pointer of a named region inside a forward workspace (for tests,
  * debugging and the backward's inputs): 0 xq, 1 xs, 2 hq, 3 hs, 4 y,
  * 5 pad_start [E+1], 6 slot_pos [T, k], 7 sorted_w, 8 the int32 device error

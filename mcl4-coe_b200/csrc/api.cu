@@ -5,6 +5,8 @@
 // serve return MCL4MOE_ERR_UNSUPPORTED.  Nothing here allocates memory.
 #include <cstring>
 
+#include <atomic>
+
 #include "kernels.cuh"
 
 using namespace mcl4;
@@ -364,6 +366,20 @@ int check_forward_args(const mcl4moe_moe_args* a, bool routed) {
   return MCL4MOE_OK;
 }
 
+// Expert GEMM tiling: 0 = by shape, 1 = CTA-pair 256-row tiles, 2 = single-CTA 128-row tiles.
+std::atomic<int> g_expert_tiling{0};
+
+// Single-CTA 128-row tiles for the inference forward when experts average at most 64
+// routed rows (decode): a pair tile would multiply mostly padding rows, while a 128-row
+// block without routed rows is skipped.  The training forward keeps the pair tiles
+// (its saves and the backward read every padded row).
+bool use_solo_tiles(const mcl4moe_moe_args* a) {
+  const int policy = g_expert_tiling.load(std::memory_order_relaxed);
+  if (policy == 1 || a->up_save != nullptr || a->y_save != nullptr) return false;
+  if (policy == 2) return true;
+  return int64_t(a->T) * a->k <= int64_t(a->E) * 64;
+}
+
 // Permutation + NVFP4 activation quantisation, gate/up GEMM with SwiGLU, down
 // GEMM with the routing weight, combine: everything after the expert layout.
 int forward_experts(const mcl4moe_moe_args* a, const MoeWorkspace& w, const int32_t* topk_idx, const float* topk_w,
@@ -374,6 +390,7 @@ int forward_experts(const mcl4moe_moe_args* a, const MoeWorkspace& w, const int3
   if (st != MCL4MOE_OK) return st;
   if ((st = mark(a, 2, s)) != MCL4MOE_OK) return st;
   const int64_t mcap = padded_rows_cap(T, E, k);
+  const int solo = use_solo_tiles(a) ? 1 : 0;
 
   GemmArgs g1{};
   g1.pad_start = w.route.pad_start;
@@ -393,6 +410,7 @@ int forward_experts(const mcl4moe_moe_args* a, const MoeWorkspace& w, const int3
   g1.h_dbg = a->h_debug;
   g1.up_save = a->up_save;
   g1.err = err;
+  g1.solo = solo;
   st = launch_grouped_gemm(w.xq, mcap, a->w_up, g1, s);
   if (st != MCL4MOE_OK) return st;
   if ((st = mark(a, 3, s)) != MCL4MOE_OK) return st;
@@ -413,6 +431,7 @@ int forward_experts(const mcl4moe_moe_args* a, const MoeWorkspace& w, const int3
   g2.y = a->y_save ? a->y_save : w.y;
   g2.ldy = d;
   g2.err = err;
+  g2.solo = solo;
   st = launch_grouped_gemm(w.hq, mcap, a->w_dn, g2, s);
   if (st != MCL4MOE_OK) return st;
   if ((st = mark(a, 4, s)) != MCL4MOE_OK) return st;
@@ -439,6 +458,11 @@ int32_t* error_word(const mcl4moe_moe_args* a, const MoeWorkspace& w, cudaStream
 }  // namespace
 
 extern "C" {
+
+int mcl4moe_set_expert_tiling(int mode) {
+  if (mode < 0 || mode > 2) return -1;
+  return g_expert_tiling.exchange(mode);
+}
 
 int mcl4moe_moe_forward(const mcl4moe_moe_args* a, mcl4moe_stream_t stream) {
   int st = check_forward_args(a, false);

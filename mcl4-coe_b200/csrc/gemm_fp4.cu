@@ -68,8 +68,8 @@ constexpr uint32_t kSFA = kBM * kBK / 16;           // 2048
 constexpr uint32_t kSFBHalf = 128 * kBK / 16;       // 2048
 constexpr uint32_t kABBytes = kATile + kBHalf;      // 32768 per CTA and stage
 constexpr uint32_t kSFBytes = kSFA + 2 * kSFBHalf;  // 6144 per CTA and stage (full-N B scales)
-constexpr uint32_t kStageBytes = kABBytes + kSFBytes;  // 38912
-constexpr uint32_t kOffB = kATile, kOffSFA = kABBytes, kOffSFB = kABBytes + kSFA;
+constexpr uint32_t kStageBytes = kABBytes + kSFBytes;  // 38912 (pair); scale offsets per variant in Cfg
+constexpr uint32_t kOffB = kATile;
 constexpr int kSfWarps = 4;
 constexpr int kEpiWarps = 16;
 constexpr int kEpiWarp0 = 2 + kSfWarps;
@@ -78,20 +78,30 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kSfCol0 = 256;         // accumulator uses columns [0, 256)
 constexpr uint32_t kSfColsPerStage = 48;  // SFA 4 x 4 + SFB 4 x 8
 constexpr uint32_t kIdesc = idesc_nvf4(256, 256);
+constexpr uint32_t kIdescSolo = idesc_nvf4(128, 256);
 constexpr uint32_t kBarBytes = 256;
 constexpr uint32_t kWarpStoreBytes = 32 * 64 * 2;  // one epilogue warp's 32 rows x 64 bf16 (MODES 1, 3)
 
-template <int MODE>
+// SOLO: each CTA computes its own 128 x 256 tiles with cta_group::1 MMAs (M = 128),
+// staging the full 256 B rows of the tile; used when experts hold few rows
+// (decode), where a pair's 256-row tile would mostly multiply padding.
+template <int MODE, bool SOLO = false>
 struct Cfg {
-  static constexpr int kStages = MODE == 0 ? 5 : 4;
-  static constexpr uint32_t kStoreBytes = (MODE == 1 || MODE == 3) ? kEpiWarps * kWarpStoreBytes : 0;
-  static constexpr size_t kSmem = 1024 /*align*/ + size_t(kStages) * kStageBytes + kStoreBytes + kBarBytes +
+  static constexpr uint32_t kAB = SOLO ? kATile + 2 * kBHalf : kABBytes;
+  static constexpr uint32_t kStage = kAB + kSFBytes;
+  static constexpr uint32_t kOffSfa = kAB, kOffSfb = kAB + kSFA;
+  static constexpr int kStages = SOLO ? 4 : (MODE == 0 ? 5 : 4);
+  static constexpr uint32_t kStoreBytes = (!SOLO && (MODE == 1 || MODE == 3)) ? kEpiWarps * kWarpStoreBytes : 0;
+  static constexpr size_t kSmem = 1024 /*align*/ + size_t(kStages) * kStage + kStoreBytes + kBarBytes +
                                   sizeof(int32_t) * (kMaxExperts + 1) + sizeof(float) * 128;
 };
 
 static_assert(kStageBytes % 1024 == 0, "stage must keep 1024-byte alignment for 128B swizzle");
 static_assert(Cfg<0>::kSmem <= 232448 && Cfg<1>::kSmem <= 232448 && Cfg<2>::kSmem <= 232448 && Cfg<3>::kSmem <= 232448,
               "shared memory");
+static_assert(Cfg<0, true>::kSmem <= 232448 && Cfg<1, true>::kSmem <= 232448, "shared memory (solo)");
+static_assert(Cfg<0, true>::kStage % 1024 == 0, "solo stage alignment");
+static_assert(kSfCol0 + Cfg<0, true>::kStages * kSfColsPerStage <= kTmemCols, "TMEM budget (solo)");
 static_assert(kSfCol0 + Cfg<0>::kStages * kSfColsPerStage <= kTmemCols, "TMEM budget");
 static_assert(8 * (3 * Cfg<0>::kStages + 2) + 4 <= kBarBytes, "barrier area");
 static_assert(kSegRows == 2 * kBM, "a CTA pair covers one 256-row segment block");
@@ -112,18 +122,20 @@ __device__ __forceinline__ int find_expert(const int32_t* pad_s, int E, int row)
 
 }  // namespace
 
-template <int MODE>
+template <int MODE, bool SOLO>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     grouped_gemm_fp4_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                             const __grid_constant__ CUtensorMap tmap_y, const __grid_constant__ CUtensorMap tmap_sfa,
                             GemmArgs args) {
-  constexpr int S = Cfg<MODE>::kStages;
+  using C_ = Cfg<MODE, SOLO>;
+  constexpr int S = C_::kStages;
+  constexpr uint32_t kStageBytes = C_::kStage, kOffSFA = C_::kOffSfa, kOffSFB = C_::kOffSfb;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
   uint8_t* smem = smem_raw + (base - raw_addr);
   const uint32_t store_base = base + S * kStageBytes;  // MODE 1 / 3 output staging (1024-aligned)
-  const uint32_t bar_base = store_base + Cfg<MODE>::kStoreBytes;
+  const uint32_t bar_base = store_base + C_::kStoreBytes;
   // full: even CTA only; A/B bytes of both CTAs plus the scale writers of both
   // CTAs (their TMEM scales are in place), so the MMA issuer waits once per stage.
   auto full_bar = [&](int s) { return bar_base + 8u * s; };
@@ -137,19 +149,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int E = args.E;
-  const uint32_t rank = cluster_ctarank();
+  const uint32_t rank = SOLO ? 0u : cluster_ctarank();
   const bool leader = rank == 0;
-  const int pair = int(cluster_id_x()), npairs = int(cluster_count_x());
+  // work unit: a CTA pair, or (SOLO) a single CTA
+  const int pair = SOLO ? int(blockIdx.x) : int(cluster_id_x());
+  const int npairs = SOLO ? int(gridDim.x) : int(cluster_count_x());
 
   if ((MODE == 0 || MODE == 3) && tid < 128) s_inv[tid] = inverse_decoding(e4m3_to_f32(uint32_t(tid)));
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(full_bar(s), 1 + 2 * kSfWarps);
+      mbar_init(full_bar(s), 1 + (SOLO ? 1 : 2) * kSfWarps);
       mbar_init(sfull_bar(s), 1);
       mbar_init(empty_bar(s), 1);
     }
     mbar_init(tfull_bar, 1);
-    mbar_init(tempty_bar, 2 * kEpiWarps);
+    mbar_init(tempty_bar, (SOLO ? 1 : 2) * kEpiWarps);
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -159,8 +173,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (args.a_sf_rowmajor) prefetch_tmap(&tmap_sfa);
   }
   if (warp == 1) {
-    tmem_alloc_pair(smem_u32(tmem_slot), kTmemCols);
-    tmem_relinquish_pair();
+    if (SOLO) {
+      tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+      tmem_relinquish();
+    } else {
+      tmem_alloc_pair(smem_u32(tmem_slot), kTmemCols);
+      tmem_relinquish_pair();
+    }
   }
   // Everything above is independent of the previous kernel's output; from here on
   // its writes (expert layout, A operand) are read.
@@ -172,7 +191,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int total_pm = pad_s[E] / kSegRows;
+  // tile rows: 256-row pair blocks, or (SOLO) 128-row blocks
+  const int total_pm = pad_s[E] / (SOLO ? kBM : kSegRows);
   const int n_tiles = args.n_tiles;
   const int total_tiles = total_pm * n_tiles;
   const int kblocks = args.K / kBK;
@@ -181,8 +201,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     TileCoord c;
     c.pm = t / n_tiles;
     c.nt = t - c.pm * n_tiles;
-    c.e = find_expert(pad_s, E, c.pm * kSegRows);
+    c.e = find_expert(pad_s, E, c.pm * (SOLO ? kBM : kSegRows));
     return c;
+  };
+  // first A row of this CTA's part of the tile
+  auto tile_row0 = [&](const TileCoord& c) { return SOLO ? c.pm * kBM : c.pm * kSegRows + int(rank) * kBM; };
+  // SOLO skips 128-row blocks that hold only padding rows (every role skips the same tiles)
+  auto live = [&](const TileCoord& c) {
+    return !SOLO || args.row_count == nullptr || c.pm * kBM - pad_s[c.e] < __ldg(args.row_count + c.e);
   };
   auto b_rows = [&](const TileCoord& c, int& lr0, int& lr1) {  // local B rows of the tile's two 128-row halves
     if (MODE == 0 || MODE == 3) {
@@ -202,9 +228,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int t = pair; t < total_tiles && ok; t += npairs) {
         const TileCoord c = coord(t);
+        if (!live(c)) continue;
         int lr0, lr1;
         b_rows(c, lr0, lr1);
-        const int row0 = c.pm * kSegRows + int(rank) * kBM;
+        const int row0 = tile_row0(c);
         const int brow = c.e * args.N_total + (rank == 0 ? lr0 : lr1);
         const uint8_t* bsc = args.b_scales + size_t(c.e) * (size_t(args.N_total) * args.K / 16);
         const uint8_t* bsc0 = bsc + size_t(lr0 / 128) * sf_row_stride;
@@ -216,11 +243,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             break;
           }
           const uint32_t st = base + stage * kStageBytes;
-          if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * kABBytes);
           mbar_arrive_expect_tx(sfull_bar(stage), kSFBytes);
-          const uint32_t fb = map_shared_rank(full_bar(stage), 0);
-          tma_load_2d_pair(st, &tmap_a, kb * (kBK / 2), row0, fb);
-          tma_load_2d_pair(st + kOffB, &tmap_b, kb * (kBK / 2), brow, fb);
+          if (SOLO) {  // own A tile and both 128-row halves of the tile's B rows
+            mbar_arrive_expect_tx(full_bar(stage), C_::kAB);
+            tma_load_2d(st, &tmap_a, kb * (kBK / 2), row0, full_bar(stage));
+            tma_load_2d(st + kOffB, &tmap_b, kb * (kBK / 2), c.e * args.N_total + lr0, full_bar(stage));
+            tma_load_2d(st + kOffB + kBHalf, &tmap_b, kb * (kBK / 2), c.e * args.N_total + lr1, full_bar(stage));
+          } else {
+            if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * kABBytes);
+            const uint32_t fb = map_shared_rank(full_bar(stage), 0);
+            tma_load_2d_pair(st, &tmap_a, kb * (kBK / 2), row0, fb);
+            tma_load_2d_pair(st + kOffB, &tmap_b, kb * (kBK / 2), brow, fb);
+          }
           if (args.a_sf_rowmajor)  // this CTA's 128 rows x 16 scales of the K block, row-major
             tma_load_2d(st + kOffSFA, &tmap_sfa, kb * (kBK / 16), row0, sfull_bar(stage));
           else
@@ -259,6 +293,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
       for (int t = pair; t < total_tiles && ok; t += npairs) {
+        if (SOLO && !live(coord(t))) continue;
         if (!mbar_wait(tempty_bar, acc_phase ^ 1u, args.err, 201)) break;
         tc_fence_after();
         for (int kb = 0; kb < kblocks; ++kb) {
@@ -270,20 +305,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint64_t adesc = adesc0 + uint64_t(stage) * (kStageBytes >> 4);
           const uint64_t bdesc = bdesc0 + uint64_t(stage) * (kStageBytes >> 4);
           const uint32_t sf_col = sf0 + uint32_t(stage) * kSfColsPerStage;
+          if (SOLO) {
 #pragma unroll
-          for (int ks = 0; ks < 4; ++ks)
-            tc_mma_nvf4_pair(tmem_base, adesc + 2 * ks, bdesc + 2 * ks, kIdesc, sf_col + 4 * ks,
-                             sf_col + 16 + 8 * ks, (kb | ks) != 0 ? 1u : 0u);
-          tc_commit_pair(empty0_own + 8u * stage);
-          tc_commit_pair(empty0_peer + 8u * stage);
+            for (int ks = 0; ks < 4; ++ks)
+              tc_mma_nvf4(tmem_base, adesc + 2 * ks, bdesc + 2 * ks, kIdescSolo, sf_col + 4 * ks, sf_col + 16 + 8 * ks,
+                          (kb | ks) != 0 ? 1u : 0u);
+            tc_commit(empty_bar(stage));
+          } else {
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+              tc_mma_nvf4_pair(tmem_base, adesc + 2 * ks, bdesc + 2 * ks, kIdesc, sf_col + 4 * ks,
+                               sf_col + 16 + 8 * ks, (kb | ks) != 0 ? 1u : 0u);
+            tc_commit_pair(empty0_own + 8u * stage);
+            tc_commit_pair(empty0_peer + 8u * stage);
+          }
           if (++stage == S) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        tc_commit_pair(tfull_own);
-        tc_commit_pair(tfull_peer);
+        if (SOLO) {
+          tc_commit(tfull_bar);
+        } else {
+          tc_commit_pair(tfull_own);
+          tc_commit_pair(tfull_peer);
+        }
         acc_phase ^= 1u;
       }
     }
@@ -301,6 +348,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     uint32_t phase = 0;
     bool ok = true;
     for (int t = pair; t < total_tiles && ok; t += npairs) {
+      if (SOLO && !live(coord(t))) continue;
       for (int kb = 0; kb < kblocks; ++kb) {
         if (!mbar_wait(sfull_bar(stage), phase, args.err, 121)) {
           ok = false;
@@ -337,7 +385,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(map_shared_rank(full_bar(stage), 0));
+        if (lane == 0) {
+          if (SOLO) mbar_arrive(full_bar(stage));
+          else mbar_arrive_cluster(map_shared_rank(full_bar(stage), 0));
+        }
         if (++stage == S) {
           stage = 0;
           phase ^= 1u;
@@ -357,8 +408,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     uint32_t acc_phase = 0;
     for (int t = pair; t < total_tiles; t += npairs) {
       const TileCoord c = coord(t);
+      if (!live(c)) continue;
       // per-tile scalars first: their load latency overlaps the MMAs of this tile
-      const int64_t p = int64_t(c.pm) * kSegRows + int64_t(rank) * kBM + row_in_tile;  // padded row
+      const int64_t p = int64_t(tile_row0(c)) + row_in_tile;  // padded row
       const int local = int(p - pad_s[c.e]);
       // acc * (g_a * g_b), the reference's order (src/mcl4_coe/nvfp4.py:869); g_a = 1 unless given
       const float gb = args.a_g != nullptr ? __fmul_rn(__ldg(args.a_g), __ldg(args.b_g + c.e)) : __ldg(args.b_g + c.e);
@@ -378,7 +430,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(tempty_leader);  // accumulator may be overwritten now
+      if (lane == 0) {  // accumulator may be overwritten now
+        if (SOLO) mbar_arrive(tempty_bar);
+        else mbar_arrive_cluster(tempty_leader);
+      }
 
       if (MODE == 0 || MODE == 3) {
         // up = bf16(acc * g); h = bf16(bf16(silu(gate)) * value) (src/mcl4_coe/backbone.py:572-574),
@@ -456,7 +511,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         *reinterpret_cast<uint16_t*>(args.hs +
                                      swizzled_scale_offset(uint64_t(p), uint32_t(hb0), uint32_t(F / 16))) =
             uint16_t(sword);
-      } else if (MODE == 1) {
+      } else if (MODE == 1 && !SOLO) {
         // y = bf16(acc * g) [* bf16(routing weight), rounded to bf16] (src/mcl4_coe/backbone.py:903),
         // every padded row (padding rows hold zeros), through a 32 x 64 swizzled smem tile.
         const uint32_t ww = pack_bf16x2(wrow, wrow);
@@ -499,7 +554,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           dst[i] = make_float4(o[0], o[1], o[2], o[3]);
         }
       } else if (local < rows_e) {
-        // y rows into unpadded destination rows, valid rows only
+        // y rows into unpadded destination rows (or, SOLO, their padded rows), valid rows only
         const int64_t dst_row = args.out_row_base ? int64_t(args.out_row_base[c.e]) + local : p;
         const uint32_t ww = pack_bf16x2(wrow, wrow);
         uint4* dst = reinterpret_cast<uint4*>(args.y + dst_row * args.ldy + c.nt * kBN + sub * 64);
@@ -525,7 +580,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   cluster_sync_all();  // no pair MMA or peer access is outstanding past this point
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc_pair(tmem_base, kTmemCols);
+    if (SOLO) tmem_dealloc(tmem_base, kTmemCols);
+    else tmem_dealloc_pair(tmem_base, kTmemCols);
   }
 }
 
@@ -601,16 +657,16 @@ bool make_tmap_up_save(CUtensorMap* m, const void* base, uint64_t cols, uint64_t
 }
 
 // Number of CTA pairs that can be resident at once (one CTA per SM).
-template <int MODE>
+template <int MODE, bool SOLO>
 int resident_pairs() {
   static int n = 0;
   if (n == 0) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * 74);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = Cfg<MODE>::kSmem;
+    cfg.dynamicSmemBytes = Cfg<MODE, SOLO>::kSmem;
     int clusters = 0;
-    if (cudaOccupancyMaxActiveClusters(&clusters, grouped_gemm_fp4_kernel<MODE>, &cfg) != cudaSuccess ||
+    if (cudaOccupancyMaxActiveClusters(&clusters, grouped_gemm_fp4_kernel<MODE, SOLO>, &cfg) != cudaSuccess ||
         clusters <= 0) {
       (void)cudaGetLastError();
       clusters = num_sms() / 2;
@@ -620,14 +676,15 @@ int resident_pairs() {
   return n;
 }
 
-template <int MODE>
+template <int MODE, bool SOLO = false>
 int launch_mode(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ty, const CUtensorMap& tsa,
                 const GemmArgs& args, cudaStream_t stream) {
   static std::atomic<uint64_t> configured{0};
-  if (!raise_smem_limit(grouped_gemm_fp4_kernel<MODE>, int(Cfg<MODE>::kSmem), configured)) return MCL4MOE_ERR_CUDA;
-  const int pairs = resident_pairs<MODE>();
-  return launch_pdl(grouped_gemm_fp4_kernel<MODE>, dim3(2 * pairs), dim3(kThreads), Cfg<MODE>::kSmem, stream, ta, tb,
-                    ty, tsa, args) == cudaSuccess
+  if (!raise_smem_limit(grouped_gemm_fp4_kernel<MODE, SOLO>, int(Cfg<MODE, SOLO>::kSmem), configured))
+    return MCL4MOE_ERR_CUDA;
+  const int pairs = resident_pairs<MODE, SOLO>();
+  return launch_pdl(grouped_gemm_fp4_kernel<MODE, SOLO>, dim3(2 * pairs), dim3(kThreads), Cfg<MODE, SOLO>::kSmem,
+                    stream, ta, tb, ty, tsa, args) == cudaSuccess
              ? MCL4MOE_OK
              : MCL4MOE_ERR_CUDA;
 }
@@ -660,11 +717,18 @@ int launch_grouped_gemm(const uint8_t* a, int64_t a_rows, const uint8_t* b, cons
     return MCL4MOE_ERR_CUDA;
   if (args.mode == 0) {
     memset(&ty, 0, sizeof(ty));
-    if (args.up_save == nullptr) return launch_mode<0>(ta, tb, ty, tsa, args, stream);
+    if (args.up_save == nullptr)
+      return args.solo ? launch_mode<0, true>(ta, tb, ty, tsa, args, stream) : launch_mode<0>(ta, tb, ty, tsa, args, stream);
     // MODE 3: the same gate/up kernel that also stores gate | value for the backward
     if ((reinterpret_cast<uintptr_t>(args.up_save) & 15) || args.F % 128 != 0) return MCL4MOE_ERR_INVALID;
     if (!make_tmap_up_save(&ty, args.up_save, 2 * uint64_t(args.F), uint64_t(a_rows))) return MCL4MOE_ERR_CUDA;
     return launch_mode<3>(ta, tb, ty, tsa, args, stream);
+  }
+  if (args.out_row_base == nullptr && args.solo && args.row_count != nullptr) {
+    // SOLO: valid rows only, plain stores
+    if ((reinterpret_cast<uintptr_t>(args.y) & 15) || (args.ldy * 2) % 16 != 0) return MCL4MOE_ERR_INVALID;
+    memset(&ty, 0, sizeof(ty));
+    return launch_mode<1, true>(ta, tb, ty, tsa, args, stream);
   }
   if (args.out_row_base == nullptr) {
     // Tile stores write every padded row: y holds a_rows rows of ldy elements.

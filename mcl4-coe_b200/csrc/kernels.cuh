@@ -228,6 +228,8 @@ struct GemmArgs {
   const float* bias;            // mode 2 with y32: [N_total] added after the scale, or nullptr
   int64_t ldy;
   int32_t* err;
+  int solo;                     // modes 0 (inference) / 1: single-CTA 128-row tiles that skip padding-only
+                                // blocks (decode); mode 1 then writes valid rows only
 };
 
 int launch_grouped_gemm(const uint8_t* a, int64_t a_rows, const uint8_t* b, const GemmArgs& args, cudaStream_t stream);

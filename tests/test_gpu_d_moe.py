@@ -319,3 +319,36 @@ def test_cuda_graph_replay_matches_eager(moe_pkg):
     for (o1, a1, z1, c1), (o2, a2, z2, c2) in zip(eager, graphed):
         assert torch.equal(o1, o2) and torch.equal(c1, c2)
         assert float(a1) == float(a2) and float(z1) == float(z2)
+
+
+@pytest.mark.parametrize("shape", [(64, 2048, 64, 8, 1024, False), (200, 512, 16, 4, 256, True),
+                                   (700, 512, 8, 2, 256, False)], ids=["decode_c4", "zipf_dead", "over128"])
+def test_expert_tilings_agree(moe_pkg, shape):
+    """Single-CTA 128-row tiles (decode: padding-only blocks skipped) and CTA-pair 256-row
+    tiles give the same layer output and the same h / NVFP4 h bytes on every routed row;
+    shapes with empty experts and experts of more than 128 rows included."""
+    t, d, e, k, f, zipf = shape
+    c = moe_case(31 + t, t, d, e, k, f, zipf_bias=zipf, dead_experts=2 if zipf else 0)
+    moe = build_module(moe_pkg, c, DEV)
+    moe.debug_capture_h = True
+    x = x_tensor(c, DEV)
+    lib = moe_pkg.library()
+    res = {}
+    try:
+        for mode in (1, 2):
+            lib.mcl4moe_set_expert_tiling(mode)
+            det = moe.forward_details(x)
+            torch.cuda.synchronize()
+            assert moe.read_device_error() == 0
+            res[mode] = {key: v.clone() for key, v in det.items() if isinstance(v, torch.Tensor)}
+    finally:
+        lib.mcl4moe_set_expert_tiling(0)
+    a, b = res[1], res[2]
+    assert torch.equal(a["out"], b["out"])
+    pad = a["pad_start"].cpu().numpy()
+    counts = np.diff(np.concatenate([[0], a["offs"].cpu().numpy()]))
+    rows = torch.from_numpy(np.concatenate([np.arange(pad[i], pad[i] + counts[i]) for i in range(e)])).to(DEV)
+    for key in ("h", "hq"):
+        assert torch.equal(a[key][rows], b[key][rows]), key
+    if t * k > e * 128:  # some expert exceeds one 128-row block
+        assert counts.max() > 128
