@@ -28,6 +28,8 @@ struct RouteWorkspace {
   uint32_t* done;        // [1]     finished-expert counter of the scan (zeroed by the router)
   uint16_t* wsplit;      // [3][E_pad][d] bf16 parts of the router weight (hi, mid, lo)
   float* small_logits;   // [T, E] logits of small batches (T <= kRouteGemvMaxT), else null
+  float* small_tok;      // [2][128] lse^2 and routed flag per token of a one-chunk batch (T <= 128),
+                         // then 17 uint32 completion counters
   size_t bytes;
 };
 
@@ -60,6 +62,7 @@ inline RouteWorkspace route_workspace(void* base, int T, int E, int k, int d) {
   w.done = reinterpret_cast<uint32_t*>(take(sizeof(uint32_t)));
   w.wsplit = reinterpret_cast<uint16_t*>(take(sizeof(uint16_t) * 3 * size_t((E + 15) / 16 * 16) * size_t(d)));
   w.small_logits = T <= kRouteGemvMaxT ? reinterpret_cast<float*>(take(sizeof(float) * size_t(T) * E)) : nullptr;
+  w.small_tok = T <= kRouteTokens ? reinterpret_cast<float*>(take(sizeof(float) * 2 * kRouteTokens + 17 * 4)) : nullptr;
   w.bytes = off;
   return w;
 }

@@ -76,6 +76,10 @@ __device__ inline TailSmem carve_tail(uint8_t* base, int E, int k) {
 // order when NT > 256); stable ranks come from one ballot per expert and 32-token
 // group.  Semantics: src/mcl4_coe/backbone.py:787-883.
 template <int EW, int NT, class Sync>
+__device__ void route_chunk_stats(const TailSmem& s, int g, int chunk, int T, int E, int k, const RouteWorkspace& ws,
+                                  Sync sync);
+
+template <int EW, int NT, class Sync>
 __device__ void route_tail(const TailSmem& s, int g, int chunk, int T, int E, int k, int norm_topk,
                            const uint8_t* __restrict__ valid, int32_t* __restrict__ topk_idx,
                            float* __restrict__ topk_w, float* __restrict__ logits_out, float* __restrict__ sel_mask,
@@ -169,7 +173,18 @@ __device__ void route_tail(const TailSmem& s, int g, int chunk, int T, int E, in
     }
   }
   sync();
+  route_chunk_stats<EW, NT>(s, g, chunk, T, E, k, ws, sync);
+}
 
+// The chunk's statistics and stable ranks from its per-token results in shared memory
+// (routed probabilities in ``s.logits``, selections in ``s.sel``, ``s.lse2``, ``s.nval``):
+// per-expert probability sums and the lse^2 / routed-token sums (column sums in token
+// order, in NT/256 consecutive token ranges added in order when NT > 256), per-expert
+// chunk counts and each slot's rank among the chunk's slots of its expert.
+template <int EW, int NT, class Sync>
+__device__ void route_chunk_stats(const TailSmem& s, int g, int chunk, int T, int E, int k, const RouteWorkspace& ws,
+                                  Sync sync) {
+  const int t0 = chunk * kRouteTokens;
   // per-chunk statistics: column sums in token order (P consecutive token ranges)
   constexpr int P = NT / 256 > 0 ? NT / 256 : 1;
   constexpr int kRange = kRouteTokens / P;
@@ -271,7 +286,7 @@ __global__ void __launch_bounds__(256) router_split_kernel(const float* __restri
 
 // fp32 logits of a small batch on the CUDA cores: CTA (token block of 8, expert
 // block of 8); warp w owns expert e0 + w, lane l accumulates the 4-element groups
-// 4l, 4l + 128, ... of d for the 8 tokens with fp32 fma (16-byte weight loads, four
+// 4l, 4l + 128, ... of d for the 8 tokens with fp32 fma (16-byte weight loads, eight
 // groups in flight), then a fixed xor tree sums the lanes (deterministic).
 // logits[t, e] = sum_k x[t, k] * Wr[e, k] (+ bias[e]).
 __global__ void __launch_bounds__(256) router_gemv_kernel(const uint16_t* __restrict__ x,
@@ -304,7 +319,7 @@ __global__ void __launch_bounds__(256) router_gemv_kernel(const uint16_t* __rest
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   const float4* wrow = reinterpret_cast<const float4*>(wr + int64_t(e) * d);
   const int groups = d / 4;  // d % 64 == 0
-#pragma unroll 4
+#pragma unroll 8
   for (int gq = lane; gq < groups; gq += 32) {
     const float4 wv = __ldg(wrow + gq);
 #pragma unroll
@@ -595,6 +610,198 @@ __global__ void __launch_bounds__(kLogitsThreads) router_logits_kernel(const flo
   }
 }
 
+// One-chunk batches (T <= 128) from x in one launch.  CTA (b, c) computes the fp32
+// logits of tokens [8b, 8b + 8) and experts [8c, 8c + 8) exactly as the small-batch
+// GEMV does (warp w owns expert 8c + w); the last CTA of token block b to finish runs
+// one warp per token: softmax / top-k, the token's outputs and its per-token results
+// (routed probabilities into the logits scratch, lse^2 and the routed flag); the last
+// token block to finish gathers the chunk's results and computes its statistics, ranks
+// and expert segments, as the tail-only kernel does for one chunk.  Completion
+// counters (small_cnt: one per token block, then one for the chunk) are zeroed before
+// the launch.  Semantics: src/mcl4_coe/backbone.py:787-883.
+constexpr int kSmallTokPerCta = 8;
+
+template <int EW>
+__global__ void __launch_bounds__(256) router_small_kernel(const uint16_t* __restrict__ x,
+                                                           const float* __restrict__ wr,
+                                                           const float* __restrict__ bias, RouterTcArgs a,
+                                                           RouteWorkspace ws) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const int d = a.d, E = a.E, k = a.k, T = a.T;
+  uint16_t* xs = reinterpret_cast<uint16_t*>(smem_raw);  // [8][d] bf16
+  float* lg = reinterpret_cast<float*>(smem_raw);         // [8][E] logits (after the GEMV part)
+  __shared__ bool is_last;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int t0 = blockIdx.x * kSmallTokPerCta;
+  uint32_t* cnt = reinterpret_cast<uint32_t*>(ws.small_tok + 2 * kRouteTokens);
+  const int nt = min(kSmallTokPerCta, T - t0);
+  pdl_wait();  // x and the router weight are complete (PDL launch)
+  {
+    const int nchunk = 8 * d / 8;  // 16-byte chunks of the 8 rows, 8 loads in flight per thread
+    for (int base = threadIdx.x; base < nchunk; base += 8 * 256) {
+      uint4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = base + u * 256;
+        const int r = i / (d / 8), c = i - r * (d / 8);
+        v[u] = make_uint4(0, 0, 0, 0);
+        if (i < nchunk && r < nt) v[u] = __ldg(reinterpret_cast<const uint4*>(x + int64_t(t0 + r) * d) + c);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (base + u * 256 < nchunk) reinterpret_cast<uint4*>(xs)[base + u * 256] = v[u];
+    }
+  }
+  __syncthreads();
+  pdl_trigger();
+  // logits: the GEMV's per-lane fp32 fma order and xor tree, so the values are the GEMV's
+  for (int e = blockIdx.y * 8 + warp; e < min(E, int(blockIdx.y) * 8 + 8); e += 8) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    const float4* wrow = reinterpret_cast<const float4*>(wr + int64_t(e) * d);
+    const int groups = d / 4;
+#pragma unroll 8
+    for (int gq = lane; gq < groups; gq += 32) {
+      const float4 wv = __ldg(wrow + gq);
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const uint2 xv = *reinterpret_cast<const uint2*>(xs + r * d + 4 * gq);
+        acc[r] = __fmaf_rn(bf16x2_lo(xv.x), wv.x, acc[r]);
+        acc[r] = __fmaf_rn(bf16x2_hi(xv.x), wv.y, acc[r]);
+        acc[r] = __fmaf_rn(bf16x2_lo(xv.y), wv.z, acc[r]);
+        acc[r] = __fmaf_rn(bf16x2_hi(xv.y), wv.w, acc[r]);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc[r] = __fadd_rn(acc[r], __shfl_xor_sync(0xffffffffu, acc[r], o));
+    }
+    if (lane < nt) {
+      float v = acc[0];
+#pragma unroll
+      for (int r = 1; r < 8; ++r)
+        if (lane == r) v = acc[r];
+      ws.small_logits[int64_t(t0 + lane) * E + e] = bias ? __fadd_rn(v, __ldg(bias + e)) : v;
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) is_last = atomicAdd(cnt + blockIdx.x, 1u) == gridDim.y - 1;
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  // the token block's logits (all experts) from the other CTAs of the block
+  for (int i = threadIdx.x; i < nt * E; i += 256) lg[i] = __ldcg(ws.small_logits + int64_t(t0) * E + i);
+  __syncthreads();
+  // one warp per token: lane l holds experts l + 32 i
+  if (warp < nt) {
+    const int t = t0 + warp;
+    const bool routed = a.valid == nullptr || a.valid[t] != 0;
+    float v[EW];
+#pragma unroll
+    for (int i = 0; i < EW; ++i) {
+      const int e = lane + 32 * i;
+      v[i] = e < E ? lg[warp * E + e] : -INFINITY;
+      if (a.logits_out != nullptr && e < E) a.logits_out[int64_t(t) * E + e] = v[i];
+    }
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < EW; ++i) m = fmaxf(m, v[i]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < EW; ++i) {
+      v[i] = lane + 32 * i < E ? expf(__fsub_rn(v[i], m)) : 0.f;
+      sum = __fadd_rn(sum, v[i]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+    const float inv_s = __frcp_rn(sum);
+#pragma unroll
+    for (int i = 0; i < EW; ++i) {
+      v[i] = __fmul_rn(v[i], inv_s);
+      const int e = lane + 32 * i;
+      if (e < E) ws.small_logits[int64_t(t) * E + e] = routed ? v[i] : 0.f;  // column sums of the last CTA
+    }
+    if (lane == 0) {
+      const float lse = routed ? __fadd_rn(m, logf(sum)) : 0.f;
+      ws.small_tok[t] = __fmul_rn(lse, lse);
+      ws.small_tok[kRouteTokens + t] = routed ? 1.f : 0.f;
+    }
+    // top-k: largest probability first, ties to the lower expert index
+    uint32_t taken = 0;
+    float total = 0.f;
+    int my_e = -1;
+    float my_p = 0.f;
+    for (int j = 0; j < k; ++j) {
+      float bp = -1.f;
+      int bi = 0;
+#pragma unroll
+      for (int i = 0; i < EW; ++i)
+        if (lane + 32 * i < E && !((taken >> i) & 1u) && v[i] > bp) {
+          bp = v[i];
+          bi = i;
+        }
+      const uint32_t be = uint32_t(lane + 32 * bi);
+      unsigned long long best =
+          bp >= 0.f ? (static_cast<unsigned long long>(__float_as_uint(bp)) << 32) | (0xFFFFFFFFu - be) : 0ull;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+        best = other > best ? other : best;
+      }
+      const int e_star = int(0xFFFFFFFFu - uint32_t(best & 0xFFFFFFFFull));
+      const float p_star = __uint_as_float(uint32_t(best >> 32));
+      if ((e_star & 31) == lane) taken |= 1u << (e_star >> 5);
+      total = __fadd_rn(total, p_star);
+      if (lane == j) {
+        my_e = e_star;
+        my_p = p_star;
+      }
+    }
+    if (lane < k) {
+      const float w = a.norm_topk ? __fdiv_rn(my_p, fmaxf(total, 1e-9f)) : my_p;
+      a.topk_idx[int64_t(t) * k + lane] = routed ? my_e : -1;
+      a.topk_w[int64_t(t) * k + lane] = routed ? w : 0.f;
+    }
+    if (a.sel_mask != nullptr)
+#pragma unroll
+      for (int i = 0; i < EW; ++i) {
+        const int e = lane + 32 * i;
+        if (e < E) a.sel_mask[int64_t(t) * E + e] = (routed && ((taken >> i) & 1u)) ? 1.f : 0.f;
+      }
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) is_last = atomicAdd(cnt + 16, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  // the last token block: the chunk's per-token results into the tail layout (tokens >= T empty)
+  const TailSmem s = carve_tail(smem_raw, E, k);
+  for (int i = threadIdx.x; i < kRouteTokens * E; i += 256) {
+    const int tok = i / E, e = i - tok * E;
+    s.logits[tok * s.lds + e] = tok < T ? __ldcg(ws.small_logits + i) : 0.f;
+  }
+  for (int i = threadIdx.x; i < kRouteTokens * k; i += 256) s.sel[i] = i < T * k ? __ldcg(a.topk_idx + i) : -1;
+  for (int i = threadIdx.x; i < kRouteTokens; i += 256) {
+    s.lse2[i] = i < T ? __ldcg(ws.small_tok + i) : 0.f;
+    s.nval[i] = i < T ? __ldcg(ws.small_tok + kRouteTokens + i) : 0.f;
+  }
+  __syncthreads();
+  route_chunk_stats<EW, 256>(s, threadIdx.x, 0, T, E, k, ws, BlockSync());
+  __syncthreads();  // the chunk counts and sums (global memory of this block) are complete
+  finish_single_chunk(E, k, ws, a.counts_out, a.stats, a.offs_out);
+}
+
+inline size_t small_router_smem(int d, int E, int k) {
+  const size_t xrows = sizeof(uint16_t) * 8 * size_t(d), logits = sizeof(float) * 8 * size_t(E);
+  const size_t own = xrows > logits ? xrows : logits;
+  const size_t tail = tail_smem_bytes(E, k);
+  return own > tail ? own : tail;
+}
+
 // ---------------------------------------------------------------- scan
 
 
@@ -836,6 +1043,33 @@ int launch_route(const uint16_t* x, const float* wr, const float* bias, const fl
     // The GEMV stages 8 bf16 token rows in shared memory (16 d bytes); wider rows take
     // the tensor-core router, which streams d in 64-column boxes at any width.
     const size_t gemv_smem = sizeof(uint16_t) * 8 * size_t(d);
+    if (logits_in == nullptr && T <= kRouteTokens && ws.small_logits != nullptr && ws.small_tok != nullptr &&
+        small_router_smem(d, E, k) <= kRouteGemvMaxSmem) {
+      // one chunk from x: logits, per-token routing and the chunk's statistics in one launch
+      a.counts_out = counts_out;
+      a.stats = stats;
+      a.offs_out = offs_out;
+      if (cudaMemsetAsync(ws.small_tok + 2 * kRouteTokens, 0, 17 * sizeof(uint32_t), stream) != cudaSuccess)
+        return MCL4MOE_ERR_CUDA;  // completion counters
+      const size_t smem = small_router_smem(d, E, k);
+      const dim3 grid((T + kSmallTokPerCta - 1) / kSmallTokPerCta, (E + 7) / 8);
+      cudaError_t e;
+      static std::atomic<uint64_t> c1{0}, c2{0}, c4{0}, c8{0};
+      if (E <= 32) {
+        if (!raise_smem_limit(router_small_kernel<1>, int(kRouteGemvMaxSmem), c1)) return MCL4MOE_ERR_CUDA;
+        e = launch_pdl(router_small_kernel<1>, grid, dim3(256), smem, stream, x, wr, bias, a, ws);
+      } else if (E <= 64) {
+        if (!raise_smem_limit(router_small_kernel<2>, int(kRouteGemvMaxSmem), c2)) return MCL4MOE_ERR_CUDA;
+        e = launch_pdl(router_small_kernel<2>, grid, dim3(256), smem, stream, x, wr, bias, a, ws);
+      } else if (E <= 128) {
+        if (!raise_smem_limit(router_small_kernel<4>, int(kRouteGemvMaxSmem), c4)) return MCL4MOE_ERR_CUDA;
+        e = launch_pdl(router_small_kernel<4>, grid, dim3(256), smem, stream, x, wr, bias, a, ws);
+      } else {
+        if (!raise_smem_limit(router_small_kernel<8>, int(kRouteGemvMaxSmem), c8)) return MCL4MOE_ERR_CUDA;
+        e = launch_pdl(router_small_kernel<8>, grid, dim3(256), smem, stream, x, wr, bias, a, ws);
+      }
+      return e == cudaSuccess && cudaGetLastError() == cudaSuccess ? MCL4MOE_OK : MCL4MOE_ERR_CUDA;
+    }
     if (logits_in == nullptr && T <= kRouteGemvMaxT && ws.small_logits != nullptr && gemv_smem <= kRouteGemvMaxSmem) {
       const size_t smem = gemv_smem;
       if (smem > 48 * 1024) {
