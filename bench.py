@@ -14,10 +14,13 @@ quantised-weight cache is reused across steps, as in the reference).
 Multi-GPU (torchrun, one process per GPU): weak scaling with expert
 parallelism.  Every rank routes its own T tokens; the experts are sharded in
 contiguous blocks of E/N (``ExpertParallelMoE``), each rank sends its tokens'
-NVFP4 rows to the ranks holding their experts and gets bf16 partial sums back
-(copy-engine copies into CUDA-IPC-mapped peer buffers, ordered by a
-one-element NCCL all-reduce).  ``value`` is the tokens of all ranks over the
-slowest rank's device time.
+NVFP4 rows to the ranks holding their experts (copy-engine copies into
+CUDA-IPC-mapped peer buffers, ordered by a one-element NCCL all-reduce); by
+default (``--ep-back h``) the receivers' gate/up GEMMs store each slot's NVFP4 h
+straight into its source's layout and every rank runs the down projection and
+combine of its own tokens (all experts' down weights on every rank), else
+(``--ep-back partials``) bf16 partial sums come back.  ``value`` is the tokens
+of all ranks over the slowest rank's device time.
 
 CPU baselines (rank 0, 1 GPU): the reference's own ``SparseMoE.forward``
 (installed under ``baseline/_ref``) on the host cores with its expert
@@ -67,6 +70,7 @@ KERNELS_PER_FORWARD = 7  # router-weight split, router, route-scan, permute+quan
 # sums (1) + combine (1)
 KERNELS_PER_EP_FORWARD = 14
 EP_STAGES = ("route", "dispatch", "counts", "exchange_rows", "experts", "exchange_partials", "combine")
+EP_STAGES_H = ("route_layout", "dispatch", "counts", "exchange_rows", "gateup_h_to_home", "h_arrival", "down_combine")
 
 
 def load_peaks() -> dict:
@@ -491,6 +495,8 @@ def run_ours(args) -> None:
         # expert parallel: the same layer on every rank, each keeps its E / N experts
         moe = pkg.ExpertParallelMoE.from_dense(moe, chunks=args.ep_chunks)
         moe.partials_via = args.ep_partials
+        if args.ep_back == "partials":
+            moe.down_experts = None
 
     def barrier():
         if world > 1:
@@ -546,7 +552,7 @@ def run_ours(args) -> None:
             allst = [None] * world
             dist.all_gather_object(allst, stage_ms)
             stage_spread = {name: [round(min(r[i] for r in allst), 4), round(max(r[i] for r in allst), 4)]
-                            for i, name in enumerate(EP_STAGES)}
+                            for i, name in enumerate(EP_STAGES if moe.down_experts is None else EP_STAGES_H)}
 
         # end to end through the public API with host buffers: every step copies its x from
         # pinned host memory and its output (plus aux / z) back; uploads, layer and downloads
@@ -634,11 +640,13 @@ def run_ours(args) -> None:
         "config": {"workload": cfg["name"], "tokens_per_gpu": T, "d_model": d, "num_experts": E, "top_k": k,
                    "expert_ffn": F, "parallelism": f"ep{world}" if ep else "single",
                    **({"ep_chunks": len(moe._chunk_bounds(T)), "ep_chunk_weights": moe.chunk_weights,
-                      "ep_partials": moe.partials_via} if ep else {}),
+                      "ep_back": "h" if moe.down_experts is not None else "partials",
+                      **({"ep_partials": moe.partials_via} if moe.down_experts is None else {})} if ep else {}),
                    **({"cuda_graph": True} if graph else {}),
                    "l2": "no flush: x (%.0f MB) and NVFP4 weights (%.0f MB) exceed the 126 MB L2" % (
                        T * d * 2 / 1e6, E * 3 * d * F * (0.5 + 1 / 16) / 1e6)},
-        "stages_ms": dict(zip(EP_STAGES if ep else ("route", "permute_quant", "gateup_gemm", "down_gemm", "combine"),
+        "stages_ms": dict(zip((EP_STAGES if moe.down_experts is None else EP_STAGES_H) if ep
+                              else ("route", "permute_quant", "gateup_gemm", "down_gemm", "combine"),
                               [round(s, 4) for s in stage_ms])),
         **({"stages_ms_over_ranks": stage_spread} if ep else {}),
         "layer_fp4_tflops": layer_tflops,
@@ -774,6 +782,9 @@ def main() -> None:
                     help="1 GPU: serve the timed forwards from a captured CUDA graph (SparseMoE.enable_cuda_graph)")
     ap.add_argument("--ep-partials", default="copy", choices=("kernel", "copy"),
                     help="expert parallel: partial sums stored to their sources by the summing kernel or copied")
+    ap.add_argument("--ep-back", default="h", choices=("h", "partials"),
+                    help="expert parallel: NVFP4 h stored to the tokens' home ranks (down projection there), "
+                         "or bf16 partial sums returned")
     ap.add_argument("--ep-chunks", type=int, default=0,
                     help="expert parallel (N > 1): token chunks whose exchange overlaps another chunk's experts")
     args = ap.parse_args()

@@ -483,6 +483,44 @@ int mcl4moe_ep_experts_to_peers(const uint8_t* recv_buf, int R, int slots, int d
                                 size_t workspace_bytes, mcl4moe_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Expert parallelism with the down projection at the token's home GPU ("h
+ * back"; no counterpart in the reference).  The gate/up projections stay
+ * sharded; the receiving GPU sends back each slot's NVFP4 h (F/2 codes + F/16
+ * scales) instead of a bf16 partial sum (d values), and the source runs the
+ * down projection (all E experts' down weights on every GPU) and the combine
+ * of the single-device layer, so its output is the single-device output bit
+ * for bit.
+ *
+ * mcl4moe_moe_forward_layout: the first half of mcl4moe_moe_forward (routing
+ * and the expert-major layout of the call's slots, as mcl4moe_moe_args /
+ * workspace); w_up / w_dn are not read.  The layout's slot_pos
+ * (mcl4moe_workspace_region 6, int32 [T, k]) is what _dispatch_pack_h needs.
+ * mcl4moe_ep_dispatch_pack_h: mcl4moe_ep_dispatch_pack whose rows carry, in
+ * place of the k weights, the k destinations of the slots' h on this rank
+ * (rank << 28 | slot_pos row; -1 for slots on other ranks).
+ * mcl4moe_ep_gateup_to_peers: on the receiver, the gate/up GEMM with SwiGLU and
+ * NVFP4 re-quantisation of the received slots, each slot's h stored into
+ * hq_dst[rank] (codes [M_cap, F/2]) and hs_dst[rank] (128x4 swizzled scales for
+ * M_cap rows) of its source; hq_dst / hs_dst (host arrays of G device
+ * pointers) may map other GPUs' memory (mcl4moe_ipc_import).  The stores are
+ * complete when the stream reaches the end of the call.
+ * mcl4moe_moe_forward_down: the second half of mcl4moe_moe_forward on the same
+ * args and workspace, the down projection reading h from hq / hs (NULL: the
+ * workspace's own), then the combine into args->out.
+ * ------------------------------------------------------------------------ */
+int mcl4moe_moe_forward_layout(const mcl4moe_moe_args* args, mcl4moe_stream_t stream);
+int mcl4moe_moe_forward_down(const mcl4moe_moe_args* args, const uint8_t* hq, const uint8_t* hs,
+                             mcl4moe_stream_t stream);
+int mcl4moe_ep_dispatch_pack_h(const uint16_t* x, const int32_t* topk_idx, const uint8_t* valid, int T, int d, int k,
+                               int G, int E_loc, int rank, const int32_t* slot_pos, const int32_t* send_counts,
+                               int32_t* send_pos, uint8_t* send_buf, void* workspace, size_t workspace_bytes,
+                               mcl4moe_stream_t stream);
+int mcl4moe_ep_gateup_to_peers(const uint8_t* recv_buf, int R, int slots, int d, int k, int E_loc, int F,
+                               const uint8_t* w_up, const uint8_t* w_up_scales, const float* w_up_g, int G,
+                               void* const* hq_dst, void* const* hs_dst, int32_t* error_word, void* workspace,
+                               size_t workspace_bytes, mcl4moe_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Peer-memory transport for the expert-parallel exchange (no counterpart in
  * the reference).  mcl4moe_ipc_export: CUDA IPC handle (64 bytes) of the
  * allocation holding ptr, and ptr's offset in it.  mcl4moe_ipc_import (another

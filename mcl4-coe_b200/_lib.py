@@ -37,6 +37,10 @@ EXPORTS = (
     "mcl4moe_moe_forward_routed",
     "mcl4moe_padded_rows",
     "mcl4moe_set_expert_tiling",
+    "mcl4moe_moe_forward_layout",
+    "mcl4moe_moe_forward_down",
+    "mcl4moe_ep_dispatch_pack_h",
+    "mcl4moe_ep_gateup_to_peers",
     "mcl4moe_workspace_region",
     "mcl4moe_grouped_linear_workspace_size",
     "mcl4moe_grouped_linear",
@@ -257,6 +261,17 @@ def load() -> ctypes.CDLL:
     lib.mcl4moe_nvfp4_linear_wgrad.argtypes = [c_void_p, c_int, c_void_p, c_int, c_int64, c_int, c_int,
                                                ctypes.c_uint64, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
                                                c_void_p]
+    lib.mcl4moe_moe_forward_layout.restype = c_int
+    lib.mcl4moe_moe_forward_layout.argtypes = [POINTER(MoeArgs), c_void_p]
+    lib.mcl4moe_moe_forward_down.restype = c_int
+    lib.mcl4moe_moe_forward_down.argtypes = [POINTER(MoeArgs), c_void_p, c_void_p, c_void_p]
+    lib.mcl4moe_ep_dispatch_pack_h.restype = c_int
+    lib.mcl4moe_ep_dispatch_pack_h.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,
+                                               c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]
+    lib.mcl4moe_ep_gateup_to_peers.restype = c_int
+    lib.mcl4moe_ep_gateup_to_peers.argtypes = [c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
+                                               c_void_p, c_int, POINTER(c_void_p), POINTER(c_void_p), c_void_p,
+                                               c_void_p, c_size_t, c_void_p]
     lib.mcl4moe_set_expert_tiling.restype = c_int
     lib.mcl4moe_set_expert_tiling.argtypes = [c_int]
     lib.mcl4moe_moe_backward_dx.restype = c_int

@@ -440,6 +440,33 @@ int forward_experts(const mcl4moe_moe_args* a, const MoeWorkspace& w, const int3
   return mark(a, 5, s);
 }
 
+// Down projection with the routing weight and combine, on h rows already in the expert-major
+// layout (hq codes [M_cap, F/2], swizzled hs scales) that the permute of this call laid out.
+int experts_down(const mcl4moe_moe_args* a, const MoeWorkspace& w, const uint8_t* hq, const uint8_t* hs,
+                 int32_t* err, cudaStream_t s) {
+  const int T = a->T, d = a->d, E = a->E, k = a->k, F = a->F;
+  const int64_t mcap = padded_rows_cap(T, E, k);
+  GemmArgs g2{};
+  g2.pad_start = w.route.pad_start;
+  g2.row_count = w.route.counts;
+  g2.a_scales = hs;
+  g2.b_scales = a->w_dn_scales;
+  g2.b_g = a->w_dn_g;
+  g2.E = E;
+  g2.K = F;
+  g2.N_total = d;
+  g2.n_tiles = d / 256;
+  g2.mode = 1;
+  g2.row_w = w.sorted_w;
+  g2.y = w.y;
+  g2.ldy = d;
+  g2.err = err;
+  g2.solo = use_solo_tiles(a) ? 1 : 0;
+  int st = launch_grouped_gemm(hq, mcap, a->w_dn, g2, s);
+  if (st != MCL4MOE_OK) return st;
+  return launch_combine(w.y, w.slot_pos, a->valid, T, k, d, a->out, s, nullptr);
+}
+
 int mark_stage(const mcl4moe_moe_args* a, int i, cudaStream_t s) {
   if (a->stage_events == nullptr || a->stage_events[i] == nullptr) return MCL4MOE_OK;
   return cudaEventRecord(static_cast<cudaEvent_t>(a->stage_events[i]), s) == cudaSuccess ? MCL4MOE_OK
@@ -486,6 +513,44 @@ int mcl4moe_moe_forward(const mcl4moe_moe_args* a, mcl4moe_stream_t stream) {
     return MCL4MOE_OK;
   }
   return forward_experts(a, w, topk_idx, topk_w, err, s, mark_stage);
+}
+
+int mcl4moe_moe_forward_layout(const mcl4moe_moe_args* a, mcl4moe_stream_t stream) {
+  if (!a) return MCL4MOE_ERR_INVALID;
+  int st = check_moe_shape(a->T, a->d, a->E, a->k, a->F);
+  if (st != MCL4MOE_OK) return st;
+  if (!a->workspace || !a->stats || (a->T > 0 && (!a->x || !a->router_w))) return MCL4MOE_ERR_INVALID;
+  if (!aligned16(a->x) || !aligned16(a->router_w)) return MCL4MOE_ERR_INVALID;
+  const MoeWorkspace w = moe_workspace(a->workspace, a->T, a->d, a->E, a->k, a->F);
+  if (a->workspace_bytes < w.bytes) return MCL4MOE_ERR_WORKSPACE;
+  cudaStream_t s = stream;
+  const int T = a->T, d = a->d, E = a->E, k = a->k;
+  int32_t* err = error_word(a, w, s, &st);
+  if (st != MCL4MOE_OK) return st;
+  int32_t* topk_idx = a->topk_idx ? a->topk_idx : w.topk_idx;
+  float* topk_w = a->topk_w ? a->topk_w : w.topk_w;
+  st = launch_route(a->x, a->router_w, a->logit_bias, nullptr, a->valid, T, d, E, k, a->norm_topk_prob, topk_idx,
+                    topk_w, a->logits_out, a->sel_mask, w.counts, a->stats, a->offs, err, w.route, s);
+  if (st != MCL4MOE_OK || T == 0) return st;
+  return launch_permute_quantize(a->x, a->valid, topk_idx, topk_w, T, d, E, k, w.route, w.slot_pos, w.sorted_w,
+                                 a->perm, w.xq, w.xs, s, nullptr);
+}
+
+int mcl4moe_moe_forward_down(const mcl4moe_moe_args* a, const uint8_t* hq, const uint8_t* hs,
+                             mcl4moe_stream_t stream) {
+  if (!a) return MCL4MOE_ERR_INVALID;
+  int st = check_moe_shape(a->T, a->d, a->E, a->k, a->F);
+  if (st != MCL4MOE_OK) return st;
+  if (!a->workspace || !a->w_dn || !a->w_dn_scales || !a->w_dn_g || (a->T > 0 && !a->out)) return MCL4MOE_ERR_INVALID;
+  if (!aligned16(a->out) || !aligned16(a->w_dn) || !aligned16(a->w_dn_scales) || !aligned16(hq) || !aligned16(hs))
+    return MCL4MOE_ERR_INVALID;
+  const MoeWorkspace w = moe_workspace(a->workspace, a->T, a->d, a->E, a->k, a->F);
+  if (a->workspace_bytes < w.bytes) return MCL4MOE_ERR_WORKSPACE;
+  if (a->T == 0) return MCL4MOE_OK;
+  cudaStream_t s = stream;
+  int32_t* err = error_word(a, w, s, &st);
+  if (st != MCL4MOE_OK) return st;
+  return experts_down(a, w, hq ? hq : w.hq, hs ? hs : w.hs, err, s);
 }
 
 int mcl4moe_moe_forward_routed(const mcl4moe_moe_args* a, mcl4moe_stream_t stream) {

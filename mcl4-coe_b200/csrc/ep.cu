@@ -122,7 +122,8 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const uint16_t* __restrict
                                                       int E_loc, const int32_t* __restrict__ grp_offs,
                                                       const int32_t* __restrict__ send_rows,
                                                       uint8_t* __restrict__ send_buf,
-                                                      int32_t* __restrict__ send_pos) {
+                                                      int32_t* __restrict__ send_pos,
+                                                      const int32_t* __restrict__ slot_src, int me) {
   __shared__ int32_t s_pos[32][kMaxRanks];
   __shared__ int32_t s_start[kMaxRanks];
   __shared__ float inv_tab[128];
@@ -161,16 +162,21 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const uint16_t* __restrict
     bool any = false;
     for (int g = 0; g < G; ++g) any |= s_pos[tl][g] >= 0;
     if (!any) continue;
-    // metadata: local ids on each destination and the k weights
+    // metadata: local ids on each destination and the k weights, or (slot_src) the k
+    // destinations of the slots' h in this rank's expert-major layout (me << 28 | row)
     const int e = lane < k ? topk_idx[int64_t(t) * k + lane] : -1;
-    const float wt = lane < k ? topk_w[int64_t(t) * k + lane] : 0.f;
+    const float wt = (lane < k && slot_src == nullptr) ? topk_w[int64_t(t) * k + lane] : 0.f;
+    const int32_t code = (lane < k && slot_src != nullptr && e >= 0) ? ((me << 28) | slot_src[int64_t(t) * k + lane]) : -1;
     for (int g = 0; g < G; ++g) {
       const int p = s_pos[tl][g];
       if (p < 0) continue;
       uint8_t* row = send_buf + int64_t(p) * L.bytes;
-      if (lane < (k + 15) / 16 * 16)
-        row[L.ids + lane] = uint8_t(int8_t((lane < k && e >= 0 && e / E_loc == g) ? e - g * E_loc : -1));
-      if (lane < k) reinterpret_cast<float*>(row + L.weights)[lane] = wt;
+      const bool here = lane < k && e >= 0 && e / E_loc == g;
+      if (lane < (k + 15) / 16 * 16) row[L.ids + lane] = uint8_t(int8_t(here ? e - g * E_loc : -1));
+      if (lane < k) {
+        if (slot_src != nullptr) reinterpret_cast<int32_t*>(row + L.weights)[lane] = here ? code : -1;
+        else reinterpret_cast<float*>(row + L.weights)[lane] = wt;
+      }
     }
     // codes and scales (the activation quantiser of the single-GPU path)
     for (int b0 = 0; b0 < nblk; b0 += 32) {
@@ -550,7 +556,28 @@ int mcl4moe_ep_dispatch_pack(const uint16_t* x, const int32_t* topk_idx, const f
   if (T == 0) return MCL4MOE_OK;
   const int W = (T + 31) / 32;
   return launch_pdl(ep_pack_kernel, dim3(W), dim3(256), 0, stream, x, topk_idx, topk_w, valid, T, d, k, G, E_loc,
-                    static_cast<const int32_t*>(workspace), send_counts, send_buf, send_pos) == cudaSuccess
+                    static_cast<const int32_t*>(workspace), send_counts, send_buf, send_pos,
+                    static_cast<const int32_t*>(nullptr), 0) == cudaSuccess
+             ? MCL4MOE_OK
+             : MCL4MOE_ERR_CUDA;
+}
+
+int mcl4moe_ep_dispatch_pack_h(const uint16_t* x, const int32_t* topk_idx, const uint8_t* valid, int T, int d, int k,
+                               int G, int E_loc, int rank, const int32_t* slot_pos, const int32_t* send_counts,
+                               int32_t* send_pos, uint8_t* send_buf, void* workspace, size_t workspace_bytes,
+                               mcl4moe_stream_t stream) {
+  int st = check_ep_shape(d, k, G, E_loc, 256);
+  if (st != MCL4MOE_OK) return st;
+  if (T < 0 || rank < 0 || rank >= G || !send_counts || !workspace ||
+      (T > 0 && (!x || !topk_idx || !slot_pos || !send_pos || !send_buf)))
+    return MCL4MOE_ERR_INVALID;
+  if (!aligned16(x) || !aligned16(send_buf)) return MCL4MOE_ERR_INVALID;
+  if (workspace_bytes < dispatch_ws_bytes(T, G)) return MCL4MOE_ERR_WORKSPACE;
+  if (T == 0) return MCL4MOE_OK;
+  const int W = (T + 31) / 32;
+  return launch_pdl(ep_pack_kernel, dim3(W), dim3(256), 0, stream, x, topk_idx, static_cast<const float*>(nullptr),
+                    valid, T, d, k, G, E_loc, static_cast<const int32_t*>(workspace), send_counts, send_buf, send_pos,
+                    slot_pos, rank) == cudaSuccess
              ? MCL4MOE_OK
              : MCL4MOE_ERR_CUDA;
 }
@@ -676,6 +703,51 @@ int mcl4moe_ep_experts_to_peers(const uint8_t* recv_buf, int R, int slots, int d
   }
   return ep_experts_impl(recv_buf, R, slots, d, k, E_loc, F, w_up, w_up_scales, w_up_g, w_dn, w_dn_scales, w_dn_g,
                          nullptr, &e, error_word, workspace, workspace_bytes, stream);
+}
+
+int mcl4moe_ep_gateup_to_peers(const uint8_t* recv_buf, int R, int slots, int d, int k, int E_loc, int F,
+                               const uint8_t* w_up, const uint8_t* w_up_scales, const float* w_up_g, int G,
+                               void* const* hq_dst, void* const* hs_dst, int32_t* error_word, void* workspace,
+                               size_t workspace_bytes, mcl4moe_stream_t stream) {
+  int st = check_ep_shape(d, k, G, E_loc, F);
+  if (st != MCL4MOE_OK) return st;
+  if (R < 0 || slots < 0 || !workspace || !hq_dst || !hs_dst || (R > 0 && !recv_buf)) return MCL4MOE_ERR_INVALID;
+  if (!w_up || !w_up_scales || !w_up_g || !aligned16(recv_buf) || !aligned16(w_up) || !aligned16(w_up_scales))
+    return MCL4MOE_ERR_INVALID;
+  for (int g = 0; g < G; ++g)
+    if (!hq_dst[g] || !hs_dst[g] || !aligned16(hq_dst[g]) || (reinterpret_cast<uintptr_t>(hs_dst[g]) & 1))
+      return MCL4MOE_ERR_INVALID;
+  const ExpertsWs w = experts_ws(workspace, R, slots, d, k, E_loc, F);
+  if (workspace_bytes < w.bytes) return MCL4MOE_ERR_WORKSPACE;
+  if (R == 0) return MCL4MOE_OK;
+  cudaStream_t s = stream;
+  int32_t* err = error_word ? error_word : w.err;
+  if (!error_word && cudaMemsetAsync(w.err, 0, sizeof(int32_t), s) != cudaSuccess) return MCL4MOE_ERR_CUDA;
+  const cudaError_t le = E_loc <= 32    ? launch_recv_layout<1>(recv_buf, R, d, k, E_loc, w, s)
+                         : E_loc <= 64  ? launch_recv_layout<2>(recv_buf, R, d, k, E_loc, w, s)
+                         : E_loc <= 128 ? launch_recv_layout<4>(recv_buf, R, d, k, E_loc, w, s)
+                                        : launch_recv_layout<8>(recv_buf, R, d, k, E_loc, w, s);
+  if (le != cudaSuccess || cudaGetLastError() != cudaSuccess) return MCL4MOE_ERR_CUDA;
+  GemmArgs g1{};
+  g1.pad_start = w.pad_start;
+  g1.row_count = w.counts;
+  g1.a_scales = w.xs;
+  g1.a_sf_rowmajor = 1;
+  g1.b_scales = w_up_scales;
+  g1.b_g = w_up_g;
+  g1.E = E_loc;
+  g1.K = d;
+  g1.N_total = 2 * F;
+  g1.n_tiles = F / 128;
+  g1.mode = 4;
+  g1.F = F;
+  g1.row_w = w.sorted_w;  // the rows' h destinations, from the dispatched rows
+  g1.err = err;
+  for (int g = 0; g < G; ++g) {
+    g1.peer_hq[g] = static_cast<uint8_t*>(hq_dst[g]);
+    g1.peer_hs[g] = static_cast<uint8_t*>(hs_dst[g]);
+  }
+  return launch_grouped_gemm(w.xq, w.mcap, w_up, g1, s);
 }
 
 int mcl4moe_ep_combine(const uint16_t* back_buf, const int32_t* send_pos, int T, int d, int G, uint16_t* out,

@@ -90,7 +90,7 @@ struct Cfg {
   static constexpr uint32_t kAB = SOLO ? kATile + 2 * kBHalf : kABBytes;
   static constexpr uint32_t kStage = kAB + kSFBytes;
   static constexpr uint32_t kOffSfa = kAB, kOffSfb = kAB + kSFA;
-  static constexpr int kStages = SOLO ? 4 : (MODE == 0 ? 5 : 4);
+  static constexpr int kStages = SOLO ? 4 : ((MODE == 0 || MODE == 4) ? 5 : 4);
   static constexpr uint32_t kStoreBytes = (!SOLO && (MODE == 1 || MODE == 3)) ? kEpiWarps * kWarpStoreBytes : 0;
   static constexpr size_t kSmem = 1024 /*align*/ + size_t(kStages) * kStage + kStoreBytes + kBarBytes +
                                   sizeof(int32_t) * (kMaxExperts + 1) + sizeof(float) * 128;
@@ -100,6 +100,7 @@ static_assert(kStageBytes % 1024 == 0, "stage must keep 1024-byte alignment for 
 static_assert(Cfg<0>::kSmem <= 232448 && Cfg<1>::kSmem <= 232448 && Cfg<2>::kSmem <= 232448 && Cfg<3>::kSmem <= 232448,
               "shared memory");
 static_assert(Cfg<0, true>::kSmem <= 232448 && Cfg<1, true>::kSmem <= 232448, "shared memory (solo)");
+static_assert(Cfg<4>::kSmem <= 232448, "shared memory (mode 4)");
 static_assert(Cfg<0, true>::kStage % 1024 == 0, "solo stage alignment");
 static_assert(kSfCol0 + Cfg<0, true>::kStages * kSfColsPerStage <= kTmemCols, "TMEM budget (solo)");
 static_assert(kSfCol0 + Cfg<0>::kStages * kSfColsPerStage <= kTmemCols, "TMEM budget");
@@ -155,7 +156,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int pair = SOLO ? int(blockIdx.x) : int(cluster_id_x());
   const int npairs = SOLO ? int(gridDim.x) : int(cluster_count_x());
 
-  if ((MODE == 0 || MODE == 3) && tid < 128) s_inv[tid] = inverse_decoding(e4m3_to_f32(uint32_t(tid)));
+  constexpr bool kGateUp = MODE == 0 || MODE == 3 || MODE == 4;
+  if (kGateUp && tid < 128) s_inv[tid] = inverse_decoding(e4m3_to_f32(uint32_t(tid)));
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(full_bar(s), 1 + (SOLO ? 1 : 2) * kSfWarps);
@@ -211,7 +213,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     return !SOLO || args.row_count == nullptr || c.pm * kBM - pad_s[c.e] < __ldg(args.row_count + c.e);
   };
   auto b_rows = [&](const TileCoord& c, int& lr0, int& lr1) {  // local B rows of the tile's two 128-row halves
-    if (MODE == 0 || MODE == 3) {
+    if (kGateUp) {
       lr0 = c.nt * 128;           // gate rows
       lr1 = args.F + c.nt * 128;  // value rows
     } else {
@@ -415,12 +417,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       // acc * (g_a * g_b), the reference's order (src/mcl4_coe/nvfp4.py:869); g_a = 1 unless given
       const float gb = args.a_g != nullptr ? __fmul_rn(__ldg(args.a_g), __ldg(args.b_g + c.e)) : __ldg(args.b_g + c.e);
       const int rows_e = args.row_count ? __ldg(args.row_count + c.e) : (1 << 30);
-      const float wrow = (MODE != 0 && MODE != 3 && args.row_w && local < rows_e) ? __ldg(args.row_w + p) : 0.f;
+      const float wrow = (!kGateUp && args.row_w && local < rows_e) ? __ldg(args.row_w + p) : 0.f;
+      // MODE 4: destination (rank << 28 | row) of this row's h in its source's layout
+      const int32_t hdst = (MODE == 4 && local < rows_e) ? __float_as_int(__ldg(args.row_w + p)) : -1;
       if (!mbar_wait(tfull_bar, acc_phase, args.err, 301)) break;
       acc_phase ^= 1u;
       tc_fence_after();
       uint32_t va[32], vb[32];
-      if (MODE == 0 || MODE == 3) {
+      if (kGateUp) {
         tmem_ld32(lane_addr + sub * 32, va);        // gate columns
         tmem_ld32(lane_addr + 128 + sub * 32, vb);  // value columns
       } else {
@@ -435,7 +439,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         else mbar_arrive_cluster(tempty_leader);
       }
 
-      if (MODE == 0 || MODE == 3) {
+      if (kGateUp) {
         // up = bf16(acc * g); h = bf16(bf16(silu(gate)) * value) (src/mcl4_coe/backbone.py:572-574),
         // then NVFP4 with 1x16 row scales (src/mcl4_coe/nvfp4.py:197-225).
         const int F = args.F;
@@ -506,11 +510,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             bulk_commit_group();
           }
         }
-        *reinterpret_cast<uint4*>(args.hq + p * (F / 2) + hb0 * 8) =
-            make_uint4(packed[0], packed[1], packed[2], packed[3]);
-        *reinterpret_cast<uint16_t*>(args.hs +
-                                     swizzled_scale_offset(uint64_t(p), uint32_t(hb0), uint32_t(F / 16))) =
-            uint16_t(sword);
+        if (MODE == 4) {
+          // expert parallelism: h goes straight to the token's home GPU (peer stores over
+          // NVLink into its expert-major layout), where the down projection runs
+          if (hdst >= 0) {
+            const int rk = hdst >> 28;
+            const uint64_t row = uint64_t(hdst & 0x0FFFFFFF);
+            *reinterpret_cast<uint4*>(args.peer_hq[rk] + row * (F / 2) + hb0 * 8) =
+                make_uint4(packed[0], packed[1], packed[2], packed[3]);
+            *reinterpret_cast<uint16_t*>(args.peer_hs[rk] + swizzled_scale_offset(row, uint32_t(hb0), uint32_t(F / 16))) =
+                uint16_t(sword);
+          }
+        } else {
+          *reinterpret_cast<uint4*>(args.hq + p * (F / 2) + hb0 * 8) =
+              make_uint4(packed[0], packed[1], packed[2], packed[3]);
+          *reinterpret_cast<uint16_t*>(args.hs +
+                                       swizzled_scale_offset(uint64_t(p), uint32_t(hb0), uint32_t(F / 16))) =
+              uint16_t(sword);
+        }
       } else if (MODE == 1 && !SOLO) {
         // y = bf16(acc * g) [* bf16(routing weight), rounded to bf16] (src/mcl4_coe/backbone.py:903),
         // every padded row (padding rows hold zeros), through a 32 x 64 swizzled smem tile.
@@ -715,6 +732,11 @@ int launch_grouped_gemm(const uint8_t* a, int64_t a_rows, const uint8_t* b, cons
   memset(&tsa, 0, sizeof(tsa));
   if (args.a_sf_rowmajor && !make_tmap_scales(&tsa, args.a_scales, uint64_t(args.K) / 16, uint64_t(a_rows)))
     return MCL4MOE_ERR_CUDA;
+  if (args.mode == 4) {  // gate/up with h stored into the rows' home GPUs
+    memset(&ty, 0, sizeof(ty));
+    if (args.row_w == nullptr || args.row_count == nullptr || args.F % 128 != 0) return MCL4MOE_ERR_INVALID;
+    return launch_mode<4>(ta, tb, ty, tsa, args, stream);
+  }
   if (args.mode == 0) {
     memset(&ty, 0, sizeof(ty));
     if (args.up_save == nullptr)

@@ -233,6 +233,10 @@ struct GemmArgs {
   int32_t* err;
   int solo;                     // modes 0 (inference) / 1: single-CTA 128-row tiles that skip padding-only
                                 // blocks (decode); mode 1 then writes valid rows only
+  // mode 4 (gate/up for expert parallelism): row_w holds each valid row's h destination
+  // (rank << 28 | row, as float bits); h codes / swizzled scales go to peer_hq / peer_hs[rank]
+  uint8_t* peer_hq[8];
+  uint8_t* peer_hs[8];
 };
 
 int launch_grouped_gemm(const uint8_t* a, int64_t a_rows, const uint8_t* b, const GemmArgs& args, cudaStream_t stream);

@@ -163,6 +163,85 @@ class CudaEPOps:
                                                    ws.data_ptr(), ws.numel(), _stream_handle()),
                    "mcl4moe_ep_experts_to_peers")
 
+    # ---- "h back": gate/up sharded, the down projection at the token's home GPU
+
+    def layout(self, x: Tensor, wr: Tensor, bias: Tensor | None, valid: Tensor | None, k: int, norm: bool,
+               dn_all, F: int, slot: int = 0) -> dict:
+        """Routing and this rank's expert-major layout of its own slots
+        (``mcl4moe_moe_forward_layout``); the state that ``down`` continues from."""
+        lib = _lib.load()
+        T, d = x.shape
+        E = wr.shape[0]
+        dev = x.device
+        st = dict(T=T, d=d, E=E, k=k, F=F)
+        st["idx"] = torch.empty((T, k), dtype=torch.int32, device=dev)
+        st["w"] = torch.empty((T, k), dtype=torch.float32, device=dev)
+        st["stats"] = torch.empty((3 + E,), dtype=torch.float32, device=dev)
+        st["out"] = torch.empty((T, d), dtype=torch.bfloat16, device=dev)
+        ws = self._scratch(f"moe{slot}", lib.mcl4moe_moe_workspace_size(T, d, E, k, F), dev)
+        if T > 0 and ws.numel() < lib.mcl4moe_moe_workspace_size(T, d, E, k, F):
+            raise ValueError("unsupported layer shape for the expert-parallel layout")
+        p = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+        args = _lib.MoeArgs(
+            x=x.data_ptr(), router_w=wr.data_ptr(), logit_bias=p(bias), valid=p(valid),
+            w_dn=dn_all.packed.data_ptr(), w_dn_scales=dn_all.scales.data_ptr(), w_dn_g=dn_all.g.data_ptr(),
+            T=T, d=d, E=E, k=k, F=F, norm_topk_prob=int(norm), out=st["out"].data_ptr(),
+            stats=st["stats"].data_ptr(), topk_idx=st["idx"].data_ptr(), topk_w=st["w"].data_ptr(),
+            workspace=ws.data_ptr(), workspace_bytes=ws.numel())
+        _lib.check(lib.mcl4moe_moe_forward_layout(args, _stream_handle()), "mcl4moe_moe_forward_layout")
+        st["args"], st["ws"] = args, ws
+        mcap = lib.mcl4moe_padded_rows(T, E, k)
+        st["mcap"] = mcap
+        st["slot_pos"] = torch.empty((0, k), dtype=torch.int32, device=dev)
+        if T > 0:
+            base = ws.data_ptr()
+            off = lib.mcl4moe_workspace_region(base, 6, T, d, E, k, F) - base
+            st["slot_pos"] = ws[off:off + 4 * T * k].view(torch.int32).view(T, k)
+        return st
+
+    def dispatch_pack_h(self, x: Tensor, idx: Tensor, valid: Tensor | None, G: int, E_loc: int, rank: int,
+                        slot_pos: Tensor, counts: Tensor, slot: int = 0):
+        """``dispatch_pack`` whose rows carry the slots' h destinations on this rank."""
+        lib = _lib.load()
+        T, d = x.shape
+        k = idx.shape[1]
+        dev = x.device
+        rb = self.row_bytes(d, k)
+        send_buf = self._scratch(f"send{slot}", T * G * rb, dev)
+        pos = torch.empty((T, G), dtype=torch.int32, device=dev)
+        ws = self._scratch(f"dispatch{slot}", lib.mcl4moe_ep_dispatch_workspace_size(T, G), dev)
+        _lib.check(lib.mcl4moe_ep_dispatch_pack_h(x.data_ptr(), idx.data_ptr(),
+                                                  None if valid is None else valid.data_ptr(), T, d, k, G, E_loc,
+                                                  rank, slot_pos.data_ptr(), counts.data_ptr(), pos.data_ptr(),
+                                                  send_buf.data_ptr(), ws.data_ptr(), ws.numel(), _stream_handle()),
+                   "mcl4moe_ep_dispatch_pack_h")
+        return send_buf[: T * G * rb].view(T * G, rb), counts, pos
+
+    def gateup_to_peers(self, recv: Tensor, R: int, slots: int, d: int, k: int, experts: nn.ModuleList,
+                        hq_dst: list[int], hs_dst: list[int], up_cache=None) -> None:
+        """The received slots' gate/up GEMM with each slot's NVFP4 h stored into its
+        source's layout (``hq_dst[s]`` / ``hs_dst[s]``, peer mappings for other ranks)."""
+        lib = _lib.load()
+        dev = recv.device
+        E_loc = len(experts)
+        F = experts[0].down_proj.weight.shape[1]
+        up = up_cache if up_cache is not None else get_or_build_grouped_cache(experts, "up_proj")
+        G = len(hq_dst)
+        hq = (ctypes.c_void_p * G)(*hq_dst)
+        hs = (ctypes.c_void_p * G)(*hs_dst)
+        ws = self._scratch("experts", lib.mcl4moe_ep_experts_workspace_size(R, slots, d, k, E_loc, F), dev)
+        _lib.check(lib.mcl4moe_ep_gateup_to_peers(recv.data_ptr(), R, slots, d, k, E_loc, F, up.packed.data_ptr(),
+                                                  up.scales.data_ptr(), up.g.data_ptr(), G, hq, hs, None,
+                                                  ws.data_ptr(), ws.numel(), _stream_handle()),
+                   "mcl4moe_ep_gateup_to_peers")
+
+    def down(self, st: dict, hq: Tensor, hs: Tensor) -> Tensor:
+        """Down projection and combine of this rank's slots from the h rows in hq / hs."""
+        if st["T"] > 0:
+            _lib.check(_lib.load().mcl4moe_moe_forward_down(st["args"], hq.data_ptr(), hs.data_ptr(),
+                                                            _stream_handle()), "mcl4moe_moe_forward_down")
+        return st["out"]
+
     def combine(self, back: Tensor, pos: Tensor, T: int, d: int, G: int, out: Tensor | None = None) -> Tensor:
         if out is None:
             out = torch.empty((T, d), dtype=torch.bfloat16, device=pos.device)
@@ -385,6 +464,13 @@ class ExpertParallelMoE(nn.Module):
         # summing kernel) or "kernel" (stored over NVLink by the summing kernel itself; its
         # stores from all ranks at once contend: slower at 8 GPUs)
         self.partials_via = "copy"
+        # "h back" (peer transport): receivers return each slot's NVFP4 h (F/2 + F/16 bytes)
+        # instead of bf16 partial sums (2d bytes per row), and every rank runs the down
+        # projection of its own tokens with all experts' down weights (``down_experts``,
+        # all E experts; set by ``from_dense``): 2.7x fewer bytes back at 8 GPUs for the
+        # OLMoE shape, h stored straight into the source by the gate/up GEMM, and the
+        # output is the single-device layer's bit for bit.  None: partial sums.
+        self.down_experts: nn.ModuleList | None = None
 
     @classmethod
     def from_dense(cls, moe: nn.Module, group: dist.ProcessGroup | None = None, ops: Any = None,
@@ -410,12 +496,13 @@ class ExpertParallelMoE(nn.Module):
         mod.router = moe.router
         lo = mod.expert_offset
         mod.experts = nn.ModuleList(list(moe.experts)[lo:lo + mod.experts_per_rank])
+        mod.down_experts = nn.ModuleList(list(moe.experts))
         mod.router_logit_bias = getattr(moe, "router_logit_bias", None)
         return mod
 
     @torch.no_grad()
     def reshard(self, router: nn.Linear, old_to_new, *, parents: dict | None = None,
-                new_experts: dict | None = None) -> dict:
+                new_experts: dict | None = None, dense_experts: nn.ModuleList | None = None) -> dict:
         """Follow a change of the expert set between calls (ExpertLifecycle's
         ``grow_experts`` / ``prune_experts``, src/mcl4_coe/ornith_rl.py:468-595, and the
         trainer's in-place mitosis, src/mcl4_coe/trainer.py:1624-1712) while the experts
@@ -427,7 +514,10 @@ class ExpertParallelMoE(nn.Module):
         ``ExpertMorphResult.old_to_new`` of the reference);
         ``parents[j] = p``: new expert j is a copy of old expert p (mitosis);
         ``new_experts[j]``: a module (``up_proj`` / ``down_proj``) for a new expert that
-        is neither kept nor copied, given on every rank.
+        is neither kept nor copied, given on every rank;
+        ``dense_experts``: all E' experts of the changed dense layer, for the "h back"
+        exchange (every rank runs the down projection of its own tokens); without it the
+        layer returns partial sums.
         Experts whose owner changes travel to their new rank with their weights and, on
         CUDA, their NVFP4 bytes (one all-to-all); a copy takes its parent's bytes; only
         the ``new_experts`` are quantised (by the next forward).  Experts that keep their
@@ -543,6 +633,7 @@ class ExpertParallelMoE(nn.Module):
         self.num_experts = E_new
         self.experts_per_rank = loc_new
         self.expert_offset = me * loc_new
+        self.down_experts = dense_experts
         return stats
 
     def _all_to_all(self, out: Tensor, inp: Tensor, out_splits: list[int], in_splits: list[int]) -> None:
@@ -565,13 +656,15 @@ class ExpertParallelMoE(nn.Module):
         ev = self.stage_events
         mark = (lambda i: ev[i].record()) if ev is not None else (lambda i: None)
         mark(0)
+        use_peer = self.transport == "peer" or (
+            self.transport == "auto" and xb.is_cuda and dist.get_backend(self.group) == "nccl")
+        if use_peer and self.down_experts is not None and hasattr(self.ops, "gateup_to_peers"):
+            return self._forward_h_back(x, xb, wr, bias, vmask, mark)
         caches = self.ops.prepare(self.experts) if hasattr(self.ops, "prepare") else None
         idx, w, stats = self.ops.route(xb, wr, bias, vmask, k, self.norm_topk_prob)
         mark(1)
         bounds = self._chunk_bounds(T)
         out = torch.empty((T, d), dtype=torch.bfloat16, device=xb.device)
-        use_peer = self.transport == "peer" or (
-            self.transport == "auto" and xb.is_cuda and dist.get_backend(self.group) == "nccl")
         if use_peer:
             disp, backs = self._exchange_peer(xb, idx, w, vmask, bounds, caches, mark)
         else:
@@ -586,6 +679,81 @@ class ExpertParallelMoE(nn.Module):
             self.ops.combine(backs[c], disp[c][2], hi - lo, d, G, out[lo:hi])
         mark(7)
         return out.to(x.dtype).view_as(x), stats[0], stats[1], stats[3:3 + self.num_experts]
+
+    def _forward_h_back(self, x: Tensor, xb: Tensor, wr: Tensor, bias: Tensor | None, vmask: Tensor | None,
+                        mark) -> tuple[Tensor, Tensor, Tensor, Tensor]:
+        """Peer transport, "h back": route and lay out this rank's slots; rows out per
+        chunk (the rows of chunk c+1 travel while the receivers' gate/up GEMMs of chunk c
+        run and store each slot's NVFP4 h straight into its source's layout); a
+        one-element all-reduce orders every rank after every rank's stores; down
+        projection and combine of this rank's tokens (the single-device kernels)."""
+        T, d = xb.shape
+        G, me, k, E = self.world, self.rank, self.top_k, self.num_experts
+        E_loc = self.experts_per_rank
+        F = self.experts[0].down_proj.weight.shape[1]
+        dev = xb.device
+        lib = _lib.load()
+        up = get_or_build_grouped_cache(self.experts, "up_proj")
+        dn_all = get_or_build_grouped_cache(self.down_experts, "down_proj")
+        st = self.ops.layout(xb, wr, bias, vmask, k, self.norm_topk_prob, dn_all, F)
+        idx, stats = st["idx"], st["stats"]
+        mark(1)
+        if self._peer is None:
+            self._peer = PeerExchange(self.group, dev)
+        px = self._peer
+        bounds = self._chunk_bounds(T)
+        n = len(bounds)
+        vm = (lambda lo, hi: None) if vmask is None else (lambda lo, hi: vmask[lo:hi])
+        cnts = torch.empty((n, 2 * G + 1), dtype=torch.int32, device=dev)
+        for c, (lo, hi) in enumerate(bounds):
+            self.ops.dispatch_count(idx[lo:hi], vm(lo, hi), G, E_loc, c, out=cnts[c, :2 * G])
+        host, arrived = self._counts_tab(cnts, bounds)
+        disp = [self.ops.dispatch_pack_h(xb[lo:hi], idx[lo:hi], vm(lo, hi), G, E_loc, me, st["slot_pos"][lo:hi],
+                                         cnts[c, :2 * G], c)
+                for c, (lo, hi) in enumerate(bounds)]
+        mark(2)
+        arrived.synchronize()
+        tab = host.view(G, n, 2 * G + 1).tolist()
+        mark(3)
+        rb = disp[0][0].shape[1]
+        t_tot = [sum(tab[s][c][2 * G] for c in range(n)) for s in range(G)]
+        mcap_max = max(lib.mcl4moe_padded_rows(t, E, k) for t in t_tot)
+        sizes = {"hq": mcap_max * (F // 2), "hs": mcap_max * (F // 16)}
+        for c in range(n):
+            t_max = max(tab[s][c][2 * G] for s in range(G))
+            sizes[f"rows{c}"] = G * t_max * rb
+        px.reserve(sizes)
+        ex = dict(rows_to=[0] * G, rows_from=[0] * G, slots=[0])
+        for c in range(n):
+            ex["rows_to"] = [a + tab[me][c][g] for a, g in zip(ex["rows_to"], range(G))]
+            ex["rows_from"] = [a + tab[s][c][me] for a, s in zip(ex["rows_from"], range(G))]
+            ex["slots"][0] += sum(tab[s][c][G + me] for s in range(G))
+        self.last_exchange = ex
+
+        def rows_pieces(c):
+            base = disp[c][0].data_ptr()
+            return [(g, base + src * rb, cnt * rb, dst * rb) for g, src, cnt, dst in row_plan(tab, c, me)]
+
+        hq_dst = [px.address(s, "hq") for s in range(G)]
+        hs_dst = [px.address(s, "hs") for s in range(G)]
+        px.complete(px.issue("rows0", rows_pieces(0)))
+        mark(4)
+        for c in range(n):
+            nxt = px.issue(f"rows{c + 1}", rows_pieces(c + 1)) if c + 1 < n else None
+            R = sum(tab[s][c][me] for s in range(G))
+            slots_here = sum(tab[s][c][G + me] for s in range(G))
+            if R > 0:
+                recv = px.local(f"rows{c}", R * rb).view(R, rb)
+                self.ops.gateup_to_peers(recv, R, slots_here, d, k, self.experts, hq_dst, hs_dst, up)
+            if nxt is not None:
+                px.complete(nxt)
+        mark(5)
+        px.complete([])  # every rank's h stores into this rank's layout are done
+        mark(6)
+        mcap = lib.mcl4moe_padded_rows(T, E, k)
+        out = self.ops.down(st, px.local("hq", mcap * (F // 2)), px.local("hs", mcap * (F // 16)))
+        mark(7)
+        return out.to(x.dtype).view_as(x), stats[0], stats[1], stats[3:3 + E]
 
     def _chunk_bounds(self, T: int) -> list[tuple[int, int]]:
         """Token ranges of the chunks (``chunk_weights`` or ``chunks`` equal parts); one

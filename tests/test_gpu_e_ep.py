@@ -135,3 +135,64 @@ def test_split_dispatch_matches_one_call(moe_pkg):
         assert torch.equal(pos, pos2)
         n = int(counts[:G].sum())
         assert torch.equal(send[:n], send2[:n])
+
+
+def _emulate_h_back(pkg, moe, xs, G):
+    """G source ranks emulated on one GPU with the "h back" exchange: every source
+    routes and lays out its own tokens, receiver g runs the gate/up GEMM of the rows
+    addressed to it (sources in rank order) and stores each slot's h into its source's
+    buffers, every source runs the down projection and combine."""
+    E, k = len(moe.experts), moe.top_k
+    E_loc = E // G
+    d = xs[0].shape[1]
+    F = moe.experts[0].down_proj.weight.shape[1]
+    wr = moe.router.weight.detach().float().contiguous()
+    dn_all = pkg.get_or_build_grouped_cache(moe.experts, "down_proj")
+    lib = pkg.library()
+    ops = [pkg.CudaEPOps() for _ in range(G)]
+    st, sends, counts, hq, hs = [], [], [], [], []
+    for s in range(G):
+        state = ops[s].layout(xs[s], wr, None, None, k, moe.norm_topk_prob, dn_all, F)
+        cnt = ops[s].dispatch_count(state["idx"], None, G, E_loc)
+        send, _, _ = ops[s].dispatch_pack_h(xs[s], state["idx"], None, G, E_loc, s, state["slot_pos"], cnt)
+        mcap = lib.mcl4moe_padded_rows(xs[s].shape[0], E, k)
+        st.append(state)
+        sends.append(send)
+        counts.append(cnt.cpu().tolist())
+        hq.append(torch.zeros((mcap, F // 2), dtype=torch.uint8, device=DEV))
+        hs.append(torch.zeros((mcap * (F // 16),), dtype=torch.uint8, device=DEV))
+    for g in range(G):
+        parts, slots = [], 0
+        for s in range(G):
+            start = sum(counts[s][:g])
+            parts.append(sends[s][start:start + counts[s][g]])
+            slots += counts[s][G + g]
+        recv = torch.cat(parts, dim=0).contiguous()
+        ops[g].gateup_to_peers(recv, recv.shape[0], slots, d, k, moe.experts[g * E_loc:(g + 1) * E_loc],
+                               [t.data_ptr() for t in hq], [t.data_ptr() for t in hs])
+    outs = [ops[s].down(st[s], hq[s], hs[s]) for s in range(G)]
+    torch.cuda.synchronize()
+    return outs, st
+
+
+@pytest.mark.parametrize("G", [2, 4])
+def test_h_back_exchange_is_the_single_gpu_layer_bit_for_bit(moe_pkg, G):
+    """With the gate/up GEMMs sharded and the down projection at each token's home rank,
+    every source's output, routing and statistics equal the single-GPU layer's on its
+    tokens bit for bit (the h bytes are the same whichever rank computes them)."""
+    c = moe_case(41, 1024, 512, 16, 4, 512)
+    moe = build_module(moe_pkg, c, DEV)
+    x = x_tensor(c, DEV)
+    sizes = [1024 // G] * G  # uneven token counts per rank
+    sizes[0] += 37
+    sizes[-1] -= 37
+    xs = list(torch.split(x, sizes, dim=0))
+    xs = [t.contiguous() for t in xs]
+    outs, st = _emulate_h_back(moe_pkg, moe, xs, G)
+    for s in range(G):
+        with torch.no_grad():
+            ref = moe.forward_details(xs[s])
+        torch.cuda.synchronize()
+        assert torch.equal(st[s]["idx"], ref["topk_idx"]), s
+        assert torch.equal(outs[s], ref["out"]), s
+        assert torch.equal(st[s]["stats"][:2], torch.stack([ref["aux_loss"], ref["router_z_loss"]]).float()), s

@@ -45,8 +45,10 @@ def _worker(rank, world, port):
         c = moe_case(41, 2048, 1024, 16, 4, 512)  # same weights on every rank
         dense = build_module(pkg, c, dev)
         r = np.random.default_rng(500 + rank)
-        for transport in ("peer", "collective"):
+        for transport, h_back in (("peer", True), ("peer", False), ("collective", False)):
             ep = pkg.ExpertParallelMoE.from_dense(dense, transport=transport)
+            if not h_back:
+                ep.down_experts = None  # partial sums back
             # ranks hold different token counts; the second call is larger (the peer arena regrows)
             for T in (1536 - 512 * rank, 3072 + 256 * rank):
                 x = torch.from_numpy(r.standard_normal((T, 1024)).astype(np.float32)).to(dev, torch.bfloat16)
@@ -59,6 +61,8 @@ def _worker(rank, world, port):
                 assert rel < 5e-3, (transport, rank, T, rel)
                 assert (a - b).abs().max().item() < 1e-1
                 assert torch.equal(counts, rcounts) and float(aux) == float(raux) and float(z) == float(rz)
+                if transport == "peer" and h_back:  # the down projection ran at home: bit for bit
+                    assert torch.equal(out, ref), (rank, T)
             if ep._peer is not None:
                 ep._peer.close()
         # growth 16 -> 20 under expert parallelism (8 -> 10 experts per rank): experts 8 and 9
@@ -89,6 +93,12 @@ def _worker(rank, world, port):
         a, b = out.float(), ref.float()
         assert (torch.linalg.norm(a - b) / torch.linalg.norm(b)).item() < 5e-3
         assert torch.equal(counts, rcounts)
+        # the grown layer with h back (every rank holds the 20 experts' down projections)
+        ep.down_experts = dense20.experts
+        with torch.no_grad():
+            out, aux, z, counts = ep(x)
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref) and torch.equal(counts, rcounts)
         if ep._peer is not None:
             ep._peer.close()
         dist.barrier()
