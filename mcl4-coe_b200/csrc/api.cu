@@ -532,8 +532,11 @@ int mcl4moe_moe_forward_layout(const mcl4moe_moe_args* a, mcl4moe_stream_t strea
   st = launch_route(a->x, a->router_w, a->logit_bias, nullptr, a->valid, T, d, E, k, a->norm_topk_prob, topk_idx,
                     topk_w, a->logits_out, a->sel_mask, w.counts, a->stats, a->offs, err, w.route, s);
   if (st != MCL4MOE_OK || T == 0) return st;
+  // the layout only: the dispatched rows carry the NVFP4 codes (rows of up to 4096 elements;
+  // wider rows take the generic permute, which also writes the codes)
+  const bool codes = d / 16 > 256;
   return launch_permute_quantize(a->x, a->valid, topk_idx, topk_w, T, d, E, k, w.route, w.slot_pos, w.sorted_w,
-                                 a->perm, w.xq, w.xs, s, nullptr);
+                                 a->perm, codes ? w.xq : nullptr, codes ? w.xs : nullptr, s, nullptr);
 }
 
 int mcl4moe_moe_forward_down(const mcl4moe_moe_args* a, const uint8_t* hq, const uint8_t* hs,

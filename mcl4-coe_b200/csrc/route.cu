@@ -105,6 +105,7 @@ __global__ void __launch_bounds__(256) permute_quant_row_kernel(
   const int nblk = d / 16;
   const int token_blocks = (T + 7) / 8;
   if (int(blockIdx.x) >= token_blocks) {  // zero the scales (and bf16 copies) of the expert's padding rows
+    if (xs == nullptr) return;             // layout only
     const int e = blockIdx.x - token_blocks;
     const int start = ws.pad_start[e] + ws.counts[e];
     const int end = ws.pad_start[e + 1];
@@ -130,7 +131,7 @@ __global__ void __launch_bounds__(256) permute_quant_row_kernel(
 #pragma unroll
   for (int i = 0; i < BPL; ++i) {
     const int b = lane + 32 * i;
-    if (b < nblk) {
+    if (b < nblk && xq != nullptr) {
       const uint4* src = reinterpret_cast<const uint4*>(x + int64_t(t) * d + b * 16);
       u[i][0] = __ldg(src);
       u[i][1] = __ldg(src + 1);
@@ -149,6 +150,7 @@ __global__ void __launch_bounds__(256) permute_quant_row_kernel(
     }
     slot_pos[int64_t(t) * k + lane] = my_pos;
   }
+  if (xq == nullptr) return;  // layout only (slot positions, weights, permutation)
   uint2 pk[BPL];
   uint32_t word[BPL];
   const int base_lane = lane & ~3;
