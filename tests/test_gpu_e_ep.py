@@ -137,7 +137,7 @@ def test_split_dispatch_matches_one_call(moe_pkg):
         assert torch.equal(send[:n], send2[:n])
 
 
-def _emulate_h_back(pkg, moe, xs, G):
+def _emulate_h_back(pkg, moe, xs, G, valids=None):
     """G source ranks emulated on one GPU with the "h back" exchange: every source
     routes and lays out its own tokens, receiver g runs the gate/up GEMM of the rows
     addressed to it (sources in rank order) and stores each slot's h into its source's
@@ -152,9 +152,10 @@ def _emulate_h_back(pkg, moe, xs, G):
     ops = [pkg.CudaEPOps() for _ in range(G)]
     st, sends, counts, hq, hs = [], [], [], [], []
     for s in range(G):
-        state = ops[s].layout(xs[s], wr, None, None, k, moe.norm_topk_prob, dn_all, F)
-        cnt = ops[s].dispatch_count(state["idx"], None, G, E_loc)
-        send, _, _ = ops[s].dispatch_pack_h(xs[s], state["idx"], None, G, E_loc, s, state["slot_pos"], cnt)
+        vm = None if valids is None else valids[s]
+        state = ops[s].layout(xs[s], wr, None, vm, k, moe.norm_topk_prob, dn_all, F)
+        cnt = ops[s].dispatch_count(state["idx"], vm, G, E_loc)
+        send, _, _ = ops[s].dispatch_pack_h(xs[s], state["idx"], vm, G, E_loc, s, state["slot_pos"], cnt)
         mcap = lib.mcl4moe_padded_rows(xs[s].shape[0], E, k)
         st.append(state)
         sends.append(send)
@@ -196,3 +197,22 @@ def test_h_back_exchange_is_the_single_gpu_layer_bit_for_bit(moe_pkg, G):
         assert torch.equal(st[s]["idx"], ref["topk_idx"]), s
         assert torch.equal(outs[s], ref["out"]), s
         assert torch.equal(st[s]["stats"][:2], torch.stack([ref["aux_loss"], ref["router_z_loss"]]).float()), s
+
+
+def test_h_back_exchange_with_masked_tokens(moe_pkg):
+    """Masked tokens are neither dispatched nor combined; the rest is the single-GPU
+    layer with the same mask, bit for bit."""
+    G = 2
+    c = moe_case(43, 600, 512, 8, 2, 256)
+    moe = build_module(moe_pkg, c, DEV)
+    x = x_tensor(c, DEV)
+    xs = [t.contiguous() for t in torch.split(x, [350, 250], dim=0)]
+    r = np.random.default_rng(9)
+    valids = [torch.from_numpy((r.uniform(size=t.shape[0]) < 0.7).astype(np.uint8)).to(DEV) for t in xs]
+    outs, st = _emulate_h_back(moe_pkg, moe, xs, G, valids)
+    for s in range(G):
+        with torch.no_grad():
+            ref = moe.forward_details(xs[s], valids[s])
+        torch.cuda.synchronize()
+        assert torch.equal(st[s]["idx"], ref["topk_idx"]), s
+        assert torch.equal(outs[s], ref["out"]), s
