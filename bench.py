@@ -65,10 +65,19 @@ CONFIGS = {
     "c3": dict(name="c3_granite_zipf", seed=3, t=65536, d=1536, e=32, k=8, f=512, zipf=True),
     "c4": dict(name="c4_decode", seed=4, t=64, d=2048, e=64, k=8, f=1024),
 }
-KERNELS_PER_FORWARD = 7  # router-weight split, router, route-scan, permute+quantise, gate/up GEMM, down GEMM, combine
-# expert parallel: route (3) + dispatch count/scan/pack (3) + receive count/scan/pad/scatter (4) + 2 GEMMs + partial
-# sums (1) + combine (1)
-KERNELS_PER_EP_FORWARD = 14
+def kernels_per_forward(T: int, ep: bool = False, h_back: bool = False, chunks: int = 1) -> int:
+    """This library's kernel launches per layer forward.
+    1 GPU: routing (router-weight split, router, route-scan; one fused kernel for a single
+    128-token chunk), permute + quantise, gate/up GEMM, down GEMM, combine.
+    Expert parallel, per chunk: dispatch count / scan / pack (3) and on the receiver the
+    count / scan / pad / scatter of the received rows (4) with, for partial sums, both GEMMs and
+    the partial-sum kernel (3) and the combine (1), or for h back the gate/up GEMM (1); once:
+    routing (3), and for h back the layout permute (1), the down GEMM and the combine (2)."""
+    if not ep:
+        return (1 if T <= 128 else 3) + 4
+    if h_back:
+        return 3 + 1 + 8 * chunks + 2
+    return 3 + 11 * chunks
 EP_STAGES = ("route", "dispatch", "counts", "exchange_rows", "experts", "exchange_partials", "combine")
 EP_STAGES_H = ("route_layout", "dispatch", "counts", "exchange_rows", "gateup_h_to_home", "h_arrival", "down_combine")
 
@@ -663,7 +672,8 @@ def run_ours(args) -> None:
                                      "(MEASURED_PEAKS.json; FP4 dense = 4x BF16 dense)"}),
         "e2e": {"value": T * world / (e2e_ms / K / 1e3), "unit": UNIT, "h2d_bytes_per_step": T * d * 2,
                 "d2h_bytes_per_step": T * d * 2 + 8},
-        "gpu_launches": (KERNELS_PER_EP_FORWARD if ep else KERNELS_PER_FORWARD) * K,
+        "gpu_launches": (kernels_per_forward(T, True, moe.down_experts is not None, len(moe._chunk_bounds(T))) if ep
+                         else kernels_per_forward(T)) * K,
         "clocks": clocks,
     }
     if world == 1 and not ep and not decode:
