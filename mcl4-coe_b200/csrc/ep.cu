@@ -178,27 +178,41 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const uint16_t* __restrict
         else reinterpret_cast<float*>(row + L.weights)[lane] = wt;
       }
     }
-    // codes and scales (the activation quantiser of the single-GPU path)
-    for (int b0 = 0; b0 < nblk; b0 += 32) {
-      const int b = b0 + lane;
-      uint32_t s = 0;
-      uint2 pk = make_uint2(0, 0);
-      if (b < nblk) {
-        const uint4* src = reinterpret_cast<const uint4*>(x + int64_t(t) * d + b * 16);
-        const uint4 u0 = __ldg(src), u1 = __ldg(src + 1);
-        const uint32_t wds[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-        s = quantize_block16_bf16(wds, pk, inv_tab);
-      }
-      const int base_lane = lane & ~3;
-      uint32_t word = 0;
+    // codes and scales (the activation quantiser of the single-GPU path); the row's loads
+    // for up to four 32-block passes are issued together
+    for (int b0 = 0; b0 < nblk; b0 += 128) {
+      uint4 u[4][2];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) word |= (__shfl_sync(0xffffffffu, s, base_lane + q) & 0xFFu) << (8 * q);
-      for (int g = 0; g < G; ++g) {
-        const int p = s_pos[tl][g];
-        if (p < 0 || b >= nblk) continue;
-        uint8_t* row = send_buf + int64_t(p) * L.bytes;
-        *reinterpret_cast<uint2*>(row + L.codes + b * 8) = pk;
-        if ((lane & 3) == 0) *reinterpret_cast<uint32_t*>(row + L.scales + b) = word;
+      for (int q = 0; q < 4; ++q) {
+        const int b = b0 + 32 * q + lane;
+        if (b < nblk) {
+          const uint4* src = reinterpret_cast<const uint4*>(x + int64_t(t) * d + b * 16);
+          u[q][0] = __ldg(src);
+          u[q][1] = __ldg(src + 1);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if (b0 + 32 * q >= nblk) break;  // uniform over the warp
+        const int b = b0 + 32 * q + lane;
+        uint32_t s = 0;
+        uint2 pk = make_uint2(0, 0);
+        if (b < nblk) {
+          const uint32_t wds[8] = {u[q][0].x, u[q][0].y, u[q][0].z, u[q][0].w,
+                                   u[q][1].x, u[q][1].y, u[q][1].z, u[q][1].w};
+          s = quantize_block16_bf16(wds, pk, inv_tab);
+        }
+        const int base_lane = lane & ~3;
+        uint32_t word = 0;
+#pragma unroll
+        for (int j4 = 0; j4 < 4; ++j4) word |= (__shfl_sync(0xffffffffu, s, base_lane + j4) & 0xFFu) << (8 * j4);
+        for (int g = 0; g < G; ++g) {
+          const int p = s_pos[tl][g];
+          if (p < 0 || b >= nblk) continue;
+          uint8_t* row = send_buf + int64_t(p) * L.bytes;
+          *reinterpret_cast<uint2*>(row + L.codes + b * 8) = pk;
+          if ((lane & 3) == 0) *reinterpret_cast<uint32_t*>(row + L.scales + b) = word;
+        }
       }
     }
   }
