@@ -35,6 +35,7 @@ with ``ValueError`` like the reference's ``quantize_nvfp4`` (:245-246).
 from __future__ import annotations
 
 import ctypes
+import operator
 
 import torch
 from torch import Tensor, nn
@@ -67,10 +68,26 @@ _MASK_MODE = {"2to4_row": 1, "2to4_transposable": 2}
 
 
 def _sparsity_mode(layer: nn.Module) -> str:
-    mode = str(getattr(layer, "sparsity_mode", "none"))
+    mode = layer.__dict__.get("sparsity_mode")  # instance attribute: no nn.Module.__getattr__ walk
+    if mode is None:
+        mode = getattr(layer, "sparsity_mode", "none")
+    mode = str(mode)
     if mode not in SPARSITY_MODES:
         raise ValueError(f"sparsity mode must be one of {SPARSITY_MODES}, got {mode!r}")
     return mode
+
+
+def _submodule(module: nn.Module, name: str) -> nn.Module:
+    """``getattr(module, name)`` for a registered submodule through the module's own dict
+    (nn.Module.__getattr__ costs ~0.5 us a call, and the weight caches are checked for
+    every expert on every forward)."""
+    sub = module.__dict__.get("_modules", {}).get(name)
+    return sub if sub is not None else getattr(module, name)
+
+
+def _weight(layer: nn.Module):
+    w = layer.__dict__.get("_parameters", {}).get("weight")
+    return w if w is not None else layer.weight
 
 
 def _mask_2to4(weight: Tensor, mode: str) -> tuple[Tensor, Tensor]:
@@ -123,6 +140,47 @@ class GroupedNVFP4Cache:
         # W^T in the kernel layout (the backward's input-gradient operand), made on demand
         self.packed_t: Tensor | None = None
         self.scales_t: Tensor | None = None
+        self._owners: tuple | None = None  # what ``versions`` was read from (see still_current)
+
+    def remember_owners(self, experts: nn.ModuleList, proj_name: str, layers: list, weights: list) -> None:
+        """Record the module dicts, Parameters, versions and storages ``versions`` was read
+        from, so that the next forward can confirm them without a walk through
+        nn.Module.__getattr__ per expert (which cost ~150 us per projection at 64 experts)."""
+        self._owners = None
+        try:
+            mods = list(experts.__dict__["_modules"].values())
+            subdicts = [m.__dict__["_modules"] for m in mods]
+            pdicts = [layer.__dict__["_parameters"] for layer in layers]
+        except (KeyError, AttributeError):
+            return
+        ldicts = [layer.__dict__ for layer in layers]
+        if not (all(map(operator.is_, [sd.get(proj_name) for sd in subdicts], layers))
+                and all(map(operator.is_, [pd.get("weight") for pd in pdicts], weights))):
+            return
+        self._owners = (proj_name, mods, subdicts, list(layers), pdicts, ldicts, list(weights),
+                        [w._version for w in weights], [w.data_ptr() for w in weights],
+                        [ld.get("sparsity_mode") for ld in ldicts])
+
+    def still_current(self, experts: nn.ModuleList, proj_name: str) -> bool:
+        """True when the same expert modules hold the same projection modules, whose
+        ``weight`` Parameters are the recorded objects at the recorded ``_version`` and
+        storage, with the recorded sparsity modes and no bias: ``versions`` is then exact
+        for every expert and no slot needs quantising."""
+        own = self._owners
+        if own is None or own[0] != proj_name:
+            return False
+        _, mods, subdicts, layers, pdicts, ldicts, weights, versions, ptrs, modes = own
+        md = experts.__dict__.get("_modules")
+        if md is None or len(md) != len(mods) or not all(map(operator.is_, md.values(), mods)):
+            return False
+        if not all(map(operator.is_, [sd.get(proj_name) for sd in subdicts], layers)):
+            return False
+        if not all(map(operator.is_, [pd.get("weight") for pd in pdicts], weights)):
+            return False
+        if not all(pd.get("bias") is None for pd in pdicts):
+            return False
+        return ([w._version for w in weights] == versions and [w.data_ptr() for w in weights] == ptrs
+                and [ld.get("sparsity_mode") for ld in ldicts] == modes)
 
     def enable_transposed(self) -> None:
         """Allocate the transposed copy (packed [E, K, N/2], swizzled scales [E, K*N/16]);
@@ -134,6 +192,7 @@ class GroupedNVFP4Cache:
         self.scales_t = torch.zeros((e_count, (self.k + 127) // 128 * 128 * (self.n // 16)), dtype=torch.uint8,
                                     device=dev)
         self.versions = [None] * e_count
+        self._owners = None
 
 
 def quantize_weight_slots(weights: list[Tensor], slots: list[int], cache: GroupedNVFP4Cache,
@@ -169,19 +228,26 @@ def quantize_weight_slots(weights: list[Tensor], slots: list[int], cache: Groupe
 @torch.no_grad()
 def get_or_build_grouped_cache(experts: nn.ModuleList, proj_name: str, with_bwd: bool = False) -> GroupedNVFP4Cache:
     """src/mcl4_coe/nvfp4.py:962-1048 on the B200 kernels (see module docstring)."""
-    layers = [getattr(e, proj_name) for e in experts]
-    weights = [layer.weight for layer in layers]
+    store = experts.__dict__.get(CACHE_ATTR)
+    if store:
+        entry = store.get(proj_name)
+        if (entry is not None and (not with_bwd or entry.packed_t is not None)
+                and entry.still_current(experts, proj_name)):
+            return entry
+    layers = [_submodule(e, proj_name) for e in experts]
+    weights = [_weight(layer) for layer in layers]
     if not weights:
         raise ValueError("experts must be non-empty")
     for layer in layers:
-        if getattr(layer, "bias", None) is not None:
+        params = layer.__dict__.get("_parameters")
+        if (params.get("bias") if params is not None else getattr(layer, "bias", None)) is not None:
             raise ValueError("grouped NVFP4 experts must be bias-free (src/mcl4_coe/backbone.py:543-544)")
     e_count = len(weights)
     n, k = weights[0].shape
     device = weights[0].device
     _require_cuda(weights[0], "the NVFP4 weight cache")
-    modes = [_sparsity_mode(layer) for layer in layers]
-    cur = _current_versions(layers)
+    cur = _current_versions(layers, weights)
+    modes = [v[3] for v in cur]
     store = getattr(experts, CACHE_ATTR, None)
     if store is None:
         store = {}
@@ -199,6 +265,7 @@ def get_or_build_grouped_cache(experts: nn.ModuleList, proj_name: str, with_bwd:
     elif with_bwd and entry.packed_t is None:
         entry.enable_transposed()  # training starts: every expert also needs its transposed copy
     if entry.versions == cur:
+        entry.remember_owners(experts, proj_name, layers, weights)
         return entry
     dirty = [i for i, (old, new) in enumerate(zip(entry.versions, cur)) if old != new]
     staged = []
@@ -215,6 +282,7 @@ def get_or_build_grouped_cache(experts: nn.ModuleList, proj_name: str, with_bwd:
     entry.versions = cur
     for i in dirty:
         setattr(layers[i], SLOT_ATTR, (entry, i))
+    entry.remember_owners(experts, proj_name, layers, weights)
     return entry
 
 
@@ -252,9 +320,10 @@ def _carry_over(layers: list, cur: list, entry: GroupedNVFP4Cache) -> None:
         CACHE_STATS["carried"] += len(pairs)
 
 
-def _current_versions(layers: list) -> list:
-    return [(layer.weight._version, layer.weight.data_ptr(), tuple(layer.weight.shape), _sparsity_mode(layer))
-            for layer in layers]
+def _current_versions(layers: list, weights: list | None = None) -> list:
+    if weights is None:
+        weights = [_weight(layer) for layer in layers]
+    return [(w._version, w.data_ptr(), tuple(w.shape), _sparsity_mode(layer)) for layer, w in zip(layers, weights)]
 
 
 @torch.no_grad()
@@ -276,6 +345,7 @@ def seed_grouped_cache(experts: nn.ModuleList, proj_name: str, filled: dict) -> 
         entry = GroupedNVFP4Cache(len(layers), n, k, device)
         store[proj_name] = entry
         _carry_over(layers, cur, entry)
+    entry._owners = None  # versions change below
     for i, (packed, scales, g) in filled.items():
         entry.packed[i].copy_(packed.view(entry.packed[i].shape))
         entry.scales[i].copy_(scales.view(entry.scales[i].shape))

@@ -174,3 +174,50 @@ def test_expert_parallel_refuses_routing_variants(moe_pkg):
             moe_pkg.ExpertParallelMoE.from_dense(moe)
     finally:
         dist.destroy_process_group()
+
+
+def test_weight_cache_owner_check_sees_every_change(moe_pkg):
+    """The per-forward check of the grouped NVFP4 cache (owner snapshot instead of one
+    nn.Module attribute walk per expert) must still see each change that makes a slot
+    stale, as the reference's per-expert version keys do (src/mcl4_coe/nvfp4.py:962-1048):
+    an in-place update, a replaced Parameter, a swapped .data, a changed sparsity mode,
+    a replaced projection, growth, and an added bias."""
+    import sys
+
+    nv = sys.modules[moe_pkg.__name__ + ".nvfp4"]
+    moe = moe_pkg.SparseMoE(_cfg(moe_pkg))
+    experts = moe.experts
+    entry = nv.GroupedNVFP4Cache(len(experts), 2 * moe.experts[0].down_proj.weight.shape[1],
+                                 moe.experts[0].down_proj.weight.shape[0], torch.device("cpu"))
+
+    def remember():
+        layers = [e.up_proj for e in experts]
+        entry.remember_owners(experts, "up_proj", layers, [lay.weight for lay in layers])
+        assert entry.still_current(experts, "up_proj")
+        assert not entry.still_current(experts, "down_proj")
+
+    remember()
+    with torch.no_grad():
+        experts[1].up_proj.weight.mul_(2.0)
+    assert not entry.still_current(experts, "up_proj")
+    remember()
+    experts[0].up_proj.weight = torch.nn.Parameter(experts[0].up_proj.weight.detach().clone())
+    assert not entry.still_current(experts, "up_proj")
+    remember()
+    experts[2].up_proj.weight.data = experts[2].up_proj.weight.detach().clone()
+    assert not entry.still_current(experts, "up_proj")
+    remember()
+    experts[3].up_proj.sparsity_mode = "2to4_row"
+    assert not entry.still_current(experts, "up_proj")
+    del experts[3].up_proj.sparsity_mode
+    remember()
+    old = experts[1].up_proj
+    experts[1].up_proj = torch.nn.Linear(old.in_features, old.out_features, bias=False)
+    assert not entry.still_current(experts, "up_proj")
+    remember()
+    experts.append(type(experts[0])(experts[0].up_proj.in_features, experts[0].down_proj.in_features))
+    assert not entry.still_current(experts, "up_proj")
+    del experts[len(experts) - 1]
+    assert entry.still_current(experts, "up_proj")
+    experts[0].up_proj.bias = torch.nn.Parameter(torch.zeros(experts[0].up_proj.out_features))
+    assert not entry.still_current(experts, "up_proj")
