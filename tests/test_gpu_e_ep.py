@@ -40,7 +40,7 @@ def _emulate(pkg, moe, x, G, valid=None):
     return out, dict(idx=idx, w=w, send=send, rows=rows, slots=slots, pos=pos, stats=stats)
 
 
-@pytest.mark.parametrize("G", [2, 4])
+@pytest.mark.parametrize("G", [2, 4, 8])
 def test_emulated_ranks_match_single_gpu_layer(moe_pkg, G):
     c = moe_case(31, 1024, 512, 16, 4, 512)
     moe = build_module(moe_pkg, c, DEV)
@@ -176,7 +176,7 @@ def _emulate_h_back(pkg, moe, xs, G, valids=None):
     return outs, st
 
 
-@pytest.mark.parametrize("G", [2, 4])
+@pytest.mark.parametrize("G", [2, 4, 8])
 def test_h_back_exchange_is_the_single_gpu_layer_bit_for_bit(moe_pkg, G):
     """With the gate/up GEMMs sharded and the down projection at each token's home rank,
     every source's output, routing and statistics equal the single-GPU layer's on its
