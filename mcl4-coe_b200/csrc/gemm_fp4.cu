@@ -81,6 +81,10 @@ constexpr uint32_t kIdesc = idesc_nvf4(256, 256);
 constexpr uint32_t kIdescSolo = idesc_nvf4(128, 256);
 constexpr uint32_t kBarBytes = 256;
 constexpr uint32_t kWarpStoreBytes = 32 * 64 * 2;  // one epilogue warp's 32 rows x 64 bf16 (MODES 1, 3)
+// MODE 4: per TMEM lane quarter, the tile's 32 rows of h assembled from its four column
+// warps before they leave for the peers: codes 32 x 64 B, scales 32 x 8 B, destinations 32 x 4 B
+constexpr uint32_t kH4Codes = 0, kH4Scales = 32 * 64, kH4Dst = kH4Scales + 32 * 8;
+constexpr uint32_t kH4Quarter = kH4Dst + 32 * 4;
 
 // SOLO: each CTA computes its own 128 x 256 tiles with cta_group::1 MMAs (M = 128),
 // staging the full 256 B rows of the tile; used when experts hold few rows
@@ -91,7 +95,8 @@ struct Cfg {
   static constexpr uint32_t kStage = kAB + kSFBytes;
   static constexpr uint32_t kOffSfa = kAB, kOffSfb = kAB + kSFA;
   static constexpr int kStages = SOLO ? 4 : ((MODE == 0 || MODE == 4) ? 5 : 4);
-  static constexpr uint32_t kStoreBytes = (!SOLO && (MODE == 1 || MODE == 3)) ? kEpiWarps * kWarpStoreBytes : 0;
+  static constexpr uint32_t kStoreBytes = (!SOLO && (MODE == 1 || MODE == 3)) ? kEpiWarps * kWarpStoreBytes
+                                          : (MODE == 4 ? 4 * kH4Quarter : 0);
   static constexpr size_t kSmem = 1024 /*align*/ + size_t(kStages) * kStage + kStoreBytes + kBarBytes +
                                   sizeof(int32_t) * (kMaxExperts + 1) + sizeof(float) * 128;
 };
@@ -105,6 +110,7 @@ static_assert(Cfg<0, true>::kStage % 1024 == 0, "solo stage alignment");
 static_assert(kSfCol0 + Cfg<0, true>::kStages * kSfColsPerStage <= kTmemCols, "TMEM budget (solo)");
 static_assert(kSfCol0 + Cfg<0>::kStages * kSfColsPerStage <= kTmemCols, "TMEM budget");
 static_assert(8 * (3 * Cfg<0>::kStages + 2) + 4 <= kBarBytes, "barrier area");
+static_assert(8 * (3 * Cfg<4>::kStages + 3) + 8 * 8 <= kBarBytes, "barrier area (mode 4 quarter barriers)");
 static_assert(kSegRows == 2 * kBM, "a CTA pair covers one 256-row segment block");
 
 struct TileCoord {
@@ -145,6 +151,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const uint32_t tfull_bar = bar_base + 8u * (3 * S);       // accumulator ready (both CTAs)
   const uint32_t tempty_bar = bar_base + 8u * (3 * S + 1);  // even CTA: both epilogues read it
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + (bar_base - base) + 8 * (3 * S + 2));
+  // MODE 4: per lane quarter, "the four column warps staged their h" and "... wrote it out"
+  auto h4_staged = [&](int q) { return bar_base + 8u * (3 * S + 3 + q); };
+  auto h4_drained = [&](int q) { return bar_base + 8u * (3 * S + 7 + q); };
   int32_t* pad_s = reinterpret_cast<int32_t*>(smem + (bar_base - base) + kBarBytes);
   float* s_inv = reinterpret_cast<float*>(pad_s + kMaxExperts + 1);  // 1/decoded scale per E4M3 code
 
@@ -166,6 +175,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
     mbar_init(tfull_bar, 1);
     mbar_init(tempty_bar, (SOLO ? 1 : 2) * kEpiWarps);
+    if (MODE == 4)
+      for (int q = 0; q < 4; ++q) {
+        mbar_init(h4_staged(q), 4);
+        mbar_init(h4_drained(q), 4);
+      }
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -407,7 +421,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t lane_addr = tmem_base + (uint32_t(q * 32) << 16);
     const uint32_t tempty_leader = map_shared_rank(tempty_bar, 0);
     const uint32_t my_buf = store_base + uint32_t(warp - kEpiWarp0) * kWarpStoreBytes;
-    uint32_t acc_phase = 0;
+    uint8_t* const h4q = smem + (store_base - base) + uint32_t(q) * kH4Quarter;  // MODE 4 staging
+    uint32_t acc_phase = 0, h4_phase = 0;
+    bool h4_first = true;
     for (int t = pair; t < total_tiles; t += npairs) {
       const TileCoord c = coord(t);
       if (!live(c)) continue;
@@ -512,15 +528,41 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         if (MODE == 4) {
           // expert parallelism: h goes straight to the token's home GPU (peer stores over
-          // NVLink into its expert-major layout), where the down projection runs
-          if (hdst >= 0) {
-            const int rk = hdst >> 28;
-            const uint64_t row = uint64_t(hdst & 0x0FFFFFFF);
-            *reinterpret_cast<uint4*>(args.peer_hq[rk] + row * (F / 2) + hb0 * 8) =
-                make_uint4(packed[0], packed[1], packed[2], packed[3]);
-            *reinterpret_cast<uint16_t*>(args.peer_hs[rk] + swizzled_scale_offset(row, uint32_t(hb0), uint32_t(F / 16))) =
-                uint16_t(sword);
+          // NVLink into its expert-major layout), where the down projection runs.  The four
+          // column warps of this lane quarter first assemble their rows in shared memory, so
+          // that each row leaves as one 64-byte run of codes and two 4-byte scale words
+          // instead of four 16-byte and four 2-byte stores.
+          bool h4_ok = true;
+          if (!h4_first) h4_ok = mbar_wait(h4_drained(q), h4_phase ^ 1u, args.err, 331);  // previous tile out
+          *reinterpret_cast<uint4*>(h4q + kH4Codes + lane * 64 + sub * 16) =
+              make_uint4(packed[0], packed[1], packed[2], packed[3]);
+          *reinterpret_cast<uint16_t*>(h4q + kH4Scales + lane * 8 + sub * 2) = uint16_t(sword);
+          if (sub == 0) *reinterpret_cast<int32_t*>(h4q + kH4Dst + lane * 4) = hdst;
+          __syncwarp();
+          if (lane == 0) mbar_arrive(h4_staged(q));
+          h4_ok = mbar_wait(h4_staged(q), h4_phase, args.err, 332) && h4_ok;
+          if (!h4_ok) break;
+          {
+            const int i = sub * 32 + lane;  // one 16-byte piece of the 32 rows' codes per thread
+            const int r = i >> 2, ch = i & 3;
+            const int32_t dst = *reinterpret_cast<const int32_t*>(h4q + kH4Dst + r * 4);
+            if (dst >= 0)
+              *reinterpret_cast<uint4*>(args.peer_hq[dst >> 28] + uint64_t(dst & 0x0FFFFFFF) * (F / 2) + c.nt * 64 +
+                                        ch * 16) = *reinterpret_cast<const uint4*>(h4q + kH4Codes + r * 64 + ch * 16);
+            if (i < 64) {  // the 8 scales of a row: blocks nt*8 .. nt*8+3 and nt*8+4 .. nt*8+7, one word each
+              const int rr = i >> 1, w = i & 1;
+              const int32_t d2 = *reinterpret_cast<const int32_t*>(h4q + kH4Dst + rr * 4);
+              if (d2 >= 0)
+                *reinterpret_cast<uint32_t*>(args.peer_hs[d2 >> 28] +
+                                             swizzled_scale_offset(uint64_t(d2 & 0x0FFFFFFF), uint32_t(c.nt * 8 + 4 * w),
+                                                                   uint32_t(F / 16))) =
+                    *reinterpret_cast<const uint32_t*>(h4q + kH4Scales + rr * 8 + w * 4);
+            }
           }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(h4_drained(q));
+          h4_phase ^= 1u;
+          h4_first = false;
         } else {
           *reinterpret_cast<uint4*>(args.hq + p * (F / 2) + hb0 * 8) =
               make_uint4(packed[0], packed[1], packed[2], packed[3]);
